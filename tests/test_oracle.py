@@ -1,0 +1,211 @@
+"""Pins the CPU oracle before anything is checked against it.
+
+1. Against reef's own golden vectors (tests/golden, written by the reference's
+   gen_golden.cpp): bit for bit.
+2. Against reef's known-answer tests (inference-engine/reference/cpp/tests/
+   test_quant.cpp, test_int8.cpp), restated here.
+3. Against reef's engine compiled in place (oracle/_ref) on fresh seeded
+   inputs, where that library was built.
+No GPU is needed.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as ro
+from tests import goldens
+
+
+def bits(a):
+    a = np.asarray(a)
+    return a.view(np.uint32) if a.dtype == np.float32 else a
+
+
+# ---- 1. golden vectors -----------------------------------------------------
+
+@pytest.mark.parametrize("table", ["kW8a8", "kW8a8Bias"])
+def test_w8a8_linear_matches_reef_goldens(table):
+    for c in goldens.cases("linear", table):
+        x = c["x"].reshape(c["rows"], c["in"])
+        w = c["qt"].reshape(c["in"], c["out"]).T  # [in][out] -> [out][in]
+        y = ro.linear_w8a8(x, w, c["qs"], c.get("bias"))
+        np.testing.assert_array_equal(bits(y.ravel()), bits(c["y"]))
+
+
+@pytest.mark.parametrize("table", ["kInt8Linear", "kInt8LinearBias"])
+def test_int8_linear_matches_reef_goldens(table):
+    for c in goldens.cases("int8", table):
+        x = c["x"].reshape(c["rows"], c["in"])
+        w = c["wt"].reshape(c["in"], c["out"]).T
+        y = ro.linear_int8(x, w, c["shift"], c.get("bias"))
+        np.testing.assert_array_equal(y.ravel(), c["y"])
+
+
+def test_softmax_int8_matches_reef_goldens():
+    for c in goldens.cases("int8", "kInt8Softmax"):
+        np.testing.assert_array_equal(ro.exp_table(), c["table"])
+        s = c["scores"].reshape(c["rows"], c["n"])
+        p = ro.softmax_int8(s, c["shift"], c["table"])
+        np.testing.assert_array_equal(p.ravel(), c["probs"])
+
+
+def test_attention_int8_matches_reef_goldens():
+    for c in goldens.cases("int8", "kInt8Attention"):
+        d = c["head_dim"]
+        y = ro.attention_head_int8(
+            c["q"].reshape(-1, d), c["k"].reshape(-1, d), c["v"].reshape(-1, d),
+            c["query_start"], c["window"], c["score_shift"], c["out_shift"],
+            c["table"])
+        np.testing.assert_array_equal(y.ravel(), c["y"])
+
+
+def test_attention_f32_matches_reef_goldens():
+    for c in goldens.cases("attention", "kAttention"):
+        d = c["head_dim"]
+        y = ro.attention_head_f32(
+            c["q"].reshape(-1, d), c["k"].reshape(-1, d), c["v"].reshape(-1, d),
+            c["query_start"], c["window"])
+        np.testing.assert_array_equal(bits(y.ravel()), bits(c["y"]))
+
+
+def test_exp_tanh_gelu_match_reef_goldens():
+    (e,) = goldens.cases("math", "kExp")
+    np.testing.assert_array_equal(bits(ro.exp_nonpositive(e["x"])), bits(e["y"]))
+    (g,) = goldens.cases("math", "kGelu")
+    np.testing.assert_array_equal(bits(ro.gelu(g["x"])), bits(g["y"]))
+
+
+def test_layernorm_matches_reef_goldens():
+    for c in goldens.cases("layernorm", "kLayerNorm"):
+        x = c["x"].reshape(c["rows"], c["width"])
+        y = ro.layernorm(x, c["gain"], c["shift"], np.float32(c["eps"]))
+        np.testing.assert_array_equal(bits(y.ravel()), bits(c["y"]))
+
+
+# ---- 2. reef's known-answer tests -------------------------------------------
+
+def test_quant_kats():
+    # test_quant.cpp:38-53
+    f = ro.lib().ro_int8_scale
+    assert f(254.0) == 2.0 and f(127.0) == 1.0 and f(0.0) == 1.0
+    q, s = ro.quantize_rows(np.array(
+        [[254.0, 127.0, -127.0], [0, 0, 0], [1.0, -0.5, 0.25]], np.float32))
+    assert list(q[0]) == [127, 64, -64] and s[0] == 2.0  # 63.5 ties to 64
+    assert s[1] == 1.0 and list(q[1]) == [0, 0, 0]
+    assert s[2] == np.float32(1.0) / np.float32(127.0) and q[2, 0] == 127
+    q, _ = ro.quantize_rows(np.array([[2.5, 3.5, -2.5, 2.4, 127.0]], np.float32))
+    assert list(q[0]) == [2, 4, -2, 2, 127]
+
+
+def test_w8a8_hand_computed_kat():
+    # test_quant.cpp:78-95
+    x = np.array([[127.0, -2.5, 3.5]], np.float32)
+    wq, ws = ro.quantize_rows(np.array(
+        [[1.0, 0.0, -1.0], [254.0, 127.0, -127.0]], np.float32))
+    y = ro.linear_w8a8(x, wq, ws, np.array([0.5, -1.0], np.float32))
+    first = np.float32(15621.0) * (np.float32(1.0) * (np.float32(1.0) / np.float32(127.0)))
+    assert y[0, 0] == first + np.float32(0.5)
+    assert y[0, 1] == np.float32(15745.0) * np.float32(2.0) - np.float32(1.0)
+
+
+def test_int8_kats():
+    # test_int8.cpp:37-86, 117-159
+    rs = ro.rounding_shift
+    assert [rs(3, 1), rs(-3, 1), rs(5, 2), rs(6, 2), rs(-6, 2), rs(-7, 2),
+            rs(-7, 0)] == [2, -1, 1, 2, -1, -2, -7]
+    assert [ro.saturate_int8(v) for v in (127, 128, -128, -100000)] == \
+        [127, 127, -128, -128]
+    x = np.array([[1, 2]], np.int8)
+    w = np.array([[3, -4], [127, 127]], np.int8)
+    y = ro.linear_int8(x, w, 2, np.array([100, 0], np.int32))
+    assert list(y[0]) == [24, 95]
+    assert ro.linear_int8(x, w, 0)[0, 1] == 127
+    t = ro.exp_table()
+    assert t[0] == 32768 and t[16] == 12055 and t[255] == 0
+    assert np.all(np.diff(t.astype(np.int32)) <= 0)
+    p = ro.softmax_int8(np.array([[5, 5]], np.int32), 0)
+    assert list(p[0]) == [128, 128]
+
+
+# ---- 3. the engine itself, compiled in place --------------------------------
+
+needs_ref = pytest.mark.skipif(not ro.ref_available(),
+                               reason="oracle/_ref not built")
+
+
+def _c(a, t):
+    return a.ctypes.data_as(t)
+
+
+@needs_ref
+@pytest.mark.parametrize("rows,k,n,seed", [(5, 96, 40, 11), (17, 130, 33, 12),
+                                           (1, 256, 64, 13)])
+def test_w8a8_matches_engine(rows, k, n, seed):
+    import ctypes as C
+    x = ro.normal(seed, (rows, k))
+    x[0] = 0.0  # the all-zero scale
+    w, ws = ro.quantize_rows(ro.normal(seed + 100, (n, k), 0.0, 0.02))
+    b = ro.normal(seed + 200, (n,), 0.0, 0.02)
+    want = np.empty((rows, n), np.float32)
+    rc = ro.ref().ref_linear_w8a8(rows, k, n, _c(x, C.POINTER(C.c_float)),
+                                  _c(w, C.POINTER(C.c_int8)),
+                                  _c(ws, C.POINTER(C.c_float)),
+                                  _c(b, C.POINTER(C.c_float)),
+                                  _c(want, C.POINTER(C.c_float)))
+    assert rc == 0
+    got = ro.linear_w8a8(x, w, ws, b)
+    np.testing.assert_array_equal(bits(got), bits(want))
+
+
+@needs_ref
+def test_attention_int8_matches_engine():
+    import ctypes as C
+    i8 = C.POINTER(C.c_int8)
+    for (ql, kl, d, qs, win, sh, seed) in [(7, 33, 32, 26, 0, 8, 1),
+                                           (9, 40, 16, 31, 5, 6, 2),
+                                           (64, 64, 64, 0, 0, 10, 3)]:
+        q = ro.int8_uniform(seed, (ql, d))
+        k = ro.int8_uniform(seed + 1, (kl, d))
+        v = ro.int8_uniform(seed + 2, (kl, d))
+        want = np.empty((ql, d), np.int8)
+        assert ro.ref().ref_attend_head_int8(ql, kl, d, qs, win, _c(q, i8),
+                                             _c(k, i8), _c(v, i8), sh, 8,
+                                             _c(want, i8)) == 0
+        got = ro.attention_head_int8(q, k, v, qs, win, sh, 8)
+        np.testing.assert_array_equal(got, want)
+
+
+@needs_ref
+def test_gptneo_block_matches_engine():
+    """Config 1 shape (d 256, 4 heads, FFN 1024) at a short sequence."""
+    import ctypes as C
+    f = C.POINTER(C.c_float)
+    seq, d, heads, ffn = 16, 256, 4, 1024
+    fw = block_float_weights(d, ffn, seed=70)
+    x = ro.normal(69, (seq, d))
+    want = np.empty((seq, d), np.float32)
+    args = [fw[k] for k in ("ln1_g", "ln1_b", "wq", "wk", "wv", "wo", "bo",
+                            "ln2_g", "ln2_b", "wfc", "bfc", "wproj", "bproj")]
+    rc = ro.ref().ref_block_w8a8(seq, d, heads, ffn, 0, 0, np.float32(1e-5),
+                                 _c(x, f), *[_c(a, f) for a in args],
+                                 _c(want, f))
+    assert rc == 0
+    got = ro.gptneo_block_w8a8(x, ro.quantize_block(fw), heads)
+    np.testing.assert_array_equal(bits(got), bits(want))
+
+
+def block_float_weights(d, ffn, seed):
+    """Config-1 block weights: projections N(0, 0.02), biases N(0, 0.02),
+    LayerNorm gains 1 and shifts 0."""
+    return {
+        "ln1_g": np.ones(d, np.float32), "ln1_b": np.zeros(d, np.float32),
+        "ln2_g": np.ones(d, np.float32), "ln2_b": np.zeros(d, np.float32),
+        "wq": ro.normal(seed + 1, (d, d), 0, 0.02),
+        "wk": ro.normal(seed + 2, (d, d), 0, 0.02),
+        "wv": ro.normal(seed + 3, (d, d), 0, 0.02),
+        "wo": ro.normal(seed + 4, (d, d), 0, 0.02),
+        "bo": ro.normal(seed + 5, (d,), 0, 0.02),
+        "wfc": ro.normal(seed + 6, (ffn, d), 0, 0.02),
+        "bfc": ro.normal(seed + 7, (ffn,), 0, 0.02),
+        "wproj": ro.normal(seed + 8, (d, ffn), 0, 0.02),
+        "bproj": ro.normal(seed + 9, (d,), 0, 0.02),
+    }
