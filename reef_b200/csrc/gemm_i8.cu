@@ -1,0 +1,349 @@
+// gemm_i8.cu -- int8 x int8 -> int32 GEMM on sm_100a tensor cores
+// (tcgen05.mma kind::i8) with fused requantisation epilogues.
+//
+//   D[m][n] = sum_k A[m][k] * B[n][k]       A: [M][lda] int8, B: [N][ldb] int8
+//
+// Both operands are K-major, which is the engine's own layout: activations
+// are rows of in_features, weights are QuantizedWeight [out][in]
+// (quant.hpp:38-43 of reef's inference engine).  Integer sums are
+// order-free, so the accumulation order of the tensor cores gives exactly the
+// sums of matmul<int8,int32> (tensor.hpp:178-246).
+//
+// Epilogues (all read the int32 accumulator from TMEM):
+//   kF32W8A8  y = float(acc) * (x_scale[m] * w_scale[n])  [+ bias[n]]
+//             -- linear() W8A8, operator/linear.hpp:122-130, each step a
+//                single round-to-nearest IEEE operation (__fmul_rn/__fadd_rn).
+//   kI8Shift  y = sat8(rounding_shift(acc [+ bias32[n]], shift))
+//             -- linear_int8, int8.hpp:74-101.
+//   kI32      y = acc   (the raw partial sums of a row-parallel shard)
+//
+// Kernel structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: 128 x 128-byte A tile and BN x 128-byte B tile
+//               per stage, 128-byte swizzle, STAGES-deep mbarrier ring.
+//   warp 1      allocates TMEM; one elected thread issues tcgen05.mma
+//               (128 x BN x 32 per instruction, 4 per stage) into one of two
+//               TMEM accumulators, commits stage frees and accumulator-ready
+//               to mbarriers.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)...), requantise, transpose through shared
+//               memory so each store instruction writes contiguous bytes of
+//               one output row, then release the accumulator.
+// Double-buffered accumulators let the epilogue of tile i overlap the MMAs of
+// tile i+1.  No TMA multicast anywhere.
+#include "common.cuh"
+#include "ops.h"
+
+#include <algorithm>
+
+namespace reef {
+
+namespace {
+
+constexpr int kBM = 128;         // UMMA M (TMEM lanes)
+constexpr int kBK = 128;         // bytes of K per stage (one 128-byte swizzle row)
+constexpr int kUmmaK = 32;       // K per tcgen05.mma kind::i8
+constexpr int kThreads = 192;    // 6 warps
+constexpr int kEpiWarps = 4;
+constexpr int kTransposeFloats = 32 * 33;  // per epilogue warp
+
+template <int BN, int STAGES>
+struct Layout {
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = BN * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTransposeOff = STAGES * kStageBytes;
+  static constexpr int kBarOff = kTransposeOff + kEpiWarps * kTransposeFloats * 4;
+  // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
+  static constexpr int kNumBars = 2 * STAGES + 5;
+  static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+  static constexpr int kBytes = kTmemSlotOff + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack to align the base
+  static_assert(kAlloc <= 232448, "shared memory budget");
+  static_assert((kStageBytes % 1024) == 0, "stages stay 1024-byte aligned");
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group,
+                                            int& mb, int& nb) {
+  // Grouped raster: `group` m-blocks walk the n-blocks together, so the CTAs
+  // in flight share B tiles (weights) and A tiles in L2.
+  const int per_group = group * num_n;
+  const int g = t / per_group;
+  const int first_m = g * group;
+  const int gsize = min(group, num_m - first_m);
+  const int r = t - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a,
+                   const __grid_constant__ CUtensorMap tma_b, GemmArgs args) {
+  using L = Layout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlotOff);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int M = args.M, N = args.N, K = args.K;
+  const int num_m = (M + kBM - 1) / kBM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_k = (K + kBK - 1) / kBK;
+  const int num_tiles = num_m * num_n;
+  int* err = args.err;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps * 32);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, args.group_m, mb, nb);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          tma_load_2d(sa, &tma_a, &full[stage], kb * kBK, mb * kBM);
+          tma_load_2d(sb, &tma_b, &full[stage], kb * kBK, nb * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Copies still in flight land before the CTA may exit: wait (bounded)
+      // for the last load issued into each stage.
+      const long long tail = issued < STAGES ? issued : STAGES;
+      for (long long i = 0; i < tail; ++i) {
+        // walk back from the most recent issue
+        int s = stage - 1 - static_cast<int>(i);
+        uint32_t ph = phase;
+        while (s < 0) {
+          s += STAGES;
+          ph ^= 1u;
+        }
+        mbar_wait(&full[s], ph, err, kDevTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_i8(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, err, kDevTimeoutAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+            mma_i8(d_tmem, smem_desc_k_sw128(sa + kk * kUmmaK),
+                   smem_desc_k_sw128(sb + kk * kUmmaK), kIdesc,
+                   (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Every MMA issued by this thread completes before TMEM is released.
+      mma_commit(drain);
+      mbar_wait(drain, 0, err, kDevTimeoutDrain);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may read
+    float* tbuf = reinterpret_cast<float*>(smem + L::kTransposeOff) +
+                  (warp - 2) * kTransposeFloats;
+    uint32_t* tbuf_u = reinterpret_cast<uint32_t*>(tbuf);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, args.group_m, mb, nb);
+      if (!mbar_wait(&acc_full[acc], acc_phase, err, kDevTimeoutAccFull)) break;
+      tc_fence_after();
+      const int row0 = mb * kBM + q * 32;  // first output row of this warp
+      const int my_row = row0 + lane;
+      float row_scale = 0.0f;
+      if constexpr (EPI == kEpiF32W8A8) {
+        if (my_row < M) row_scale = args.x_scale[my_row];
+      }
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = nb * BN + c * 32;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                               static_cast<uint32_t>(acc * BN + c * 32),
+                           r);
+        tmem_ld_wait();
+        if (col0 < N) {
+          // compute this thread's 32 outputs (row my_row, columns col0..+31)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = col0 + j;
+            const int nn = n < N ? n : N - 1;
+            const int32_t a = static_cast<int32_t>(r[j]);
+            if constexpr (EPI == kEpiF32W8A8) {
+              const float combined = __fmul_rn(row_scale, args.w_scale[nn]);
+              float v = __fmul_rn(__int2float_rn(a), combined);
+              if (args.bias_f != nullptr) v = __fadd_rn(v, args.bias_f[nn]);
+              tbuf[lane * 33 + j] = v;
+            } else if constexpr (EPI == kEpiI8Shift) {
+              int32_t s = a;
+              if (args.bias_i != nullptr) s += args.bias_i[nn];
+              tbuf_u[lane * 33 + j] =
+                  static_cast<uint32_t>(static_cast<uint8_t>(requant_rnu_sat8(s, args.shift)));
+            } else {
+              tbuf_u[lane * 33 + j] = r[j];
+            }
+          }
+          __syncwarp();
+          // write out: iteration j stores row (row0 + j), 32 consecutive columns
+          const int n = col0 + lane;
+          if (n < N) {
+#pragma unroll 4
+            for (int j = 0; j < 32; ++j) {
+              const int m = row0 + j;
+              if (m < M) {
+                const long long off = static_cast<long long>(m) * args.ldy + n;
+                if constexpr (EPI == kEpiF32W8A8) {
+                  static_cast<float*>(args.y)[off] = tbuf[j * 33 + lane];
+                } else if constexpr (EPI == kEpiI8Shift) {
+                  static_cast<int8_t*>(args.y)[off] =
+                      static_cast<int8_t>(tbuf_u[j * 33 + lane]);
+                } else {
+                  static_cast<int32_t*>(args.y)[off] =
+                      static_cast<int32_t>(tbuf_u[j * 33 + lane]);
+                }
+              }
+            }
+          }
+          __syncwarp();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+template <int BN, int STAGES, int EPI>
+int launch(const GemmProblem& p, cudaStream_t stream) {
+  using L = Layout<BN, STAGES>;
+  CUtensorMap ma, mb;
+  int rc = make_tma_2d_i8(&ma, p.a, p.M, p.K, p.lda, kBK, kBM);
+  if (rc) return rc;
+  rc = make_tma_2d_i8(&mb, p.b, p.N, p.K, p.ldb, kBK, BN);
+  if (rc) return rc;
+  auto kernel = gemm_i8_kernel<BN, STAGES, EPI>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             L::kAlloc) != cudaSuccess)
+      return kErrCuda;
+    configured[dev] = true;
+  }
+  const int num_tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+  const int grid = std::min(num_tiles, num_sms());
+  GemmArgs args = p.args;
+  args.M = p.M;
+  args.N = p.N;
+  args.K = p.K;
+  if (args.group_m <= 0) args.group_m = 8;
+  args.err = device_error_ptr();
+  kernel<<<grid, kThreads, L::kAlloc, stream>>>(ma, mb, args);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+}  // namespace
+
+int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream) {
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return kErrInvalid;
+  const bool wide = p.N > 128;
+  switch (epilogue) {
+    case kEpiF32W8A8:
+      return wide ? launch<256, 4, kEpiF32W8A8>(p, stream)
+                  : launch<128, 6, kEpiF32W8A8>(p, stream);
+    case kEpiI8Shift:
+      return wide ? launch<256, 4, kEpiI8Shift>(p, stream)
+                  : launch<128, 6, kEpiI8Shift>(p, stream);
+    case kEpiI32:
+      return wide ? launch<256, 4, kEpiI32>(p, stream)
+                  : launch<128, 6, kEpiI32>(p, stream);
+    default:
+      return kErrInvalid;
+  }
+}
+
+}  // namespace reef

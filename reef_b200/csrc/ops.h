@@ -1,0 +1,86 @@
+// ops.h -- internal C++ interface of libreef_b200 (kernel launchers).
+//
+// The public surface is the C ABI in include/reef_b200.h; capi.cpp validates
+// arguments and forwards here.  Every launcher returns a status code from the
+// enum below (the same values as REEF_B200_* in the public header).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace reef {
+
+enum Status : int {
+  kOk = 0,
+  kErrInvalid = 1,
+  kErrAlignment = 2,
+  kErrCuda = 3,
+  kErrUnsupported = 4,
+  kErrNccl = 5,
+  kErrTimeout = 6,
+  kErrTooLarge = 7,
+};
+
+enum Epilogue : int {
+  kEpiF32W8A8 = 0,  // y = float(acc) * (x_scale[m] * w_scale[n]) [+ bias[n]]
+  kEpiI8Shift = 1,  // y = sat8(rnu_shift(acc [+ bias32[n]], shift))
+  kEpiI32 = 2,      // y = acc
+};
+
+// Row stride (bytes) of every int8 matrix the tensor cores read: TMA needs
+// 16-byte aligned row strides.
+inline size_t kpad(size_t in) { return (in + 15) / 16 * 16; }
+
+struct GemmArgs {
+  int M, N, K;
+  const float* x_scale;   // [M]   (kEpiF32W8A8)
+  const float* w_scale;   // [N]   (kEpiF32W8A8)
+  const float* bias_f;    // [N] or null (kEpiF32W8A8)
+  const int32_t* bias_i;  // [N] or null (kEpiI8Shift)
+  void* y;                // [M][ldy] output
+  long long ldy;          // elements
+  uint32_t shift;         // kEpiI8Shift
+  int group_m;            // raster group (0 = default)
+  int* err;               // device error word (set by the launcher)
+};
+
+struct GemmProblem {
+  int M, N, K;
+  const int8_t* a;  // [M][lda]
+  long long lda;    // bytes, multiple of 16
+  const int8_t* b;  // [N][ldb]
+  long long ldb;    // bytes, multiple of 16
+  GemmArgs args;
+};
+
+// ---- device plumbing (device.cu) ----------------------------------------------
+int num_sms();
+int* device_error_ptr();               // this device's error word
+int check_device();                    // kOk on sm_100, else kErrUnsupported
+int read_device_error(int* code);      // synchronizes, returns and clears
+int make_tma_2d_i8(CUtensorMap* map, const void* base, long long rows,
+                   long long cols, long long ld_bytes, int box_cols, int box_rows);
+int make_tma_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes,
+                const void* base, long long rows, long long cols, long long ld_elems,
+                int box_cols, int box_rows, CUtensorMapSwizzle swizzle);
+
+// ---- kernels ------------------------------------------------------------------
+int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream);
+
+// quant.cu
+int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q,
+                  long long ldq, float* x_scale, const float* row_max,
+                  cudaStream_t stream);
+int row_absmax(long long rows, long long in, const float* x, float* row_max,
+               cudaStream_t stream);
+int pack_weight_i8(long long in, long long out, const int8_t* wt, int8_t* w,
+                   long long ldw, cudaStream_t stream);
+int pad_rows_i8(long long rows, long long in, const int8_t* x, long long ldx,
+                int8_t* y, long long ldy, cudaStream_t stream);
+int w8a8_epilogue_i32(long long rows, long long out, const int32_t* acc,
+                      const float* x_scale, const float* w_scale, const float* bias,
+                      float* y, cudaStream_t stream);
+
+}  // namespace reef

@@ -1,0 +1,215 @@
+// quant.cu -- per-token activation quantisation and int8 repacking.
+//
+// quantize_rows follows reef's quant.hpp:90-133 bit for bit:
+//   scale = max|x| > 0 ? max|x| / 127 : 1          (int8_scale, :51-57)
+//   q     = clamp(nearbyint(x / scale), -127, 127)  (quantize_int8, :68-81)
+// The maximum is order-free; x / scale is one IEEE division (__fdiv_rn) and
+// nearbyint in the default mode is round-half-to-even (__float2int_rn).
+// These passes are HBM-bound: one read of x (4 B/elem) and one write of
+// x_q (1 B/elem); each CTA owns one row and keeps it in registers when it
+// fits, so x is read from HBM once.
+#include "common.cuh"
+#include "ops.h"
+
+namespace reef {
+
+namespace {
+
+constexpr int kQuantThreads = 256;
+constexpr int kCache = 16;  // float4 per thread kept in registers (16 KiB rows)
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (blockDim.x >> 5) ? red[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ int8_t q8(float x, float scale) {
+  int v = __float2int_rn(__fdiv_rn(x, scale));
+  v = v < -127 ? -127 : (v > 127 ? 127 : v);
+  return static_cast<int8_t>(v);
+}
+
+// One CTA per row.  row_max (optional) supplies a precomputed max |x| per
+// row (the all-reduced maximum of a tensor-parallel shard).
+__global__ void __launch_bounds__(kQuantThreads)
+    quantize_rows_vec4(int in, const float* __restrict__ x, int8_t* __restrict__ xq,
+                       long long ldq, float* __restrict__ xs,
+                       const float* __restrict__ row_max) {
+  __shared__ float red[32];
+  const long long row = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * in);
+  const int n4 = in >> 2;
+  float4 cache[kCache];
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kCache; ++i) {
+    const int idx = threadIdx.x + i * kQuantThreads;
+    if (idx < n4) {
+      cache[i] = __ldg(xr + idx);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(cache[i].x), fabsf(cache[i].y)),
+                         fmaxf(fabsf(cache[i].z), fabsf(cache[i].w))));
+    }
+  }
+  for (int idx = threadIdx.x + kCache * kQuantThreads; idx < n4; idx += kQuantThreads) {
+    const float4 v = __ldg(xr + idx);
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  float mx;
+  if (row_max != nullptr) {
+    mx = row_max[row];
+  } else {
+    mx = block_max(m, red);
+  }
+  const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  if (threadIdx.x == 0) xs[row] = scale;
+  char4* out = reinterpret_cast<char4*>(xq + row * ldq);
+#pragma unroll
+  for (int i = 0; i < kCache; ++i) {
+    const int idx = threadIdx.x + i * kQuantThreads;
+    if (idx < n4) {
+      const float4 v = cache[i];
+      out[idx] = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
+    }
+  }
+  for (int idx = threadIdx.x + kCache * kQuantThreads; idx < n4; idx += kQuantThreads) {
+    const float4 v = __ldg(xr + idx);
+    out[idx] = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
+  }
+  // zero the stride padding [in, ldq)
+  for (long long c = in + threadIdx.x; c < ldq; c += kQuantThreads) xq[row * ldq + c] = 0;
+}
+
+// Any width / alignment.
+__global__ void __launch_bounds__(kQuantThreads)
+    quantize_rows_scalar(int in, const float* __restrict__ x, int8_t* __restrict__ xq,
+                         long long ldq, float* __restrict__ xs,
+                         const float* __restrict__ row_max) {
+  __shared__ float red[32];
+  const long long row = blockIdx.x;
+  const float* xr = x + row * in;
+  float m = 0.0f;
+  for (int c = threadIdx.x; c < in; c += kQuantThreads) m = fmaxf(m, fabsf(xr[c]));
+  const float mx = row_max != nullptr ? row_max[row] : block_max(m, red);
+  const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  if (threadIdx.x == 0) xs[row] = scale;
+  for (long long c = threadIdx.x; c < ldq; c += kQuantThreads)
+    xq[row * ldq + c] = c < in ? q8(xr[c], scale) : static_cast<int8_t>(0);
+}
+
+__global__ void __launch_bounds__(kQuantThreads)
+    row_absmax_kernel(int in, const float* __restrict__ x, float* __restrict__ out) {
+  __shared__ float red[32];
+  const float* xr = x + static_cast<long long>(blockIdx.x) * in;
+  float m = 0.0f;
+  for (int c = threadIdx.x; c < in; c += kQuantThreads) m = fmaxf(m, fabsf(xr[c]));
+  m = block_max(m, red);
+  if (threadIdx.x == 0) out[blockIdx.x] = m;
+}
+
+// [in][out] (Coral's transposed layout, kernels.hpp:15-16) -> [out][ldw].
+__global__ void pack_weight_kernel(int in, int out, const int8_t* __restrict__ wt,
+                                   int8_t* __restrict__ w, long long ldw) {
+  __shared__ int8_t tile[32][33];
+  const int k0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int i = ty; i < 32; i += 8) {
+    const int k = k0 + i, n = n0 + tx;
+    tile[i][tx] = (k < in && n < out) ? wt[static_cast<long long>(k) * out + n] : 0;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int n = n0 + i, k = k0 + tx;
+    if (n < out && k < ldw) w[static_cast<long long>(n) * ldw + k] = k < in ? tile[tx][i] : 0;
+  }
+}
+
+__global__ void pad_rows_kernel(long long rows, int in, const int8_t* __restrict__ x,
+                                long long ldx, int8_t* __restrict__ y, long long ldy) {
+  const long long row = blockIdx.x;
+  for (long long c = threadIdx.x; c < ldy; c += blockDim.x)
+    y[row * ldy + c] = c < in ? x[row * ldx + c] : static_cast<int8_t>(0);
+}
+
+__global__ void w8a8_epilogue_kernel(long long rows, int out, const int32_t* __restrict__ acc,
+                                     const float* __restrict__ xs,
+                                     const float* __restrict__ ws,
+                                     const float* __restrict__ bias, float* __restrict__ y) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * out) return;
+  const long long r = i / out;
+  const int c = static_cast<int>(i - r * out);
+  float v = __fmul_rn(__int2float_rn(acc[i]), __fmul_rn(xs[r], ws[c]));
+  if (bias != nullptr) v = __fadd_rn(v, bias[c]);
+  y[i] = v;
+}
+
+}  // namespace
+
+int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q, long long ldq,
+                  float* x_scale, const float* row_max, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (in <= 0 || ldq < in || x == nullptr || x_q == nullptr || x_scale == nullptr)
+    return kErrInvalid;
+  const bool vec = (in % 4 == 0) && (ldq % 4 == 0) &&
+                   (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(x_q) % 4 == 0);
+  if (vec) {
+    quantize_rows_vec4<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
+        static_cast<int>(in), x, x_q, ldq, x_scale, row_max);
+  } else {
+    quantize_rows_scalar<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
+        static_cast<int>(in), x, x_q, ldq, x_scale, row_max);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int row_absmax(long long rows, long long in, const float* x, float* row_max,
+               cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (in <= 0 || x == nullptr || row_max == nullptr) return kErrInvalid;
+  row_absmax_kernel<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
+      static_cast<int>(in), x, row_max);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int pack_weight_i8(long long in, long long out, const int8_t* wt, int8_t* w, long long ldw,
+                   cudaStream_t stream) {
+  if (in <= 0 || out <= 0 || ldw < in || wt == nullptr || w == nullptr) return kErrInvalid;
+  dim3 grid(static_cast<unsigned>((ldw + 31) / 32), static_cast<unsigned>((out + 31) / 32));
+  pack_weight_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<int>(in),
+                                                       static_cast<int>(out), wt, w, ldw);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int pad_rows_i8(long long rows, long long in, const int8_t* x, long long ldx, int8_t* y,
+                long long ldy, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (in <= 0 || ldy < in || ldx < in || x == nullptr || y == nullptr) return kErrInvalid;
+  pad_rows_kernel<<<static_cast<unsigned>(rows), 128, 0, stream>>>(rows, static_cast<int>(in),
+                                                                   x, ldx, y, ldy);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int w8a8_epilogue_i32(long long rows, long long out, const int32_t* acc, const float* x_scale,
+                      const float* w_scale, const float* bias, float* y, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  const long long n = rows * out;
+  w8a8_epilogue_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+      rows, static_cast<int>(out), acc, x_scale, w_scale, bias, y);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+}  // namespace reef

@@ -1,0 +1,51 @@
+"""The C ABI loads and exports every symbol include/reef_b200.h declares.
+
+CPU only: no call here reaches the GPU (only argument validation that returns
+before any CUDA call, and pure helpers).
+"""
+import ctypes as C
+
+import pytest
+
+from reef_b200 import _lib
+
+
+@pytest.fixture(scope="module")
+def L():
+    return _lib.lib()
+
+
+def test_exports_every_declared_symbol(L):
+    declared = _lib.header_functions()
+    assert declared, "header declares nothing"
+    missing = [f for f in declared if not hasattr(L, f)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_binding_covers_the_header():
+    declared = set(_lib.header_functions())
+    assert declared == set(_lib.SIGNATURES), (
+        declared ^ set(_lib.SIGNATURES))
+
+
+def test_pure_helpers(L):
+    assert L.reef_b200_version() >= 100
+    assert [L.reef_b200_kpad(n) for n in (1, 7, 16, 17, 4096, 11008)] == \
+        [16, 16, 16, 32, 4096, 11008]
+    assert L.reef_b200_status_string(0) == b"ok"
+    assert b"invalid" in L.reef_b200_status_string(1)
+
+
+def test_argument_validation_without_gpu(L):
+    p = C.c_void_p(16)  # never dereferenced: validation fails or rows == 0 first
+    # rows == 0 is a no-op, as the Coral loops are
+    assert L.reef_b200_linear_w8a8(0, 8, 8, p, p, p, p, p, p, None) == 0
+    assert L.reef_b200_linear_int8(0, 8, 8, p, p, 3, p, None) == 0
+    # empty feature dims and null pointers are invalid (the engine rejects them)
+    assert L.reef_b200_linear_w8a8(4, 0, 8, p, p, p, p, p, p, None) == 1
+    assert L.reef_b200_linear_w8a8(4, 8, 0, p, p, p, p, p, p, None) == 1
+    assert L.reef_b200_linear_w8a8(4, 8, 8, None, p, p, p, p, p, None) == 1
+    assert L.reef_b200_gemm_w8a8(4, 8, 8, p, p, p, None, None, p, None) == 1
+    # shifts above 31 are not a rounding_shift the engine defines
+    assert L.reef_b200_linear_int8(4, 8, 8, p, p, 32, p, None) == 1
+    assert L.reef_b200_quantize_rows(4, 0, p, p, p, None) == 1
