@@ -131,6 +131,93 @@ int reef_b200_linear_bias_int8(size_t rows, size_t in, size_t out, const int8_t*
 int reef_b200_gemm_i8_i32(size_t m, size_t n, size_t k, const int8_t* a,
                           const int8_t* b, int32_t* c, reef_b200_stream_t stream);
 
+/* ---- integer softmax and attention (int8.hpp:156-279) ------------------- */
+
+/* reef_kernels::softmax_int8 (kernels.hpp:114-117), batched: each of `rows`
+ * rows of n int32 scores -> uint8 probabilities summing to about 255, through
+ * a 256-entry exp_table (int8.hpp:156-164; a device pointer). */
+int reef_b200_softmax_int8(size_t rows, size_t n, const int32_t* scores, unsigned shift,
+                           const uint16_t* table, uint8_t* probs,
+                           reef_b200_stream_t stream);
+
+/* reef_kernels::attention_head_int8 (kernels.hpp:122-129) = attend_head_int8
+ * (int8.hpp:250-279) with causal_visibility (attention.hpp:82-100):
+ * query row i sits at position query_start + i; window 0 = global.
+ * q rows are q_stride apart, k/v [key_len][head_dim] contiguous, out rows
+ * out_stride apart.  scores/probs are Coral's per-row scratch; the GPU
+ * kernel keeps them in shared memory, so they may be NULL.  key_len <= 32768
+ * (REEF_B200_ERR_TOO_LARGE beyond).  Every query row must see a key
+ * (REEF_B200_ERR_INVALID otherwise, as the engine throws). Bit-identical. */
+int reef_b200_attention_head_int8(size_t query_len, size_t key_len, size_t head_dim,
+                                  size_t query_start, size_t window, const int8_t* q,
+                                  size_t q_stride, const int8_t* k, const int8_t* v,
+                                  unsigned score_shift, const uint16_t* table,
+                                  unsigned out_shift, int32_t* scores, uint8_t* probs,
+                                  int8_t* out, size_t out_stride,
+                                  reef_b200_stream_t stream);
+
+/* reef_kernels::attention_head_f32 (kernels.hpp:75-79) = attend_head
+ * (attention.hpp:117-123): unscaled float scores, masked softmax with
+ * exp_nonpositive and in-order sums, in-order P.V.  Same argument meaning as
+ * the int8 head; bit-identical to the engine. */
+int reef_b200_attention_head_f32(size_t query_len, size_t key_len, size_t head_dim,
+                                 size_t query_start, size_t window, const float* q,
+                                 size_t q_stride, const float* k, const float* v,
+                                 float* scores, float* out, size_t out_stride,
+                                 reef_b200_stream_t stream);
+
+/* Attention::context (attention.hpp:374-432) over `heads` heads in one
+ * launch: head h reads q + h*q_head, k + h*kv_head, v + h*kv_head and writes
+ * out + h*out_head (strides in elements; key/value rows kv_stride apart).
+ * For a [len][d_model] projection split into heads, q_stride = kv_stride =
+ * out_stride = d_model and the head strides are head_dim. */
+int reef_b200_attention_heads_f32(size_t heads, size_t query_len, size_t key_len,
+                                  size_t head_dim, size_t query_start, size_t window,
+                                  const float* q, size_t q_stride, size_t q_head,
+                                  const float* k, const float* v, size_t kv_stride,
+                                  size_t kv_head, float* out, size_t out_stride,
+                                  size_t out_head, reef_b200_stream_t stream);
+
+/* The int8 head (reef_b200_attention_head_int8) over `heads` heads in one
+ * launch, with the strides of reef_b200_attention_heads_f32. */
+int reef_b200_attention_heads_int8(size_t heads, size_t query_len, size_t key_len,
+                                   size_t head_dim, size_t query_start, size_t window,
+                                   const int8_t* q, size_t q_stride, size_t q_head,
+                                   const int8_t* k, const int8_t* v, size_t kv_stride,
+                                   size_t kv_head, unsigned score_shift,
+                                   const uint16_t* table, unsigned out_shift, int8_t* out,
+                                   size_t out_stride, size_t out_head,
+                                   reef_b200_stream_t stream);
+
+/* ---- int8 flash attention (the fast head) ------------------------------- */
+
+/* Packs one QKV projection output for the flash head.  qkv [batch*seq]
+ * [(heads_q + 2*heads_kv) * 128] fp32 rows (q heads, then k, then v).  q and
+ * k get Llama rotate-half RoPE (theta_i = pos * rope_base^(-2i/128), pos =
+ * token index within its sequence); then every (token, head) row of 128 is
+ * quantised with reef's rule (quant.hpp:51-81: scale = max|x|/127, rne,
+ * clamp +-127).  Outputs: q8 [tokens][heads_q*128], k8 and v8
+ * [tokens][heads_kv*128] (the int8 KV-cache rows), scales [batch][heads][seq],
+ * and vt [batch][heads_kv][128][seq] f16 holding v8's codes transposed (the
+ * operand layout of the P.V tensor-core product).  head_dim is 128.  RoPE
+ * and this scale granularity are not in reef (parity unpinned there). */
+int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t heads_kv,
+                             float rope_base, const float* qkv, int8_t* q8, int8_t* k8,
+                             int8_t* v8, float* q_scale, float* k_scale, float* v_scale,
+                             void* vt, reef_b200_stream_t stream);
+
+/* Flash attention over int8 q / k / v (attend_head, attention.hpp:117-123,
+ * on the dequantised values, with score scale sm_scale and GQA: query head h
+ * reads kv head h / (heads_q / heads_kv)).  causal != 0 applies
+ * causal_visibility with query_start 0.  out [batch*seq][heads_q*128] fp32.
+ * head_dim must be 128 and seq a multiple of 8.  Matches reef's float head
+ * on the dequantised inputs within 1e-2 (fp32 online softmax, f16 P). */
+int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t heads_kv,
+                            size_t head_dim, int causal, float sm_scale, const int8_t* q8,
+                            const float* q_scale, const int8_t* k8, const float* k_scale,
+                            const void* vt, const float* v_scale, float* out,
+                            reef_b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

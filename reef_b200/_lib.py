@@ -37,6 +37,17 @@ SIGNATURES = {
     "reef_b200_linear_int8": ([_sz, _sz, _sz, _p, _p, _u, _p, _p], _i),
     "reef_b200_linear_bias_int8": ([_sz, _sz, _sz, _p, _p, _p, _u, _p, _p], _i),
     "reef_b200_gemm_i8_i32": ([_sz, _sz, _sz, _p, _p, _p, _p], _i),
+    "reef_b200_softmax_int8": ([_sz, _sz, _p, _u, _p, _p, _p], _i),
+    "reef_b200_attention_head_int8": ([_sz, _sz, _sz, _sz, _sz, _p, _sz, _p, _p, _u, _p,
+                                       _u, _p, _p, _p, _sz, _p], _i),
+    "reef_b200_attention_head_f32": ([_sz, _sz, _sz, _sz, _sz, _p, _sz, _p, _p, _p, _p,
+                                      _sz, _p], _i),
+    "reef_b200_attention_heads_f32": ([_sz] * 6 + [_p, _sz, _sz, _p, _p, _sz, _sz, _p, _sz,
+                                                   _sz, _p], _i),
+    "reef_b200_attention_heads_int8": ([_sz] * 6 + [_p, _sz, _sz, _p, _p, _sz, _sz, _u, _p,
+                                                    _u, _p, _sz, _sz, _p], _i),
+    "reef_b200_rope_qkv_quant": ([_sz, _sz, _sz, _sz, C.c_float] + [_p] * 9, _i),
+    "reef_b200_flash_attn_i8": ([_sz, _sz, _sz, _sz, _sz, _i, C.c_float] + [_p] * 8, _i),
 }
 
 

@@ -209,7 +209,46 @@ __global__ void __launch_bounds__(kHeadThreads)
   }
 }
 
+// masked_softmax_int8 (int8.hpp:180-232) of one row with every key visible:
+// the Coral softmax_int8 entry point (kernels.hpp:114-117), one CTA per row.
+__global__ void __launch_bounds__(kHeadThreads)
+    softmax_int8_kernel(int n, const int32_t* __restrict__ scores, uint32_t shift,
+                        const uint16_t* __restrict__ table_g, uint8_t* __restrict__ probs) {
+  __shared__ uint16_t table[256];
+  __shared__ int32_t red_i[32];
+  __shared__ uint32_t red_u[32];
+  const long long row = blockIdx.x;
+  scores += row * n;
+  probs += row * n;
+  for (int t = threadIdx.x; t < 256; t += blockDim.x) table[t] = table_g[t];
+  int32_t mx = INT32_MIN;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) mx = scores[j] > mx ? scores[j] : mx;
+  mx = block_reduce<int32_t>(mx, red_i, true);  // also orders the table load
+  uint32_t sum = 0;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const uint32_t d = static_cast<uint32_t>((mx - scores[j]) >> static_cast<int32_t>(shift));
+    sum += table[d < 255u ? d : 255u];
+  }
+  sum = block_reduce<uint32_t>(sum, red_u, false);
+  const uint32_t reciprocal = (255u << 16) / sum;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const uint32_t d = static_cast<uint32_t>((mx - scores[j]) >> static_cast<int32_t>(shift));
+    const uint32_t scaled = static_cast<uint32_t>(table[d < 255u ? d : 255u]) * reciprocal;
+    const uint32_t rounded = (scaled >> 16) + ((scaled >> 15) & 1u);
+    probs[j] = static_cast<uint8_t>(rounded < 255u ? rounded : 255u);
+  }
+}
+
 }  // namespace
+
+int softmax_int8_rows(long long rows, int n, const int32_t* scores, uint32_t shift,
+                      const uint16_t* table, uint8_t* probs, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (n <= 0 || shift > 31 || !scores || !table || !probs) return kErrInvalid;
+  softmax_int8_kernel<<<static_cast<unsigned>(rows), kHeadThreads, 0, stream>>>(
+      n, scores, shift, table, probs);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
 
 int attention_head_int8(const AttnHeadArgs& a, const int8_t* q, const int8_t* k,
                         const int8_t* v, uint32_t score_shift, const uint16_t* table,

@@ -5,6 +5,8 @@
 
 #include "ops.h"
 
+#include <cuda_fp16.h>
+
 using namespace reef;
 
 namespace {
@@ -140,6 +142,154 @@ int reef_b200_gemm_i8_i32(size_t m, size_t n, size_t k, const int8_t* a, const i
   if (!dims_ok(m, k, n) || !a || !b || !c) return REEF_B200_ERR_INVALID;
   GemmArgs args{};
   return gemm(m, k, n, a, b, kEpiI32, args, c, S(stream));
+}
+
+int reef_b200_softmax_int8(size_t rows, size_t n, const int32_t* scores, unsigned shift,
+                           const uint16_t* table, uint8_t* probs, reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (!dims_ok(rows, n, 1) || !scores || !table || !probs || shift > 31)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return softmax_int8_rows(rows, static_cast<int>(n), scores, shift, table, probs, S(stream));
+}
+
+namespace {
+
+// Every query row must see at least one key (the engine throws otherwise,
+// attention.hpp:82-100 + activation.hpp:204-207 / int8.hpp:211-214).
+int attn_args(size_t heads, size_t query_len, size_t key_len, size_t head_dim,
+              size_t query_start, size_t window, AttnHeadArgs* a) {
+  if (heads == 0 || query_len == 0) return REEF_B200_OK;
+  if (key_len == 0 || head_dim == 0 || head_dim > kMaxDim || query_len > kMaxDim ||
+      heads > 65535 || window > kMaxDim)
+    return REEF_B200_ERR_INVALID;
+  if (key_len > static_cast<size_t>(kMaxKeysExact)) return REEF_B200_ERR_TOO_LARGE;
+  const size_t last = query_start + query_len;  // position of the last row + 1
+  if (window > 0 && last > window && last - window >= key_len) return REEF_B200_ERR_INVALID;
+  a->heads = static_cast<int>(heads);
+  a->query_len = static_cast<int>(query_len);
+  a->key_len = static_cast<int>(key_len);
+  a->head_dim = static_cast<int>(head_dim);
+  a->window = static_cast<int>(window);
+  a->query_start = static_cast<long long>(query_start);
+  return -1;  // valid, non-empty
+}
+
+}  // namespace
+
+int reef_b200_attention_heads_int8(size_t heads, size_t query_len, size_t key_len,
+                                   size_t head_dim, size_t query_start, size_t window,
+                                   const int8_t* q, size_t q_stride, size_t q_head,
+                                   const int8_t* k, const int8_t* v, size_t kv_stride,
+                                   size_t kv_head, unsigned score_shift,
+                                   const uint16_t* table, unsigned out_shift, int8_t* out,
+                                   size_t out_stride, size_t out_head,
+                                   reef_b200_stream_t stream) {
+  AttnHeadArgs a{};
+  const int v0 = attn_args(heads, query_len, key_len, head_dim, query_start, window, &a);
+  if (v0 >= 0) return v0;
+  if (!q || !k || !v || !table || !out || score_shift > 31 || out_shift > 31)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  a.q_stride = static_cast<long long>(q_stride);
+  a.q_head = static_cast<long long>(q_head);
+  a.kv_stride = static_cast<long long>(kv_stride);
+  a.kv_head = static_cast<long long>(kv_head);
+  a.out_stride = static_cast<long long>(out_stride);
+  a.out_head = static_cast<long long>(out_head);
+  return attention_head_int8(a, q, k, v, score_shift, table, out_shift, out, S(stream));
+}
+
+int reef_b200_attention_head_int8(size_t query_len, size_t key_len, size_t head_dim,
+                                  size_t query_start, size_t window, const int8_t* q,
+                                  size_t q_stride, const int8_t* k, const int8_t* v,
+                                  unsigned score_shift, const uint16_t* table,
+                                  unsigned out_shift, int32_t* /*scores*/,
+                                  uint8_t* /*probs*/, int8_t* out, size_t out_stride,
+                                  reef_b200_stream_t stream) {
+  return reef_b200_attention_heads_int8(1, query_len, key_len, head_dim, query_start, window,
+                                        q, q_stride, 0, k, v, head_dim, 0, score_shift, table,
+                                        out_shift, out, out_stride, 0, stream);
+}
+
+int reef_b200_attention_heads_f32(size_t heads, size_t query_len, size_t key_len,
+                                  size_t head_dim, size_t query_start, size_t window,
+                                  const float* q, size_t q_stride, size_t q_head,
+                                  const float* k, const float* v, size_t kv_stride,
+                                  size_t kv_head, float* out, size_t out_stride,
+                                  size_t out_head, reef_b200_stream_t stream) {
+  AttnHeadArgs a{};
+  const int v0 = attn_args(heads, query_len, key_len, head_dim, query_start, window, &a);
+  if (v0 >= 0) return v0;
+  if (!q || !k || !v || !out) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  a.q_stride = static_cast<long long>(q_stride);
+  a.q_head = static_cast<long long>(q_head);
+  a.kv_stride = static_cast<long long>(kv_stride);
+  a.kv_head = static_cast<long long>(kv_head);
+  a.out_stride = static_cast<long long>(out_stride);
+  a.out_head = static_cast<long long>(out_head);
+  return attention_head_f32(a, q, k, v, out, S(stream));
+}
+
+int reef_b200_attention_head_f32(size_t query_len, size_t key_len, size_t head_dim,
+                                 size_t query_start, size_t window, const float* q,
+                                 size_t q_stride, const float* k, const float* v,
+                                 float* /*scores*/, float* out, size_t out_stride,
+                                 reef_b200_stream_t stream) {
+  return reef_b200_attention_heads_f32(1, query_len, key_len, head_dim, query_start, window, q,
+                                       q_stride, 0, k, v, head_dim, 0, out, out_stride, 0,
+                                       stream);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t heads_kv,
+                             float rope_base, const float* qkv, int8_t* q8, int8_t* k8,
+                             int8_t* v8, float* q_scale, float* k_scale, float* v_scale,
+                             void* vt, reef_b200_stream_t stream) {
+  if (batch == 0 || seq == 0) return REEF_B200_OK;
+  if (heads_q == 0 || heads_kv == 0 || heads_q % heads_kv != 0 || batch * seq > kMaxDim ||
+      !qkv || !q8 || !k8 || !v8 || !q_scale || !k_scale || !v_scale || !vt)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return rope_qkv_quant(static_cast<int>(batch), static_cast<int>(seq),
+                        static_cast<int>(heads_q), static_cast<int>(heads_kv), rope_base, qkv,
+                        q8, k8, v8, q_scale, k_scale, v_scale, vt,
+                        S(stream));
+}
+
+int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t heads_kv,
+                            size_t head_dim, int causal, float sm_scale, const int8_t* q8,
+                            const float* q_scale, const int8_t* k8, const float* k_scale,
+                            const void* vt, const float* v_scale, float* out,
+                            reef_b200_stream_t stream) {
+  if (batch == 0 || seq == 0) return REEF_B200_OK;
+  if (head_dim != 128 || heads_q == 0 || heads_kv == 0 || heads_q % heads_kv != 0 ||
+      batch * seq > kMaxDim || heads_q > 4096 || !q8 || !q_scale || !k8 || !k_scale || !vt ||
+      !v_scale || !out)
+    return REEF_B200_ERR_INVALID;
+  if (seq % 8 != 0) return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  FlashProblem p{};
+  p.batch = static_cast<int>(batch);
+  p.heads_q = static_cast<int>(heads_q);
+  p.heads_kv = static_cast<int>(heads_kv);
+  p.seq = static_cast<int>(seq);
+  p.head_dim = 128;
+  p.causal = causal != 0;
+  p.sm_scale = sm_scale;
+  p.q8 = q8;
+  p.k8 = k8;
+  p.vt = vt;
+  p.q_scale = q_scale;
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
+  p.out = out;
+  p.out_ld = static_cast<long long>(heads_q) * 128;
+  return flash_prefill_i8(p, S(stream));
 }
 
 }  // extern "C"

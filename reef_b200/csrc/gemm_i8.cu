@@ -44,7 +44,7 @@ constexpr int kBK = 128;         // bytes of K per stage (one 128-byte swizzle r
 constexpr int kUmmaK = 32;       // K per tcgen05.mma kind::i8
 constexpr int kThreads = 192;    // 6 warps
 constexpr int kEpiWarps = 4;
-constexpr int kTransposeFloats = 32 * 33;  // per epilogue warp
+constexpr int kTransposeWords = 32 * 36;  // per epilogue warp
 
 template <int BN, int STAGES>
 struct Layout {
@@ -52,7 +52,8 @@ struct Layout {
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTransposeOff = STAGES * kStageBytes;
-  static constexpr int kBarOff = kTransposeOff + kEpiWarps * kTransposeFloats * 4;
+  static constexpr int kRowScaleOff = kTransposeOff + kEpiWarps * kTransposeWords * 4;
+  static constexpr int kBarOff = kRowScaleOff + kEpiWarps * 32 * 4;
   // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
@@ -211,22 +212,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue ----------------
+    // Per 32-column chunk: tcgen05.ld gives thread `lane` row (row0 + lane);
+    // the raw int32 values go through this warp's shared-memory buffer
+    // (row stride 36 words: 16-byte accesses are bank-conflict free both
+    // ways), then each thread requantises 4 consecutive columns of 8 rows,
+    // so a store instruction writes 4 rows x 32 contiguous columns and the
+    // per-column scale / bias are loaded once per chunk.
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
-    float* tbuf = reinterpret_cast<float*>(smem + L::kTransposeOff) +
-                  (warp - 2) * kTransposeFloats;
-    uint32_t* tbuf_u = reinterpret_cast<uint32_t*>(tbuf);
+    uint32_t* tbuf = reinterpret_cast<uint32_t*>(smem + L::kTransposeOff) +
+                     (warp - 2) * kTransposeWords;
+    float* rs_s = reinterpret_cast<float*>(smem + L::kRowScaleOff) + (warp - 2) * 32;
+    const int sub_row = lane >> 3;       // 0..3
+    const int sub_col = (lane & 7) * 4;  // 0, 4, ..., 28
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, num_m, num_n, args.group_m, mb, nb);
-      if (!mbar_wait(&acc_full[acc], acc_phase, err, kDevTimeoutAccFull)) break;
+      // warp-uniform outcome: the tcgen05.ld below is warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, err, kDevTimeoutAccFull)))
+        break;
       tc_fence_after();
       const int row0 = mb * kBM + q * 32;  // first output row of this warp
-      const int my_row = row0 + lane;
-      float row_scale = 0.0f;
       if constexpr (EPI == kEpiF32W8A8) {
-        if (my_row < M) row_scale = args.x_scale[my_row];
+        const int my_row = row0 + lane;
+        rs_s[lane] = my_row < M ? args.x_scale[my_row] : 0.0f;
       }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -236,44 +246,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                                static_cast<uint32_t>(acc * BN + c * 32),
                            r);
         tmem_ld_wait();
-        if (col0 < N) {
-          // compute this thread's 32 outputs (row my_row, columns col0..+31)
+        if (col0 < N) {  // warp-uniform
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = col0 + j;
-            const int nn = n < N ? n : N - 1;
-            const int32_t a = static_cast<int32_t>(r[j]);
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<uint4*>(&tbuf[lane * 36 + j]) =
+                make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          __syncwarp();
+          const int n = col0 + sub_col;
+          float ws[4] = {0.f, 0.f, 0.f, 0.f}, bf[4] = {0.f, 0.f, 0.f, 0.f};
+          int32_t bi[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int nn = n + e < N ? n + e : N - 1;
             if constexpr (EPI == kEpiF32W8A8) {
-              const float combined = __fmul_rn(row_scale, args.w_scale[nn]);
-              float v = __fmul_rn(__int2float_rn(a), combined);
-              if (args.bias_f != nullptr) v = __fadd_rn(v, args.bias_f[nn]);
-              tbuf[lane * 33 + j] = v;
+              ws[e] = args.w_scale[nn];
+              if (args.bias_f != nullptr) bf[e] = args.bias_f[nn];
             } else if constexpr (EPI == kEpiI8Shift) {
-              int32_t s = a;
-              if (args.bias_i != nullptr) s += args.bias_i[nn];
-              tbuf_u[lane * 33 + j] =
-                  static_cast<uint32_t>(static_cast<uint8_t>(requant_rnu_sat8(s, args.shift)));
-            } else {
-              tbuf_u[lane * 33 + j] = r[j];
+              if (args.bias_i != nullptr) bi[e] = args.bias_i[nn];
             }
           }
-          __syncwarp();
-          // write out: iteration j stores row (row0 + j), 32 consecutive columns
-          const int n = col0 + lane;
-          if (n < N) {
-#pragma unroll 4
-            for (int j = 0; j < 32; ++j) {
-              const int m = row0 + j;
-              if (m < M) {
-                const long long off = static_cast<long long>(m) * args.ldy + n;
-                if constexpr (EPI == kEpiF32W8A8) {
-                  static_cast<float*>(args.y)[off] = tbuf[j * 33 + lane];
-                } else if constexpr (EPI == kEpiI8Shift) {
-                  static_cast<int8_t*>(args.y)[off] =
-                      static_cast<int8_t>(tbuf_u[j * 33 + lane]);
+          const bool full_vec = args.vec_ok && (n + 3 < N);
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rl = it * 4 + sub_row;
+            const int m = row0 + rl;
+            const uint4 a4 = *reinterpret_cast<const uint4*>(&tbuf[rl * 36 + sub_col]);
+            if (m < M && n < N) {
+              const uint32_t av[4] = {a4.x, a4.y, a4.z, a4.w};
+              const long long off = static_cast<long long>(m) * args.ldy + n;
+              if constexpr (EPI == kEpiF32W8A8) {
+                const float rsv = rs_s[rl];
+                float o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  // linear.hpp:125-127: float(sum) * (row_scale * w_scale[c])
+                  o[e] = __fmul_rn(__int2float_rn(static_cast<int32_t>(av[e])),
+                                   __fmul_rn(rsv, ws[e]));
+                  if (args.bias_f != nullptr) o[e] = __fadd_rn(o[e], bf[e]);
+                }
+                float* y = static_cast<float*>(args.y) + off;
+                if (full_vec) {
+                  *reinterpret_cast<float4*>(y) = make_float4(o[0], o[1], o[2], o[3]);
                 } else {
-                  static_cast<int32_t*>(args.y)[off] =
-                      static_cast<int32_t>(tbuf_u[j * 33 + lane]);
+                  for (int e = 0; e < 4 && n + e < N; ++e) y[e] = o[e];
+                }
+              } else if constexpr (EPI == kEpiI8Shift) {
+                int8_t o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  o[e] = requant_rnu_sat8(static_cast<int32_t>(av[e]) + bi[e], args.shift);
+                int8_t* y = static_cast<int8_t*>(args.y) + off;
+                if (full_vec) {
+                  *reinterpret_cast<char4*>(y) = make_char4(o[0], o[1], o[2], o[3]);
+                } else {
+                  for (int e = 0; e < 4 && n + e < N; ++e) y[e] = o[e];
+                }
+              } else {
+                int32_t* y = static_cast<int32_t*>(args.y) + off;
+                if (full_vec) {
+                  *reinterpret_cast<uint4*>(y) = a4;
+                } else {
+                  for (int e = 0; e < 4 && n + e < N; ++e) y[e] = static_cast<int32_t>(av[e]);
                 }
               }
             }
@@ -322,6 +355,11 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
   args.K = p.K;
   if (args.group_m <= 0) args.group_m = 8;
   args.err = device_error_ptr();
+  {
+    const uintptr_t y = reinterpret_cast<uintptr_t>(args.y);
+    const int align = EPI == kEpiI8Shift ? 4 : 16;
+    args.vec_ok = (y % align == 0) && (args.ldy % 4 == 0) ? 1 : 0;
+  }
   kernel<<<grid, kThreads, L::kAlloc, stream>>>(ma, mb, args);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }

@@ -43,6 +43,7 @@ struct GemmArgs {
   long long ldy;          // elements
   uint32_t shift;         // kEpiI8Shift
   int group_m;            // raster group (0 = default)
+  int vec_ok;             // 16-byte (int8: 4-byte) output stores allowed (launcher)
   int* err;               // device error word (set by the launcher)
 };
 
@@ -82,5 +83,44 @@ int pad_rows_i8(long long rows, long long in, const int8_t* x, long long ldx,
 int w8a8_epilogue_i32(long long rows, long long out, const int32_t* acc,
                       const float* x_scale, const float* w_scale, const float* bias,
                       float* y, cudaStream_t stream);
+
+// attention_exact.cu -- reef's integer and float heads, bit for bit.
+// Scores stay in shared memory, which bounds the key length.
+constexpr int kMaxKeysExact = 32768;
+
+struct AttnHeadArgs {
+  int heads;            // heads in this launch (blockIdx.y)
+  int query_len, key_len, head_dim, window;
+  long long query_start;
+  long long q_stride, q_head;      // elements between query rows / heads
+  long long kv_stride, kv_head;    // elements between key rows / heads
+  long long out_stride, out_head;  // elements between output rows / heads
+};
+
+int attention_head_int8(const AttnHeadArgs& a, const int8_t* q, const int8_t* k,
+                        const int8_t* v, uint32_t score_shift, const uint16_t* table,
+                        uint32_t out_shift, int8_t* out, cudaStream_t stream);
+int attention_head_f32(const AttnHeadArgs& a, const float* q, const float* k, const float* v,
+                       float* out, cudaStream_t stream);
+int softmax_int8_rows(long long rows, int n, const int32_t* scores, uint32_t shift,
+                      const uint16_t* table, uint8_t* probs, cudaStream_t stream);
+
+// flash_attn.cu -- int8 flash attention (prefill) and its input packing.
+struct FlashProblem {
+  int batch, heads_q, heads_kv, seq, head_dim, causal;
+  float sm_scale;
+  const int8_t* q8;       // [B*S][Hq*128]  token-major
+  const int8_t* k8;       // [B*S][Hkv*128] token-major
+  const void* vt;         // [B][Hkv][128][S] f16 (int8 codes)
+  const float* q_scale;   // [B][Hq][S]
+  const float* k_scale;   // [B][Hkv][S]
+  const float* v_scale;   // [B][Hkv][S]
+  float* out;             // [B*S][out_ld]
+  long long out_ld;
+};
+int flash_prefill_i8(const FlashProblem& p, cudaStream_t stream);
+int rope_qkv_quant(int batch, int seq, int heads_q, int heads_kv, float rope_base,
+                   const float* qkv, int8_t* q8, int8_t* k8, int8_t* v8, float* q_scale,
+                   float* k_scale, float* v_scale, void* vt, cudaStream_t stream);
 
 }  // namespace reef

@@ -123,3 +123,55 @@ def gemm_i8_i32(a: torch.Tensor, b: torch.Tensor, k: int | None = None) -> torch
     c = torch.empty((m, n), dtype=torch.int32, device=a.device)
     _lib.call("reef_b200_gemm_i8_i32", m, n, k, _ptr(a), _ptr(b), _ptr(c), _stream())
     return c
+
+
+# ---- integer softmax and attention heads ---------------------------------------
+
+def exp_table_device(table) -> torch.Tensor:
+    """A 256-entry exp_table (int8.hpp:156-164, uint16 values) on the device.
+    The bits are held in an int16 tensor; the kernels read them as uint16."""
+    import numpy as np
+    bits16 = np.ascontiguousarray(np.asarray(table, dtype=np.uint16)).view(np.int16)
+    return torch.from_numpy(bits16.copy()).cuda()
+
+
+def softmax_int8(scores: torch.Tensor, shift: int, table: torch.Tensor) -> torch.Tensor:
+    """reef_kernels::softmax_int8 (kernels.hpp:114-117), every row of scores."""
+    rows, n = scores.shape
+    probs = torch.empty((rows, n), dtype=torch.uint8, device=scores.device)
+    _lib.call("reef_b200_softmax_int8", rows, n, _ptr(scores), shift, _ptr(table),
+              _ptr(probs), _stream())
+    return probs
+
+
+def attention_head_int8(q, k, v, query_start: int, window: int, score_shift: int,
+                        table: torch.Tensor, out_shift: int = 8) -> torch.Tensor:
+    """reef_kernels::attention_head_int8 (kernels.hpp:122-129), one head."""
+    ql, d = q.shape
+    kl = k.shape[0]
+    out = torch.empty((ql, d), dtype=torch.int8, device=q.device)
+    _lib.call("reef_b200_attention_head_int8", ql, kl, d, query_start, window, _ptr(q), d,
+              _ptr(k), _ptr(v), score_shift, _ptr(table), out_shift, None, None, _ptr(out),
+              d, _stream())
+    return out
+
+
+def attention_head_f32(q, k, v, query_start: int, window: int) -> torch.Tensor:
+    """reef_kernels::attention_head_f32 (kernels.hpp:75-79), one head."""
+    ql, d = q.shape
+    kl = k.shape[0]
+    out = torch.empty((ql, d), dtype=torch.float32, device=q.device)
+    _lib.call("reef_b200_attention_head_f32", ql, kl, d, query_start, window, _ptr(q), d,
+              _ptr(k), _ptr(v), None, _ptr(out), d, _stream())
+    return out
+
+
+def attention_heads_f32(q, k, v, heads: int, query_start: int = 0, window: int = 0):
+    """Attention::context over all heads of [len][d_model] q/k/v."""
+    ql, dm = q.shape
+    kl = k.shape[0]
+    hd = dm // heads
+    out = torch.empty((ql, dm), dtype=torch.float32, device=q.device)
+    _lib.call("reef_b200_attention_heads_f32", heads, ql, kl, hd, query_start, window,
+              _ptr(q), dm, hd, _ptr(k), _ptr(v), dm, hd, _ptr(out), dm, hd, _stream())
+    return out

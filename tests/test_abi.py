@@ -49,3 +49,18 @@ def test_argument_validation_without_gpu(L):
     # shifts above 31 are not a rounding_shift the engine defines
     assert L.reef_b200_linear_int8(4, 8, 8, p, p, 32, p, None) == 1
     assert L.reef_b200_quantize_rows(4, 0, p, p, p, None) == 1
+
+
+def test_attention_validation_without_gpu(L):
+    p = C.c_void_p(16)
+    # a row that sees no key: query 9 at window 3 over 5 keys
+    assert L.reef_b200_attention_head_int8(1, 5, 8, 9, 3, p, 8, p, p, 4, p, 8,
+                                           None, None, p, 8, None) == 1
+    assert L.reef_b200_attention_head_f32(1, 5, 8, 9, 3, p, 8, p, p, None, p, 8, None) == 1
+    # no keys at all
+    assert L.reef_b200_attention_head_f32(1, 0, 8, 0, 0, p, 8, p, p, None, p, 8, None) == 1
+    # longer than the shared-memory score buffer
+    assert L.reef_b200_attention_head_int8(1, 40000, 8, 0, 0, p, 8, p, p, 4, p, 8,
+                                           None, None, p, 8, None) == 7
+    # empty query is a no-op
+    assert L.reef_b200_attention_head_f32(0, 5, 8, 0, 0, p, 8, p, p, None, p, 8, None) == 0
