@@ -1,0 +1,427 @@
+#!/usr/bin/env python3
+"""Benchmark: int8 TP decoder-layer TOPS and tokens/s on B200.
+
+Workload: one Llama-7B-shape W8A8 decoder layer, prefill
+of batch 8 x seq 2048 = 16384 tokens (hidden 4096, 32 heads x 128, SwiGLU
+FFN 11008), synthetic seeded inputs and random-init weights.  At N GPUs the
+layer runs Megatron tensor-parallel over N ranks (one process per GPU, launched
+by torchrun): total work is fixed, so scaling is "strong".
+
+A step = one forward of the layer over all 16384 tokens.  `value` is the
+whole-job throughput in TOPS (algorithmic int ops: 2 per MAC of the four
+projections, plus the causal q.k and p.v of attention) over the device-timed
+steps (CUDA events, max over ranks), inputs resident in HBM (x is 256 MiB,
+the weights 200 MiB: both larger than L2, so no flush is needed between
+steps).  `e2e` is the same metric through the C ABI with host buffers: each
+step copies x from pinned host memory and y back inside the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+--impl reference times reef's own engine (inference-engine/reference/cpp,
+compiled in place into oracle/_ref) on the host cores, on a bounded sample of
+the same workload; rank 0 prints its line, other ranks exit without work.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import ctypes as C
+import datetime as dt
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = "llama7b-w8a8-prefill-layer"
+BATCH, SEQ = 8, 2048
+METRIC = "int8 TP decoder-layer TOPS (Llama-7B-shape W8A8 prefill layer, 8 x 2048 tokens)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="reef_b200", choices=["reef_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def shape():
+    from reef_b200.layer import LLAMA_7B
+    return LLAMA_7B
+
+
+def layer_ops(s, tokens: int, seq: int) -> dict:
+    per = s.ops_per_token(seq)
+    return dict(gemm=per["gemm"] * tokens, attention=per["attention"] * tokens,
+                total=(per["gemm"] + per["attention"]) * tokens)
+
+
+# ---- reef's engine on the host cores (CPU baseline / reference arm) ---------------
+
+class RefSample:
+    """reef's own W8A8 linear (operator/linear.hpp:106-134) and float head
+    (attention.hpp:117-123), compiled in place (oracle/_ref), run on a
+    bounded sample of the layer: each host thread pushes one token through
+    the four projections (a fraction `frac` of their output columns) and its
+    32 heads of causal attention at a position spread over the sequence."""
+
+    def __init__(self, s, threads: int):
+        import numpy as np
+
+        from oracle import oracle as ro
+        self.ro, self.np, self.s, self.threads = ro, np, s, threads
+        self.lib = ro.ref()
+        rng = np.random.default_rng(5)
+        h, d = s.hidden, s.head_dim
+        dims = [((s.heads_q + 2 * s.heads_kv) * d, h), (h, s.heads_q * d), (2 * s.ffn, h),
+                (h, s.ffn)]
+        self.w = [rng.integers(-127, 128, (n, k), dtype=np.int8) for n, k in dims]
+        self.ws = [np.full(n, 1e-3, np.float32) for n, _ in dims]
+        self.kv = rng.standard_normal((2, SEQ, d)).astype(np.float32)
+
+    def _token(self, i: int, frac: float) -> float:
+        np, s, L = self.np, self.s, self.lib
+        f = C.POINTER(C.c_float)
+        i8 = C.POINTER(C.c_int8)
+        ops = 0.0
+        for w, ws in zip(self.w, self.ws):
+            n = max(1, int(round(w.shape[0] * frac)))
+            k = w.shape[1]
+            x = np.random.default_rng(i).standard_normal((1, k)).astype(np.float32)
+            y = np.empty((1, n), np.float32)
+            wn = w[:n]
+            L.ref_linear_w8a8(1, k, n, x.ctypes.data_as(f), wn.ctypes.data_as(i8),
+                              ws.ctypes.data_as(f), None, y.ctypes.data_as(f))
+            ops += 2.0 * k * n
+        pos = (i * SEQ) // self.threads + SEQ // (2 * self.threads)
+        heads = max(1, int(round(s.heads_q * frac)))
+        q = np.random.default_rng(i + 99).standard_normal((1, s.head_dim)).astype(np.float32)
+        kk = np.ascontiguousarray(self.kv[0, :pos + 1])
+        vv = np.ascontiguousarray(self.kv[1, :pos + 1])
+        o = np.empty((1, s.head_dim), np.float32)
+        for _ in range(heads):
+            L.ref_attend_head_f32(1, pos + 1, s.head_dim, pos, 0, q.ctypes.data_as(f),
+                                  kk.ctypes.data_as(f), vv.ctypes.data_as(f),
+                                  o.ctypes.data_as(f))
+            ops += 2.0 * 2 * s.head_dim * (pos + 1)
+        return ops
+
+    def run(self, frac: float = 1.0):
+        t0 = time.perf_counter()
+        with cf.ThreadPoolExecutor(self.threads) as ex:
+            ops = sum(ex.map(lambda i: self._token(i, frac), range(self.threads)))
+        return ops, time.perf_counter() - t0
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(s, threads: int, frac: float = 1.0) -> dict:
+    from oracle import oracle as ro
+    if not ro.ref_available():
+        return {"value": None, "unit": "TOPS", "cores": threads, "kind": "reference",
+                "sample": "unavailable: oracle/_ref was not built (needs the reference checkout)"}
+    rs = RefSample(s, threads)
+    ops, sec = rs.run(frac)
+    return {"value": ops / sec / 1e12, "unit": "TOPS", "cores": threads, "kind": "reference",
+            "seconds": sec, "tokens_per_s": threads / sec,
+            "sample": (f"reef engine (oracle/_ref, -O2 -ffp-contract=off): {threads} threads x 1 "
+                       f"token through the 4 W8A8 projections ({frac:.3g} of their output "
+                       f"columns) + its 32-head causal float attention at positions spread over "
+                       f"0..{SEQ - 1}; W8A8 linear re-transposes W per call as reef does")}
+
+
+def run_reference(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    s = shape()
+    threads = host_threads()
+    from oracle import oracle as ro
+    if not ro.ref_available():
+        print(json.dumps({"impl": "reference",
+                          "unavailable": "oracle/_ref not built: reef's engine headers were "
+                                         "absent when build() ran"}))
+        return 0
+    rs = RefSample(s, threads)
+    # warm-up steps: a token through 1% of every projection
+    for _ in range(max(args.warmup, 0)):
+        rs.run(0.01)
+    # timed steps: each a bounded sample; the whole run stays within minutes
+    frac = min(1.0, 150.0 / (7.0 * max(args.steps, 1)))
+    total_ops, total_s = 0.0, 0.0
+    for _ in range(args.steps):
+        ops, sec = rs.run(frac)
+        total_ops += ops
+        total_s += sec
+    v = total_ops / total_s / 1e12
+    out = {
+        "metric": METRIC, "value": v, "unit": "TOPS", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_s / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": BATCH, "seq_len": SEQ, "tokens": BATCH * SEQ,
+                   "hidden": s.hidden, "heads": s.heads_q, "ffn": s.ffn},
+        "tokens_per_s": threads * args.steps / total_s,
+        "cpu_baseline": {"value": v, "unit": "TOPS", "cores": threads, "kind": "reference",
+                         "sample": f"per step: {threads} threads x 1 token through {frac:.3g} of "
+                                   f"the projections' output columns + attention"},
+        "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
+    return 0
+
+
+# ---- clocks during the timed region ----------------------------------------------
+
+class Clocks:
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        rows = []
+        for (t, line) in self.lines:
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 10:
+                continue
+            try:
+                rows.append(dict(t=t, sm=float(p[2]), smax=float(p[3]), power=float(p[4]),
+                                 hw=p[6], hwt=p[7], swt=p[8], pcap=p[9]))
+            except ValueError:
+                continue
+        inside = [r for r in rows if t0 <= r["t"] <= t1 + 0.05] or rows[-3:]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        reasons = set()
+        for r in inside:
+            if r["hw"].lower() == "active":
+                reasons.add("hw_slowdown")
+            if r["hwt"].lower() == "active":
+                reasons.add("hw_thermal_slowdown")
+            if r["swt"].lower() == "active":
+                reasons.add("sw_thermal_slowdown")
+            if r["pcap"].lower() == "active":
+                reasons.add("sw_power_cap")
+        return {"sm_mhz": statistics.median(r["sm"] for r in inside),
+                "sm_max_mhz": max(r["smax"] for r in inside), "reasons": sorted(reasons),
+                "samples": len(inside), "power_w_max": max(r["power"] for r in inside)}
+
+
+def peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            m = json.load(fh)
+        return {"bf16_sustained": m["bf16_tflops_sustained"], "bf16": m["bf16_tflops"],
+                "hbm": m["hbm_gbs"], "source": "measured"}
+    except Exception:
+        return {"bf16_sustained": 1400.0, "bf16": 1590.0, "hbm": 6650.0, "source": "fallback"}
+
+
+# ---- the product ---------------------------------------------------------------
+
+def run_reef(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from reef_b200 import _lib, tp
+    from reef_b200 import kernels as K
+    from reef_b200.layer import LlamaLayer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=dt.timedelta(seconds=180), device_id=dev)
+    s = shape()
+    T = BATCH * SEQ
+    comm = tp.Comm(rank, world, timeout_s=120.0) if world > 1 else None
+    L = LlamaLayer(s, BATCH, SEQ, seed=1, world=world, rank=rank, comm=comm, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    x = torch.randn((T, s.hidden), generator=g, device=dev)
+    y = torch.empty_like(x)
+    lib = _lib.lib()
+    launches = lib.reef_b200_llama_layer_kernel_launches(C.byref(L.desc))
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        L.forward(x, y)
+    torch.cuda.synchronize(dev)
+    K.check_device_error()
+
+    # events: 10 per step around the GEMMs and the flash kernel
+    K_steps = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(10)] for _ in range(K_steps)]
+    for row in evs:
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize(dev)
+    handles = [(C.c_void_p * 10)(*[e.cuda_event for e in row]) for row in evs]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.6)  # the sampler is up before the timed region
+    barrier()
+    torch.cuda.synchronize(dev)
+    w0 = time.time()
+    t_start.record(stream)
+    for k in range(K_steps):
+        _lib.call("reef_b200_llama_layer_forward_events", C.byref(L.desc), x.data_ptr(),
+                  y.data_ptr(), L.workspace.data_ptr(), L.workspace.numel(), handles[k],
+                  stream.cuda_stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    w1 = time.time()
+    barrier()
+    time.sleep(0.25)
+    clocks.stop()
+    K.check_device_error()
+    ms = t_start.elapsed_time(t_end) / K_steps
+    spans = [[row[2 * i].elapsed_time(row[2 * i + 1]) for i in range(5)] for row in evs]
+    gemm_ms = statistics.mean(sum(r[i] for i in (0, 2, 3, 4)) for r in spans)
+    flash_ms = statistics.mean(r[1] for r in spans)
+    per_gemm = [statistics.mean(r[i] for r in spans) for i in (0, 2, 3, 4)]
+
+    # end to end through the C ABI with host buffers
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(x)
+    e_steps = max(3, min(K_steps, 20))
+    for _ in range(2):
+        xd.copy_(xh, non_blocking=True)
+        L.forward(xd, y)
+        yh.copy_(y, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        xd.copy_(xh, non_blocking=True)
+        L.forward(xd, y)
+        yh.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+    barrier()
+
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms, gemm_ms, flash_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, gemm_ms_max, flash_ms_max = t.tolist()
+
+    ops = layer_ops(s, T, SEQ)
+    value = ops["total"] / (ms * 1e-3) / 1e12
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16_sustained"]
+    rank_gemm_ops = ops["gemm"] / world
+    achieved = rank_gemm_ops / (gemm_ms * 1e-3) / 1e12
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "gemm_i8_llama7b_traffic.json")
+    if os.path.exists(tf):
+        try:
+            with open(tf) as fh:
+                traffic = json.load(fh).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+    out = {
+        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": K_steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": BATCH, "seq_len": SEQ, "tokens": T,
+                   "hidden": s.hidden, "heads": s.heads_q, "kv_heads": s.heads_kv,
+                   "ffn": s.ffn, "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2 (x 256 MiB, weights 200 MiB): no flush"},
+        "tokens_per_s": T / (ms * 1e-3),
+        "ops_per_step": ops["total"],
+        "roofline": {"bound": "tensor", "kernel": "gemm_i8 (tcgen05 kind::i8)",
+                     "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+                     "frac": achieved / int8_peak, "traffic": traffic,
+                     "peak_source": (f"2 x bf16_tflops_sustained of {pk['source']} "
+                                     "(B200 dense int8 rate = 2 x dense bf16)"),
+                     "per_launch_ms": per_gemm,
+                     "launch_ops": [2.0 * T * s.hidden * (s.heads_q + 2 * s.heads_kv) * 128 / world,
+                                    2.0 * T * s.heads_q * 128 * s.hidden / world,
+                                    2.0 * T * s.hidden * 2 * s.ffn / world,
+                                    2.0 * T * s.ffn * s.hidden / world]},
+        "attention": {"kernel": "flash_prefill_i8", "ms": flash_ms,
+                      "achieved_tops": ops["attention"] / world / (flash_ms * 1e-3) / 1e12},
+        "e2e": {"value": ops["total"] / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                "h2d_bytes_per_step": T * s.hidden * 4, "d2h_bytes_per_step": T * s.hidden * 4,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": int(launches) * K_steps,
+        "clocks": clocks.summary(w0, w1),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(s, host_threads())
+    if comm is not None:
+        torch.cuda.synchronize(dev)
+        comm.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out))
+    return 0
+
+
+def main() -> int:
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_reef(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

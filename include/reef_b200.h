@@ -218,6 +218,114 @@ int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t hea
                             const void* vt, const float* v_scale, float* out,
                             reef_b200_stream_t stream);
 
+/* ---- tensor parallelism (new: reef runs on one core) -------------------- */
+
+/* One communicator per rank (one process or host thread per GPU, over NCCL
+ * on NVLink).  Rank 0 makes an id (reef_b200_comm_unique_id_bytes() bytes),
+ * the host shares it with the other ranks, every rank calls
+ * reef_b200_comm_init with the current device set.  Init is non-blocking
+ * internally: when a rank never joins, it returns REEF_B200_ERR_TIMEOUT
+ * after timeout_s seconds (<= 0: 60 s) instead of hanging. */
+typedef struct reef_b200_comm reef_b200_comm;
+size_t reef_b200_comm_unique_id_bytes(void);
+int reef_b200_comm_unique_id(void* id, size_t bytes);
+int reef_b200_comm_init(int rank, int world, const void* id, double timeout_s,
+                        reef_b200_comm** comm);
+/* Finalizes and frees; REEF_B200_ERR_TIMEOUT (and an abort) when peers stall. */
+int reef_b200_comm_destroy(reef_b200_comm* comm);
+/* Frees without waiting for peers (after a peer failed). */
+int reef_b200_comm_abort(reef_b200_comm* comm);
+
+/* Megatron row-parallel W8A8 linear: linear() (operator/linear.hpp:106-134)
+ * with x split by columns (K) and W by input features across the ranks of
+ * `comm`.  x_local [rows][in_local] (this rank's K-slice), w_shard
+ * [out][kpad(in_local)], w_scale [out], bias [out] or NULL (added once).
+ * Each rank quantises its slice with the FULL row's scale (all-reduce MAX of
+ * row maxima), multiplies in int32, all-reduces the int32 partial sums (SUM,
+ * exact) and dequantises: y [rows][out], identical on every rank and
+ * bit-identical to reef_b200_linear_w8a8_bias on the unsplit x and W.
+ * Scratch: x_q [rows][kpad(in_local)], x_scale [rows], row_max [rows], acc
+ * [rows][out] int32 (row_max / acc may be NULL when comm is NULL).  The
+ * column-parallel form needs no collective: it is reef_b200_linear_w8a8 on
+ * the rank's rows of W. */
+int reef_b200_linear_w8a8_rowpar(reef_b200_comm* comm, size_t rows, size_t in_local,
+                                 size_t out, const float* x_local, const int8_t* w_shard,
+                                 const float* w_scale, const float* bias, int8_t* x_q,
+                                 float* x_scale, float* row_max, int32_t* acc, float* y,
+                                 reef_b200_stream_t stream);
+
+/* ---- decoder layers ------------------------------------------------------- */
+
+/* One Llama-shape W8A8 decoder layer (BASELINE configs 3 and 4 shapes) on
+ * this rank's shard: pre-RMSNorm, column-parallel QKV, rotate-half RoPE,
+ * causal int8 flash attention, row-parallel o_proj + residual, pre-RMSNorm,
+ * column-parallel gate/up, SwiGLU, row-parallel down + residual.  Every
+ * projection is reef's W8A8 linear (per-token activation scale, per-channel
+ * weight scale, int32 accumulation).  RMSNorm, RoPE and SwiGLU are not in
+ * reef (parity unpinned; see the GPT-Neo block below for the pinned one).
+ * Weights are this rank's shards, K-major; scales fp32.  Sizes are local
+ * (heads_q, heads_kv, ffn = totals / TP degree); hidden is the full width. */
+typedef struct reef_b200_llama_layer {
+  size_t batch, seq;         /* tokens = batch * seq; seq % 8 == 0 */
+  size_t hidden;             /* model width, multiple of 16 */
+  size_t heads_q, heads_kv;  /* this rank's heads */
+  size_t head_dim;           /* 128 */
+  size_t ffn;                /* this rank's FFN width, multiple of 16 */
+  float rms_eps, rope_base;
+  const float* attn_norm;                       /* [hidden] */
+  const int8_t* w_qkv; const float* s_qkv;      /* [(heads_q+2 heads_kv)*128][hidden] */
+  const int8_t* w_o; const float* s_o;          /* [hidden][heads_q*128] */
+  const float* mlp_norm;                        /* [hidden] */
+  const int8_t* w_gu; const float* s_gu;        /* [2 ffn][hidden]: gate, then up */
+  const int8_t* w_down; const float* s_down;    /* [hidden][ffn] */
+  reef_b200_comm* comm;                         /* NULL: TP = 1 */
+} reef_b200_llama_layer;
+
+/* Bytes of device workspace reef_b200_llama_layer_forward needs (0 when the
+ * description is invalid). */
+size_t reef_b200_llama_layer_workspace_bytes(const reef_b200_llama_layer* layer);
+/* y [tokens][hidden] = layer(x [tokens][hidden]); fp32; y may not alias x.
+ * workspace: 256-byte aligned device memory of at least the queried size. */
+int reef_b200_llama_layer_forward(const reef_b200_llama_layer* layer, const float* x,
+                                  float* y, void* workspace, size_t workspace_bytes,
+                                  reef_b200_stream_t stream);
+
+/* Kernels one forward launches (for launch accounting). */
+size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* layer);
+/* reef_b200_llama_layer_forward that also records 10 caller-created CUDA
+ * events (cudaEvent_t, timing enabled) on `stream`: begin/end of the QKV
+ * GEMM, the flash kernel, the o-proj GEMM, the gate/up GEMM and the down
+ * GEMM, in that order (for per-kernel timing in a live run). */
+int reef_b200_llama_layer_forward_events(const reef_b200_llama_layer* layer, const float* x,
+                                         float* y, void* workspace, size_t workspace_bytes,
+                                         void* const* events, reef_b200_stream_t stream);
+
+/* reef's GPT-Neo W8A8 block, Block<float>::forward (operator/block.hpp:97-108)
+ * on `seq` positions of an empty cache (BASELINE configs 1 and 2): LayerNorm,
+ * q/k/v W8A8 projections (no bias), reef's float head per head (unscaled,
+ * causal, window 0 = global), o_proj + bias + residual, LayerNorm, c_fc +
+ * bias, tanh GELU, c_proj + bias + residual.  Bit-identical to the engine at
+ * every TP degree.  heads / ffn are this rank's (column-parallel q/k/v by
+ * heads and c_fc by columns; row-parallel o_proj and c_proj). */
+typedef struct reef_b200_gptneo_block {
+  size_t seq, hidden, heads, head_dim, ffn, window;
+  float eps;
+  const float* ln1_g; const float* ln1_b;       /* [hidden] */
+  const int8_t* wq; const float* sq;            /* [heads*head_dim][hidden] */
+  const int8_t* wk; const float* sk;
+  const int8_t* wv; const float* sv;
+  const int8_t* wo; const float* so; const float* bo;            /* [hidden][heads*head_dim] */
+  const float* ln2_g; const float* ln2_b;
+  const int8_t* wfc; const float* sfc; const float* bfc;         /* [ffn][hidden] */
+  const int8_t* wproj; const float* sproj; const float* bproj;   /* [hidden][ffn] */
+  reef_b200_comm* comm;                                          /* NULL: TP = 1 */
+} reef_b200_gptneo_block;
+
+size_t reef_b200_gptneo_block_workspace_bytes(const reef_b200_gptneo_block* block);
+int reef_b200_gptneo_block_forward(const reef_b200_gptneo_block* block, const float* x,
+                                   float* y, void* workspace, size_t workspace_bytes,
+                                   reef_b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

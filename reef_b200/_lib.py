@@ -48,7 +48,38 @@ SIGNATURES = {
                                                     _u, _p, _sz, _sz, _p], _i),
     "reef_b200_rope_qkv_quant": ([_sz, _sz, _sz, _sz, C.c_float] + [_p] * 9, _i),
     "reef_b200_flash_attn_i8": ([_sz, _sz, _sz, _sz, _sz, _i, C.c_float] + [_p] * 8, _i),
+    "reef_b200_comm_unique_id_bytes": ([], _sz),
+    "reef_b200_comm_unique_id": ([_p, _sz], _i),
+    "reef_b200_comm_init": ([_i, _i, _p, C.c_double, _p], _i),
+    "reef_b200_comm_destroy": ([_p], _i),
+    "reef_b200_comm_abort": ([_p], _i),
+    "reef_b200_linear_w8a8_rowpar": ([_p, _sz, _sz, _sz] + [_p] * 9 + [_p], _i),
+    "reef_b200_llama_layer_workspace_bytes": ([_p], _sz),
+    "reef_b200_llama_layer_forward": ([_p, _p, _p, _p, _sz, _p], _i),
+    "reef_b200_llama_layer_kernel_launches": ([_p], _sz),
+    "reef_b200_llama_layer_forward_events": ([_p, _p, _p, _p, _sz, _p, _p], _i),
+    "reef_b200_gptneo_block_workspace_bytes": ([_p], _sz),
+    "reef_b200_gptneo_block_forward": ([_p, _p, _p, _p, _sz, _p], _i),
 }
+
+
+class LlamaLayerDesc(C.Structure):
+    """reef_b200_llama_layer (include/reef_b200.h)."""
+    _fields_ = [("batch", _sz), ("seq", _sz), ("hidden", _sz), ("heads_q", _sz),
+                ("heads_kv", _sz), ("head_dim", _sz), ("ffn", _sz), ("rms_eps", C.c_float),
+                ("rope_base", C.c_float), ("attn_norm", _p), ("w_qkv", _p), ("s_qkv", _p),
+                ("w_o", _p), ("s_o", _p), ("mlp_norm", _p), ("w_gu", _p), ("s_gu", _p),
+                ("w_down", _p), ("s_down", _p), ("comm", _p)]
+
+
+class GptNeoBlockDesc(C.Structure):
+    """reef_b200_gptneo_block (include/reef_b200.h)."""
+    _fields_ = [("seq", _sz), ("hidden", _sz), ("heads", _sz), ("head_dim", _sz), ("ffn", _sz),
+                ("window", _sz), ("eps", C.c_float), ("ln1_g", _p), ("ln1_b", _p),
+                ("wq", _p), ("sq", _p), ("wk", _p), ("sk", _p), ("wv", _p), ("sv", _p),
+                ("wo", _p), ("so", _p), ("bo", _p), ("ln2_g", _p), ("ln2_b", _p),
+                ("wfc", _p), ("sfc", _p), ("bfc", _p), ("wproj", _p), ("sproj", _p),
+                ("bproj", _p), ("comm", _p)]
 
 
 class ReefError(RuntimeError):

@@ -266,6 +266,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           const bool full_vec = args.vec_ok && (n + 3 < N);
+          // The residual rows of this chunk are loaded before any store: y may
+          // alias nothing, but the compiler cannot know, and loads ordered
+          // behind stores would serialise on memory latency.
+          float4 res[8];
+          if constexpr (EPI == kEpiF32W8A8) {
+            if (args.residual != nullptr) {
+#pragma unroll
+              for (int it = 0; it < 8; ++it) {
+                const int m = row0 + it * 4 + sub_row;
+                res[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (m < M && n < N) {
+                  const float* rp = args.residual + static_cast<long long>(m) * args.ldy + n;
+                  if (full_vec) {
+                    res[it] = __ldg(reinterpret_cast<const float4*>(rp));
+                  } else {
+                    float t4[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int e = 0; e < 4 && n + e < N; ++e) t4[e] = __ldg(rp + e);
+                    res[it] = make_float4(t4[0], t4[1], t4[2], t4[3]);
+                  }
+                }
+              }
+            }
+          }
 #pragma unroll
           for (int it = 0; it < 8; ++it) {
             const int rl = it * 4 + sub_row;
@@ -283,6 +306,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                   o[e] = __fmul_rn(__int2float_rn(static_cast<int32_t>(av[e])),
                                    __fmul_rn(rsv, ws[e]));
                   if (args.bias_f != nullptr) o[e] = __fadd_rn(o[e], bf[e]);
+                }
+                if (args.residual != nullptr) {  // residual_add(input, sublayer), block.hpp:27-39
+                  o[0] = __fadd_rn(res[it].x, o[0]);
+                  o[1] = __fadd_rn(res[it].y, o[1]);
+                  o[2] = __fadd_rn(res[it].z, o[2]);
+                  o[3] = __fadd_rn(res[it].w, o[3]);
                 }
                 float* y = static_cast<float*>(args.y) + off;
                 if (full_vec) {
@@ -358,7 +387,8 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
   {
     const uintptr_t y = reinterpret_cast<uintptr_t>(args.y);
     const int align = EPI == kEpiI8Shift ? 4 : 16;
-    args.vec_ok = (y % align == 0) && (args.ldy % 4 == 0) ? 1 : 0;
+    const uintptr_t r = reinterpret_cast<uintptr_t>(args.residual);
+    args.vec_ok = (y % align == 0) && (r % 16 == 0) && (args.ldy % 4 == 0) ? 1 : 0;
   }
   kernel<<<grid, kThreads, L::kAlloc, stream>>>(ma, mb, args);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;

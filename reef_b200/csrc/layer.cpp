@@ -1,0 +1,452 @@
+// layer.cpp -- decoder layers assembled from the sm_100a kernels, with
+// Megatron tensor parallelism over the NCCL communicator of comm.cpp.
+//
+// reef runs one GPT-Neo block per layer on one core (operator/block.hpp
+// :97-108) and has no tensor parallelism.  Here a layer is sharded across TP
+// ranks (one process or thread per GPU):
+//   column-parallel  q/k/v (by heads), FFN up / gate / c_fc (by FFN columns):
+//                    each rank owns output rows of W; no communication, and
+//                    every output column equals TP=1's bit for bit.
+//   row-parallel     attention output and FFN down / c_proj (by K): the
+//                    rank's K-slice of the activation is quantised with the
+//                    FULL row's scale (all-reduce MAX of the row maxima), its
+//                    int32 partial sums are all-reduced (SUM, exact), and the
+//                    dequant epilogue adds the bias once and the residual.
+// So y is identical on every rank and bit-identical to TP=1 for the W8A8
+// GEMMs; the GPT-Neo block is bit-identical to reef's Block<float>.
+#include "../../include/reef_b200.h"
+
+#include "comm.h"
+#include "ops.h"
+
+#include <algorithm>
+#include <cstdint>
+
+namespace reef {
+
+int layernorm_exact(long long rows, int width, float eps, const float* x, const float* gain,
+                    const float* shift, float* y, cudaStream_t stream);
+int gelu_exact(long long n, const float* x, float* y, cudaStream_t stream);
+
+namespace {
+
+#define REEF_TRY(expr)            \
+  do {                            \
+    const int rc_ = (expr);       \
+    if (rc_ != kOk) return rc_;   \
+  } while (0)
+
+// Bump allocator over the caller's workspace (256-byte aligned pieces).
+struct Carve {
+  uint8_t* base;
+  size_t used = 0;
+  size_t cap;
+  explicit Carve(void* b, size_t c) : base(static_cast<uint8_t*>(b)), cap(c) {}
+  template <typename T>
+  T* take(size_t count) {
+    used = (used + 255) & ~static_cast<size_t>(255);
+    T* p = reinterpret_cast<T*>(base ? base + used : nullptr);
+    used += count * sizeof(T);
+    return p;
+  }
+  bool fits() const { return base == nullptr || used <= cap; }
+};
+
+GemmProblem problem(long long rows, int in, int out, const int8_t* a, const int8_t* w) {
+  GemmProblem p{};
+  p.M = static_cast<int>(rows);
+  p.N = out;
+  p.K = in;
+  p.a = a;
+  p.lda = static_cast<long long>(kpad(in));
+  p.b = w;
+  p.ldb = static_cast<long long>(kpad(in));
+  return p;
+}
+
+int gemm_w8a8_f32(long long rows, int in, int out, const int8_t* xq, const float* xs,
+                  const int8_t* w, const float* ws, const float* bias, const float* residual,
+                  float* y, cudaStream_t st) {
+  GemmProblem p = problem(rows, in, out, xq, w);
+  p.args.x_scale = xs;
+  p.args.w_scale = ws;
+  p.args.bias_f = bias;
+  p.args.residual = residual;
+  p.args.y = y;
+  p.args.ldy = out;
+  return gemm_i8(p, kEpiF32W8A8, st);
+}
+
+}  // namespace
+
+// Row-parallel W8A8 linear.  `quant` fills xq/xs from the local input given
+// the full-row maximum (or computes it itself when row_max is null);
+// `absmax` writes the local row maxima.
+// Optional instrumentation: record ev[0] / ev[1] around one kernel launch.
+struct Span {
+  cudaEvent_t* ev;
+  cudaStream_t st;
+  Span(cudaEvent_t* e, cudaStream_t s) : ev(e), st(s) {
+    if (ev) cudaEventRecord(ev[0], st);
+  }
+  ~Span() {
+    if (ev) cudaEventRecord(ev[1], st);
+  }
+};
+
+template <typename Quant, typename AbsMax>
+int rowpar_linear(Comm* c, long long rows, int in_local, int out, Quant quant, AbsMax absmax,
+                  const int8_t* w, const float* ws, const float* bias, const float* residual,
+                  int8_t* xq, float* xs, float* row_max, int32_t* acc, float* y,
+                  cudaStream_t st, cudaEvent_t* ev = nullptr) {
+  if (comm_world(c) == 1) {
+    REEF_TRY(quant(static_cast<const float*>(nullptr)));
+    Span sp(ev, st);
+    return gemm_w8a8_f32(rows, in_local, out, xq, xs, w, ws, bias, residual, y, st);
+  }
+  REEF_TRY(absmax(row_max));
+  REEF_TRY(allreduce_max_f32(c, row_max, static_cast<size_t>(rows), st));
+  REEF_TRY(quant(static_cast<const float*>(row_max)));
+  GemmProblem p = problem(rows, in_local, out, xq, w);
+  p.args.y = acc;
+  p.args.ldy = out;
+  {
+    Span sp(ev, st);
+    REEF_TRY(gemm_i8(p, kEpiI32, st));
+  }
+  REEF_TRY(allreduce_sum_i32(c, acc, static_cast<size_t>(rows) * out, st));
+  return w8a8_epilogue_i32(rows, out, acc, xs, ws, bias, residual, y, st);
+}
+
+}  // namespace reef
+
+using namespace reef;
+
+namespace {
+
+inline cudaStream_t S(reef_b200_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+inline Comm* C(reef_b200_comm* c) { return reinterpret_cast<Comm*>(c); }
+
+// ---- Llama-shape layer ----------------------------------------------------------
+
+struct LlamaBufs {
+  int8_t* xq;
+  float* xs;
+  float* row_max;
+  float* big;     // qkv, later gate/up
+  int8_t* q8;
+  int8_t* k8;
+  int8_t* v8;
+  float* qs;
+  float* ks;
+  float* vs;
+  void* vt;
+  float* attn;
+  float* h;
+  int32_t* acc;
+};
+
+size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
+  const size_t T = L->batch * L->seq;
+  const size_t H = L->hidden, hq = L->heads_q, hkv = L->heads_kv, F = L->ffn, D = 128;
+  Carve c(ws, ~static_cast<size_t>(0));
+  const size_t widest = std::max({kpad(H), kpad(hq * D), kpad(F)});
+  b->xq = c.take<int8_t>(T * widest);
+  b->xs = c.take<float>(T);
+  b->row_max = c.take<float>(T);
+  b->big = c.take<float>(T * std::max((hq + 2 * hkv) * D, 2 * F));
+  b->q8 = c.take<int8_t>(T * hq * D);
+  b->k8 = c.take<int8_t>(T * hkv * D);
+  b->v8 = c.take<int8_t>(T * hkv * D);
+  b->qs = c.take<float>(T * hq);
+  b->ks = c.take<float>(T * hkv);
+  b->vs = c.take<float>(T * hkv);
+  b->vt = c.take<uint16_t>(T * hkv * D);
+  b->attn = c.take<float>(T * hq * D);
+  b->h = c.take<float>(T * H);
+  b->acc = c.take<int32_t>(L->comm != nullptr ? T * H : 0);
+  return c.used + 256;
+}
+
+int llama_check(const reef_b200_llama_layer* L) {
+  if (L == nullptr) return REEF_B200_ERR_INVALID;
+  if (L->batch == 0 || L->seq == 0 || L->hidden == 0 || L->heads_q == 0 || L->heads_kv == 0 ||
+      L->ffn == 0 || L->head_dim != 128 || L->heads_q % L->heads_kv != 0 ||
+      L->hidden % 16 != 0 || L->ffn % 16 != 0 || L->seq % 8 != 0 ||
+      L->batch * L->seq > (1u << 30))
+    return REEF_B200_ERR_INVALID;
+  if (!L->attn_norm || !L->w_qkv || !L->s_qkv || !L->w_o || !L->s_o || !L->mlp_norm ||
+      !L->w_gu || !L->s_gu || !L->w_down || !L->s_down)
+    return REEF_B200_ERR_INVALID;
+  return REEF_B200_OK;
+}
+
+// ---- GPT-Neo block ------------------------------------------------------------
+
+struct NeoBufs {
+  float* h;
+  float* q;
+  float* k;
+  float* v;
+  float* ctx;
+  float* a;
+  float* f;
+  int8_t* xq;
+  float* xs;
+  float* row_max;
+  int32_t* acc;
+};
+
+size_t neo_carve(const reef_b200_gptneo_block* B, void* ws, NeoBufs* b) {
+  const size_t T = B->seq, d = B->hidden, dl = B->heads * B->head_dim, F = B->ffn;
+  Carve c(ws, ~static_cast<size_t>(0));
+  b->h = c.take<float>(T * d);
+  b->q = c.take<float>(T * dl);
+  b->k = c.take<float>(T * dl);
+  b->v = c.take<float>(T * dl);
+  b->ctx = c.take<float>(T * dl);
+  b->a = c.take<float>(T * d);
+  b->f = c.take<float>(T * F);
+  b->xq = c.take<int8_t>(T * std::max({kpad(d), kpad(dl), kpad(F)}));
+  b->xs = c.take<float>(T);
+  b->row_max = c.take<float>(T);
+  b->acc = c.take<int32_t>(B->comm != nullptr ? T * d : 0);
+  return c.used + 256;
+}
+
+int neo_check(const reef_b200_gptneo_block* B) {
+  if (B == nullptr) return REEF_B200_ERR_INVALID;
+  if (B->seq == 0 || B->hidden == 0 || B->heads == 0 || B->head_dim == 0 || B->ffn == 0 ||
+      B->seq > static_cast<size_t>(kMaxKeysExact))
+    return REEF_B200_ERR_INVALID;
+  if (!B->ln1_g || !B->ln2_g || !B->wq || !B->wk || !B->wv || !B->sq || !B->sk || !B->sv ||
+      !B->wo || !B->so || !B->wfc || !B->sfc || !B->wproj || !B->sproj)
+    return REEF_B200_ERR_INVALID;
+  return REEF_B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+// ---- communicator -----------------------------------------------------------------
+
+size_t reef_b200_comm_unique_id_bytes(void) { return comm_unique_id_bytes(); }
+
+int reef_b200_comm_unique_id(void* id, size_t bytes) { return comm_unique_id(id, bytes); }
+
+int reef_b200_comm_init(int rank, int world, const void* id, double timeout_s,
+                        reef_b200_comm** comm) {
+  if (comm == nullptr) return REEF_B200_ERR_INVALID;
+  Comm* c = nullptr;
+  const int rc = comm_init(rank, world, id, timeout_s, &c);
+  *comm = reinterpret_cast<reef_b200_comm*>(c);
+  return rc;
+}
+
+int reef_b200_comm_destroy(reef_b200_comm* comm) { return comm_destroy(C(comm)); }
+
+int reef_b200_comm_abort(reef_b200_comm* comm) { return comm_abort(C(comm)); }
+
+// ---- tensor-parallel linears -----------------------------------------------------
+
+int reef_b200_linear_w8a8_rowpar(reef_b200_comm* comm, size_t rows, size_t in_local,
+                                 size_t out, const float* x_local, const int8_t* w_shard,
+                                 const float* w_scale, const float* bias, int8_t* x_q,
+                                 float* x_scale, float* row_max, int32_t* acc, float* y,
+                                 reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (in_local == 0 || out == 0 || rows > (1u << 31) - 1 || !x_local || !w_shard || !w_scale ||
+      !x_q || !x_scale || !y)
+    return REEF_B200_ERR_INVALID;
+  if (comm != nullptr && comm_world(C(comm)) > 1 && (!row_max || !acc))
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  const long long R = static_cast<long long>(rows);
+  const int K = static_cast<int>(in_local), N = static_cast<int>(out);
+  cudaStream_t st = S(stream);
+  auto quant = [&](const float* rm) {
+    return quantize_rows(R, K, x_local, x_q, static_cast<long long>(kpad(in_local)), x_scale, rm,
+                         st);
+  };
+  auto absmax = [&](float* rm) { return row_absmax(R, K, x_local, rm, st); };
+  return rowpar_linear(C(comm), R, K, N, quant, absmax, w_shard, w_scale, bias, nullptr, x_q,
+                       x_scale, row_max, acc, y, st);
+}
+
+// ---- Llama-shape layer -------------------------------------------------------------
+
+size_t reef_b200_llama_layer_workspace_bytes(const reef_b200_llama_layer* L) {
+  if (llama_check(L) != REEF_B200_OK) return 0;
+  LlamaBufs b;
+  return llama_carve(L, nullptr, &b);
+}
+
+size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* L) {
+  if (llama_check(L) != REEF_B200_OK) return 0;
+  // rmsnorm+quant, qkv GEMM, rope q/k, quant v, flash, o-proj, rmsnorm+quant,
+  // gate/up GEMM, down; a row-parallel linear is quant + GEMM (TP=1) or
+  // absmax + quant + int32 GEMM + dequant epilogue (TP>1)
+  return L->comm != nullptr ? 15 : 11;
+}
+
+static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* y,
+                         void* workspace, size_t workspace_bytes, cudaEvent_t* ev,
+                         reef_b200_stream_t stream);
+
+int reef_b200_llama_layer_forward(const reef_b200_llama_layer* L, const float* x, float* y,
+                                  void* workspace, size_t workspace_bytes,
+                                  reef_b200_stream_t stream) {
+  return llama_forward(L, x, y, workspace, workspace_bytes, nullptr, stream);
+}
+
+int reef_b200_llama_layer_forward_events(const reef_b200_llama_layer* L, const float* x,
+                                         float* y, void* workspace, size_t workspace_bytes,
+                                         void* const* events, reef_b200_stream_t stream) {
+  if (events == nullptr) return REEF_B200_ERR_INVALID;
+  cudaEvent_t ev[10];
+  for (int i = 0; i < 10; ++i) {
+    if (events[i] == nullptr) return REEF_B200_ERR_INVALID;
+    ev[i] = static_cast<cudaEvent_t>(events[i]);
+  }
+  return llama_forward(L, x, y, workspace, workspace_bytes, ev, stream);
+}
+
+static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* y,
+                         void* workspace, size_t workspace_bytes, cudaEvent_t* ev,
+                         reef_b200_stream_t stream) {
+  if (int rc = llama_check(L)) return rc;
+  if (!x || !y || !workspace) return REEF_B200_ERR_INVALID;
+  LlamaBufs b;
+  if (llama_carve(L, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = S(stream);
+  Comm* c = C(L->comm);
+  const long long T = static_cast<long long>(L->batch * L->seq);
+  const int H = static_cast<int>(L->hidden), hq = static_cast<int>(L->heads_q),
+            hkv = static_cast<int>(L->heads_kv), F = static_cast<int>(L->ffn), D = 128;
+  const int qkv_w = (hq + 2 * hkv) * D;
+
+  // attention block: y_attn = x + o_proj(attn(rope(qkv(rmsnorm(x)))))
+  REEF_TRY(rmsnorm_quant(T, H, L->rms_eps, x, L->attn_norm, b.xq, b.xs, st));
+  {
+    Span sp(ev ? ev + 0 : nullptr, st);
+    REEF_TRY(gemm_w8a8_f32(T, H, qkv_w, b.xq, b.xs, L->w_qkv, L->s_qkv, nullptr, nullptr, b.big,
+                           st));
+  }
+  REEF_TRY(rope_qkv_quant(static_cast<int>(L->batch), static_cast<int>(L->seq), hq, hkv,
+                          L->rope_base, b.big, b.q8, b.k8, b.v8, b.qs, b.ks, b.vs, b.vt, st));
+  FlashProblem fp{};
+  fp.batch = static_cast<int>(L->batch);
+  fp.heads_q = hq;
+  fp.heads_kv = hkv;
+  fp.seq = static_cast<int>(L->seq);
+  fp.head_dim = D;
+  fp.causal = 1;
+  fp.sm_scale = 0.08838834764831845f;  // 1 / sqrt(128)
+  fp.q8 = b.q8;
+  fp.k8 = b.k8;
+  fp.vt = b.vt;
+  fp.q_scale = b.qs;
+  fp.k_scale = b.ks;
+  fp.v_scale = b.vs;
+  fp.out = b.attn;
+  fp.out_ld = static_cast<long long>(hq) * D;
+  {
+    Span sp(ev ? ev + 2 : nullptr, st);
+    REEF_TRY(flash_prefill_i8(fp, st));
+  }
+  {
+    auto quant = [&](const float* rm) {
+      return quantize_rows(T, hq * D, b.attn, b.xq, static_cast<long long>(kpad(hq * D)), b.xs,
+                           rm, st);
+    };
+    auto absmax = [&](float* rm) { return row_absmax(T, hq * D, b.attn, rm, st); };
+    REEF_TRY(rowpar_linear(c, T, hq * D, H, quant, absmax, L->w_o, L->s_o, nullptr, x, b.xq,
+                           b.xs, b.row_max, b.acc, b.h, st, ev ? ev + 4 : nullptr));
+  }
+  // MLP block: y = h + down(swiglu(gate_up(rmsnorm(h))))
+  REEF_TRY(rmsnorm_quant(T, H, L->rms_eps, b.h, L->mlp_norm, b.xq, b.xs, st));
+  {
+    Span sp(ev ? ev + 6 : nullptr, st);
+    REEF_TRY(gemm_w8a8_f32(T, H, 2 * F, b.xq, b.xs, L->w_gu, L->s_gu, nullptr, nullptr, b.big,
+                           st));
+  }
+  {
+    auto quant = [&](const float* rm) { return swiglu_quant(T, F, b.big, rm, b.xq, b.xs, st); };
+    auto absmax = [&](float* rm) { return swiglu_absmax(T, F, b.big, rm, st); };
+    REEF_TRY(rowpar_linear(c, T, F, H, quant, absmax, L->w_down, L->s_down, nullptr, b.h, b.xq,
+                           b.xs, b.row_max, b.acc, y, st, ev ? ev + 8 : nullptr));
+  }
+  return REEF_B200_OK;
+}
+
+// ---- GPT-Neo W8A8 block ---------------------------------------------------------------
+
+size_t reef_b200_gptneo_block_workspace_bytes(const reef_b200_gptneo_block* B) {
+  if (neo_check(B) != REEF_B200_OK) return 0;
+  NeoBufs b;
+  return neo_carve(B, nullptr, &b);
+}
+
+int reef_b200_gptneo_block_forward(const reef_b200_gptneo_block* B, const float* x, float* y,
+                                   void* workspace, size_t workspace_bytes,
+                                   reef_b200_stream_t stream) {
+  if (int rc = neo_check(B)) return rc;
+  if (!x || !y || !workspace) return REEF_B200_ERR_INVALID;
+  NeoBufs b;
+  if (neo_carve(B, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = S(stream);
+  Comm* c = C(B->comm);
+  const long long T = static_cast<long long>(B->seq);
+  const int d = static_cast<int>(B->hidden), dl = static_cast<int>(B->heads * B->head_dim),
+            F = static_cast<int>(B->ffn);
+  const long long ld = static_cast<long long>(kpad(d));
+
+  // Attention::forward (attention.hpp:354-372): ln_1, q/k/v projections
+  // (column-parallel by heads), every local head, o_proj (row-parallel) with
+  // the residual of Block::forward (block.hpp:99-102) fused in.
+  REEF_TRY(layernorm_exact(T, d, B->eps, x, B->ln1_g, B->ln1_b, b.h, st));
+  REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
+  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wq, B->sq, nullptr, nullptr, b.q, st));
+  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wk, B->sk, nullptr, nullptr, b.k, st));
+  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wv, B->sv, nullptr, nullptr, b.v, st));
+  AttnHeadArgs aa{};
+  aa.heads = static_cast<int>(B->heads);
+  aa.query_len = static_cast<int>(T);
+  aa.key_len = static_cast<int>(T);
+  aa.head_dim = static_cast<int>(B->head_dim);
+  aa.window = static_cast<int>(B->window);
+  aa.query_start = 0;
+  aa.q_stride = aa.kv_stride = aa.out_stride = dl;
+  aa.q_head = aa.kv_head = aa.out_head = static_cast<long long>(B->head_dim);
+  REEF_TRY(attention_head_f32(aa, b.q, b.k, b.v, b.ctx, st));
+  {
+    auto quant = [&](const float* rm) {
+      return quantize_rows(T, dl, b.ctx, b.xq, static_cast<long long>(kpad(dl)), b.xs, rm, st);
+    };
+    auto absmax = [&](float* rm) { return row_absmax(T, dl, b.ctx, rm, st); };
+    REEF_TRY(rowpar_linear(c, T, dl, d, quant, absmax, B->wo, B->so, B->bo, x, b.xq, b.xs,
+                           b.row_max, b.acc, b.a, st));
+  }
+  // MLP::forward (mlp.hpp:108-133): ln_2, c_fc (column-parallel) + gelu,
+  // c_proj (row-parallel) with the second residual fused in.
+  REEF_TRY(layernorm_exact(T, d, B->eps, b.a, B->ln2_g, B->ln2_b, b.h, st));
+  REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
+  REEF_TRY(gemm_w8a8_f32(T, d, F, b.xq, b.xs, B->wfc, B->sfc, B->bfc, nullptr, b.f, st));
+  REEF_TRY(gelu_exact(T * F, b.f, b.f, st));
+  {
+    auto quant = [&](const float* rm) {
+      return quantize_rows(T, F, b.f, b.xq, static_cast<long long>(kpad(F)), b.xs, rm, st);
+    };
+    auto absmax = [&](float* rm) { return row_absmax(T, F, b.f, rm, st); };
+    REEF_TRY(rowpar_linear(c, T, F, d, quant, absmax, B->wproj, B->sproj, B->bproj, b.a, b.xq,
+                           b.xs, b.row_max, b.acc, y, st));
+  }
+  return REEF_B200_OK;
+}
+
+}  // extern "C"

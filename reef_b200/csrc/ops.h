@@ -39,6 +39,7 @@ struct GemmArgs {
   const float* w_scale;   // [N]   (kEpiF32W8A8)
   const float* bias_f;    // [N] or null (kEpiF32W8A8)
   const int32_t* bias_i;  // [N] or null (kEpiI8Shift)
+  const float* residual;  // [M][ldy] or null (kEpiF32W8A8): y = residual + y
   void* y;                // [M][ldy] output
   long long ldy;          // elements
   uint32_t shift;         // kEpiI8Shift
@@ -82,7 +83,15 @@ int pad_rows_i8(long long rows, long long in, const int8_t* x, long long ldx,
                 int8_t* y, long long ldy, cudaStream_t stream);
 int w8a8_epilogue_i32(long long rows, long long out, const int32_t* acc,
                       const float* x_scale, const float* w_scale, const float* bias,
-                      float* y, cudaStream_t stream);
+                      const float* residual, float* y, cudaStream_t stream);
+
+// llama.cu -- fused RMSNorm / SwiGLU + per-token quantisation
+int rmsnorm_quant(long long rows, int width, float eps, const float* x, const float* gain,
+                  int8_t* x_q, float* x_scale, cudaStream_t stream);
+int swiglu_quant(long long rows, int ffn, const float* gu, const float* row_max, int8_t* x_q,
+                 float* x_scale, cudaStream_t stream);
+int swiglu_absmax(long long rows, int ffn, const float* gu, float* row_max,
+                  cudaStream_t stream);
 
 // attention_exact.cu -- reef's integer and float heads, bit for bit.
 // Scores stay in shared memory, which bounds the key length.

@@ -146,13 +146,15 @@ __global__ void pad_rows_kernel(long long rows, int in, const int8_t* __restrict
 __global__ void w8a8_epilogue_kernel(long long rows, int out, const int32_t* __restrict__ acc,
                                      const float* __restrict__ xs,
                                      const float* __restrict__ ws,
-                                     const float* __restrict__ bias, float* __restrict__ y) {
+                                     const float* __restrict__ bias,
+                                     const float* __restrict__ residual, float* __restrict__ y) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= rows * out) return;
   const long long r = i / out;
   const int c = static_cast<int>(i - r * out);
   float v = __fmul_rn(__int2float_rn(acc[i]), __fmul_rn(xs[r], ws[c]));
   if (bias != nullptr) v = __fadd_rn(v, bias[c]);
+  if (residual != nullptr) v = __fadd_rn(residual[i], v);
   y[i] = v;
 }
 
@@ -204,11 +206,12 @@ int pad_rows_i8(long long rows, long long in, const int8_t* x, long long ldx, in
 }
 
 int w8a8_epilogue_i32(long long rows, long long out, const int32_t* acc, const float* x_scale,
-                      const float* w_scale, const float* bias, float* y, cudaStream_t stream) {
+                      const float* w_scale, const float* bias, const float* residual, float* y,
+                      cudaStream_t stream) {
   if (rows == 0) return kOk;
   const long long n = rows * out;
   w8a8_epilogue_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
-      rows, static_cast<int>(out), acc, x_scale, w_scale, bias, y);
+      rows, static_cast<int>(out), acc, x_scale, w_scale, bias, residual, y);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
