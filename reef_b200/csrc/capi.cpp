@@ -257,7 +257,7 @@ int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t he
   if (int rc = check_device()) return rc;
   return rope_qkv_quant(static_cast<int>(batch), static_cast<int>(seq),
                         static_cast<int>(heads_q), static_cast<int>(heads_kv), rope_base, qkv,
-                        q8, k8, v8, q_scale, k_scale, v_scale, vt,
+                        q8, k8, v8, q_scale, k_scale, v_scale, vt, nullptr,
                         S(stream));
 }
 

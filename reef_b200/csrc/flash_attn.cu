@@ -43,14 +43,15 @@ constexpr int kHeadDim = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;
 
+constexpr int kKStages = 4;  // K tiles in flight (16 KB each)
 struct FL {
-  static constexpr int kQ = 0;                    // 16 KB
-  static constexpr int kK = 16384;                // 2 x 16 KB
-  static constexpr int kV = kK + 2 * 16384;       // 2 x 32 KB
-  static constexpr int kP = kV + 2 * 32768;       // 2 x 32 KB
-  static constexpr int kScales = kP + 2 * 32768;  // sk[2][128], sv[2][128]
+  static constexpr int kQ = 0;                            // 16 KB
+  static constexpr int kK = 16384;                        // kKStages x 16 KB
+  static constexpr int kV = kK + kKStages * 16384;        // 2 x 32 KB
+  static constexpr int kP = kV + 2 * 32768;               // 2 x 32 KB
+  static constexpr int kScales = kP + 2 * 32768;          // sk[2][128], sv[2][128]
   static constexpr int kBars = kScales + 4 * 128 * 4;
-  static constexpr int kNumBars = 18;
+  static constexpr int kNumBars = 14 + 2 * kKStages;
   static constexpr int kTmemSlot = kBars + kNumBars * 8;
   static constexpr int kAlloc = kTmemSlot + 16 + 1024;
 };
@@ -84,15 +85,15 @@ __global__ void __launch_bounds__(kFThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FL::kBars);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;  // [2]
-  uint64_t* o_ready = bars + 15; // [2]
-  uint64_t* drain = bars + 17;
+  uint64_t* v_full = bars + 1;   // [2]
+  uint64_t* v_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;   // [2]
+  uint64_t* s_empty = bars + 7;  // [2]
+  uint64_t* p_full = bars + 9;   // [2]
+  uint64_t* o_ready = bars + 11; // [2]
+  uint64_t* drain = bars + 13;
+  uint64_t* k_full = bars + 14;              // [kKStages]
+  uint64_t* k_empty = bars + 14 + kKStages;  // [kKStages]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + FL::kTmemSlot);
   float* sk_s = reinterpret_cast<float*>(smem + FL::kScales);  // [2][128]
   float* sv_s = sk_s + 256;                                    // [2][128]
@@ -100,9 +101,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = a.seq;
   const int num_q_tiles = (S + kTile - 1) / kTile;
-  const int bh_count = a.batch * a.heads_q;
-  const int bh = blockIdx.x % bh_count;
-  const int q_tile = num_q_tiles - 1 - static_cast<int>(blockIdx.x / bh_count);
+  // head-major order: the query tiles of one head run together and share its
+  // K / V in L2; within a head the longest (causal) tiles start first
+  const int bh = static_cast<int>(blockIdx.x / num_q_tiles);
+  const int q_tile = num_q_tiles - 1 - static_cast<int>(blockIdx.x % num_q_tiles);
   const int b = bh / a.heads_q, h = bh % a.heads_q;
   const int hkv = h / (a.heads_q / a.heads_kv);
   const int q0 = q_tile * kTile;
@@ -115,9 +117,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
     prefetch_tensormap(&tk);
     prefetch_tensormap(&tv);
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKStages; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
@@ -140,32 +144,38 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const uint32_t tO = tmem + 256;  // O: columns [256, 384)
 
   if (warp == 0) {
+    // ---------------- TMA producers ----------------
+    // lane 0: Q, then the K ring; lane 1: the V ring.  Independent threads,
+    // so a V refill waiting for P.V never holds back the next K tile.
+    const int vrow = (b * a.heads_kv + hkv) * kHeadDim;
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      bool ok = true;
       mbar_arrive_expect_tx(q_full, 16384);
       tma_load_2d(smem + FL::kQ, &tq, q_full, h * kHeadDim, b * S + q0);
-      const int vrow = (b * a.heads_kv + hkv) * kHeadDim;
       int issued = 0;
-      for (int j = 0; j < n && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = ((j >> 1) & 1) ^ 1u;
-        if (!mbar_wait(&k_empty[s], ph, err, kDevTimeoutEmpty)) { ok = false; break; }
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kKStages;
+        if (!mbar_wait(&k_empty[s], ((j / kKStages) & 1) ^ 1u, err, kDevTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&k_full[s], 16384);
         tma_load_2d(smem + FL::kK + s * 16384, &tk, &k_full[s], hkv * kHeadDim, b * S + j * kTile);
-        if (!mbar_wait(&v_empty[s], ph, err, kDevTimeoutEmpty)) { ok = false; break; }
+        issued = j + 1;
+      }
+      // let in-flight copies land before exit
+      mbar_wait(q_full, 0, err, kDevTimeoutDrain);
+      for (int j = issued > kKStages ? issued - kKStages : 0; j < issued; ++j)
+        mbar_wait(&k_full[j % kKStages], (j / kKStages) & 1, err, kDevTimeoutDrain);
+    } else if (lane == 1) {
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1u, err, kDevTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&v_full[s], 32768);
         uint8_t* vs = smem + FL::kV + s * 32768;
         tma_load_2d(vs, &tv, &v_full[s], j * kTile, vrow);
         tma_load_2d(vs + 16384, &tv, &v_full[s], j * kTile + 64, vrow);
         issued = j + 1;
       }
-      // let in-flight copies land before exit
-      mbar_wait(q_full, 0, err, kDevTimeoutDrain);
-      for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
-        mbar_wait(&k_full[j & 1], (j >> 1) & 1, err, kDevTimeoutDrain);
+      for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
         mbar_wait(&v_full[j & 1], (j >> 1) & 1, err, kDevTimeoutDrain);
-      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -176,16 +186,17 @@ __global__ void __launch_bounds__(kFThreads, 1)
       tc_fence_after();
       const uint32_t sq = smem_u32(smem + FL::kQ);
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1, err, kDevTimeoutFull)) return false;
+        const int ks = j % kKStages;  // K ring slot
+        const int sb = j & 1;         // TMEM score buffer
+        if (!mbar_wait(&k_full[ks], (j / kKStages) & 1, err, kDevTimeoutFull)) return false;
         tc_fence_after();
-        const uint32_t sk = smem_u32(smem + FL::kK + s * 16384);
+        const uint32_t sk = smem_u32(smem + FL::kK + ks * 16384);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_i8(tS + s * 128, smem_desc_k_sw128(sq + kk * 32), smem_desc_k_sw128(sk + kk * 32),
+          mma_i8(tS + sb * 128, smem_desc_k_sw128(sq + kk * 32), smem_desc_k_sw128(sk + kk * 32),
                  kIdescS, kk > 0 ? 1u : 0u);
-        mma_commit(&k_empty[s]);
-        mma_commit(&s_full[s]);
+        mma_commit(&k_empty[ks]);
+        mma_commit(&s_full[sb]);
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -226,13 +237,21 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const long long kv_base = (static_cast<long long>(b) * a.heads_kv + hkv) * S;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
+    // per-key scales of the next tile are loaded a tile ahead, into registers
+    float nk = t < S ? __ldg(a.k_scale + kv_base + t) : 0.0f;
+    float nv = t < S ? __ldg(a.v_scale + kv_base + t) : 0.0f;
     for (int j = 0; j < n; ++j) {
       const int bb = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      const int key_t = j * kTile + t;
-      sk_s[bb * 128 + t] = key_t < S ? a.k_scale[kv_base + key_t] : 0.0f;
-      sv_s[bb * 128 + t] = key_t < S ? a.v_scale[kv_base + key_t] : 0.0f;
+      sk_s[bb * 128 + t] = nk;
+      sv_s[bb * 128 + t] = nv;
       named_barrier(1, 128);
+      {
+        const int key_n = (j + 1) * kTile + t;
+        const bool has = j + 1 < n && key_n < S;
+        nk = has ? __ldg(a.k_scale + kv_base + key_n) : 0.0f;
+        nv = has ? __ldg(a.v_scale + kv_base + key_n) : 0.0f;
+      }
       if (ok) ok = mbar_wait(&s_full[bb], ph, err, kDevTimeoutAccFull);
       ok = __all_sync(0xffffffffu, ok);  // reconverge before warp-collective tcgen05.ld
       tc_fence_after();
@@ -341,7 +360,20 @@ __global__ void __launch_bounds__(kFThreads, 1)
 // (i, i+64)), then the head's 128 values quantised with reef's rule
 // (quant.hpp:51-81: scale = max|x|/127, rne, clamp).  Outputs: q8 [T][Hq*128],
 // k8 [T][Hkv*128] token-major (the int8 cache rows) and scales [B][H][S].
+// (cos, sin) of pos * base^(-2i/128) for pos < seq, i < 64: computed once per
+// forward so the per-element RoPE is two table loads.
+__global__ void rope_table_kernel(int seq, float base, float2* __restrict__ table) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= seq * 64) return;
+  const int pos = idx >> 6, i = idx & 63;
+  const float inv_freq = powf(base, -static_cast<float>(2 * i) / kHeadDim);
+  float sn, cs;
+  sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
+  table[idx] = make_float2(cs, sn);
+}
+
 __global__ void rope_qk_quant_kernel(int tokens, int seq, int hq, int hkv, float base,
+                                     const float2* __restrict__ table,
                                      const float* __restrict__ qkv, int8_t* __restrict__ q8,
                                      int8_t* __restrict__ k8, float* __restrict__ qs,
                                      float* __restrict__ ks) {
@@ -358,9 +390,15 @@ __global__ void rope_qk_quant_kernel(int tokens, int seq, int hq, int hkv, float
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     const int i = lane + 32 * p;
-    const float inv_freq = powf(base, -static_cast<float>(2 * i) / kHeadDim);
     float sn, cs;
-    sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
+    if (table != nullptr) {
+      const float2 t = __ldg(table + pos * 64 + i);
+      cs = t.x;
+      sn = t.y;
+    } else {
+      const float inv_freq = powf(base, -static_cast<float>(2 * i) / kHeadDim);
+      sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
+    }
     const float lo = p == 0 ? lo0 : lo1, hi = p == 0 ? hi0 : hi1;
     v[p] = lo * cs - hi * sn;
     v[p + 2] = hi * cs + lo * sn;
@@ -483,12 +521,16 @@ int flash_prefill_i8(const FlashProblem& p, cudaStream_t stream) {
 
 int rope_qkv_quant(int batch, int seq, int heads_q, int heads_kv, float rope_base,
                    const float* qkv, int8_t* q8, int8_t* k8, int8_t* v8, float* q_scale,
-                   float* k_scale, float* v_scale, void* vt, cudaStream_t stream) {
+                   float* k_scale, float* v_scale, void* vt, void* rope_table,
+                   cudaStream_t stream) {
   const int tokens = batch * seq;
   if (tokens <= 0 || heads_q <= 0 || heads_kv <= 0) return kErrInvalid;
+  float2* table = static_cast<float2*>(rope_table);
+  if (table != nullptr)
+    rope_table_kernel<<<(seq * 64 + 255) / 256, 256, 0, stream>>>(seq, rope_base, table);
   const long long warps = static_cast<long long>(tokens) * (heads_q + heads_kv);
   rope_qk_quant_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(
-      tokens, seq, heads_q, heads_kv, rope_base, qkv, q8, k8, q_scale, k_scale);
+      tokens, seq, heads_q, heads_kv, rope_base, table, qkv, q8, k8, q_scale, k_scale);
   dim3 grid(static_cast<unsigned>((tokens + 31) / 32), static_cast<unsigned>(heads_kv));
   v_quant_kernel<<<grid, 128, 0, stream>>>(tokens, seq, heads_q, heads_kv, qkv, v8, v_scale,
                                            static_cast<__half*>(vt));

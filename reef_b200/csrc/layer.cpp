@@ -144,6 +144,7 @@ struct LlamaBufs {
   float* attn;
   float* h;
   int32_t* acc;
+  void* rope;     // [seq][64] (cos, sin)
 };
 
 size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
@@ -165,6 +166,7 @@ size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
   b->attn = c.take<float>(T * hq * D);
   b->h = c.take<float>(T * H);
   b->acc = c.take<int32_t>(L->comm != nullptr ? T * H : 0);
+  b->rope = c.take<float>(L->seq * 64 * 2);
   return c.used + 256;
 }
 
@@ -284,10 +286,10 @@ size_t reef_b200_llama_layer_workspace_bytes(const reef_b200_llama_layer* L) {
 
 size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* L) {
   if (llama_check(L) != REEF_B200_OK) return 0;
-  // rmsnorm+quant, qkv GEMM, rope q/k, quant v, flash, o-proj, rmsnorm+quant,
-  // gate/up GEMM, down; a row-parallel linear is quant + GEMM (TP=1) or
-  // absmax + quant + int32 GEMM + dequant epilogue (TP>1)
-  return L->comm != nullptr ? 15 : 11;
+  // rmsnorm+quant, qkv GEMM, rope table, rope q/k, quant v, flash, o-proj,
+  // rmsnorm+quant, gate/up GEMM, down; a row-parallel linear is quant + GEMM
+  // (TP=1) or absmax + quant + int32 GEMM + dequant epilogue (TP>1)
+  return L->comm != nullptr ? 16 : 12;
 }
 
 static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* y,
@@ -336,7 +338,8 @@ static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* 
                            st));
   }
   REEF_TRY(rope_qkv_quant(static_cast<int>(L->batch), static_cast<int>(L->seq), hq, hkv,
-                          L->rope_base, b.big, b.q8, b.k8, b.v8, b.qs, b.ks, b.vs, b.vt, st));
+                          L->rope_base, b.big, b.q8, b.k8, b.v8, b.qs, b.ks, b.vs, b.vt, b.rope,
+                          st));
   FlashProblem fp{};
   fp.batch = static_cast<int>(L->batch);
   fp.heads_q = hq;

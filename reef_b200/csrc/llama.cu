@@ -21,7 +21,6 @@ namespace reef {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kCache = 16;  // float4 per thread held in registers
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
@@ -81,7 +80,10 @@ __device__ __forceinline__ float4 swiglu4(float4 g, float4 u) {
                      silu_mul(g.w, u.w));
 }
 
-// width % 4 == 0, width <= 4 * kCache * kThreads
+// width % 4 == 0, width <= 4 * CACHE * kThreads.  CACHE (float4 per
+// thread) is the smallest that holds the row, so registers, and with them
+// occupancy and loads in flight, follow the row width.
+template <int CACHE>
 __global__ void __launch_bounds__(kThreads)
     rmsnorm_quant_kernel(int width, float eps, const float* __restrict__ x,
                          const float* __restrict__ gain, int8_t* __restrict__ xq,
@@ -91,10 +93,10 @@ __global__ void __launch_bounds__(kThreads)
   const float4* xr = reinterpret_cast<const float4*>(x + row * width);
   const float4* gr = reinterpret_cast<const float4*>(gain);
   const int n4 = width >> 2;
-  float4 c[kCache];
+  float4 c[CACHE];
   float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kCache; ++i) {
+  for (int i = 0; i < CACHE; ++i) {
     const int idx = threadIdx.x + i * kThreads;
     if (idx < n4) {
       c[i] = __ldg(xr + idx);
@@ -105,7 +107,7 @@ __global__ void __launch_bounds__(kThreads)
   const float r = 1.0f / sqrtf(ss / static_cast<float>(width) + eps);
   float m = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kCache; ++i) {
+  for (int i = 0; i < CACHE; ++i) {
     const int idx = threadIdx.x + i * kThreads;
     if (idx < n4) {
       const float4 g = __ldg(gr + idx);
@@ -118,7 +120,7 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) xs[row] = scale;
   char4* out = reinterpret_cast<char4*>(xq + row * ldq);
 #pragma unroll
-  for (int i = 0; i < kCache; ++i) {
+  for (int i = 0; i < CACHE; ++i) {
     const int idx = threadIdx.x + i * kThreads;
     if (idx < n4) out[idx] = q8x4(c[i], scale);
   }
@@ -127,6 +129,7 @@ __global__ void __launch_bounds__(kThreads)
 // gu [rows][2*ffn]: gate in [0, ffn), up in [ffn, 2 ffn).  ffn % 4 == 0.
 // row_max == nullptr: quantise with this row's own maximum; else with the
 // given (all-reduced) maximum.
+template <int CACHE>
 __global__ void __launch_bounds__(kThreads)
     swiglu_quant_kernel(int ffn, const float* __restrict__ gu, const float* __restrict__ row_max,
                         int8_t* __restrict__ xq, long long ldq, float* __restrict__ xs) {
@@ -135,10 +138,10 @@ __global__ void __launch_bounds__(kThreads)
   const float4* g4 = reinterpret_cast<const float4*>(gu + row * 2 * ffn);
   const float4* u4 = g4 + (ffn >> 2);
   const int n4 = ffn >> 2;
-  float4 c[kCache];
+  float4 c[CACHE];
   float m = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kCache; ++i) {
+  for (int i = 0; i < CACHE; ++i) {
     const int idx = threadIdx.x + i * kThreads;
     if (idx < n4) {
       c[i] = swiglu4(__ldg(g4 + idx), __ldg(u4 + idx));
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) xs[row] = scale;
   char4* out = reinterpret_cast<char4*>(xq + row * ldq);
 #pragma unroll
-  for (int i = 0; i < kCache; ++i) {
+  for (int i = 0; i < CACHE; ++i) {
     const int idx = threadIdx.x + i * kThreads;
     if (idx < n4) out[idx] = q8x4(c[i], scale);
   }
@@ -171,21 +174,44 @@ __global__ void __launch_bounds__(kThreads)
 
 }  // namespace
 
+// Smallest supported per-thread cache (float4) that holds n4 float4.
+static int cache_for(int n4) {
+  const int per = (n4 + kThreads - 1) / kThreads;
+  for (int c : {1, 2, 4, 6, 8, 12, 16})
+    if (per <= c) return c;
+  return 0;
+}
+
+#define REEF_DISPATCH_CACHE(c, KERNEL, ...)                                   \
+  switch (c) {                                                              \
+    case 1: KERNEL<1><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
+    case 2: KERNEL<2><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
+    case 4: KERNEL<4><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
+    case 6: KERNEL<6><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
+    case 8: KERNEL<8><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
+    case 12: KERNEL<12><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break; \
+    default: KERNEL<16><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break; \
+  }
+
 int rmsnorm_quant(long long rows, int width, float eps, const float* x, const float* gain,
                   int8_t* x_q, float* x_scale, cudaStream_t stream) {
   if (rows == 0) return kOk;
-  if (width <= 0 || width % 4 != 0 || width > 4 * kCache * kThreads) return kErrInvalid;
-  rmsnorm_quant_kernel<<<static_cast<unsigned>(rows), kThreads, 0, stream>>>(
-      width, eps, x, gain, x_q, static_cast<long long>(width), x_scale);
+  const int c = cache_for(width / 4);
+  if (width <= 0 || width % 4 != 0 || c == 0) return kErrInvalid;
+  const unsigned grid = static_cast<unsigned>(rows);
+  REEF_DISPATCH_CACHE(c, rmsnorm_quant_kernel, width, eps, x, gain, x_q,
+                      static_cast<long long>(width), x_scale);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int swiglu_quant(long long rows, int ffn, const float* gu, const float* row_max, int8_t* x_q,
                  float* x_scale, cudaStream_t stream) {
   if (rows == 0) return kOk;
-  if (ffn <= 0 || ffn % 4 != 0 || ffn > 4 * kCache * kThreads) return kErrInvalid;
-  swiglu_quant_kernel<<<static_cast<unsigned>(rows), kThreads, 0, stream>>>(
-      ffn, gu, row_max, x_q, static_cast<long long>(ffn), x_scale);
+  const int c = cache_for(ffn / 4);
+  if (ffn <= 0 || ffn % 4 != 0 || c == 0) return kErrInvalid;
+  const unsigned grid = static_cast<unsigned>(rows);
+  REEF_DISPATCH_CACHE(c, swiglu_quant_kernel, ffn, gu, row_max, x_q,
+                      static_cast<long long>(ffn), x_scale);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

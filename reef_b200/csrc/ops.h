@@ -130,6 +130,7 @@ struct FlashProblem {
 int flash_prefill_i8(const FlashProblem& p, cudaStream_t stream);
 int rope_qkv_quant(int batch, int seq, int heads_q, int heads_kv, float rope_base,
                    const float* qkv, int8_t* q8, int8_t* k8, int8_t* v8, float* q_scale,
-                   float* k_scale, float* v_scale, void* vt, cudaStream_t stream);
+                   float* k_scale, float* v_scale, void* vt, void* rope_table,
+                   cudaStream_t stream);  // rope_table: [seq][64] float2 scratch or null
 
 }  // namespace reef

@@ -16,7 +16,6 @@ namespace reef {
 namespace {
 
 constexpr int kQuantThreads = 256;
-constexpr int kCache = 16;  // float4 per thread kept in registers (16 KiB rows)
 
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
@@ -43,7 +42,10 @@ __device__ __forceinline__ int8_t q8(float x, float scale) {
 }
 
 // One CTA per row.  row_max (optional) supplies a precomputed max |x| per
-// row (the all-reduced maximum of a tensor-parallel shard).
+// row (the all-reduced maximum of a tensor-parallel shard).  CACHE float4
+// per thread stay in registers (the smallest that holds the row, so
+// registers and occupancy follow the width); longer rows re-read the rest.
+template <int CACHE>
 __global__ void __launch_bounds__(kQuantThreads)
     quantize_rows_vec4(int in, const float* __restrict__ x, int8_t* __restrict__ xq,
                        long long ldq, float* __restrict__ xs,
@@ -52,10 +54,10 @@ __global__ void __launch_bounds__(kQuantThreads)
   const long long row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * in);
   const int n4 = in >> 2;
-  float4 cache[kCache];
+  float4 cache[CACHE];
   float m = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kCache; ++i) {
+  for (int i = 0; i < CACHE; ++i) {
     const int idx = threadIdx.x + i * kQuantThreads;
     if (idx < n4) {
       cache[i] = __ldg(xr + idx);
@@ -63,7 +65,7 @@ __global__ void __launch_bounds__(kQuantThreads)
                          fmaxf(fabsf(cache[i].z), fabsf(cache[i].w))));
     }
   }
-  for (int idx = threadIdx.x + kCache * kQuantThreads; idx < n4; idx += kQuantThreads) {
+  for (int idx = threadIdx.x + CACHE * kQuantThreads; idx < n4; idx += kQuantThreads) {
     const float4 v = __ldg(xr + idx);
     m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
@@ -77,14 +79,14 @@ __global__ void __launch_bounds__(kQuantThreads)
   if (threadIdx.x == 0) xs[row] = scale;
   char4* out = reinterpret_cast<char4*>(xq + row * ldq);
 #pragma unroll
-  for (int i = 0; i < kCache; ++i) {
+  for (int i = 0; i < CACHE; ++i) {
     const int idx = threadIdx.x + i * kQuantThreads;
     if (idx < n4) {
       const float4 v = cache[i];
       out[idx] = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
     }
   }
-  for (int idx = threadIdx.x + kCache * kQuantThreads; idx < n4; idx += kQuantThreads) {
+  for (int idx = threadIdx.x + CACHE * kQuantThreads; idx < n4; idx += kQuantThreads) {
     const float4 v = __ldg(xr + idx);
     out[idx] = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
   }
@@ -169,8 +171,22 @@ int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q, lon
                    (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(x_q) % 4 == 0);
   if (vec) {
-    quantize_rows_vec4<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
-        static_cast<int>(in), x, x_q, ldq, x_scale, row_max);
+    const int per = static_cast<int>((in / 4 + kQuantThreads - 1) / kQuantThreads);
+    const unsigned grid = static_cast<unsigned>(rows);
+    const int ii = static_cast<int>(in);
+    if (per <= 1) {
+      quantize_rows_vec4<1><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+    } else if (per <= 2) {
+      quantize_rows_vec4<2><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+    } else if (per <= 4) {
+      quantize_rows_vec4<4><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+    } else if (per <= 8) {
+      quantize_rows_vec4<8><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+    } else if (per <= 12) {
+      quantize_rows_vec4<12><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+    } else {
+      quantize_rows_vec4<16><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+    }
   } else {
     quantize_rows_scalar<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
         static_cast<int>(in), x, x_q, ldq, x_scale, row_max);
