@@ -109,6 +109,28 @@ int reef_b200_gemm_w8a8(size_t rows, size_t in, size_t out, const int8_t* x_q,
                         const float* x_scale, const int8_t* w, const float* w_scale,
                         const float* bias, float* y, reef_b200_stream_t stream);
 
+/* reef_b200_linear_w8a8_bias for callers that cannot allocate device memory
+ * at all (a host that owns every byte through its own arena, a port of
+ * reef's never-allocating Coral firmware, or a latency-critical path that
+ * cannot take cudaMalloc's synchronisation).  No counterpart in the
+ * reference: reef's kernels take their scratch from the caller.  Same
+ * arguments and bit-identical result as reef_b200_linear_w8a8_bias (bias may
+ * be NULL), but no scratch arguments: the int8 rows and row scales live in a
+ * fixed array of REEF_B200_NOALLOC_SCRATCH_BYTES inside the library, held by
+ * every GPU that loads it until the process exits.  Limit:
+ *   round_up(rows * reef_b200_kpad(in), 256) + 4 * rows
+ *     <= REEF_B200_NOALLOC_SCRATCH_BYTES,
+ * else REEF_B200_ERR_TOO_LARGE (e.g. 2048 rows of 4096, or 128 rows of
+ * 65536).  The first call on a device looks up the array's device address
+ * (with that device current); make that first call before any stream
+ * capture.  Every call shares the array and it keeps the last call's
+ * contents, so calls that overlap on the GPU (other streams or host threads
+ * on the same device) race: serialise them.  No device memory is allocated. */
+#define REEF_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
+int reef_b200_linear_w8a8_noalloc(size_t rows, size_t in, size_t out, const float* x,
+                                  const int8_t* w, const float* w_scale, const float* bias,
+                                  float* y, reef_b200_stream_t stream);
+
 /* ---- integer-only linear (int8.hpp:74-101) ------------------------------ */
 
 /* reef_kernels::linear_int8 (kernels.hpp:101-103):

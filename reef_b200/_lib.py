@@ -34,6 +34,7 @@ SIGNATURES = {
     "reef_b200_linear_w8a8": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p], _i),
     "reef_b200_linear_w8a8_bias": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _p], _i),
     "reef_b200_gemm_w8a8": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p], _i),
+    "reef_b200_linear_w8a8_noalloc": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p], _i),
     "reef_b200_linear_int8": ([_sz, _sz, _sz, _p, _p, _u, _p, _p], _i),
     "reef_b200_linear_bias_int8": ([_sz, _sz, _sz, _p, _p, _p, _u, _p, _p], _i),
     "reef_b200_gemm_i8_i32": ([_sz, _sz, _sz, _p, _p, _p, _p], _i),
