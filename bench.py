@@ -152,9 +152,9 @@ def run_reference(args) -> int:
     threads = host_threads()
     from oracle import oracle as ro
     if not ro.ref_available():
-        print(json.dumps({"impl": "reference",
-                          "unavailable": "oracle/_ref not built: reef's engine headers were "
-                                         "absent when build() ran"}))
+        emit({"impl": "reference",
+              "unavailable": "oracle/_ref not built: reef's engine headers were absent when "
+                             "build() ran"})
         return 0
     rs = RefSample(s, threads)
     # warm-up steps: a token through 1% of every projection
@@ -181,7 +181,7 @@ def run_reference(args) -> int:
                                    f"the projections' output columns + attention"},
         "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(out))
+    emit(out)
     return 0
 
 
@@ -412,12 +412,28 @@ def run_reef(args) -> int:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(out))
+        emit(out)
     return 0
 
 
+_JSON_OUT = None
+
+
+def emit(obj: dict) -> None:
+    """Print the one JSON line on the real stdout."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
+
+
 def main() -> int:
+    global _JSON_OUT
     args = parse()
+    # Libraries (NCCL, the CUDA runtime) may print to fd 1; keep stdout for the
+    # one JSON line and send everything else to stderr.
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         return run_reference(args)
     return run_reef(args)
