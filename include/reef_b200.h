@@ -131,6 +131,17 @@ int reef_b200_linear_w8a8_noalloc(size_t rows, size_t in, size_t out, const floa
                                   const int8_t* w, const float* w_scale, const float* bias,
                                   float* y, reef_b200_stream_t stream);
 
+/* The W8A8 GEMM for few rows (decode: one token per sequence, rows <= 128):
+ * same result as reef_b200_gemm_w8a8 (bias may be NULL), computed with the
+ * weights as the tensor cores' 128-row operand and K split across SMs, so a
+ * 64-row GEMM streams its weights on every SM.  The int32 partial sums need
+ * reef_b200_gemm_skinny_workspace_bytes(rows, in, out) of scratch. */
+size_t reef_b200_gemm_skinny_workspace_bytes(size_t rows, size_t in, size_t out);
+int reef_b200_gemm_w8a8_skinny(size_t rows, size_t in, size_t out, const int8_t* x_q,
+                               const float* x_scale, const int8_t* w, const float* w_scale,
+                               const float* bias, void* workspace, size_t workspace_bytes,
+                               float* y, reef_b200_stream_t stream);
+
 /* ---- integer-only linear (int8.hpp:74-101) ------------------------------ */
 
 /* reef_kernels::linear_int8 (kernels.hpp:101-103):
@@ -240,6 +251,26 @@ int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t hea
                             const void* vt, const float* v_scale, float* out,
                             reef_b200_stream_t stream);
 
+/* Decode: one new query per sequence against an int8 KV cache (BASELINE
+ * config 4).  attend_head (attention.hpp:117-123) for the query at the last
+ * cached position (it sees every cached key), on the dequantised int8
+ * q / k / v, score scale sm_scale, GQA (query head h reads kv head
+ * h / (heads_q / heads_kv); heads_q / heads_kv in {1, 2, 4, 8, 16}).
+ * q8 [batch][heads_q][128] + q_scale [batch][heads_q]; k_cache / v_cache
+ * [batch][heads_kv][max_len][128] int8 (16-byte aligned) + k_scale / v_scale
+ * [batch][heads_kv][max_len] fp32; lens [batch] int32 on the device (each in
+ * [1, max_len]) or NULL for `len` keys in every sequence.  Split across CTAs
+ * along the keys (flash-decoding); the partial results need
+ * reef_b200_decode_attn_workspace_bytes() of scratch.  out
+ * [batch][heads_q][128] fp32.  Within 1e-2 of the float head. */
+size_t reef_b200_decode_attn_workspace_bytes(size_t batch, size_t heads_q, size_t max_len);
+int reef_b200_decode_attn_i8(size_t batch, size_t heads_q, size_t heads_kv, size_t head_dim,
+                             size_t max_len, const int32_t* lens, size_t len, float sm_scale,
+                             const int8_t* q8, const float* q_scale, const int8_t* k_cache,
+                             const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                             void* workspace, size_t workspace_bytes, float* out,
+                             reef_b200_stream_t stream);
+
 /* ---- tensor parallelism (new: reef runs on one core) -------------------- */
 
 /* One communicator per rank (one process or host thread per GPU, over NCCL
@@ -321,6 +352,24 @@ size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* layer)
 int reef_b200_llama_layer_forward_events(const reef_b200_llama_layer* layer, const float* x,
                                          float* y, void* workspace, size_t workspace_bytes,
                                          void* const* events, reef_b200_stream_t stream);
+
+/* One decode step of the same layer: `batch` sequences
+ * (layer->batch, <= 128; layer->seq is ignored) each add one token.  x / y
+ * [batch][hidden] fp32.  positions [batch] int32 (device): the new token's
+ * position in its sequence; its rotated k and its v are quantised per head
+ * and appended to the int8 cache at that row, then the query attends over
+ * rows [0, position].  Caches: k_cache / v_cache [batch][heads_kv][max_len]
+ * [128] int8 (16-byte aligned), k_scale / v_scale [batch][heads_kv][max_len]
+ * fp32 (one scale per token and head).  Every projection uses the skinny
+ * W8A8 GEMM; the row-parallel ones all-reduce exactly as in the prefill
+ * layer, so every rank's y is bit-identical to TP=1. */
+size_t reef_b200_llama_decode_workspace_bytes(const reef_b200_llama_layer* layer,
+                                              size_t max_len);
+int reef_b200_llama_decode_forward(const reef_b200_llama_layer* layer, const float* x, float* y,
+                                   const int32_t* positions, int8_t* k_cache, float* k_scale,
+                                   int8_t* v_cache, float* v_scale, size_t max_len,
+                                   void* workspace, size_t workspace_bytes,
+                                   reef_b200_stream_t stream);
 
 /* reef's GPT-Neo W8A8 block, Block<float>::forward (operator/block.hpp:97-108)
  * on `seq` positions of an empty cache (BASELINE configs 1 and 2): LayerNorm,

@@ -34,6 +34,8 @@ SIGNATURES = {
     "reef_b200_linear_w8a8": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p], _i),
     "reef_b200_linear_w8a8_bias": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _p], _i),
     "reef_b200_gemm_w8a8": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p], _i),
+    "reef_b200_gemm_skinny_workspace_bytes": ([_sz, _sz, _sz], _sz),
+    "reef_b200_gemm_w8a8_skinny": ([_sz, _sz, _sz] + [_p] * 6 + [_sz, _p, _p], _i),
     "reef_b200_linear_w8a8_noalloc": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p], _i),
     "reef_b200_linear_int8": ([_sz, _sz, _sz, _p, _p, _u, _p, _p], _i),
     "reef_b200_linear_bias_int8": ([_sz, _sz, _sz, _p, _p, _p, _u, _p, _p], _i),
@@ -49,6 +51,9 @@ SIGNATURES = {
                                                     _u, _p, _sz, _sz, _p], _i),
     "reef_b200_rope_qkv_quant": ([_sz, _sz, _sz, _sz, C.c_float] + [_p] * 9, _i),
     "reef_b200_flash_attn_i8": ([_sz, _sz, _sz, _sz, _sz, _i, C.c_float] + [_p] * 8, _i),
+    "reef_b200_decode_attn_workspace_bytes": ([_sz, _sz, _sz], _sz),
+    "reef_b200_decode_attn_i8": ([_sz, _sz, _sz, _sz, _sz, _p, _sz, C.c_float] + [_p] * 7
+                                 + [_sz, _p, _p], _i),
     "reef_b200_comm_unique_id_bytes": ([], _sz),
     "reef_b200_comm_unique_id": ([_p, _sz], _i),
     "reef_b200_comm_init": ([_i, _i, _p, C.c_double, _p], _i),
@@ -59,6 +64,8 @@ SIGNATURES = {
     "reef_b200_llama_layer_forward": ([_p, _p, _p, _p, _sz, _p], _i),
     "reef_b200_llama_layer_kernel_launches": ([_p], _sz),
     "reef_b200_llama_layer_forward_events": ([_p, _p, _p, _p, _sz, _p, _p], _i),
+    "reef_b200_llama_decode_workspace_bytes": ([_p, _sz], _sz),
+    "reef_b200_llama_decode_forward": ([_p] * 8 + [_sz, _p, _sz, _p], _i),
     "reef_b200_gptneo_block_workspace_bytes": ([_p], _sz),
     "reef_b200_gptneo_block_forward": ([_p, _p, _p, _p, _sz, _p], _i),
 }

@@ -293,3 +293,80 @@ int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t hea
 }
 
 }  // extern "C"
+
+extern "C" {
+
+size_t reef_b200_decode_attn_workspace_bytes(size_t batch, size_t heads_q, size_t max_len) {
+  if (batch == 0 || heads_q == 0 || max_len == 0 || batch > (1u << 20) || heads_q > 4096 ||
+      max_len > (1u << 24))
+    return 0;
+  return decode_attn_partial_floats(static_cast<int>(batch), static_cast<int>(heads_q),
+                                    static_cast<int>(max_len)) *
+         sizeof(float);
+}
+
+int reef_b200_decode_attn_i8(size_t batch, size_t heads_q, size_t heads_kv, size_t head_dim,
+                             size_t max_len, const int32_t* lens, size_t len, float sm_scale,
+                             const int8_t* q8, const float* q_scale, const int8_t* k_cache,
+                             const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                             void* workspace, size_t workspace_bytes, float* out,
+                             reef_b200_stream_t stream) {
+  if (batch == 0) return REEF_B200_OK;
+  const size_t need = reef_b200_decode_attn_workspace_bytes(batch, heads_q, max_len);
+  if (need == 0 || head_dim != 128 || heads_kv == 0 || heads_q % heads_kv != 0 ||
+      batch * heads_kv > 65535 || !q8 || !q_scale || !k_cache || !k_scale || !v_cache ||
+      !v_scale || !workspace || !out || workspace_bytes < need)
+    return REEF_B200_ERR_INVALID;
+  const size_t g = heads_q / heads_kv;
+  if (g != 1 && g != 2 && g != 4 && g != 8 && g != 16) return REEF_B200_ERR_INVALID;
+  if (lens == nullptr && (len == 0 || len > max_len)) return REEF_B200_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(q8) % 4 != 0)
+    return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  DecodeProblem p{};
+  p.batch = static_cast<int>(batch);
+  p.heads_q = static_cast<int>(heads_q);
+  p.heads_kv = static_cast<int>(heads_kv);
+  p.max_len = static_cast<int>(max_len);
+  p.sm_scale = sm_scale;
+  p.q8 = q8;
+  p.q_scale = q_scale;
+  p.k_cache = k_cache;
+  p.k_scale = k_scale;
+  p.v_cache = v_cache;
+  p.v_scale = v_scale;
+  p.lens = lens;
+  p.len = static_cast<int>(len);
+  p.partial = static_cast<float*>(workspace);
+  p.out = out;
+  return decode_attn_i8(p, S(stream));
+}
+
+}  // extern "C"
+
+extern "C" {
+
+size_t reef_b200_gemm_skinny_workspace_bytes(size_t rows, size_t in, size_t out) {
+  if (rows == 0 || rows > 128 || in == 0 || out == 0 || in > kMaxDim || out > kMaxDim) return 0;
+  if (check_device() != kOk) return 0;
+  return skinny_partial_bytes(static_cast<int>(rows), static_cast<int>(out), static_cast<int>(in));
+}
+
+int reef_b200_gemm_w8a8_skinny(size_t rows, size_t in, size_t out, const int8_t* x_q,
+                               const float* x_scale, const int8_t* w, const float* w_scale,
+                               const float* bias, void* workspace, size_t workspace_bytes,
+                               float* y, reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (rows > 128 || !dims_ok(rows, in, out) || !x_q || !x_scale || !w || !w_scale || !y ||
+      !workspace)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  if (workspace_bytes < skinny_partial_bytes(static_cast<int>(rows), static_cast<int>(out),
+                                             static_cast<int>(in)))
+    return REEF_B200_ERR_INVALID;
+  return gemm_i8_skinny(static_cast<int>(rows), static_cast<int>(out), static_cast<int>(in), x_q,
+                        w, kEpiF32W8A8, x_scale, w_scale, bias, nullptr, y, workspace, S(stream));
+}
+
+}  // extern "C"

@@ -99,6 +99,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_n = (N + BN - 1) / BN;
   const int num_k = (K + kBK - 1) / kBK;
   const int num_tiles = num_m * num_n;
+  const int splits = args.k_splits > 1 ? args.k_splits : 1;
+  const int num_items = num_tiles * splits;  // (tile, K-split) pairs
   int* err = args.err;
 
   if (threadIdx.x == 0) {
@@ -131,10 +133,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = blockIdx.x; t < num_items && ok; t += gridDim.x) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, args.group_m, mb, nb);
-        for (int kb = 0; kb < num_k; ++kb) {
+        tile_coords(t / splits, num_m, num_n, args.group_m, mb, nb);
+        const int split = t % splits;
+        const int kb0 = split * num_k / splits, kb1 = (split + 1) * num_k / splits;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutEmpty)) {
             ok = false;
             break;
@@ -174,14 +178,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = blockIdx.x; t < num_items && ok; t += gridDim.x) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, err, kDevTimeoutAccEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_k; ++kb) {
+        const int split = t % splits;
+        const int kb0 = split * num_k / splits, kb1 = (split + 1) * num_k / splits;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, kDevTimeoutFull)) {
             ok = false;
             break;
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
             mma_i8(d_tmem, smem_desc_k_sw128(sa + kk * kUmmaK),
                    smem_desc_k_sw128(sb + kk * kUmmaK), kIdesc,
-                   (kb | kk) != 0 ? 1u : 0u);
+                   (kb > kb0 || kk != 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -226,9 +232,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sub_col = (lane & 7) * 4;  // 0, 4, ..., 28
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (int t = blockIdx.x; t < num_items; t += gridDim.x) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, args.group_m, mb, nb);
+      tile_coords(t / splits, num_m, num_n, args.group_m, mb, nb);
+      // K-split partial outputs land in their own slice of y
+      const long long y_off = static_cast<long long>(t % splits) * args.split_stride;
       // warp-uniform outcome: the tcgen05.ld below is warp-collective
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, err, kDevTimeoutAccFull)))
         break;
@@ -331,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   for (int e = 0; e < 4 && n + e < N; ++e) y[e] = o[e];
                 }
               } else {
-                int32_t* y = static_cast<int32_t*>(args.y) + off;
+                int32_t* y = static_cast<int32_t*>(args.y) + y_off + off;
                 if (full_vec) {
                   *reinterpret_cast<uint4*>(y) = a4;
                 } else {
@@ -377,7 +385,8 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
     configured[dev] = true;
   }
   const int num_tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
-  const int grid = std::min(num_tiles, num_sms());
+  const int splits = p.args.k_splits > 1 ? p.args.k_splits : 1;
+  const int grid = std::min(num_tiles * splits, num_sms());
   GemmArgs args = p.args;
   args.M = p.M;
   args.N = p.N;
@@ -394,7 +403,91 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
+// Sums the K-split partials part[s][n][m] (n = weight row, m = token) and
+// applies the epilogue in token-major order: y[m][n].  A 32 x 32 tile goes
+// through shared memory so the partial reads (along m) and the output writes
+// (along n) are both contiguous.
+template <int EPI>
+__global__ void splitk_reduce_kernel(int splits, int M, int N, const int32_t* __restrict__ part,
+                                     const float* __restrict__ xs, const float* __restrict__ ws,
+                                     const float* __restrict__ bias,
+                                     const float* __restrict__ residual, void* __restrict__ y) {
+  __shared__ int32_t tile[32][33];
+  const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int n = n0 + ty + 8 * i, m = m0 + tx;
+    int32_t acc = 0;
+    if (n < N && m < M) {
+      for (int s = 0; s < splits; ++s)
+        acc += part[(static_cast<long long>(s) * N + n) * M + m];
+    }
+    tile[ty + 8 * i][tx] = acc;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty + 8 * i, n = n0 + tx;
+    if (m < M && n < N) {
+      const int32_t a = tile[tx][ty + 8 * i];
+      const long long off = static_cast<long long>(m) * N + n;
+      if constexpr (EPI == kEpiF32W8A8) {
+        float v = __fmul_rn(__int2float_rn(a), __fmul_rn(xs[m], ws[n]));
+        if (bias != nullptr) v = __fadd_rn(v, bias[n]);
+        if (residual != nullptr) v = __fadd_rn(residual[off], v);
+        static_cast<float*>(y)[off] = v;
+      } else {
+        static_cast<int32_t*>(y)[off] = a;
+      }
+    }
+  }
+}
+
+int skinny_splits(int n, int k) {
+  const int tiles = (n + kBM - 1) / kBM;
+  const int nk = (k + kBK - 1) / kBK;
+  const int want = (num_sms() + tiles - 1) / tiles;
+  return std::max(1, std::min(want, std::max(1, nk / 2)));
+}
+
 }  // namespace
+
+size_t skinny_partial_bytes(int m, int n, int k) {
+  return static_cast<size_t>(skinny_splits(n, k)) * n * m * sizeof(int32_t);
+}
+
+int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int epilogue,
+                   const float* x_scale, const float* w_scale, const float* bias,
+                   const float* residual, void* y, void* partial, cudaStream_t stream) {
+  if (m <= 0 || n <= 0 || k <= 0 || m > 128 || partial == nullptr || y == nullptr)
+    return kErrInvalid;
+  if (epilogue != kEpiF32W8A8 && epilogue != kEpiI32) return kErrInvalid;
+  const int splits = skinny_splits(n, k);
+  GemmProblem p{};
+  p.M = n;  // weight rows on the MMA's M side (swap-AB)
+  p.N = m;  // tokens on its N side
+  p.K = k;
+  p.a = w;
+  p.lda = static_cast<long long>(kpad(k));
+  p.b = x;
+  p.ldb = static_cast<long long>(kpad(k));
+  p.args.k_splits = splits;
+  p.args.split_stride = static_cast<long long>(n) * m;
+  p.args.y = partial;
+  p.args.ldy = m;
+  const int rc = m <= 64 ? launch<64, 8, kEpiI32>(p, stream) : launch<128, 6, kEpiI32>(p, stream);
+  if (rc) return rc;
+  dim3 grid(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>((m + 31) / 32));
+  if (epilogue == kEpiF32W8A8) {
+    splitk_reduce_kernel<kEpiF32W8A8><<<grid, dim3(32, 8), 0, stream>>>(
+        splits, m, n, static_cast<const int32_t*>(partial), x_scale, w_scale, bias, residual, y);
+  } else {
+    splitk_reduce_kernel<kEpiI32><<<grid, dim3(32, 8), 0, stream>>>(
+        splits, m, n, static_cast<const int32_t*>(partial), nullptr, nullptr, nullptr, nullptr, y);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
 
 int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0 || p.K <= 0) return kErrInvalid;

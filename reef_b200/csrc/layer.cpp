@@ -118,6 +118,25 @@ int rowpar_linear(Comm* c, long long rows, int in_local, int out, Quant quant, A
   return w8a8_epilogue_i32(rows, out, acc, xs, ws, bias, residual, y, st);
 }
 
+// Row-parallel linear for few rows (decode): the skinny split-K GEMM.
+template <typename Quant, typename AbsMax>
+int rowpar_skinny(Comm* c, int rows, int in_local, int out, Quant quant, AbsMax absmax,
+                  const int8_t* w, const float* ws, const float* residual, int8_t* xq, float* xs,
+                  float* row_max, int32_t* acc, void* partial, float* y, cudaStream_t st) {
+  if (comm_world(c) == 1) {
+    REEF_TRY(quant(static_cast<const float*>(nullptr)));
+    return gemm_i8_skinny(rows, out, in_local, xq, w, kEpiF32W8A8, xs, ws, nullptr, residual, y,
+                          partial, st);
+  }
+  REEF_TRY(absmax(row_max));
+  REEF_TRY(allreduce_max_f32(c, row_max, static_cast<size_t>(rows), st));
+  REEF_TRY(quant(static_cast<const float*>(row_max)));
+  REEF_TRY(gemm_i8_skinny(rows, out, in_local, xq, w, kEpiI32, nullptr, nullptr, nullptr, nullptr,
+                          acc, partial, st));
+  REEF_TRY(allreduce_sum_i32(c, acc, static_cast<size_t>(rows) * out, st));
+  return w8a8_epilogue_i32(rows, out, acc, xs, ws, nullptr, residual, y, st);
+}
+
 }  // namespace reef
 
 using namespace reef;
@@ -177,6 +196,65 @@ int llama_check(const reef_b200_llama_layer* L) {
       L->hidden % 16 != 0 || L->ffn % 16 != 0 || L->seq % 8 != 0 ||
       L->batch * L->seq > (1u << 30))
     return REEF_B200_ERR_INVALID;
+  if (!L->attn_norm || !L->w_qkv || !L->s_qkv || !L->w_o || !L->s_o || !L->mlp_norm ||
+      !L->w_gu || !L->s_gu || !L->w_down || !L->s_down)
+    return REEF_B200_ERR_INVALID;
+  return REEF_B200_OK;
+}
+
+// ---- Llama-shape decode step -------------------------------------------------------
+
+struct DecodeBufs {
+  int8_t* xq;
+  float* xs;
+  float* row_max;
+  float* big;
+  int8_t* q8;
+  float* qs;
+  int* lens;
+  float* attn;
+  float* h;
+  int32_t* acc;
+  void* partial;
+  float* dpart;
+};
+
+size_t decode_carve(const reef_b200_llama_layer* L, size_t max_len, void* ws, DecodeBufs* b) {
+  const size_t B = L->batch;
+  const size_t H = L->hidden, hq = L->heads_q, hkv = L->heads_kv, F = L->ffn, D = 128;
+  Carve c(ws, ~static_cast<size_t>(0));
+  b->xq = c.take<int8_t>(B * std::max({kpad(H), kpad(hq * D), kpad(F)}));
+  b->xs = c.take<float>(B);
+  b->row_max = c.take<float>(B);
+  b->big = c.take<float>(B * std::max((hq + 2 * hkv) * D, 2 * F));
+  b->q8 = c.take<int8_t>(B * hq * D);
+  b->qs = c.take<float>(B * hq);
+  b->lens = c.take<int>(B);
+  b->attn = c.take<float>(B * hq * D);
+  b->h = c.take<float>(B * H);
+  b->acc = c.take<int32_t>(L->comm != nullptr ? B * H : 0);
+  const int Bi = static_cast<int>(B);
+  const size_t part = std::max({skinny_partial_bytes(Bi, static_cast<int>((hq + 2 * hkv) * D),
+                                                     static_cast<int>(H)),
+                                skinny_partial_bytes(Bi, static_cast<int>(H),
+                                                     static_cast<int>(hq * D)),
+                                skinny_partial_bytes(Bi, static_cast<int>(2 * F),
+                                                     static_cast<int>(H)),
+                                skinny_partial_bytes(Bi, static_cast<int>(H), static_cast<int>(F))});
+  b->partial = c.take<uint8_t>(part);
+  b->dpart = c.take<float>(decode_attn_partial_floats(Bi, static_cast<int>(hq),
+                                                       static_cast<int>(max_len)));
+  return c.used + 256;
+}
+
+int decode_check(const reef_b200_llama_layer* L, size_t max_len) {
+  if (L == nullptr || max_len == 0 || max_len > (1u << 24)) return REEF_B200_ERR_INVALID;
+  if (L->batch == 0 || L->batch > 128 || L->hidden == 0 || L->heads_q == 0 ||
+      L->heads_kv == 0 || L->ffn == 0 || L->head_dim != 128 || L->heads_q % L->heads_kv != 0 ||
+      L->hidden % 16 != 0 || L->ffn % 16 != 0)
+    return REEF_B200_ERR_INVALID;
+  const size_t g = L->heads_q / L->heads_kv;
+  if (g != 1 && g != 2 && g != 4 && g != 8 && g != 16) return REEF_B200_ERR_INVALID;
   if (!L->attn_norm || !L->w_qkv || !L->s_qkv || !L->w_o || !L->s_o || !L->mlp_norm ||
       !L->w_gu || !L->s_gu || !L->w_down || !L->s_down)
     return REEF_B200_ERR_INVALID;
@@ -381,6 +459,76 @@ static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* 
     auto absmax = [&](float* rm) { return swiglu_absmax(T, F, b.big, rm, st); };
     REEF_TRY(rowpar_linear(c, T, F, H, quant, absmax, L->w_down, L->s_down, nullptr, b.h, b.xq,
                            b.xs, b.row_max, b.acc, y, st, ev ? ev + 8 : nullptr));
+  }
+  return REEF_B200_OK;
+}
+
+// ---- Llama-shape decode step ---------------------------------------------------------
+
+size_t reef_b200_llama_decode_workspace_bytes(const reef_b200_llama_layer* L, size_t max_len) {
+  if (decode_check(L, max_len) != REEF_B200_OK || check_device() != kOk) return 0;
+  DecodeBufs b;
+  return decode_carve(L, max_len, nullptr, &b);
+}
+
+int reef_b200_llama_decode_forward(const reef_b200_llama_layer* L, const float* x, float* y,
+                                   const int32_t* positions, int8_t* k_cache, float* k_scale,
+                                   int8_t* v_cache, float* v_scale, size_t max_len,
+                                   void* workspace, size_t workspace_bytes,
+                                   reef_b200_stream_t stream) {
+  if (int rc = decode_check(L, max_len)) return rc;
+  if (!x || !y || !positions || !k_cache || !k_scale || !v_cache || !v_scale || !workspace)
+    return REEF_B200_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0 ||
+      (reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 != 0)
+    return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  DecodeBufs b;
+  if (decode_carve(L, max_len, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
+  cudaStream_t st = S(stream);
+  Comm* c = C(L->comm);
+  const int B = static_cast<int>(L->batch), H = static_cast<int>(L->hidden),
+            hq = static_cast<int>(L->heads_q), hkv = static_cast<int>(L->heads_kv),
+            F = static_cast<int>(L->ffn), D = 128;
+  const int qkv_w = (hq + 2 * hkv) * D;
+  REEF_TRY(rmsnorm_quant(B, H, L->rms_eps, x, L->attn_norm, b.xq, b.xs, st));
+  REEF_TRY(gemm_i8_skinny(B, qkv_w, H, b.xq, L->w_qkv, kEpiF32W8A8, b.xs, L->s_qkv, nullptr,
+                          nullptr, b.big, b.partial, st));
+  REEF_TRY(decode_rope_append(B, hq, hkv, static_cast<int>(max_len), L->rope_base, positions,
+                              b.big, b.q8, b.qs, k_cache, k_scale, v_cache, v_scale, b.lens, st));
+  DecodeProblem dp{};
+  dp.batch = B;
+  dp.heads_q = hq;
+  dp.heads_kv = hkv;
+  dp.max_len = static_cast<int>(max_len);
+  dp.sm_scale = 0.08838834764831845f;  // 1 / sqrt(128)
+  dp.q8 = b.q8;
+  dp.q_scale = b.qs;
+  dp.k_cache = k_cache;
+  dp.k_scale = k_scale;
+  dp.v_cache = v_cache;
+  dp.v_scale = v_scale;
+  dp.lens = b.lens;
+  dp.partial = b.dpart;
+  dp.out = b.attn;
+  REEF_TRY(decode_attn_i8(dp, st));
+  {
+    auto quant = [&](const float* rm) {
+      return quantize_rows(B, hq * D, b.attn, b.xq, static_cast<long long>(kpad(hq * D)), b.xs,
+                           rm, st);
+    };
+    auto absmax = [&](float* rm) { return row_absmax(B, hq * D, b.attn, rm, st); };
+    REEF_TRY(rowpar_skinny(c, B, hq * D, H, quant, absmax, L->w_o, L->s_o, x, b.xq, b.xs,
+                           b.row_max, b.acc, b.partial, b.h, st));
+  }
+  REEF_TRY(rmsnorm_quant(B, H, L->rms_eps, b.h, L->mlp_norm, b.xq, b.xs, st));
+  REEF_TRY(gemm_i8_skinny(B, 2 * F, H, b.xq, L->w_gu, kEpiF32W8A8, b.xs, L->s_gu, nullptr,
+                          nullptr, b.big, b.partial, st));
+  {
+    auto quant = [&](const float* rm) { return swiglu_quant(B, F, b.big, rm, b.xq, b.xs, st); };
+    auto absmax = [&](float* rm) { return swiglu_absmax(B, F, b.big, rm, st); };
+    REEF_TRY(rowpar_skinny(c, B, F, H, quant, absmax, L->w_down, L->s_down, b.h, b.xq, b.xs,
+                           b.row_max, b.acc, b.partial, y, st));
   }
   return REEF_B200_OK;
 }

@@ -44,6 +44,8 @@ struct GemmArgs {
   long long ldy;          // elements
   uint32_t shift;         // kEpiI8Shift
   int group_m;            // raster group (0 = default)
+  int k_splits;           // > 1: K split across CTAs; split s writes y + s * split_stride
+  long long split_stride; // elements between the partial outputs of two splits
   int vec_ok;             // 16-byte (int8: 4-byte) output stores allowed (launcher)
   int* err;               // device error word (set by the launcher)
 };
@@ -70,6 +72,17 @@ int make_tma_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes,
 
 // ---- kernels ------------------------------------------------------------------
 int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream);
+
+// Skinny GEMM for few tokens (decode): y[m][n] = epi(sum_k x[m][k] w[n][k]) with
+// the weights as the 128-row MMA operand (swap-AB), tokens (m <= 128) on the
+// MMA's N side, and K split across CTAs into int32 partials in `partial`
+// (skinny_partial_bytes() of scratch), reduced and requantised by a second
+// kernel.  epilogue: kEpiF32W8A8 (x_scale, w_scale, bias, residual -> y fp32)
+// or kEpiI32 (y int32 [m][n], the sums of a row-parallel shard).
+size_t skinny_partial_bytes(int m, int n, int k);
+int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int epilogue,
+                   const float* x_scale, const float* w_scale, const float* bias,
+                   const float* residual, void* y, void* partial, cudaStream_t stream);
 
 // quant.cu
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q,
@@ -132,5 +145,27 @@ int rope_qkv_quant(int batch, int seq, int heads_q, int heads_kv, float rope_bas
                    const float* qkv, int8_t* q8, int8_t* k8, int8_t* v8, float* q_scale,
                    float* k_scale, float* v_scale, void* vt, void* rope_table,
                    cudaStream_t stream);  // rope_table: [seq][64] float2 scratch or null
+
+// decode_attn.cu -- int8 decode attention over an int8 KV cache (split-KV)
+struct DecodeProblem {
+  int batch, heads_q, heads_kv, max_len;
+  float sm_scale;
+  const int8_t* q8;       // [B][Hq][128]
+  const float* q_scale;   // [B][Hq]
+  const int8_t* k_cache;  // [B][Hkv][max_len][128]
+  const float* k_scale;   // [B][Hkv][max_len]
+  const int8_t* v_cache;
+  const float* v_scale;
+  const int* lens;        // [B] cached keys per sequence (device), or null
+  int len;                // cached keys of every sequence when lens is null
+  float* partial;         // decode_attn_partial_floats() floats of scratch
+  float* out;             // [B][Hq][128]
+};
+size_t decode_attn_partial_floats(int batch, int heads_q, int max_len);
+int decode_rope_append(int batch, int heads_q, int heads_kv, int max_len, float rope_base,
+                       const int* positions, const float* qkv, int8_t* q8, float* q_scale,
+                       int8_t* k_cache, float* k_scale, int8_t* v_cache, float* v_scale, int* lens,
+                       cudaStream_t stream);
+int decode_attn_i8(const DecodeProblem& p, cudaStream_t stream);
 
 }  // namespace reef

@@ -175,3 +175,16 @@ def attention_heads_f32(q, k, v, heads: int, query_start: int = 0, window: int =
     _lib.call("reef_b200_attention_heads_f32", heads, ql, kl, hd, query_start, window,
               _ptr(q), dm, hd, _ptr(k), _ptr(v), dm, hd, _ptr(out), dm, hd, _stream())
     return out
+
+
+def gemm_w8a8_skinny(x_q, x_scale, w, w_scale, bias=None, in_features: int | None = None):
+    """The W8A8 GEMM for rows <= 128 (decode), swap-AB + split-K."""
+    rows = x_q.shape[0]
+    k = in_features if in_features is not None else x_q.shape[1]
+    n = w.shape[0]
+    nbytes = _lib.lib().reef_b200_gemm_skinny_workspace_bytes(rows, k, n)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x_q.device)
+    y = torch.empty((rows, n), dtype=torch.float32, device=x_q.device)
+    _lib.call("reef_b200_gemm_w8a8_skinny", rows, k, n, _ptr(x_q), _ptr(x_scale), _ptr(w),
+              _ptr(w_scale), _ptr(bias), _ptr(ws), ws.numel(), _ptr(y), _stream())
+    return y

@@ -121,6 +121,35 @@ class LlamaLayer:
                   y.data_ptr(), self.workspace.data_ptr(), self.workspace.numel(), st)
         return y
 
+    def alloc_cache(self, max_len: int) -> dict:
+        """An empty int8 KV cache for `batch` sequences of this rank's KV heads:
+        k / v [batch][heads_kv][max_len][128] int8 + per-(token, head) scales."""
+        dev = self.w_qkv.device
+        shp = (self.batch, self.heads_kv, max_len)
+        return {"k": torch.zeros(shp + (128,), dtype=torch.int8, device=dev),
+                "ks": torch.zeros(shp, device=dev),
+                "v": torch.zeros(shp + (128,), dtype=torch.int8, device=dev),
+                "vs": torch.zeros(shp, device=dev), "max_len": max_len}
+
+    def decode(self, x: torch.Tensor, positions: torch.Tensor, cache: dict,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode step: x [batch][hidden] (one new token per sequence) at
+        `positions` (int32 [batch], device); appends to `cache`."""
+        max_len = cache["max_len"]
+        ws = getattr(self, "_decode_ws", None)
+        if ws is None or getattr(self, "_decode_len", None) != max_len:
+            n = _lib.lib().reef_b200_llama_decode_workspace_bytes(C.byref(self.desc), max_len)
+            if n == 0:
+                raise ValueError("invalid decode description")
+            self._decode_ws = ws = torch.empty(n, dtype=torch.uint8, device=x.device)
+            self._decode_len = max_len
+        y = torch.empty_like(x) if out is None else out
+        _lib.call("reef_b200_llama_decode_forward", C.byref(self.desc), x.data_ptr(),
+                  y.data_ptr(), positions.data_ptr(), cache["k"].data_ptr(),
+                  cache["ks"].data_ptr(), cache["v"].data_ptr(), cache["vs"].data_ptr(), max_len,
+                  ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+        return y
+
     def host_weights(self) -> dict:
         """This rank's weights on the host (numpy), for the reference checks."""
         return {k: getattr(self, k).cpu().numpy() for k in

@@ -28,6 +28,26 @@ def test_binding_covers_the_header():
         declared ^ set(_lib.SIGNATURES))
 
 
+def _declared_arity() -> dict:
+    """Parameter count of every function the header declares."""
+    import re
+    with open(_lib.HEADER) as fh:
+        text = re.sub(r"/\*.*?\*/", "", fh.read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(reef_b200_\w+)\s*\(([^;{]*?)\)\s*;", text):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_binding_arity_matches_the_header():
+    arity = _declared_arity()
+    assert set(arity) == set(_lib.SIGNATURES)
+    wrong = {f: (arity[f], len(_lib.SIGNATURES[f][0])) for f in arity
+             if arity[f] != len(_lib.SIGNATURES[f][0])}
+    assert not wrong, f"header vs binding argument counts: {wrong}"
+
+
 def test_pure_helpers(L):
     assert L.reef_b200_version() >= 100
     assert [L.reef_b200_kpad(n) for n in (1, 7, 16, 17, 4096, 11008)] == \
