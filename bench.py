@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="reef_b200", choices=["reef_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-mode", default="allgather", choices=["allgather", "allreduce"],
+                    help="tensor-parallel plan at N > 1: all-gather int8 activations "
+                         "(column-sharded residual) or Megatron int32 all-reduce")
     return ap.parse_args()
 
 
@@ -267,7 +270,7 @@ def run_reef(args) -> int:
 
     from reef_b200 import _lib, tp
     from reef_b200 import kernels as K
-    from reef_b200.layer import LlamaLayer
+    from reef_b200.layer import TP_ALLGATHER, TP_ALLREDUCE, LlamaLayer
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -281,9 +284,13 @@ def run_reef(args) -> int:
     s = shape()
     T = BATCH * SEQ
     comm = tp.Comm(rank, world, timeout_s=120.0) if world > 1 else None
-    L = LlamaLayer(s, BATCH, SEQ, seed=1, world=world, rank=rank, comm=comm, device=dev)
+    mode = TP_ALLGATHER if args.tp_mode == "allgather" else TP_ALLREDUCE
+    L = LlamaLayer(s, BATCH, SEQ, seed=1, world=world, rank=rank, comm=comm, device=dev,
+                   tp_mode=mode)
     g = torch.Generator(device=dev).manual_seed(1234)
     x = torch.randn((T, s.hidden), generator=g, device=dev)
+    if world > 1 and mode == TP_ALLGATHER:  # this rank's hidden columns
+        x = x[:, tp.col_slice(s.hidden, world, rank)].contiguous()
     y = torch.empty_like(x)
     lib = _lib.lib()
     launches = lib.reef_b200_llama_layer_kernel_launches(C.byref(L.desc))
@@ -382,6 +389,7 @@ def run_reef(args) -> int:
         "config": {"workload": WORKLOAD, "batch": BATCH, "seq_len": SEQ, "tokens": T,
                    "hidden": s.hidden, "heads": s.heads_q, "kv_heads": s.heads_kv,
                    "ffn": s.ffn, "parallelism": f"tp{world}",
+                   "tp_plan": (args.tp_mode if world > 1 else "none"),
                    "l2": "inputs larger than L2 (x 256 MiB, weights 200 MiB): no flush"},
         "tokens_per_s": T / (ms * 1e-3),
         "ops_per_step": ops["total"],
@@ -398,7 +406,7 @@ def run_reef(args) -> int:
         "attention": {"kernel": "flash_prefill_i8", "ms": flash_ms,
                       "achieved_tops": ops["attention"] / world / (flash_ms * 1e-3) / 1e12},
         "e2e": {"value": ops["total"] / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
-                "h2d_bytes_per_step": T * s.hidden * 4, "d2h_bytes_per_step": T * s.hidden * 4,
+                "h2d_bytes_per_step": x.numel() * 4, "d2h_bytes_per_step": y.numel() * 4,
                 "ms_per_step": e2e_ms},
         "gpu_launches": int(launches) * K_steps,
         "clocks": clocks.summary(w0, w1),

@@ -332,7 +332,23 @@ typedef struct reef_b200_llama_layer {
   const int8_t* w_gu; const float* s_gu;        /* [2 ffn][hidden]: gate, then up */
   const int8_t* w_down; const float* s_down;    /* [hidden][ffn] */
   reef_b200_comm* comm;                         /* NULL: TP = 1 */
+  int tp_mode;  /* with comm: REEF_B200_TP_ALLREDUCE or REEF_B200_TP_ALLGATHER */
 } reef_b200_llama_layer;
+
+/* Two tensor-parallel plans for the Llama layer (both bit-identical to TP=1):
+ *  REEF_B200_TP_ALLREDUCE  Megatron: x and y replicated; q/k/v and gate/up
+ *    column-parallel; o-proj and down row-parallel (w_o [hidden][heads_q*128],
+ *    w_down [hidden][ffn] = this rank's input features), their int32 partial
+ *    sums all-reduced.
+ *  REEF_B200_TP_ALLGATHER  every projection column-parallel on all-gathered
+ *    int8 activations (quantised with the full row's scale first): x and y are
+ *    this rank's hidden/world columns [tokens][hidden/world]; w_o
+ *    [hidden/world][hidden_q] and w_down [hidden/world][ffn_total] are this
+ *    rank's OUTPUT rows over the full K.  Moves int8 activations instead of
+ *    int32 partial sums (about a third of the bytes) and shards every
+ *    element-wise step.  world must divide 8. */
+#define REEF_B200_TP_ALLREDUCE 0
+#define REEF_B200_TP_ALLGATHER 1
 
 /* Bytes of device workspace reef_b200_llama_layer_forward needs (0 when the
  * description is invalid). */

@@ -77,7 +77,7 @@ class LlamaLayerDesc(C.Structure):
                 ("heads_kv", _sz), ("head_dim", _sz), ("ffn", _sz), ("rms_eps", C.c_float),
                 ("rope_base", C.c_float), ("attn_norm", _p), ("w_qkv", _p), ("s_qkv", _p),
                 ("w_o", _p), ("s_o", _p), ("mlp_norm", _p), ("w_gu", _p), ("s_gu", _p),
-                ("w_down", _p), ("s_down", _p), ("comm", _p)]
+                ("w_down", _p), ("s_down", _p), ("comm", _p), ("tp_mode", _i)]
 
 
 class GptNeoBlockDesc(C.Structure):

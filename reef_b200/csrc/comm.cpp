@@ -118,4 +118,16 @@ int allreduce_sum_i32(Comm* c, int32_t* buf, size_t n, cudaStream_t stream) {
   return settle(c, ncclAllReduce(buf, buf, n, ncclInt32, ncclSum, c->nccl, stream));
 }
 
+int allgather_bytes(Comm* c, const void* send, void* recv, size_t bytes, cudaStream_t stream) {
+  if (c == nullptr || c->world == 1) {
+    if (send != recv && bytes > 0)
+      return cudaMemcpyAsync(recv, send, bytes, cudaMemcpyDeviceToDevice, stream) == cudaSuccess
+                 ? kOk
+                 : kErrCuda;
+    return kOk;
+  }
+  if (bytes == 0) return kOk;
+  return settle(c, ncclAllGather(send, recv, bytes, ncclInt8, c->nccl, stream));
+}
+
 }  // namespace reef

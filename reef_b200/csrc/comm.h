@@ -16,5 +16,7 @@ int comm_rank(const Comm* c);
 int comm_world(const Comm* c);
 int allreduce_max_f32(Comm* c, float* buf, size_t n, cudaStream_t stream);
 int allreduce_sum_i32(Comm* c, int32_t* buf, size_t n, cudaStream_t stream);
+// rank-major all-gather: recv = [world][bytes] (send may not alias recv)
+int allgather_bytes(Comm* c, const void* send, void* recv, size_t bytes, cudaStream_t stream);
 
 }  // namespace reef

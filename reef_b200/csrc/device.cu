@@ -107,6 +107,28 @@ int make_tma_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes,
   return r == CUDA_SUCCESS ? kOk : kErrInvalid;
 }
 
+// int8 [segs][rows][cols] with row stride ld_bytes and segment stride
+// seg_bytes; boxes of box_rows x box_cols within one segment.
+int make_tma_3d_i8(CUtensorMap* map, const void* base, long long rows, long long cols,
+                   long long ld_bytes, long long segs, long long seg_bytes, int box_cols,
+                   int box_rows) {
+  EncodeTiled fn = encode_fn();
+  if (fn == nullptr) return kErrCuda;
+  if (segs < 1) return kErrInvalid;
+  if (segs == 1) seg_bytes = ld_bytes * rows;  // unused, but must be a valid stride
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return kErrAlignment;
+  if ((ld_bytes & 15) != 0 || (seg_bytes & 15) != 0) return kErrAlignment;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(segs)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld_bytes), static_cast<cuuint64_t>(seg_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrInvalid;
+}
+
 int make_tma_2d_i8(CUtensorMap* map, const void* base, long long rows, long long cols,
                    long long ld_bytes, int box_cols, int box_rows) {
   return make_tma_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, cols, ld_bytes,

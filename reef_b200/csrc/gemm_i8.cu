@@ -97,7 +97,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int M = args.M, N = args.N, K = args.K;
   const int num_m = (M + kBM - 1) / kBM;
   const int num_n = (N + BN - 1) / BN;
-  const int num_k = (K + kBK - 1) / kBK;
+  // K may come in `segs` equal segments read through 3-D tensor maps (an
+  // all-gathered activation is rank-major [segs][rows][K]); k-block kb is
+  // block kb % kbs of segment kb / kbs.  One segment for plain row-major.
+  const int segs = args.k_segments > 1 ? args.k_segments : 1;
+  const int kbs = (K + kBK - 1) / kBK;
+  const int num_k = kbs * segs;
   const int num_tiles = num_m * num_n;
   const int splits = args.k_splits > 1 ? args.k_splits : 1;
   const int num_items = num_tiles * splits;  // (tile, K-split) pairs
@@ -146,8 +151,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
           mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          tma_load_2d(sa, &tma_a, &full[stage], kb * kBK, mb * kBM);
-          tma_load_2d(sb, &tma_b, &full[stage], kb * kBK, nb * BN);
+          const int seg = kb / kbs, kx = (kb - seg * kbs) * kBK;
+          tma_load_3d(sa, &tma_a, &full[stage], kx, mb * kBM, seg);
+          tma_load_3d(sb, &tma_b, &full[stage], kx, nb * BN, seg);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -370,9 +376,10 @@ template <int BN, int STAGES, int EPI>
 int launch(const GemmProblem& p, cudaStream_t stream) {
   using L = Layout<BN, STAGES>;
   CUtensorMap ma, mb;
-  int rc = make_tma_2d_i8(&ma, p.a, p.M, p.K, p.lda, kBK, kBM);
+  const int segs = p.args.k_segments > 1 ? p.args.k_segments : 1;
+  int rc = make_tma_3d_i8(&ma, p.a, p.M, p.K, p.lda, segs, p.a_seg, kBK, kBM);
   if (rc) return rc;
-  rc = make_tma_2d_i8(&mb, p.b, p.N, p.K, p.ldb, kBK, BN);
+  rc = make_tma_3d_i8(&mb, p.b, p.N, p.K, p.ldb, segs, p.b_seg, kBK, BN);
   if (rc) return rc;
   auto kernel = gemm_i8_kernel<BN, STAGES, EPI>;
   static bool configured[64] = {};

@@ -189,6 +189,57 @@ size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
   return c.used + 256;
 }
 
+bool llama_allgather(const reef_b200_llama_layer* L) {
+  return L->comm != nullptr && comm_world(reinterpret_cast<Comm*>(L->comm)) > 1 &&
+         L->tp_mode == REEF_B200_TP_ALLGATHER;
+}
+
+struct LlamaAgBufs {
+  float* stats;
+  float* stats_all;
+  int8_t* xq;
+  int8_t* xq_all;
+  float* xs;
+  float* row_max;
+  float* big;
+  int8_t* q8;
+  int8_t* k8;
+  int8_t* v8;
+  float* qs;
+  float* ks;
+  float* vs;
+  void* vt;
+  float* attn;
+  float* h;
+  void* rope;
+};
+
+size_t llama_ag_carve(const reef_b200_llama_layer* L, int world, void* ws, LlamaAgBufs* b) {
+  const size_t T = L->batch * L->seq, N = static_cast<size_t>(world);
+  const size_t H = L->hidden, hq = L->heads_q, hkv = L->heads_kv, F = L->ffn, D = 128;
+  const size_t Hl = H / N, S = 8 / N + 1;
+  const size_t kmax = std::max({Hl, hq * D, F});
+  Carve c(ws, ~static_cast<size_t>(0));
+  b->stats = c.take<float>(T * S);
+  b->stats_all = c.take<float>(N * T * S);
+  b->xq = c.take<int8_t>(T * kmax);
+  b->xq_all = c.take<int8_t>(N * T * kmax);
+  b->xs = c.take<float>(T);
+  b->row_max = c.take<float>(T);
+  b->big = c.take<float>(T * std::max((hq + 2 * hkv) * D, 2 * F));
+  b->q8 = c.take<int8_t>(T * hq * D);
+  b->k8 = c.take<int8_t>(T * hkv * D);
+  b->v8 = c.take<int8_t>(T * hkv * D);
+  b->qs = c.take<float>(T * hq);
+  b->ks = c.take<float>(T * hkv);
+  b->vs = c.take<float>(T * hkv);
+  b->vt = c.take<uint16_t>(T * hkv * D);
+  b->attn = c.take<float>(T * hq * D);
+  b->h = c.take<float>(T * Hl);
+  b->rope = c.take<float>(L->seq * 64 * 2);
+  return c.used + 256;
+}
+
 int llama_check(const reef_b200_llama_layer* L) {
   if (L == nullptr) return REEF_B200_ERR_INVALID;
   if (L->batch == 0 || L->seq == 0 || L->hidden == 0 || L->heads_q == 0 || L->heads_kv == 0 ||
@@ -258,6 +309,16 @@ int decode_check(const reef_b200_llama_layer* L, size_t max_len) {
   if (!L->attn_norm || !L->w_qkv || !L->s_qkv || !L->w_o || !L->s_o || !L->mlp_norm ||
       !L->w_gu || !L->s_gu || !L->w_down || !L->s_down)
     return REEF_B200_ERR_INVALID;
+  if (L->hidden % 32 != 0) return REEF_B200_ERR_INVALID;  // 8 RMSNorm chunks of float4
+  if (L->comm != nullptr && L->tp_mode != REEF_B200_TP_ALLREDUCE &&
+      L->tp_mode != REEF_B200_TP_ALLGATHER)
+    return REEF_B200_ERR_INVALID;
+  if (llama_allgather(L)) {
+    const size_t N = static_cast<size_t>(comm_world(reinterpret_cast<Comm*>(L->comm)));
+    if (8 % N != 0 || L->hidden % (32 * N) != 0 || (L->hidden / N) % 16 != 0 ||
+        (L->heads_q * 128) % 16 != 0)
+      return REEF_B200_ERR_INVALID;
+  }
   return REEF_B200_OK;
 }
 
@@ -358,6 +419,10 @@ int reef_b200_linear_w8a8_rowpar(reef_b200_comm* comm, size_t rows, size_t in_lo
 
 size_t reef_b200_llama_layer_workspace_bytes(const reef_b200_llama_layer* L) {
   if (llama_check(L) != REEF_B200_OK) return 0;
+  if (llama_allgather(L)) {
+    LlamaAgBufs b;
+    return llama_ag_carve(L, comm_world(C(L->comm)), nullptr, &b);
+  }
   LlamaBufs b;
   return llama_carve(L, nullptr, &b);
 }
@@ -367,6 +432,7 @@ size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* L) {
   // rmsnorm+quant, qkv GEMM, rope table, rope q/k, quant v, flash, o-proj,
   // rmsnorm+quant, gate/up GEMM, down; a row-parallel linear is quant + GEMM
   // (TP=1) or absmax + quant + int32 GEMM + dequant epilogue (TP>1)
+  if (llama_allgather(L)) return 16;  // rms x2 (stats, apply) + absmax/quant x2, no epilogue pass
   return L->comm != nullptr ? 16 : 12;
 }
 
@@ -392,10 +458,104 @@ int reef_b200_llama_layer_forward_events(const reef_b200_llama_layer* L, const f
   return llama_forward(L, x, y, workspace, workspace_bytes, ev, stream);
 }
 
+// The all-gather plan (REEF_B200_TP_ALLGATHER): x, y and the residual are
+// this rank's hidden/world columns; every projection reads the all-gathered
+// int8 activation (rank-major [world][tokens][K/world], consumed as K
+// segments by the GEMM's 3-D tensor maps) and writes this rank's output rows.
+static int llama_forward_ag(const reef_b200_llama_layer* L, const float* x, float* y,
+                            void* workspace, size_t workspace_bytes, cudaEvent_t* ev,
+                            cudaStream_t st) {
+  Comm* c = C(L->comm);
+  const int N = comm_world(c), rank = comm_rank(c);
+  LlamaAgBufs b;
+  if (llama_ag_carve(L, N, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
+  const long long T = static_cast<long long>(L->batch * L->seq);
+  const int H = static_cast<int>(L->hidden), hq = static_cast<int>(L->heads_q),
+            hkv = static_cast<int>(L->heads_kv), F = static_cast<int>(L->ffn), D = 128;
+  const int Hl = H / N, S = 8 / N + 1, qkv_w = (hq + 2 * hkv) * D;
+  const float* g1 = L->attn_norm + static_cast<long long>(rank) * Hl;
+  const float* g2 = L->mlp_norm + static_cast<long long>(rank) * Hl;
+
+  // all-gathered activation [N][T][kl] times this rank's rows of W [n][N*kl]
+  auto gemm_seg = [&](int kl, const int8_t* w, int n, const float* ws, const float* residual,
+                      float* out, cudaEvent_t* e) -> int {
+    GemmProblem p{};
+    p.M = static_cast<int>(T);
+    p.N = n;
+    p.K = kl;
+    p.a = b.xq_all;
+    p.lda = kl;
+    p.a_seg = T * kl;
+    p.b = w;
+    p.ldb = static_cast<long long>(kl) * N;
+    p.b_seg = kl;
+    p.args.k_segments = N;
+    p.args.x_scale = b.xs;
+    p.args.w_scale = ws;
+    p.args.residual = residual;
+    p.args.y = out;
+    p.args.ldy = n;
+    Span sp(e, st);
+    return gemm_i8(p, kEpiF32W8A8, st);
+  };
+  auto rms = [&](const float* xin, const float* g) -> int {
+    REEF_TRY(rms_stats(T, H, N, xin, g, b.stats, st));
+    REEF_TRY(allgather_bytes(c, b.stats, b.stats_all, static_cast<size_t>(T) * S * 4, st));
+    REEF_TRY(rms_apply_quant(T, H, N, L->rms_eps, xin, g, b.stats_all, b.xq, b.xs, st));
+    return allgather_bytes(c, b.xq, b.xq_all, static_cast<size_t>(T) * Hl, st);
+  };
+
+  REEF_TRY(rms(x, g1));
+  REEF_TRY(gemm_seg(Hl, L->w_qkv, qkv_w, L->s_qkv, nullptr, b.big, ev ? ev + 0 : nullptr));
+  REEF_TRY(rope_qkv_quant(static_cast<int>(L->batch), static_cast<int>(L->seq), hq, hkv,
+                          L->rope_base, b.big, b.q8, b.k8, b.v8, b.qs, b.ks, b.vs, b.vt, b.rope,
+                          st));
+  FlashProblem fp{};
+  fp.batch = static_cast<int>(L->batch);
+  fp.heads_q = hq;
+  fp.heads_kv = hkv;
+  fp.seq = static_cast<int>(L->seq);
+  fp.head_dim = D;
+  fp.causal = 1;
+  fp.sm_scale = 0.08838834764831845f;
+  fp.q8 = b.q8;
+  fp.k8 = b.k8;
+  fp.vt = b.vt;
+  fp.q_scale = b.qs;
+  fp.k_scale = b.ks;
+  fp.v_scale = b.vs;
+  fp.out = b.attn;
+  fp.out_ld = static_cast<long long>(hq) * D;
+  {
+    Span sp(ev ? ev + 2 : nullptr, st);
+    REEF_TRY(flash_prefill_i8(fp, st));
+  }
+  // o-proj: full-row scale of the attention output, then gather its codes
+  REEF_TRY(row_absmax(T, hq * D, b.attn, b.row_max, st));
+  REEF_TRY(allreduce_max_f32(c, b.row_max, static_cast<size_t>(T), st));
+  REEF_TRY(quantize_rows(T, hq * D, b.attn, b.xq, hq * D, b.xs, b.row_max, st));
+  REEF_TRY(allgather_bytes(c, b.xq, b.xq_all, static_cast<size_t>(T) * hq * D, st));
+  REEF_TRY(gemm_seg(hq * D, L->w_o, Hl, L->s_o, x, b.h, ev ? ev + 4 : nullptr));
+  // MLP
+  REEF_TRY(rms(b.h, g2));
+  REEF_TRY(gemm_seg(Hl, L->w_gu, 2 * F, L->s_gu, nullptr, b.big, ev ? ev + 6 : nullptr));
+  REEF_TRY(swiglu_absmax(T, F, b.big, b.row_max, st));
+  REEF_TRY(allreduce_max_f32(c, b.row_max, static_cast<size_t>(T), st));
+  REEF_TRY(swiglu_quant(T, F, b.big, b.row_max, b.xq, b.xs, st));
+  REEF_TRY(allgather_bytes(c, b.xq, b.xq_all, static_cast<size_t>(T) * F, st));
+  return gemm_seg(F, L->w_down, Hl, L->s_down, b.h, y, ev ? ev + 8 : nullptr);
+}
+
 static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* y,
                          void* workspace, size_t workspace_bytes, cudaEvent_t* ev,
                          reef_b200_stream_t stream) {
   if (int rc = llama_check(L)) return rc;
+  if (llama_allgather(L)) {
+    if (!x || !y || !workspace) return REEF_B200_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return REEF_B200_ERR_ALIGNMENT;
+    if (int rc = check_device()) return rc;
+    return llama_forward_ag(L, x, y, workspace, workspace_bytes, ev, S(stream));
+  }
   if (!x || !y || !workspace) return REEF_B200_ERR_INVALID;
   LlamaBufs b;
   if (llama_carve(L, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;

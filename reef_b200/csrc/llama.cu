@@ -80,49 +80,156 @@ __device__ __forceinline__ float4 swiglu4(float4 g, float4 u) {
                      silu_mul(g.w, u.w));
 }
 
-// width % 4 == 0, width <= 4 * CACHE * kThreads.  CACHE (float4 per
-// thread) is the smallest that holds the row, so registers, and with them
-// occupancy and loads in flight, follow the row width.
-template <int CACHE>
-__global__ void __launch_bounds__(kThreads)
+// ---- RMSNorm, defined to be identical at every tensor-parallel degree ----------
+//
+// The row's sum of squares is the fixed tree ((c0+c1)+(c2+c3))+((c4+c5)+(c6+c7))
+// of 8 chunk sums (chunk c = columns [c*W/8, (c+1)*W/8)); a chunk sum is
+// computed by 128 threads (thread i: float4s i, i+128, ... of the chunk, in
+// order), an xor-shuffle tree per warp and ((w0+w1)+w2)+w3 over the chunk's 4
+// warps.  A rank of a tensor-parallel group holding 8/N of the chunks computes
+// the same chunk sums, so the all-gathered chunk sums give the same total.
+// y = (x * gain) * r with r = 1 / sqrt(total / W + eps), and since rounding is
+// monotonic, max|y| = (max|x * gain|) * r exactly, so shards combine their
+// maxima with a max and get the scale TP=1 gets.
+constexpr int kChunks = 8;
+constexpr int kChunkThreads = 128;
+
+__device__ __forceinline__ float sumsq4(float4 v) {
+  return ((v.x * v.x + v.y * v.y) + v.z * v.z) + v.w * v.w;
+}
+
+__device__ __forceinline__ float warp_sum_tree(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float chunk_tree(const float* c) {
+  return ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
+}
+
+__device__ __forceinline__ float4 mul4(float4 a, float4 b) {
+  return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w);
+}
+
+__device__ __forceinline__ float4 scale4(float4 a, float r) {
+  return make_float4(a.x * r, a.y * r, a.z * r, a.w * r);
+}
+
+// TP=1: one CTA of 8 x 128 threads per row; P float4 per thread.
+template <int P>
+__global__ void __launch_bounds__(kChunks * kChunkThreads)
     rmsnorm_quant_kernel(int width, float eps, const float* __restrict__ x,
                          const float* __restrict__ gain, int8_t* __restrict__ xq,
                          long long ldq, float* __restrict__ xs) {
+  __shared__ float wsum[kChunks * 4];
+  __shared__ float csum[kChunks];
   __shared__ float red[32];
   const long long row = blockIdx.x;
-  const float4* xr = reinterpret_cast<const float4*>(x + row * width);
-  const float4* gr = reinterpret_cast<const float4*>(gain);
-  const int n4 = width >> 2;
-  float4 c[CACHE];
-  float ss = 0.0f;
+  const int t = threadIdx.x, c = t / kChunkThreads, i = t % kChunkThreads;
+  const int n4 = width / (4 * kChunks);  // float4 per chunk
+  const float4* xr = reinterpret_cast<const float4*>(x + row * width) + c * n4;
+  const float4* gr = reinterpret_cast<const float4*>(gain) + c * n4;
+  float4 v[P];
+  float s = 0.0f, m = 0.0f;
 #pragma unroll
-  for (int i = 0; i < CACHE; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
+  for (int k = 0; k < P; ++k) {
+    const int idx = i + k * kChunkThreads;
     if (idx < n4) {
-      c[i] = __ldg(xr + idx);
-      ss += c[i].x * c[i].x + c[i].y * c[i].y + c[i].z * c[i].z + c[i].w * c[i].w;
+      v[k] = __ldg(xr + idx);
+      s = s + sumsq4(v[k]);
+      v[k] = mul4(v[k], __ldg(gr + idx));
+      m = fmaxf(m, amax4(v[k]));
     }
   }
-  ss = block_sum(ss, red);
-  const float r = 1.0f / sqrtf(ss / static_cast<float>(width) + eps);
-  float m = 0.0f;
+  s = warp_sum_tree(s);
+  if ((t & 31) == 0) wsum[t >> 5] = s;
+  m = block_max(m, red);  // syncs: wsum is visible after this
+  if (t < kChunks) csum[t] = ((wsum[4 * t] + wsum[4 * t + 1]) + wsum[4 * t + 2]) + wsum[4 * t + 3];
+  __syncthreads();
+  const float r = 1.0f / sqrtf(chunk_tree(csum) / static_cast<float>(width) + eps);
+  const float mx = m * r;
+  const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  if (t == 0) xs[row] = scale;
+  char4* out = reinterpret_cast<char4*>(xq + row * ldq) + c * n4;
 #pragma unroll
-  for (int i = 0; i < CACHE; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
+  for (int k = 0; k < P; ++k) {
+    const int idx = i + k * kChunkThreads;
+    if (idx < n4) out[idx] = q8x4(scale4(v[k], r), scale);
+  }
+}
+
+// TP>1, pass 1: this rank's chunk sums and max|x * gain| over its columns.
+// x [rows][width_local], width_local = (chunks_local / 8) * width; stats
+// [rows][chunks_local + 1].  One CTA of chunks_local x 128 threads per row.
+template <int P>
+__global__ void rms_stats_kernel(int width, int chunks_local, const float* __restrict__ x,
+                                 const float* __restrict__ gain, float* __restrict__ stats) {
+  __shared__ float wsum[kChunks * 4];
+  __shared__ float red[32];
+  const long long row = blockIdx.x;
+  const int t = threadIdx.x, c = t / kChunkThreads, i = t % kChunkThreads;
+  const int n4 = width / (4 * kChunks);
+  const int wl = chunks_local * (width / kChunks);
+  const float4* xr = reinterpret_cast<const float4*>(x + row * wl) + c * n4;
+  const float4* gr = reinterpret_cast<const float4*>(gain) + c * n4;
+  float s = 0.0f, m = 0.0f;
+#pragma unroll
+  for (int k = 0; k < P; ++k) {
+    const int idx = i + k * kChunkThreads;
     if (idx < n4) {
-      const float4 g = __ldg(gr + idx);
-      c[i] = make_float4(c[i].x * r * g.x, c[i].y * r * g.y, c[i].z * r * g.z, c[i].w * r * g.w);
-      m = fmaxf(m, amax4(c[i]));
+      const float4 v = __ldg(xr + idx);
+      s = s + sumsq4(v);
+      m = fmaxf(m, amax4(mul4(v, __ldg(gr + idx))));
     }
   }
+  s = warp_sum_tree(s);
+  if ((t & 31) == 0) wsum[t >> 5] = s;
   m = block_max(m, red);
-  const float scale = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
-  if (threadIdx.x == 0) xs[row] = scale;
-  char4* out = reinterpret_cast<char4*>(xq + row * ldq);
+  float* st = stats + row * (chunks_local + 1);
+  if (t < chunks_local)
+    st[t] = ((wsum[4 * t] + wsum[4 * t + 1]) + wsum[4 * t + 2]) + wsum[4 * t + 3];
+  if (t == 0) st[chunks_local] = m;
+}
+
+// TP>1, pass 2: from the all-gathered stats [ranks][rows][chunks_local + 1],
+// the row's r and scale (identical on every rank and to TP=1), then this
+// rank's columns quantised.
+template <int P>
+__global__ void rms_apply_kernel(int width, int chunks_local, int ranks, long long rows,
+                                 float eps, const float* __restrict__ x,
+                                 const float* __restrict__ gain,
+                                 const float* __restrict__ stats_all, int8_t* __restrict__ xq,
+                                 float* __restrict__ xs) {
+  __shared__ float rs[2];
+  const long long row = blockIdx.x;
+  const int t = threadIdx.x, c = t / kChunkThreads, i = t % kChunkThreads;
+  const int S = chunks_local + 1;
+  if (t == 0) {
+    float cs[kChunks];
+    float mx = 0.0f;
+    for (int g = 0; g < ranks; ++g) {
+      const float* st = stats_all + (static_cast<long long>(g) * rows + row) * S;
+      for (int j = 0; j < chunks_local; ++j) cs[g * chunks_local + j] = st[j];
+      mx = fmaxf(mx, st[chunks_local]);
+    }
+    const float r = 1.0f / sqrtf(chunk_tree(cs) / static_cast<float>(width) + eps);
+    const float m = mx * r;
+    rs[0] = r;
+    rs[1] = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+    xs[row] = rs[1];
+  }
+  __syncthreads();
+  const float r = rs[0], scale = rs[1];
+  const int n4 = width / (4 * kChunks);
+  const int wl = chunks_local * (width / kChunks);
+  const float4* xr = reinterpret_cast<const float4*>(x + row * wl) + c * n4;
+  const float4* gr = reinterpret_cast<const float4*>(gain) + c * n4;
+  char4* out = reinterpret_cast<char4*>(xq + row * wl) + c * n4;
 #pragma unroll
-  for (int i = 0; i < CACHE; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
-    if (idx < n4) out[idx] = q8x4(c[i], scale);
+  for (int k = 0; k < P; ++k) {
+    const int idx = i + k * kChunkThreads;
+    if (idx < n4) out[idx] = q8x4(scale4(mul4(__ldg(xr + idx), __ldg(gr + idx)), r), scale);
   }
 }
 
@@ -193,14 +300,55 @@ static int cache_for(int n4) {
     default: KERNEL<16><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break; \
   }
 
+static int per_thread(int width) {  // float4 per thread in the chunked RMSNorm
+  const int n4 = width / (4 * kChunks);
+  return (n4 + kChunkThreads - 1) / kChunkThreads;
+}
+
 int rmsnorm_quant(long long rows, int width, float eps, const float* x, const float* gain,
                   int8_t* x_q, float* x_scale, cudaStream_t stream) {
   if (rows == 0) return kOk;
-  const int c = cache_for(width / 4);
-  if (width <= 0 || width % 4 != 0 || c == 0) return kErrInvalid;
+  if (width <= 0 || width % (4 * kChunks) != 0) return kErrInvalid;
   const unsigned grid = static_cast<unsigned>(rows);
-  REEF_DISPATCH_CACHE(c, rmsnorm_quant_kernel, width, eps, x, gain, x_q,
-                      static_cast<long long>(width), x_scale);
+  const int P = per_thread(width);
+  const int T = kChunks * kChunkThreads;
+  const long long ld = width;
+  if (P <= 1) rmsnorm_quant_kernel<1><<<grid, T, 0, stream>>>(width, eps, x, gain, x_q, ld, x_scale);
+  else if (P <= 2) rmsnorm_quant_kernel<2><<<grid, T, 0, stream>>>(width, eps, x, gain, x_q, ld, x_scale);
+  else if (P <= 4) rmsnorm_quant_kernel<4><<<grid, T, 0, stream>>>(width, eps, x, gain, x_q, ld, x_scale);
+  else return kErrInvalid;
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int rms_stats(long long rows, int width, int ranks, const float* x_local, const float* gain_local,
+              float* stats, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (width % (4 * kChunks) != 0 || kChunks % ranks != 0) return kErrInvalid;
+  const int cl = kChunks / ranks, P = per_thread(width);
+  const unsigned grid = static_cast<unsigned>(rows);
+  const int T = cl * kChunkThreads;
+  if (P <= 1) rms_stats_kernel<1><<<grid, T, 0, stream>>>(width, cl, x_local, gain_local, stats);
+  else if (P <= 2) rms_stats_kernel<2><<<grid, T, 0, stream>>>(width, cl, x_local, gain_local, stats);
+  else if (P <= 4) rms_stats_kernel<4><<<grid, T, 0, stream>>>(width, cl, x_local, gain_local, stats);
+  else return kErrInvalid;
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int rms_apply_quant(long long rows, int width, int ranks, float eps, const float* x_local,
+                    const float* gain_local, const float* stats_all, int8_t* x_q, float* x_scale,
+                    cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (width % (4 * kChunks) != 0 || kChunks % ranks != 0) return kErrInvalid;
+  const int cl = kChunks / ranks, P = per_thread(width);
+  const unsigned grid = static_cast<unsigned>(rows);
+  const int T = cl * kChunkThreads;
+  if (P <= 1)
+    rms_apply_kernel<1><<<grid, T, 0, stream>>>(width, cl, ranks, rows, eps, x_local, gain_local, stats_all, x_q, x_scale);
+  else if (P <= 2)
+    rms_apply_kernel<2><<<grid, T, 0, stream>>>(width, cl, ranks, rows, eps, x_local, gain_local, stats_all, x_q, x_scale);
+  else if (P <= 4)
+    rms_apply_kernel<4><<<grid, T, 0, stream>>>(width, cl, ranks, rows, eps, x_local, gain_local, stats_all, x_q, x_scale);
+  else return kErrInvalid;
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -44,6 +44,7 @@ struct GemmArgs {
   long long ldy;          // elements
   uint32_t shift;         // kEpiI8Shift
   int group_m;            // raster group (0 = default)
+  int k_segments;         // > 1: K arrives as this many segments (3-D tensor maps)
   int k_splits;           // > 1: K split across CTAs; split s writes y + s * split_stride
   long long split_stride; // elements between the partial outputs of two splits
   int vec_ok;             // 16-byte (int8: 4-byte) output stores allowed (launcher)
@@ -51,11 +52,13 @@ struct GemmArgs {
 };
 
 struct GemmProblem {
-  int M, N, K;
-  const int8_t* a;  // [M][lda]
+  int M, N, K;      // K: per segment (args.k_segments segments; 1 = plain)
+  const int8_t* a;  // [segs][M][lda]
   long long lda;    // bytes, multiple of 16
-  const int8_t* b;  // [N][ldb]
+  const int8_t* b;  // [segs][N][ldb] (segment strides below)
   long long ldb;    // bytes, multiple of 16
+  long long a_seg;  // bytes between A segments (multiple of 16; any value for 1 segment)
+  long long b_seg;  // bytes between B segments
   GemmArgs args;
 };
 
@@ -66,6 +69,9 @@ int check_device();                    // kOk on sm_100, else kErrUnsupported
 int read_device_error(int* code);      // synchronizes, returns and clears
 int make_tma_2d_i8(CUtensorMap* map, const void* base, long long rows,
                    long long cols, long long ld_bytes, int box_cols, int box_rows);
+int make_tma_3d_i8(CUtensorMap* map, const void* base, long long rows, long long cols,
+                   long long ld_bytes, long long segs, long long seg_bytes, int box_cols,
+                   int box_rows);
 int make_tma_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes,
                 const void* base, long long rows, long long cols, long long ld_elems,
                 int box_cols, int box_rows, CUtensorMapSwizzle swizzle);
@@ -105,6 +111,13 @@ int swiglu_quant(long long rows, int ffn, const float* gu, const float* row_max,
                  float* x_scale, cudaStream_t stream);
 int swiglu_absmax(long long rows, int ffn, const float* gu, float* row_max,
                   cudaStream_t stream);
+// TP-sharded RMSNorm (columns split over `ranks`): per-rank stats, all-gather,
+// then quantise this rank's columns with the full row's scale.
+int rms_stats(long long rows, int width, int ranks, const float* x_local, const float* gain_local,
+              float* stats, cudaStream_t stream);
+int rms_apply_quant(long long rows, int width, int ranks, float eps, const float* x_local,
+                    const float* gain_local, const float* stats_all, int8_t* x_q, float* x_scale,
+                    cudaStream_t stream);
 
 // attention_exact.cu -- reef's integer and float heads, bit for bit.
 // Scores stay in shared memory, which bounds the key length.

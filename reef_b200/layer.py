@@ -55,12 +55,21 @@ def _normal(gen, shape, std, device):
     return torch.randn(shape, generator=gen, device=device) * std
 
 
+TP_ALLREDUCE = 0  # Megatron: replicated x / y, int32 partial sums all-reduced
+TP_ALLGATHER = 1  # column-sharded x / y, int8 activations all-gathered
+
+
 class LlamaLayer:
-    """This rank's shard of one Llama-shape W8A8 decoder layer."""
+    """This rank's shard of one Llama-shape W8A8 decoder layer.
+
+    tp_mode TP_ALLREDUCE: x / y are the full [tokens][hidden]; w_o and w_down
+    hold this rank's input features (row-parallel).  TP_ALLGATHER: x / y are
+    this rank's hidden/world columns; w_o and w_down hold this rank's output
+    rows over the full K."""
 
     def __init__(self, shape: LlamaShape, batch: int, seq: int, seed: int = 0,
                  world: int = 1, rank: int = 0, comm: tp.Comm | None = None,
-                 device: str | torch.device = "cuda"):
+                 device: str | torch.device = "cuda", tp_mode: int = TP_ALLREDUCE):
         s = shape
         self.shape, self.batch, self.seq = s, batch, seq
         self.world, self.rank, self.comm = world, rank, comm
@@ -93,17 +102,25 @@ class LlamaLayer:
         self.w_qkv, self.s_qkv = q_rows((s.heads_q + 2 * s.heads_kv) * d,
                                         tp.qkv_rows(s.heads_q, s.heads_kv, d, world, rank),
                                         s.hidden)
-        self.w_o, self.s_o = q_cols(s.hidden, s.heads_q * d,
-                                    tp.col_slice(s.heads_q * d, world, rank))
+        self.tp_mode = tp_mode
+        out_rows = list(range(*tp.shard_range(s.hidden, world, rank)))
+        if tp_mode == TP_ALLGATHER:
+            self.w_o, self.s_o = q_rows(s.hidden, out_rows, s.heads_q * d)
+        else:
+            self.w_o, self.s_o = q_cols(s.hidden, s.heads_q * d,
+                                        tp.col_slice(s.heads_q * d, world, rank))
         self.w_gu, self.s_gu = q_rows(2 * s.ffn, tp.gate_up_rows(s.ffn, world, rank), s.hidden)
-        self.w_down, self.s_down = q_cols(s.hidden, s.ffn, tp.col_slice(s.ffn, world, rank))
+        if tp_mode == TP_ALLGATHER:
+            self.w_down, self.s_down = q_rows(s.hidden, out_rows, s.ffn)
+        else:
+            self.w_down, self.s_down = q_cols(s.hidden, s.ffn, tp.col_slice(s.ffn, world, rank))
         torch.cuda.synchronize(dev)
         self.desc = _lib.LlamaLayerDesc(
             batch, seq, s.hidden, hq_l, hkv_l, d, ffn_l, s.rms_eps, s.rope_base,
             self.attn_norm.data_ptr(), self.w_qkv.data_ptr(), self.s_qkv.data_ptr(),
             self.w_o.data_ptr(), self.s_o.data_ptr(), self.mlp_norm.data_ptr(),
             self.w_gu.data_ptr(), self.s_gu.data_ptr(), self.w_down.data_ptr(),
-            self.s_down.data_ptr(), comm.ptr if comm is not None else None)
+            self.s_down.data_ptr(), comm.ptr if comm is not None else None, tp_mode)
         nbytes = _lib.lib().reef_b200_llama_layer_workspace_bytes(C.byref(self.desc))
         if nbytes == 0:
             raise ValueError("invalid Llama layer description")

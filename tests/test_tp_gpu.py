@@ -80,6 +80,12 @@ def _worker(rank, world, port, q):
         L1 = RL.LlamaLayer(shape, 2, 256, seed=5, device=dev)
         y1 = L1.forward(xin)
         res["llama"] = bool(np.array_equal(bits(y2), bits(y1)))
+        # the all-gather plan: x / y are this rank's hidden columns
+        cols = tp.col_slice(1024, world, rank)
+        L3 = RL.LlamaLayer(shape, 2, 256, seed=5, world=world, rank=rank, comm=comm, device=dev,
+                           tp_mode=RL.TP_ALLGATHER)
+        y3 = L3.forward(xin[:, cols].contiguous())
+        res["llama_allgather"] = bool(np.array_equal(bits(y3), bits(y1[:, cols].contiguous())))
 
         # GPT-Neo block (config 2 shape), TP=2 vs the oracle (reef's Block<float>)
         fw = block_float_weights(256, 1024, seed=80)
@@ -113,4 +119,5 @@ def test_tp2_bit_identical_to_tp1():
     for r in range(2):
         status, res = out[r]
         assert status == "ok", res
-        assert res == {"rowpar": True, "llama": True, "gptneo": True}, (r, res)
+        assert res == {"rowpar": True, "llama": True, "llama_allgather": True,
+                       "gptneo": True}, (r, res)
