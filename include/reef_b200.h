@@ -231,25 +231,29 @@ int reef_b200_attention_heads_int8(size_t heads, size_t query_len, size_t key_le
  * quantised with reef's rule (quant.hpp:51-81: scale = max|x|/127, rne,
  * clamp +-127).  Outputs: q8 [tokens][heads_q*128], k8 and v8
  * [tokens][heads_kv*128] (the int8 KV-cache rows), scales [batch][heads][seq],
- * and vt [batch][heads_kv][128][seq] f16 holding v8's codes transposed (the
- * operand layout of the P.V tensor-core product).  head_dim is 128.  RoPE
- * and this scale granularity are not in reef (parity unpinned there). */
+ * and vt [batch][heads_kv][128][seq] f16 holding the dequantised values
+ * f16(v8 code * v_scale) transposed (the operand layout of the P.V
+ * tensor-core product).  head_dim is 128 and seq even.  RoPE and this scale
+ * granularity are not in reef (parity unpinned there). */
 int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t heads_kv,
                              float rope_base, const float* qkv, int8_t* q8, int8_t* k8,
                              int8_t* v8, float* q_scale, float* k_scale, float* v_scale,
                              void* vt, reef_b200_stream_t stream);
 
-/* Flash attention over int8 q / k / v (attend_head, attention.hpp:117-123,
- * on the dequantised values, with score scale sm_scale and GQA: query head h
- * reads kv head h / (heads_q / heads_kv)).  causal != 0 applies
+/* Flash attention over int8 q / k and f16 v (attend_head,
+ * attention.hpp:117-123, on the dequantised values, with score scale
+ * sm_scale and GQA: query head h reads kv head h / (heads_q / heads_kv)).
+ * q8 / k8 with their per-(token, head) scales as reef_b200_rope_qkv_quant
+ * writes them; vt [batch][heads_kv][128][seq] f16 is the dequantised v,
+ * transposed (reef_b200_rope_qkv_quant's vt).  causal != 0 applies
  * causal_visibility with query_start 0.  out [batch*seq][heads_q*128] fp32.
- * head_dim must be 128 and seq a multiple of 8.  Matches reef's float head
- * on the dequantised inputs within 1e-2 (fp32 online softmax, f16 P). */
+ * head_dim must be 128, seq a multiple of 8 and k_scale 16-byte aligned.
+ * Matches reef's float head on the dequantised inputs within 1e-2 (fp32
+ * online softmax, f16 P). */
 int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t heads_kv,
                             size_t head_dim, int causal, float sm_scale, const int8_t* q8,
                             const float* q_scale, const int8_t* k8, const float* k_scale,
-                            const void* vt, const float* v_scale, float* out,
-                            reef_b200_stream_t stream);
+                            const void* vt, float* out, reef_b200_stream_t stream);
 
 /* Decode: one new query per sequence against an int8 KV cache (BASELINE
  * config 4).  attend_head (attention.hpp:117-123) for the query at the last

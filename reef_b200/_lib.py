@@ -50,7 +50,7 @@ SIGNATURES = {
     "reef_b200_attention_heads_int8": ([_sz] * 6 + [_p, _sz, _sz, _p, _p, _sz, _sz, _u, _p,
                                                     _u, _p, _sz, _sz, _p], _i),
     "reef_b200_rope_qkv_quant": ([_sz, _sz, _sz, _sz, C.c_float] + [_p] * 9, _i),
-    "reef_b200_flash_attn_i8": ([_sz, _sz, _sz, _sz, _sz, _i, C.c_float] + [_p] * 8, _i),
+    "reef_b200_flash_attn_i8": ([_sz, _sz, _sz, _sz, _sz, _i, C.c_float] + [_p] * 7, _i),
     "reef_b200_decode_attn_workspace_bytes": ([_sz, _sz, _sz], _sz),
     "reef_b200_decode_attn_i8": ([_sz, _sz, _sz, _sz, _sz, _p, _sz, C.c_float] + [_p] * 7
                                  + [_sz, _p, _p], _i),

@@ -254,6 +254,7 @@ int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t he
   if (heads_q == 0 || heads_kv == 0 || heads_q % heads_kv != 0 || batch * seq > kMaxDim ||
       !qkv || !q8 || !k8 || !v8 || !q_scale || !k_scale || !v_scale || !vt)
     return REEF_B200_ERR_INVALID;
+  if (seq % 2 != 0) return REEF_B200_ERR_ALIGNMENT;
   if (int rc = check_device()) return rc;
   return rope_qkv_quant(static_cast<int>(batch), static_cast<int>(seq),
                         static_cast<int>(heads_q), static_cast<int>(heads_kv), rope_base, qkv,
@@ -264,12 +265,11 @@ int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t he
 int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t heads_kv,
                             size_t head_dim, int causal, float sm_scale, const int8_t* q8,
                             const float* q_scale, const int8_t* k8, const float* k_scale,
-                            const void* vt, const float* v_scale, float* out,
-                            reef_b200_stream_t stream) {
+                            const void* vt, float* out, reef_b200_stream_t stream) {
   if (batch == 0 || seq == 0) return REEF_B200_OK;
   if (head_dim != 128 || heads_q == 0 || heads_kv == 0 || heads_q % heads_kv != 0 ||
       batch * seq > kMaxDim || heads_q > 4096 || !q8 || !q_scale || !k8 || !k_scale || !vt ||
-      !v_scale || !out)
+      !out)
     return REEF_B200_ERR_INVALID;
   if (seq % 8 != 0) return REEF_B200_ERR_ALIGNMENT;
   if (int rc = check_device()) return rc;
@@ -286,7 +286,6 @@ int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t hea
   p.vt = vt;
   p.q_scale = q_scale;
   p.k_scale = k_scale;
-  p.v_scale = v_scale;
   p.out = out;
   p.out_ld = static_cast<long long>(heads_q) * 128;
   return flash_prefill_i8(p, S(stream));

@@ -129,6 +129,26 @@ int make_tma_3d_i8(CUtensorMap* map, const void* base, long long rows, long long
   return r == CUDA_SUCCESS ? kOk : kErrInvalid;
 }
 
+// [d2][d1][d0] of elem_bytes elements, dim-1 stride s1 bytes, dim-2 stride
+// s2 bytes; boxes of box0 x box1 x 1.
+int make_tma_3d(CUtensorMap* map, CUtensorMapDataType type, const void* base, long long d0,
+                long long d1, long long d2, long long s1, long long s2, int box0, int box1,
+                CUtensorMapSwizzle swizzle) {
+  EncodeTiled fn = encode_fn();
+  if (fn == nullptr) return kErrCuda;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return kErrAlignment;
+  if ((s1 & 15) != 0 || (s2 & 15) != 0) return kErrAlignment;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1),
+                        static_cast<cuuint64_t>(d2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(s1), static_cast<cuuint64_t>(s2)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, type, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrInvalid;
+}
+
 int make_tma_2d_i8(CUtensorMap* map, const void* base, long long rows, long long cols,
                    long long ld_bytes, int box_cols, int box_rows) {
   return make_tma_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, cols, ld_bytes,

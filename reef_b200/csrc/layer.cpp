@@ -523,7 +523,6 @@ static int llama_forward_ag(const reef_b200_llama_layer* L, const float* x, floa
   fp.vt = b.vt;
   fp.q_scale = b.qs;
   fp.k_scale = b.ks;
-  fp.v_scale = b.vs;
   fp.out = b.attn;
   fp.out_ld = static_cast<long long>(hq) * D;
   {
@@ -591,7 +590,6 @@ static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* 
   fp.vt = b.vt;
   fp.q_scale = b.qs;
   fp.k_scale = b.ks;
-  fp.v_scale = b.vs;
   fp.out = b.attn;
   fp.out_ld = static_cast<long long>(hq) * D;
   {

@@ -69,6 +69,9 @@ int check_device();                    // kOk on sm_100, else kErrUnsupported
 int read_device_error(int* code);      // synchronizes, returns and clears
 int make_tma_2d_i8(CUtensorMap* map, const void* base, long long rows,
                    long long cols, long long ld_bytes, int box_cols, int box_rows);
+int make_tma_3d(CUtensorMap* map, CUtensorMapDataType type, const void* base, long long d0,
+                long long d1, long long d2, long long s1, long long s2, int box0, int box1,
+                CUtensorMapSwizzle swizzle);
 int make_tma_3d_i8(CUtensorMap* map, const void* base, long long rows, long long cols,
                    long long ld_bytes, long long segs, long long seg_bytes, int box_cols,
                    int box_rows);
@@ -146,10 +149,9 @@ struct FlashProblem {
   float sm_scale;
   const int8_t* q8;       // [B*S][Hq*128]  token-major
   const int8_t* k8;       // [B*S][Hkv*128] token-major
-  const void* vt;         // [B][Hkv][128][S] f16 (int8 codes)
+  const void* vt;         // [B][Hkv][128][S] f16, dequantised v
   const float* q_scale;   // [B][Hq][S]
   const float* k_scale;   // [B][Hkv][S]
-  const float* v_scale;   // [B][Hkv][S]
   float* out;             // [B*S][out_ld]
   long long out_ld;
 };

@@ -36,17 +36,16 @@ def flash(batch: int, seq: int, heads: int, kv_heads: int) -> None:
     T = batch * seq
     q8 = torch.randint(-127, 128, (T, heads * 128), generator=g, device="cuda", dtype=torch.int8)
     k8 = torch.randint(-127, 128, (T, kv_heads * 128), generator=g, device="cuda", dtype=torch.int8)
-    vt = torch.randint(-127, 128, (batch, kv_heads, 128, seq), generator=g,
-                       device="cuda").to(torch.float16)
+    vt = (torch.randint(-127, 128, (batch, kv_heads, 128, seq), generator=g,
+                        device="cuda") * 0.01).to(torch.float16)
     qs = torch.full((batch, heads, seq), 0.01, device="cuda")
     ks = torch.full((batch, kv_heads, seq), 0.01, device="cuda")
-    vs = torch.full((batch, kv_heads, seq), 0.01, device="cuda")
     out = torch.empty((T, heads * 128), device="cuda")
     st = torch.cuda.current_stream().cuda_stream
     for _ in range(2):
         _lib.call("reef_b200_flash_attn_i8", batch, seq, heads, kv_heads, 128, 1,
                   1.0 / math.sqrt(128), q8.data_ptr(), qs.data_ptr(), k8.data_ptr(),
-                  ks.data_ptr(), vt.data_ptr(), vs.data_ptr(), out.data_ptr(), st)
+                  ks.data_ptr(), vt.data_ptr(), out.data_ptr(), st)
     torch.cuda.synchronize()
 
 

@@ -8,8 +8,8 @@ folded into q:  attend_head(q8*qs*sm_scale, k8*ks, v8*vs, causal).
 * torch fp64 at the config-3 shape (batch 8 x seq 2048, 32 heads x 128) on
   sampled (batch, head) pairs, and at config-4's GQA grouping (8 q per kv).
 Also checks the RoPE / quantise packing kernel: v8 bit-exact with reef's
-quantize_rows, vt exactly v8 transposed, q8/k8 within one code of a
-float64 RoPE then reef's quantiser.
+quantize_rows, vt exactly f16(v8 * v_scale) transposed, q8/k8 within one code
+of a float64 RoPE then reef's quantiser.
 """
 import math
 
@@ -41,11 +41,11 @@ def quant_heads(x, heads):
     return q.reshape(t, heads * 128), scale
 
 
-def flash(q8, qs, k8, ks, vt, vs, B, S, Hq, Hkv, causal, sm):
+def flash(q8, qs, k8, ks, vt, B, S, Hq, Hkv, causal, sm):
     out = torch.empty((B * S, Hq * 128), dtype=torch.float32, device="cuda")
     _lib.call("reef_b200_flash_attn_i8", B, S, Hq, Hkv, 128, int(causal), sm,
               q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), vt.data_ptr(),
-              vs.data_ptr(), out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+              out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     return out
 
 
@@ -72,7 +72,8 @@ class Inputs:
         self.v8, self.vsc = quant_heads_dev(rnd(Hkv * 128, 1.0), Hkv)
         bhs = lambda sc, H: sc.reshape(B, S, H).permute(0, 2, 1).contiguous()
         self.qs, self.ks, self.vs = bhs(self.qsc, Hq), bhs(self.ksc, Hkv), bhs(self.vsc, Hkv)
-        self.vt = self.v8.reshape(B, S, Hkv, 128).permute(0, 2, 3, 1).to(torch.float16).contiguous()
+        vdeq = self.v8.reshape(T, Hkv, 128).float() * self.vsc[:, :, None]
+        self.vt = vdeq.to(torch.float16).reshape(B, S, Hkv, 128).permute(0, 2, 3, 1).contiguous()
         self.B, self.S, self.Hq, self.Hkv = B, S, Hq, Hkv
 
     def head(self, b, h, sm):
@@ -88,12 +89,11 @@ class Inputs:
 
 def make(B, S, Hq, Hkv, seed, qk_std=1.0):
     d = Inputs(B, S, Hq, Hkv, seed, qk_std)
-    return d, dict(q8=d.q8, k8=d.k8, qs=d.qs, ks=d.ks, vs=d.vs, vt=d.vt)
+    return d, dict(q8=d.q8, k8=d.k8, qs=d.qs, ks=d.ks, vt=d.vt)
 
 
 def run(dev, B, S, Hq, Hkv, causal, sm):
-    o = flash(dev["q8"], dev["qs"], dev["k8"], dev["ks"], dev["vt"], dev["vs"], B, S, Hq, Hkv,
-              causal, sm)
+    o = flash(dev["q8"], dev["qs"], dev["k8"], dev["ks"], dev["vt"], B, S, Hq, Hkv, causal, sm)
     torch.cuda.synchronize()
     return o.cpu().numpy()
 
@@ -102,11 +102,16 @@ def deq(d, b, h, Hq, Hkv, S, sm):
     return d.head(b, h, sm)
 
 
-@pytest.mark.parametrize("B,S,Hq,Hkv,causal", [(1, 128, 1, 1, True), (2, 256, 4, 2, True),
-                                               (1, 384, 2, 2, False), (1, 136, 2, 1, True)])
-def test_flash_matches_reef_float_head(B, S, Hq, Hkv, causal):
+# one query tile (no second tile in the CTA), an odd tile count, ragged tails
+# (136 = 128 + 8, 264 = 2*128 + 8), non-causal, and a wide score range
+# (qk_std 3) that makes the lazy rescale of O fire
+@pytest.mark.parametrize("B,S,Hq,Hkv,causal,qk_std", [
+    (1, 128, 1, 1, True, 1.0), (2, 256, 4, 2, True, 1.0), (1, 384, 2, 2, False, 1.0),
+    (1, 136, 2, 1, True, 1.0), (1, 264, 2, 2, True, 1.0), (1, 640, 2, 1, True, 1.0),
+    (1, 264, 1, 1, False, 1.0), (1, 1024, 2, 1, True, 3.0)])
+def test_flash_matches_reef_float_head(B, S, Hq, Hkv, causal, qk_std):
     sm = 1.0 / math.sqrt(128)
-    d, dev = make(B, S, Hq, Hkv, seed=B * 100 + S + Hq)
+    d, dev = make(B, S, Hq, Hkv, seed=B * 100 + S + Hq, qk_std=qk_std)
     out = run(dev, B, S, Hq, Hkv, causal, sm)
     worst = 0.0
     for b in range(B):
@@ -147,8 +152,10 @@ def test_flash_config_shapes_sampled(B, S, Hq, Hkv):
         assert float((got - want).abs().max()) < TOL
 
 
-def test_rope_qkv_quant_packing():
-    B, S, Hq, Hkv = 2, 64, 4, 2
+# (3, 40): the 64-token blocks of the V transpose straddle sequences
+@pytest.mark.parametrize("B,S", [(2, 64), (3, 40)])
+def test_rope_qkv_quant_packing(B, S):
+    Hq, Hkv = 4, 2
     T = B * S
     W = (Hq + 2 * Hkv) * 128
     rng = np.random.default_rng(3)
@@ -172,8 +179,10 @@ def test_rope_qkv_quant_packing():
     np.testing.assert_array_equal(v8.cpu().numpy().reshape(T * Hkv, 128), wq)
     np.testing.assert_array_equal(
         vs.cpu().numpy().transpose(0, 2, 1).reshape(T * Hkv).view(np.uint32), ws.view(np.uint32))
-    np.testing.assert_array_equal(
-        vt.cpu().numpy(), v8.cpu().numpy().reshape(B, S, Hkv, 128).transpose(0, 2, 3, 1))
+    vdeq = (v8.cpu().numpy().reshape(B, S, Hkv, 128).astype(np.float32) *
+            vs.cpu().numpy().transpose(0, 2, 1)[:, :, :, None]).astype(np.float16)
+    np.testing.assert_array_equal(vt.cpu().numpy().view(np.uint16),
+                                  vdeq.transpose(0, 2, 3, 1).view(np.uint16))
     # q / k: float64 rotate-half RoPE, then reef's quantiser; within one code
     pos = np.tile(np.arange(S), B)[:, None].astype(np.float64)
     inv = 10000.0 ** (-np.arange(64) * 2 / 128.0)
