@@ -109,6 +109,20 @@ int reef_b200_gemm_w8a8(size_t rows, size_t in, size_t out, const int8_t* x_q,
                         const float* x_scale, const int8_t* w, const float* w_scale,
                         const float* bias, float* y, reef_b200_stream_t stream);
 
+/* Gate/up projection of a SwiGLU MLP with the activation in the GEMM
+ * epilogue (no counterpart in reef, whose GPT-Neo MLP is GELU; the Llama
+ * layer's MLP uses it):
+ *   g = gemm_w8a8(x_q, w_gu rows [0, ffn)),  u = ... rows [ffn, 2 ffn)
+ *   h[r][c] = silu(g[r][c]) * u[r][c] = g / (1 + e^-g) * u
+ *   row_max[r] = max_c |h[r][c]|   (the scale of the int8 h that follows)
+ * x_q [rows][kpad(in)] int8 + x_scale [rows]; w_gu [2*ffn][kpad(in)] int8
+ * (gate rows, then up rows) + w_scale [2*ffn]; h [rows][ffn] fp32.  g and u
+ * are bit-identical to reef_b200_gemm_w8a8 on the same operands. */
+int reef_b200_linear_w8a8_swiglu(size_t rows, size_t in, size_t ffn, const int8_t* x_q,
+                                 const float* x_scale, const int8_t* w_gu,
+                                 const float* w_scale, float* h, float* row_max,
+                                 reef_b200_stream_t stream);
+
 /* reef_b200_linear_w8a8_bias for callers that cannot allocate device memory
  * at all (a host that owns every byte through its own arena, a port of
  * reef's never-allocating Coral firmware, or a latency-critical path that

@@ -112,6 +112,19 @@ int reef_b200_linear_w8a8_bias(size_t rows, size_t in, size_t out, const float* 
   return reef_b200_gemm_w8a8(rows, in, out, x_q, x_scale, w, w_scale, bias, y, stream);
 }
 
+int reef_b200_linear_w8a8_swiglu(size_t rows, size_t in, size_t ffn, const int8_t* x_q,
+                                 const float* x_scale, const int8_t* w_gu,
+                                 const float* w_scale, float* h, float* row_max,
+                                 reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (!dims_ok(rows, in, 2 * ffn) || !x_q || !x_scale || !w_gu || !w_scale || !h || !row_max)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return linear_w8a8_swiglu(static_cast<long long>(rows), static_cast<int>(in),
+                            static_cast<int>(ffn), x_q, x_scale, w_gu, w_scale, h, row_max,
+                            S(stream));
+}
+
 int reef_b200_linear_w8a8(size_t rows, size_t in, size_t out, const float* x,
                           const int8_t* w, const float* w_scale, int8_t* x_q,
                           float* x_scale, float* y, reef_b200_stream_t stream) {

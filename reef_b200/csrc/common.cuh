@@ -330,6 +330,11 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool b_mn_major =
 
 // ---- small math ----------------------------------------------------------------
 
+// silu(g) * u = g / (1 + e^-g) * u, the one definition every SwiGLU uses.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
 // rounding_shift then saturate_int8 (reef int8.hpp:43-60): floor(v / 2^s + 1/2)
 // clamped to [-128, 127].
 __device__ __forceinline__ int8_t requant_rnu_sat8(int32_t v, uint32_t shift) {

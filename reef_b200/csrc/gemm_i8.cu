@@ -16,6 +16,11 @@
 //   kI8Shift  y = sat8(rounding_shift(acc [+ bias32[n]], shift))
 //             -- linear_int8, int8.hpp:74-101.
 //   kI32      y = acc   (the raw partial sums of a row-parallel shard)
+//   kSwiGLU   y = silu(g) * u, g / u the kF32W8A8 values of the gate / up
+//             weight rows n and b_up + n: each B stage holds BN/2 gate rows
+//             and the BN/2 matching up rows (two TMA boxes), so one tile
+//             yields BN/2 outputs; the row maxima of |y| go to row_max by
+//             atomic max (the scale of the int8 activation that follows).
 //
 // Kernel structure (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: 128 x 128-byte A tile and BN x 128-byte B tile
@@ -95,8 +100,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int M = args.M, N = args.N, K = args.K;
+  constexpr int kOut = EPI == kEpiSwiGLU ? BN / 2 : BN;  // output columns per tile
   const int num_m = (M + kBM - 1) / kBM;
-  const int num_n = (N + BN - 1) / BN;
+  const int num_n = (N + kOut - 1) / kOut;
   // K may come in `segs` equal segments read through 3-D tensor maps (an
   // all-gathered activation is rank-major [segs][rows][K]); k-block kb is
   // block kb % kbs of segment kb / kbs.  One segment for plain row-major.
@@ -153,7 +159,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
           const int seg = kb / kbs, kx = (kb - seg * kbs) * kBK;
           tma_load_3d(sa, &tma_a, &full[stage], kx, mb * kBM, seg);
-          tma_load_3d(sb, &tma_b, &full[stage], kx, nb * BN, seg);
+          if constexpr (EPI == kEpiSwiGLU) {
+            tma_load_3d(sb, &tma_b, &full[stage], kx, nb * kOut, seg);
+            tma_load_3d(sb + kOut * kBK, &tma_b, &full[stage], kx,
+                        static_cast<int>(args.b_up) + nb * kOut, seg);
+          } else {
+            tma_load_3d(sb, &tma_b, &full[stage], kx, nb * BN, seg);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -248,9 +260,105 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       tc_fence_after();
       const int row0 = mb * kBM + q * 32;  // first output row of this warp
-      if constexpr (EPI == kEpiF32W8A8) {
+      if constexpr (EPI == kEpiF32W8A8 || EPI == kEpiSwiGLU) {
         const int my_row = row0 + lane;
         rs_s[lane] = my_row < M ? args.x_scale[my_row] : 0.0f;
+      }
+      if constexpr (EPI == kEpiSwiGLU) {
+        // gate chunk c and up chunk c (accumulator columns c*32 and BN/2 + c*32)
+        // each pass through the transpose buffer; thread (sub_row, sub_col)
+        // then owns 4 columns of 8 rows of both
+        float rmax[8];
+#pragma unroll
+        for (int it = 0; it < 8; ++it) rmax[it] = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < kOut / 32; ++c) {
+          const int col0 = nb * kOut + c * 32;
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                 static_cast<uint32_t>(acc * BN + c * 32);
+          uint32_t r[32];
+          uint4 gv[8], uv[8];
+          tmem_ld_32x32b_x32(taddr, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<uint4*>(&tbuf[lane * 36 + j]) =
+                make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 8; ++it)
+            gv[it] = *reinterpret_cast<const uint4*>(&tbuf[(it * 4 + sub_row) * 36 + sub_col]);
+          __syncwarp();
+          tmem_ld_32x32b_x32(taddr + kOut, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<uint4*>(&tbuf[lane * 36 + j]) =
+                make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 8; ++it)
+            uv[it] = *reinterpret_cast<const uint4*>(&tbuf[(it * 4 + sub_row) * 36 + sub_col]);
+          __syncwarp();
+          if (col0 >= N) continue;  // warp-uniform
+          const int n = col0 + sub_col;
+          float wg[4], wu[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int nn = n + e < N ? n + e : N - 1;
+            wg[e] = args.w_scale[nn];
+            wu[e] = args.w_scale[args.b_up + nn];
+          }
+          const bool full_vec = args.vec_ok && (n + 3 < N);
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rl = it * 4 + sub_row;
+            const int m = row0 + rl;
+            if (m < M && n < N) {
+              const float rsv = rs_s[rl];
+              const uint32_t ga[4] = {gv[it].x, gv[it].y, gv[it].z, gv[it].w};
+              const uint32_t ua[4] = {uv[it].x, uv[it].y, uv[it].z, uv[it].w};
+              float o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                // the gate / up values of the unfused W8A8 linear, then SwiGLU
+                const float g = __fmul_rn(__int2float_rn(static_cast<int32_t>(ga[e])),
+                                          __fmul_rn(rsv, wg[e]));
+                const float u = __fmul_rn(__int2float_rn(static_cast<int32_t>(ua[e])),
+                                          __fmul_rn(rsv, wu[e]));
+                o[e] = silu_mul(g, u);
+              }
+              float* y = static_cast<float*>(args.y) + static_cast<long long>(m) * args.ldy + n;
+              if (full_vec) {
+                *reinterpret_cast<float4*>(y) = make_float4(o[0], o[1], o[2], o[3]);
+                rmax[it] = fmaxf(rmax[it], fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])),
+                                                 fmaxf(fabsf(o[2]), fabsf(o[3]))));
+              } else {
+                for (int e = 0; e < 4 && n + e < N; ++e) {
+                  y[e] = o[e];
+                  rmax[it] = fmaxf(rmax[it], fabsf(o[e]));
+                }
+              }
+            }
+          }
+        }
+        // the 8 lanes of a sub-row hold its 32 columns: reduce, one atomic
+        // per row (|y| >= 0, so the int order of the bits is the float order)
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          float v = rmax[it];
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+          const int m = row0 + it * 4 + sub_row;
+          if ((lane & 7) == 0 && m < M)
+            atomicMax(reinterpret_cast<int*>(args.row_max) + m, __float_as_int(v));
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+        continue;
       }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -379,7 +487,11 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
   const int segs = p.args.k_segments > 1 ? p.args.k_segments : 1;
   int rc = make_tma_3d_i8(&ma, p.a, p.M, p.K, p.lda, segs, p.a_seg, kBK, kBM);
   if (rc) return rc;
-  rc = make_tma_3d_i8(&mb, p.b, p.N, p.K, p.ldb, segs, p.b_seg, kBK, BN);
+  if constexpr (EPI == kEpiSwiGLU) {
+    rc = make_tma_3d_i8(&mb, p.b, p.args.b_up + p.N, p.K, p.ldb, segs, p.b_seg, kBK, BN / 2);
+  } else {
+    rc = make_tma_3d_i8(&mb, p.b, p.N, p.K, p.ldb, segs, p.b_seg, kBK, BN);
+  }
   if (rc) return rc;
   auto kernel = gemm_i8_kernel<BN, STAGES, EPI>;
   static bool configured[64] = {};
@@ -391,7 +503,8 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
       return kErrCuda;
     configured[dev] = true;
   }
-  const int num_tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+  constexpr int kOut = EPI == kEpiSwiGLU ? BN / 2 : BN;
+  const int num_tiles = ((p.M + kBM - 1) / kBM) * ((p.N + kOut - 1) / kOut);
   const int splits = p.args.k_splits > 1 ? p.args.k_splits : 1;
   const int grid = std::min(num_tiles * splits, num_sms());
   GemmArgs args = p.args;
@@ -509,6 +622,9 @@ int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream) {
     case kEpiI32:
       return wide ? launch<256, 4, kEpiI32>(p, stream)
                   : launch<128, 6, kEpiI32>(p, stream);
+    case kEpiSwiGLU:
+      if (p.args.row_max == nullptr || p.args.b_up < p.N) return kErrInvalid;
+      return launch<256, 4, kEpiSwiGLU>(p, stream);
     default:
       return kErrInvalid;
   }

@@ -79,6 +79,25 @@ int gemm_w8a8_f32(long long rows, int in, int out, const int8_t* xq, const float
 
 }  // namespace
 
+// Gate/up projection fused with SwiGLU: h = silu(x W_g^T) * (x W_u^T), W_gu
+// [2*ffn][in] (gate rows, then up rows), plus row_max[m] = max |h[m]| (this
+// rank's columns).
+int linear_w8a8_swiglu(long long rows, int in, int ffn, const int8_t* xq, const float* xs,
+                       const int8_t* w_gu, const float* ws, float* h, float* row_max,
+                       cudaStream_t st) {
+  if (rows == 0) return kOk;
+  if (cudaMemsetAsync(row_max, 0, static_cast<size_t>(rows) * sizeof(float), st) != cudaSuccess)
+    return kErrCuda;
+  GemmProblem p = problem(rows, in, ffn, xq, w_gu);
+  p.args.x_scale = xs;
+  p.args.w_scale = ws;
+  p.args.y = h;
+  p.args.ldy = ffn;
+  p.args.b_up = ffn;
+  p.args.row_max = row_max;
+  return gemm_i8(p, kEpiSwiGLU, st);
+}
+
 // Row-parallel W8A8 linear.  `quant` fills xq/xs from the local input given
 // the full-row maximum (or computes it itself when row_max is null);
 // `absmax` writes the local row maxima.
@@ -432,8 +451,9 @@ size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* L) {
   // rmsnorm+quant, qkv GEMM, rope table, rope q/k, quant v, flash, o-proj,
   // rmsnorm+quant, gate/up GEMM, down; a row-parallel linear is quant + GEMM
   // (TP=1) or absmax + quant + int32 GEMM + dequant epilogue (TP>1)
-  if (llama_allgather(L)) return 16;  // rms x2 (stats, apply) + absmax/quant x2, no epilogue pass
-  return L->comm != nullptr ? 16 : 12;
+  // (the gate/up GEMM writes SwiGLU's row maxima, so the MLP has no absmax pass)
+  if (llama_allgather(L)) return 15;  // rms x2 (stats, apply), o-proj absmax + quant, no epilogue pass
+  return L->comm != nullptr ? 15 : 12;
 }
 
 static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* y,
@@ -477,8 +497,7 @@ static int llama_forward_ag(const reef_b200_llama_layer* L, const float* x, floa
   const float* g2 = L->mlp_norm + static_cast<long long>(rank) * Hl;
 
   // all-gathered activation [N][T][kl] times this rank's rows of W [n][N*kl]
-  auto gemm_seg = [&](int kl, const int8_t* w, int n, const float* ws, const float* residual,
-                      float* out, cudaEvent_t* e) -> int {
+  auto seg_problem = [&](int kl, const int8_t* w, int n, const float* ws, float* out) {
     GemmProblem p{};
     p.M = static_cast<int>(T);
     p.N = n;
@@ -492,9 +511,14 @@ static int llama_forward_ag(const reef_b200_llama_layer* L, const float* x, floa
     p.args.k_segments = N;
     p.args.x_scale = b.xs;
     p.args.w_scale = ws;
-    p.args.residual = residual;
     p.args.y = out;
     p.args.ldy = n;
+    return p;
+  };
+  auto gemm_seg = [&](int kl, const int8_t* w, int n, const float* ws, const float* residual,
+                      float* out, cudaEvent_t* e) -> int {
+    GemmProblem p = seg_problem(kl, w, n, ws, out);
+    p.args.residual = residual;
     Span sp(e, st);
     return gemm_i8(p, kEpiF32W8A8, st);
   };
@@ -537,10 +561,18 @@ static int llama_forward_ag(const reef_b200_llama_layer* L, const float* x, floa
   REEF_TRY(gemm_seg(hq * D, L->w_o, Hl, L->s_o, x, b.h, ev ? ev + 4 : nullptr));
   // MLP
   REEF_TRY(rms(b.h, g2));
-  REEF_TRY(gemm_seg(Hl, L->w_gu, 2 * F, L->s_gu, nullptr, b.big, ev ? ev + 6 : nullptr));
-  REEF_TRY(swiglu_absmax(T, F, b.big, b.row_max, st));
+  {
+    // gate/up + SwiGLU in the GEMM epilogue: h [T][F] and its local row maxima
+    if (cudaMemsetAsync(b.row_max, 0, static_cast<size_t>(T) * sizeof(float), st) != cudaSuccess)
+      return REEF_B200_ERR_CUDA;
+    GemmProblem p = seg_problem(Hl, L->w_gu, F, L->s_gu, b.big);
+    p.args.b_up = F;
+    p.args.row_max = b.row_max;
+    Span sp(ev ? ev + 6 : nullptr, st);
+    REEF_TRY(gemm_i8(p, kEpiSwiGLU, st));
+  }
   REEF_TRY(allreduce_max_f32(c, b.row_max, static_cast<size_t>(T), st));
-  REEF_TRY(swiglu_quant(T, F, b.big, b.row_max, b.xq, b.xs, st));
+  REEF_TRY(quantize_rows(T, F, b.big, b.xq, F, b.xs, b.row_max, st));
   REEF_TRY(allgather_bytes(c, b.xq, b.xq_all, static_cast<size_t>(T) * F, st));
   return gemm_seg(F, L->w_down, Hl, L->s_down, b.h, y, ev ? ev + 8 : nullptr);
 }
@@ -608,13 +640,15 @@ static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* 
   // MLP block: y = h + down(swiglu(gate_up(rmsnorm(h))))
   REEF_TRY(rmsnorm_quant(T, H, L->rms_eps, b.h, L->mlp_norm, b.xq, b.xs, st));
   {
+    // gate/up + SwiGLU in the GEMM epilogue: h [T][F] and its local row maxima
     Span sp(ev ? ev + 6 : nullptr, st);
-    REEF_TRY(gemm_w8a8_f32(T, H, 2 * F, b.xq, b.xs, L->w_gu, L->s_gu, nullptr, nullptr, b.big,
-                           st));
+    REEF_TRY(linear_w8a8_swiglu(T, H, F, b.xq, b.xs, L->w_gu, L->s_gu, b.big, b.row_max, st));
   }
   {
-    auto quant = [&](const float* rm) { return swiglu_quant(T, F, b.big, rm, b.xq, b.xs, st); };
-    auto absmax = [&](float* rm) { return swiglu_absmax(T, F, b.big, rm, st); };
+    auto quant = [&](const float*) {
+      return quantize_rows(T, F, b.big, b.xq, F, b.xs, b.row_max, st);
+    };
+    auto absmax = [&](float*) { return static_cast<int>(kOk); };  // written by the GEMM
     REEF_TRY(rowpar_linear(c, T, F, H, quant, absmax, L->w_down, L->s_down, nullptr, b.h, b.xq,
                            b.xs, b.row_max, b.acc, y, st, ev ? ev + 8 : nullptr));
   }

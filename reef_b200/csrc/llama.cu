@@ -71,10 +71,6 @@ __device__ __forceinline__ float amax4(float4 v) {
   return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 }
 
-__device__ __forceinline__ float silu_mul(float g, float u) {
-  return __fdividef(g, 1.0f + __expf(-g)) * u;
-}
-
 __device__ __forceinline__ float4 swiglu4(float4 g, float4 u) {
   return make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z),
                      silu_mul(g.w, u.w));

@@ -27,6 +27,9 @@ enum Epilogue : int {
   kEpiF32W8A8 = 0,  // y = float(acc) * (x_scale[m] * w_scale[n]) [+ bias[n]]
   kEpiI8Shift = 1,  // y = sat8(rnu_shift(acc [+ bias32[n]], shift))
   kEpiI32 = 2,      // y = acc
+  // y = silu(g) * u with g, u the kEpiF32W8A8 values of B rows n and b_up + n;
+  // row_max[m] = max(row_max[m], max_n |y|) (atomic; zero it first)
+  kEpiSwiGLU = 3,
 };
 
 // Row stride (bytes) of every int8 matrix the tensor cores read: TMA needs
@@ -46,6 +49,8 @@ struct GemmArgs {
   int group_m;            // raster group (0 = default)
   int k_segments;         // > 1: K arrives as this many segments (3-D tensor maps)
   int k_splits;           // > 1: K split across CTAs; split s writes y + s * split_stride
+  long long b_up;         // kEpiSwiGLU: first B row of the "up" half
+  float* row_max;         // kEpiSwiGLU: [M] running max |y| per row
   long long split_stride; // elements between the partial outputs of two splits
   int vec_ok;             // 16-byte (int8: 4-byte) output stores allowed (launcher)
   int* err;               // device error word (set by the launcher)
@@ -81,6 +86,11 @@ int make_tma_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes,
 
 // ---- kernels ------------------------------------------------------------------
 int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream);
+// Gate/up projection with SwiGLU in the epilogue (layer.cpp): h [rows][ffn]
+// fp32 and row_max [rows] = max |h| of each row.
+int linear_w8a8_swiglu(long long rows, int in, int ffn, const int8_t* xq, const float* xs,
+                       const int8_t* w_gu, const float* ws, float* h, float* row_max,
+                       cudaStream_t st);
 
 // Skinny GEMM for few tokens (decode): y[m][n] = epi(sum_k x[m][k] w[n][k]) with
 // the weights as the 128-row MMA operand (swap-AB), tokens (m <= 128) on the

@@ -98,6 +98,19 @@ def gemm_w8a8(x_q, x_scale, w, w_scale, bias=None, in_features: int | None = Non
     return y
 
 
+def linear_w8a8_swiglu(x_q, x_scale, w_gu, w_scale, in_features: int | None = None):
+    """Gate/up projection with SwiGLU in the GEMM epilogue: returns
+    (h [rows][ffn] = silu(gate) * up, row_max [rows] = max |h|)."""
+    rows = x_q.shape[0]
+    k = in_features if in_features is not None else x_q.shape[1]
+    ffn = w_gu.shape[0] // 2
+    h = torch.empty((rows, ffn), dtype=torch.float32, device=x_q.device)
+    row_max = torch.empty(rows, dtype=torch.float32, device=x_q.device)
+    _lib.call("reef_b200_linear_w8a8_swiglu", rows, k, ffn, _ptr(x_q), _ptr(x_scale), _ptr(w_gu),
+              _ptr(w_scale), _ptr(h), _ptr(row_max), _stream())
+    return h, row_max
+
+
 def linear_int8(x: torch.Tensor, w: torch.Tensor, shift: int,
                 bias: torch.Tensor | None = None, in_features: int | None = None):
     """reef_kernels::linear_int8 / linear_bias_int8 (kernels.hpp:101-108).

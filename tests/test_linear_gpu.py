@@ -166,3 +166,29 @@ def test_skinny_gemm_matches_oracle(m, n, k):
     acc = ro.gemm_i8(host(a)[:, :k], host(b)[:, :k])
     want = ro.w8a8_epilogue(acc, host(xs), host(ws), host(bias))
     np.testing.assert_array_equal(bits(host(y)), bits(want))
+
+
+# ---- gate/up projection with SwiGLU in the epilogue ----------------------------------
+
+# one and many tiles, ffn not a multiple of the 128-column output tile, rows not
+# a multiple of the 128-row tile, the config-3 FFN width
+@pytest.mark.parametrize("rows,k,ffn", [(128, 256, 128), (300, 512, 640), (257, 1024, 136),
+                                        (64, 4096, 11008), (1000, 64, 48)])
+def test_swiglu_gemm(rows, k, ffn):
+    """g, u: the oracle's W8A8 linear (bit-exact reference for the GEMM part);
+    h = silu(g) * u within the fast exp / divide the kernel uses (a few ulp);
+    row_max = max |h| of the returned h, exactly."""
+    g = torch.Generator(device="cuda").manual_seed(rows + k + ffn)
+    a = torch.randint(-127, 128, (rows, K.kpad(k)), generator=g, device="cuda", dtype=torch.int8)
+    w = torch.randint(-127, 128, (2 * ffn, K.kpad(k)), generator=g, device="cuda",
+                      dtype=torch.int8)
+    xs = torch.rand((rows,), generator=g, device="cuda") * 1e-3 + 1e-4
+    ws = torch.rand((2 * ffn,), generator=g, device="cuda") * 1e-3 + 1e-4
+    h, row_max = K.linear_w8a8_swiglu(a, xs, w, ws, in_features=k)
+    acc = ro.gemm_i8(host(a)[:, :k], host(w)[:, :k])
+    gu = ro.w8a8_epilogue(acc, host(xs), host(ws), None).astype(np.float64)
+    gate, up = gu[:, :ffn], gu[:, ffn:]
+    want = gate / (1.0 + np.exp(-gate)) * up
+    got = host(h)
+    np.testing.assert_allclose(got, want, rtol=2e-5, atol=1e-6)
+    np.testing.assert_array_equal(bits(host(row_max)), bits(np.abs(got).max(axis=1)))
