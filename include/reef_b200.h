@@ -254,6 +254,21 @@ int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t he
                              int8_t* v8, float* q_scale, float* k_scale, float* v_scale,
                              void* vt, reef_b200_stream_t stream);
 
+/* The QKV projection and reef_b200_rope_qkv_quant in one pass: the W8A8
+ * GEMM (as reef_b200_gemm_w8a8, no bias) of x_q [batch*seq][kpad(in)] +
+ * x_scale by w_qkv [(heads_q + 2*heads_kv)*128][kpad(in)] + w_scale, and in
+ * its epilogue, per (token, head), the RoPE and int8 packing of
+ * reef_b200_rope_qkv_quant: bit-identical outputs, without the fp32
+ * projection ever reaching memory.  v8 and v_scale may be NULL (the flash
+ * head reads only vt).  rope_table: [64][seq] float2 scratch (seq * 512
+ * bytes).  seq must be even. */
+int reef_b200_linear_w8a8_qkv_rope(size_t batch, size_t seq, size_t in, size_t heads_q,
+                                   size_t heads_kv, float rope_base, const int8_t* x_q,
+                                   const float* x_scale, const int8_t* w_qkv,
+                                   const float* w_scale, int8_t* q8, int8_t* k8, int8_t* v8,
+                                   float* q_scale, float* k_scale, float* v_scale, void* vt,
+                                   void* rope_table, reef_b200_stream_t stream);
+
 /* Flash attention over int8 q / k and f16 v (attend_head,
  * attention.hpp:117-123, on the dequantised values, with score scale
  * sm_scale and GQA: query head h reads kv head h / (heads_q / heads_kv)).

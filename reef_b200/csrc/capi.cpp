@@ -275,6 +275,35 @@ int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t he
                         S(stream));
 }
 
+int reef_b200_linear_w8a8_qkv_rope(size_t batch, size_t seq, size_t in, size_t heads_q,
+                                   size_t heads_kv, float rope_base, const int8_t* x_q,
+                                   const float* x_scale, const int8_t* w_qkv,
+                                   const float* w_scale, int8_t* q8, int8_t* k8, int8_t* v8,
+                                   float* q_scale, float* k_scale, float* v_scale, void* vt,
+                                   void* rope_table, reef_b200_stream_t stream) {
+  if (batch == 0 || seq == 0) return REEF_B200_OK;
+  if (heads_q == 0 || heads_kv == 0 || heads_q > 4096 || heads_kv > 4096 ||
+      batch * seq > kMaxDim || in == 0 || in > kMaxDim || !x_q || !x_scale || !w_qkv ||
+      !w_scale || !q8 || !k8 || !q_scale || !k_scale || !vt || !rope_table)
+    return REEF_B200_ERR_INVALID;
+  if (seq % 2 != 0) return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  QkvOut o{};
+  o.rope = static_cast<const float2*>(rope_table);
+  o.seq = static_cast<int>(seq);
+  o.heads_q = static_cast<int>(heads_q);
+  o.heads_kv = static_cast<int>(heads_kv);
+  o.q8 = q8;
+  o.k8 = k8;
+  o.v8 = v8;
+  o.qs = q_scale;
+  o.ks = k_scale;
+  o.vs = v_scale;
+  o.vt = vt;
+  return linear_w8a8_qkv_rope(static_cast<long long>(batch * seq), static_cast<int>(in), x_q,
+                              x_scale, w_qkv, w_scale, rope_base, o, S(stream));
+}
+
 int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t heads_kv,
                             size_t head_dim, int causal, float sm_scale, const int8_t* q8,
                             const float* q_scale, const int8_t* k8, const float* k_scale,

@@ -330,6 +330,22 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool b_mn_major =
 
 // ---- small math ----------------------------------------------------------------
 
+// reef's int8 code of x at `scale` (quant.hpp:51-81): rint(x / scale)
+// clamped to +-127, with x / scale the correctly rounded quotient
+// (__fdiv_rn).  rcp = __frcp_rn(scale).  Fast path: q = fl(x * rcp) differs
+// from x / scale by at most |q| * 1.5 * 2^-23 (two roundings of 2^-24), i.e.
+// < 2.3e-5 when |q| < 128, so whenever q lies further than 6.1e-5 from a
+// half-integer the correctly rounded quotient rounds to the same integer.
+// Anything else (near a tie, |q| >= 128, a non-finite q) takes the division.
+__device__ __forceinline__ int quant_code(float x, float scale, float rcp) {
+  const float q = __fmul_rn(x, rcp);
+  const float r = rintf(q);
+  const int c = (fabsf(q) < 128.0f && fabsf(q - r) < 0.49993896f)
+                    ? __float2int_rn(r)
+                    : __float2int_rn(__fdiv_rn(x, scale));
+  return c < -127 ? -127 : (c > 127 ? 127 : c);
+}
+
 // silu(g) * u = g / (1 + e^-g) * u, the one definition every SwiGLU uses.
 __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-g)) * u;

@@ -456,11 +456,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
 // (quant.hpp:51-81: scale = max|x|/127, rne, clamp).  Outputs: q8 [T][Hq*128],
 // k8 [T][Hkv*128] token-major (the int8 cache rows) and scales [B][H][S].
 // (cos, sin) of pos * base^(-2i/128) for pos < seq, i < 64: computed once per
-// forward so the per-element RoPE is two table loads.
+// forward so the per-element RoPE is two table loads.  i-major: table[i][pos],
+// so a warp of consecutive tokens reads one contiguous run per i.
 __global__ void rope_table_kernel(int seq, float base, float2* __restrict__ table) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= seq * 64) return;
-  const int pos = idx >> 6, i = idx & 63;
+  const int i = idx / seq, pos = idx - i * seq;
   const float inv_freq = powf(base, -static_cast<float>(2 * i) / kHeadDim);
   float sn, cs;
   sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
@@ -487,7 +488,7 @@ __global__ void rope_qk_quant_kernel(int tokens, int seq, int hq, int hkv, float
     const int i = lane + 32 * p;
     float sn, cs;
     if (table != nullptr) {
-      const float2 t = __ldg(table + pos * 64 + i);
+      const float2 t = __ldg(table + static_cast<long long>(i) * seq + pos);
       cs = t.x;
       sn = t.y;
     } else {
@@ -623,6 +624,13 @@ int flash_prefill_i8(const FlashProblem& p, cudaStream_t stream) {
   a.err = device_error_ptr();
   const int grid = (((p.seq + kTile - 1) / kTile + 1) / 2) * p.batch * p.heads_q;
   flash_prefill_kernel<<<grid, kFThreads, FL::kAlloc, stream>>>(mq, mk, mv, mo, a);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int rope_table(int seq, float rope_base, void* table, cudaStream_t stream) {
+  if (seq <= 0 || table == nullptr) return kErrInvalid;
+  rope_table_kernel<<<(seq * 64 + 255) / 256, 256, 0, stream>>>(seq, rope_base,
+                                                                 static_cast<float2*>(table));
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -16,6 +16,12 @@
 //   kI8Shift  y = sat8(rounding_shift(acc [+ bias32[n]], shift))
 //             -- linear_int8, int8.hpp:74-101.
 //   kI32      y = acc   (the raw partial sums of a row-parallel shard)
+//   kQkvRope  the kF32W8A8 values of a QKV projection, then per (token,
+//             head) in the epilogue: rotate-half RoPE on q / k heads and
+//             reef's int8 quantiser (quant.hpp:51-81) -> q8 / k8 / v8 rows,
+//             their scales, and the f16 V^T copy the flash head reads.  A
+//             BN = 256 tile is two whole heads; each epilogue thread holds one
+//             token's 128 values of a head (TMEM lane = token).
 //   kSwiGLU   y = silu(g) * u, g / u the kF32W8A8 values of the gate / up
 //             weight rows n and b_up + n: each B stage holds BN/2 gate rows
 //             and the BN/2 matching up rows (two TMA boxes), so one tile
@@ -38,6 +44,8 @@
 #include "common.cuh"
 #include "ops.h"
 
+#include <cuda_fp16.h>
+
 #include <algorithm>
 
 namespace reef {
@@ -49,6 +57,12 @@ constexpr int kBK = 128;         // bytes of K per stage (one 128-byte swizzle r
 constexpr int kUmmaK = 32;       // K per tcgen05.mma kind::i8
 constexpr int kThreads = 192;    // 6 warps
 constexpr int kEpiWarps = 4;
+// The QKV epilogue runs 8 warps: warps 2..5 take the tile's first head,
+// warps 6..9 its second (two warps per TMEM lane quadrant).
+template <int EPI>
+__host__ __device__ constexpr int epi_warps() { return EPI == kEpiQkvRope ? 8 : kEpiWarps; }
+template <int EPI>
+__host__ __device__ constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
 constexpr int kTransposeWords = 32 * 36;  // per epilogue warp
 
 template <int BN, int STAGES>
@@ -82,7 +96,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int gro
 }
 
 template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for<EPI>(), 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a,
                    const __grid_constant__ CUtensorMap tma_b, GemmArgs args) {
   using L = Layout<BN, STAGES>;
@@ -123,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps * 32);
+      mbar_init(&acc_empty[b], epi_warps<EPI>() * 32);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -263,6 +277,142 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == kEpiF32W8A8 || EPI == kEpiSwiGLU) {
         const int my_row = row0 + lane;
         rs_s[lane] = my_row < M ? args.x_scale[my_row] : 0.0f;
+      }
+      if constexpr (EPI == kEpiQkvRope) {
+        // One head (128 columns) of the tile per warp, 32 tokens (its TMEM
+        // lane quadrant): pass 1 dequantises, rotates and takes max |x|,
+        // writing the values back over the accumulator columns; pass 2 reads
+        // them again to quantise and store.
+        const QkvOut& qo = args.qkv;
+        const int hl = (warp - 2) >> 2;
+        const int hh = nb * (BN / 128) + hl;
+        const int heads = qo.heads_q + 2 * qo.heads_kv;
+        const int m = row0 + lane;  // this thread's token
+        const bool mok = m < M;
+        if (hh < heads) {  // warp-uniform
+          const int pos = mok ? m % qo.seq : 0, bidx = mok ? m / qo.seq : 0;
+          const float rsv = mok ? args.x_scale[m] : 0.0f;
+          float* wsb = reinterpret_cast<float*>(smem + L::kTransposeOff) + (warp - 2) * 128;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) wsb[lane + 32 * i] = args.w_scale[hh * 128 + lane + 32 * i];
+          __syncwarp();
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                 static_cast<uint32_t>(acc * BN + hl * 128);
+          const bool rope = hh < qo.heads_q + qo.heads_kv;
+          // i-major table: a warp's consecutive tokens read one run per i
+          const float2* tr = qo.rope + pos;
+          float mx0 = 0.0f, mx1 = 0.0f;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {  // columns [32h, 32h+32) and [64+32h, 96+32h)
+            uint32_t lo[32], hi[32];
+            tmem_ld_32x32b_x32(taddr + h * 32, lo);
+            tmem_ld_32x32b_x32(taddr + 64 + h * 32, hi);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k0 = 0; k0 < 32; k0 += 16) {
+              float2 cs[16];
+              if (rope) {
+#pragma unroll
+                for (int k = 0; k < 16; ++k)
+                  cs[k] = __ldg(tr + static_cast<long long>(h * 32 + k0 + k) * qo.seq);
+              }
+              // linear.hpp:125-127: float(sum) * (row_scale * w_scale[c])
+#pragma unroll
+              for (int k = 0; k < 16; ++k) {
+                const int kk = k0 + k;
+                float a = __fmul_rn(__int2float_rn(static_cast<int32_t>(lo[kk])),
+                                    __fmul_rn(rsv, wsb[h * 32 + kk]));
+                float b = __fmul_rn(__int2float_rn(static_cast<int32_t>(hi[kk])),
+                                    __fmul_rn(rsv, wsb[64 + h * 32 + kk]));
+                if (rope) {
+                  // rotate-half RoPE, pair (i, i + 64): the packing kernel's expressions
+                  const float a2 = a * cs[k].x - b * cs[k].y;
+                  b = b * cs[k].x + a * cs[k].y;
+                  a = a2;
+                }
+                mx0 = fmaxf(mx0, fabsf(a));
+                mx1 = fmaxf(mx1, fabsf(b));
+                lo[kk] = __float_as_uint(a);
+                hi[kk] = __float_as_uint(b);
+              }
+            }
+            tmem_st_32x32b_x32(taddr + h * 32, lo);
+            tmem_st_32x32b_x32(taddr + 64 + h * 32, hi);
+          }
+          tmem_st_wait();
+          const float mx = fmaxf(mx0, mx1);
+          const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+          const float rcp = __frcp_rn(scale);
+          int8_t* dst = nullptr;
+          float* sdst = nullptr;
+          const bool is_v = !rope;
+          const int kh = hh - qo.heads_q - (is_v ? qo.heads_kv : 0);
+          if (hh < qo.heads_q) {
+            dst = qo.q8 + static_cast<long long>(m) * qo.heads_q * 128 + hh * 128;
+            sdst = qo.qs + (static_cast<long long>(bidx) * qo.heads_q + hh) * qo.seq + pos;
+          } else if (!is_v) {
+            dst = qo.k8 + static_cast<long long>(m) * qo.heads_kv * 128 + kh * 128;
+            sdst = qo.ks + (static_cast<long long>(bidx) * qo.heads_kv + kh) * qo.seq + pos;
+          } else {
+            if (qo.v8 != nullptr) dst = qo.v8 + static_cast<long long>(m) * qo.heads_kv * 128 + kh * 128;
+            if (qo.vs != nullptr)
+              sdst = qo.vs + (static_cast<long long>(bidx) * qo.heads_kv + kh) * qo.seq + pos;
+          }
+          if (mok && sdst != nullptr) *sdst = scale;
+          __half* vt = is_v ? static_cast<__half*>(qo.vt) +
+                                  (static_cast<long long>(bidx) * qo.heads_kv + kh) * 128 * qo.seq + pos
+                            : nullptr;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(taddr + c * 32, v);
+            tmem_ld_wait();
+            // reef's code rint(x / scale), clamped: fast by the reciprocal,
+            // the division only for chunks holding a near-tie (see quant_code)
+            bool exact = false;
+            int code[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const float x = __uint_as_float(v[k]);
+              const float qf = __fmul_rn(x, rcp);
+              const float r = rintf(qf);
+              exact |= !(fabsf(qf) < 128.0f && fabsf(qf - r) < 0.49993896f);
+              code[k] = __float2int_rn(r);
+            }
+            if (__any_sync(0xffffffffu, exact)) {
+#pragma unroll
+              for (int k = 0; k < 32; ++k)
+                code[k] = __float2int_rn(__fdiv_rn(__uint_as_float(v[k]), scale));
+            }
+#pragma unroll
+            for (int k = 0; k < 32; ++k) code[k] = code[k] < -127 ? -127 : (code[k] > 127 ? 127 : code[k]);
+            if (mok) {
+              if (dst != nullptr) {
+                uint32_t pk[8];
+#pragma unroll
+                for (int w = 0; w < 8; ++w)
+                  pk[w] = (code[4 * w] & 0xff) | ((code[4 * w + 1] & 0xff) << 8) |
+                          ((code[4 * w + 2] & 0xff) << 16) |
+                          (static_cast<uint32_t>(code[4 * w + 3] & 0xff) << 24);
+                *reinterpret_cast<uint4*>(dst + c * 32) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<uint4*>(dst + c * 32 + 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+              }
+              if (is_v) {
+                // vt[b][kh][d][pos] = f16(code * scale): a warp's 32 tokens are
+                // consecutive positions, so each d is one contiguous run
+#pragma unroll
+                for (int k = 0; k < 32; ++k)
+                  vt[static_cast<long long>(c * 32 + k) * qo.seq] =
+                      __float2half_rn(__fmul_rn(static_cast<float>(code[k]), scale));
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+        continue;
       }
       if constexpr (EPI == kEpiSwiGLU) {
         // gate chunk c and up chunk c (accumulator columns c*32 and BN/2 + c*32)
@@ -519,7 +669,7 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
     const uintptr_t r = reinterpret_cast<uintptr_t>(args.residual);
     args.vec_ok = (y % align == 0) && (r % 16 == 0) && (args.ldy % 4 == 0) ? 1 : 0;
   }
-  kernel<<<grid, kThreads, L::kAlloc, stream>>>(ma, mb, args);
+  kernel<<<grid, threads_for<EPI>(), L::kAlloc, stream>>>(ma, mb, args);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -625,6 +775,14 @@ int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream) {
     case kEpiSwiGLU:
       if (p.args.row_max == nullptr || p.args.b_up < p.N) return kErrInvalid;
       return launch<256, 4, kEpiSwiGLU>(p, stream);
+    case kEpiQkvRope: {
+      const QkvOut& q = p.args.qkv;
+      if (q.seq <= 0 || q.heads_q <= 0 || q.heads_kv <= 0 || q.rope == nullptr || !q.q8 ||
+          !q.k8 || !q.qs || !q.ks || !q.vt || p.N != (q.heads_q + 2 * q.heads_kv) * 128 ||
+          p.M % q.seq != 0)
+        return kErrInvalid;
+      return launch<256, 4, kEpiQkvRope>(p, stream);
+    }
     default:
       return kErrInvalid;
   }

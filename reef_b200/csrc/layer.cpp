@@ -98,6 +98,18 @@ int linear_w8a8_swiglu(long long rows, int in, int ffn, const int8_t* xq, const 
   return gemm_i8(p, kEpiSwiGLU, st);
 }
 
+int linear_w8a8_qkv_rope(long long rows, int in, const int8_t* xq, const float* xs,
+                         const int8_t* w_qkv, const float* ws, float rope_base, QkvOut out,
+                         cudaStream_t st) {
+  if (rows == 0) return kOk;
+  REEF_TRY(rope_table(out.seq, rope_base, const_cast<float2*>(out.rope), st));
+  GemmProblem p = problem(rows, in, (out.heads_q + 2 * out.heads_kv) * 128, xq, w_qkv);
+  p.args.x_scale = xs;
+  p.args.w_scale = ws;
+  p.args.qkv = out;
+  return gemm_i8(p, kEpiQkvRope, st);
+}
+
 // Row-parallel W8A8 linear.  `quant` fills xq/xs from the local input given
 // the full-row maximum (or computes it itself when row_max is null);
 // `absmax` writes the local row maxima.
@@ -167,22 +179,37 @@ inline Comm* C(reef_b200_comm* c) { return reinterpret_cast<Comm*>(c); }
 
 // ---- Llama-shape layer ----------------------------------------------------------
 
+// The QKV epilogue's outputs in the layer's buffers (the int8 v rows and v
+// scales are not needed by the flash head, which reads V^T).
+QkvOut qkv_out(const reef_b200_llama_layer* L, int hq, int hkv, int8_t* q8, int8_t* k8,
+               float* qs, float* ks, void* vt, void* rope) {
+  QkvOut o{};
+  o.rope = static_cast<const float2*>(rope);
+  o.seq = static_cast<int>(L->seq);
+  o.heads_q = hq;
+  o.heads_kv = hkv;
+  o.q8 = q8;
+  o.k8 = k8;
+  o.qs = qs;
+  o.ks = ks;
+  o.vt = vt;
+  return o;
+}
+
 struct LlamaBufs {
   int8_t* xq;
   float* xs;
   float* row_max;
-  float* big;     // qkv, later gate/up
+  float* big;     // SwiGLU output h [T][ffn]
   int8_t* q8;
   int8_t* k8;
-  int8_t* v8;
   float* qs;
   float* ks;
-  float* vs;
   void* vt;
   float* attn;
   float* h;
   int32_t* acc;
-  void* rope;     // [seq][64] (cos, sin)
+  void* rope;     // [64][seq] (cos, sin)
 };
 
 size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
@@ -193,13 +220,11 @@ size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
   b->xq = c.take<int8_t>(T * widest);
   b->xs = c.take<float>(T);
   b->row_max = c.take<float>(T);
-  b->big = c.take<float>(T * std::max((hq + 2 * hkv) * D, 2 * F));
+  b->big = c.take<float>(T * F);
   b->q8 = c.take<int8_t>(T * hq * D);
   b->k8 = c.take<int8_t>(T * hkv * D);
-  b->v8 = c.take<int8_t>(T * hkv * D);
   b->qs = c.take<float>(T * hq);
   b->ks = c.take<float>(T * hkv);
-  b->vs = c.take<float>(T * hkv);
   b->vt = c.take<uint16_t>(T * hkv * D);
   b->attn = c.take<float>(T * hq * D);
   b->h = c.take<float>(T * H);
@@ -220,13 +245,11 @@ struct LlamaAgBufs {
   int8_t* xq_all;
   float* xs;
   float* row_max;
-  float* big;
+  float* big;     // SwiGLU output h [T][ffn]
   int8_t* q8;
   int8_t* k8;
-  int8_t* v8;
   float* qs;
   float* ks;
-  float* vs;
   void* vt;
   float* attn;
   float* h;
@@ -245,13 +268,11 @@ size_t llama_ag_carve(const reef_b200_llama_layer* L, int world, void* ws, Llama
   b->xq_all = c.take<int8_t>(N * T * kmax);
   b->xs = c.take<float>(T);
   b->row_max = c.take<float>(T);
-  b->big = c.take<float>(T * std::max((hq + 2 * hkv) * D, 2 * F));
+  b->big = c.take<float>(T * F);
   b->q8 = c.take<int8_t>(T * hq * D);
   b->k8 = c.take<int8_t>(T * hkv * D);
-  b->v8 = c.take<int8_t>(T * hkv * D);
   b->qs = c.take<float>(T * hq);
   b->ks = c.take<float>(T * hkv);
-  b->vs = c.take<float>(T * hkv);
   b->vt = c.take<uint16_t>(T * hkv * D);
   b->attn = c.take<float>(T * hq * D);
   b->h = c.take<float>(T * Hl);
@@ -451,9 +472,14 @@ size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* L) {
   // rmsnorm+quant, qkv GEMM, rope table, rope q/k, quant v, flash, o-proj,
   // rmsnorm+quant, gate/up GEMM, down; a row-parallel linear is quant + GEMM
   // (TP=1) or absmax + quant + int32 GEMM + dequant epilogue (TP>1)
-  // (the gate/up GEMM writes SwiGLU's row maxima, so the MLP has no absmax pass)
-  if (llama_allgather(L)) return 15;  // rms x2 (stats, apply), o-proj absmax + quant, no epilogue pass
-  return L->comm != nullptr ? 15 : 12;
+  // rmsnorm+quant, rope table, QKV GEMM (RoPE + q/k/V^T packing in its
+  // epilogue), flash, o-proj (quant + GEMM), rmsnorm+quant, gate/up GEMM (SwiGLU
+  // and its row maxima in the epilogue), quant, down GEMM.  TP>1 all-reduce
+  // plan: a row-parallel linear adds an absmax pass and an int32 epilogue pass
+  // (the MLP's absmax comes from the gate/up GEMM); all-gather plan: each
+  // RMSNorm is two passes (stats, apply) and the o-proj input an absmax pass.
+  if (llama_allgather(L)) return 13;
+  return L->comm != nullptr ? 13 : 10;
 }
 
 static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* y,
@@ -530,10 +556,14 @@ static int llama_forward_ag(const reef_b200_llama_layer* L, const float* x, floa
   };
 
   REEF_TRY(rms(x, g1));
-  REEF_TRY(gemm_seg(Hl, L->w_qkv, qkv_w, L->s_qkv, nullptr, b.big, ev ? ev + 0 : nullptr));
-  REEF_TRY(rope_qkv_quant(static_cast<int>(L->batch), static_cast<int>(L->seq), hq, hkv,
-                          L->rope_base, b.big, b.q8, b.k8, b.v8, b.qs, b.ks, b.vs, b.vt, b.rope,
-                          st));
+  // QKV projection with RoPE and the int8 q / k / V^T packing in its epilogue
+  REEF_TRY(rope_table(static_cast<int>(L->seq), L->rope_base, b.rope, st));
+  {
+    GemmProblem p = seg_problem(Hl, L->w_qkv, qkv_w, L->s_qkv, nullptr);
+    p.args.qkv = qkv_out(L, hq, hkv, b.q8, b.k8, b.qs, b.ks, b.vt, b.rope);
+    Span sp(ev ? ev + 0 : nullptr, st);
+    REEF_TRY(gemm_i8(p, kEpiQkvRope, st));
+  }
   FlashProblem fp{};
   fp.batch = static_cast<int>(L->batch);
   fp.heads_q = hq;
@@ -601,14 +631,16 @@ static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* 
 
   // attention block: y_attn = x + o_proj(attn(rope(qkv(rmsnorm(x)))))
   REEF_TRY(rmsnorm_quant(T, H, L->rms_eps, x, L->attn_norm, b.xq, b.xs, st));
+  // QKV projection with RoPE and the int8 q / k / V^T packing in its epilogue
+  REEF_TRY(rope_table(static_cast<int>(L->seq), L->rope_base, b.rope, st));
   {
+    GemmProblem p = problem(T, H, qkv_w, b.xq, L->w_qkv);
+    p.args.x_scale = b.xs;
+    p.args.w_scale = L->s_qkv;
+    p.args.qkv = qkv_out(L, hq, hkv, b.q8, b.k8, b.qs, b.ks, b.vt, b.rope);
     Span sp(ev ? ev + 0 : nullptr, st);
-    REEF_TRY(gemm_w8a8_f32(T, H, qkv_w, b.xq, b.xs, L->w_qkv, L->s_qkv, nullptr, nullptr, b.big,
-                           st));
+    REEF_TRY(gemm_i8(p, kEpiQkvRope, st));
   }
-  REEF_TRY(rope_qkv_quant(static_cast<int>(L->batch), static_cast<int>(L->seq), hq, hkv,
-                          L->rope_base, b.big, b.q8, b.k8, b.v8, b.qs, b.ks, b.vs, b.vt, b.rope,
-                          st));
   FlashProblem fp{};
   fp.batch = static_cast<int>(L->batch);
   fp.heads_q = hq;

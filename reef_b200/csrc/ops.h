@@ -30,6 +30,23 @@ enum Epilogue : int {
   // y = silu(g) * u with g, u the kEpiF32W8A8 values of B rows n and b_up + n;
   // row_max[m] = max(row_max[m], max_n |y|) (atomic; zero it first)
   kEpiSwiGLU = 3,
+  // the kEpiF32W8A8 values of a QKV projection (heads of 128 columns: q, then
+  // k, then v), then RoPE on q / k and int8 per (token, head): see QkvOut
+  kEpiQkvRope = 4,
+};
+
+// kEpiQkvRope outputs (the layout rope_qkv_quant writes).  Rows are tokens
+// b * seq + pos.
+struct QkvOut {
+  const float2* rope;  // [64][seq] (cos, sin) of pos * base^(-2i/128), i-major
+  int seq, heads_q, heads_kv;
+  int8_t* q8;          // [T][Hq*128]
+  int8_t* k8;          // [T][Hkv*128]
+  int8_t* v8;          // [T][Hkv*128] or null
+  float* qs;           // [B][Hq][S]
+  float* ks;           // [B][Hkv][S]
+  float* vs;           // [B][Hkv][S] or null
+  void* vt;            // [B][Hkv][128][S] f16, f16(v code * v scale)
 };
 
 // Row stride (bytes) of every int8 matrix the tensor cores read: TMA needs
@@ -51,6 +68,7 @@ struct GemmArgs {
   int k_splits;           // > 1: K split across CTAs; split s writes y + s * split_stride
   long long b_up;         // kEpiSwiGLU: first B row of the "up" half
   float* row_max;         // kEpiSwiGLU: [M] running max |y| per row
+  QkvOut qkv;             // kEpiQkvRope
   long long split_stride; // elements between the partial outputs of two splits
   int vec_ok;             // 16-byte (int8: 4-byte) output stores allowed (launcher)
   int* err;               // device error word (set by the launcher)
@@ -91,6 +109,12 @@ int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream);
 int linear_w8a8_swiglu(long long rows, int in, int ffn, const int8_t* xq, const float* xs,
                        const int8_t* w_gu, const float* ws, float* h, float* row_max,
                        cudaStream_t st);
+// QKV projection with RoPE + per-(token, head) int8 in the epilogue
+// (layer.cpp): the outputs of rope_qkv_quant on the projection.  `out.rope`
+// is filled here from rope_base (it must point at [64][seq] float2 scratch).
+int linear_w8a8_qkv_rope(long long rows, int in, const int8_t* xq, const float* xs,
+                         const int8_t* w_qkv, const float* ws, float rope_base, QkvOut out,
+                         cudaStream_t st);
 
 // Skinny GEMM for few tokens (decode): y[m][n] = epi(sum_k x[m][k] w[n][k]) with
 // the weights as the 128-row MMA operand (swap-AB), tokens (m <= 128) on the
@@ -169,7 +193,9 @@ int flash_prefill_i8(const FlashProblem& p, cudaStream_t stream);
 int rope_qkv_quant(int batch, int seq, int heads_q, int heads_kv, float rope_base,
                    const float* qkv, int8_t* q8, int8_t* k8, int8_t* v8, float* q_scale,
                    float* k_scale, float* v_scale, void* vt, void* rope_table,
-                   cudaStream_t stream);  // rope_table: [seq][64] float2 scratch or null
+                   cudaStream_t stream);  // rope_table: [64][seq] float2 scratch or null
+// (cos, sin) of pos * base^(-2i/128), pos < seq, i < 64, into table [64][seq] float2
+int rope_table(int seq, float rope_base, void* table, cudaStream_t stream);
 
 // decode_attn.cu -- int8 decode attention over an int8 KV cache (split-KV)
 struct DecodeProblem {

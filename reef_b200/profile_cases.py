@@ -2,6 +2,7 @@
 
     python -m reef_b200.profile_cases gemm  [--m 16384 --n 12288 --k 4096]
     python -m reef_b200.profile_cases flash [--batch 8 --seq 2048 --heads 32]
+    python -m reef_b200.profile_cases qkv   [--batch 8 --seq 2048 --heads 32]
 
 Each case allocates its seeded inputs once, launches the kernel twice (a
 warm-up launch, then the one to capture: ``ncu -k regex:<name> -s 1 -c 1``)
@@ -49,9 +50,32 @@ def flash(batch: int, seq: int, heads: int, kv_heads: int) -> None:
     torch.cuda.synchronize()
 
 
+def qkv(batch: int, seq: int, heads: int, kv_heads: int, hidden: int = 4096) -> None:
+    """The QKV projection with RoPE + int8 q / k / V^T packing in its epilogue."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    T, W = batch * seq, (heads + 2 * kv_heads) * 128
+    xq = torch.randint(-127, 128, (T, hidden), generator=g, device="cuda", dtype=torch.int8)
+    w = torch.randint(-127, 128, (W, hidden), generator=g, device="cuda", dtype=torch.int8)
+    xs = torch.rand(T, generator=g, device="cuda") * 1e-3
+    ws = torch.rand(W, generator=g, device="cuda") * 1e-3
+    q8 = torch.empty((T, heads * 128), dtype=torch.int8, device="cuda")
+    k8 = torch.empty((T, kv_heads * 128), dtype=torch.int8, device="cuda")
+    qs = torch.empty((batch, heads, seq), device="cuda")
+    ks = torch.empty((batch, kv_heads, seq), device="cuda")
+    vt = torch.empty((batch, kv_heads, 128, seq), dtype=torch.float16, device="cuda")
+    rope = torch.empty((seq, 64, 2), device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        _lib.call("reef_b200_linear_w8a8_qkv_rope", batch, seq, hidden, heads, kv_heads, 10000.0,
+                  xq.data_ptr(), xs.data_ptr(), w.data_ptr(), ws.data_ptr(), q8.data_ptr(),
+                  k8.data_ptr(), None, qs.data_ptr(), ks.data_ptr(), None, vt.data_ptr(),
+                  rope.data_ptr(), st)
+    torch.cuda.synchronize()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "flash"])
+    ap.add_argument("case", choices=["gemm", "flash", "qkv"])
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=4096)
@@ -62,6 +86,8 @@ def main() -> None:
     a = ap.parse_args()
     if a.case == "gemm":
         gemm(a.m, a.n, a.k)
+    elif a.case == "qkv":
+        qkv(a.batch, a.seq, a.heads, a.kv_heads)
     else:
         flash(a.batch, a.seq, a.heads, a.kv_heads)
     K.check_device_error()

@@ -195,3 +195,52 @@ def test_rope_qkv_quant_packing(B, S):
         want, _ = quant_heads(rot.astype(np.float32), H)
         diff = np.abs(got.cpu().numpy().astype(np.int32) - want.astype(np.int32))
         assert diff.max() <= 1
+
+
+# QKV GEMM with RoPE + int8 packing in its epilogue == GEMM, then the packing
+# kernel: one head per tile (1 + 2 heads), 40-token sequences (warps straddle
+# two sequences), an all-zero token row, config 3's per-token width
+@pytest.mark.parametrize("B,S,k,Hq,Hkv", [(2, 64, 256, 4, 2), (3, 40, 512, 2, 1),
+                                          (1, 128, 4096, 32, 32), (2, 72, 128, 1, 1)])
+def test_qkv_rope_gemm_matches_two_pass(B, S, k, Hq, Hkv):
+    T, W = B * S, (Hq + 2 * Hkv) * 128
+    g = torch.Generator(device="cuda").manual_seed(B * S + k + Hq)
+    xq = torch.randint(-127, 128, (T, K.kpad(k)), generator=g, device="cuda", dtype=torch.int8)
+    xq[5] = 0
+    w = torch.randint(-127, 128, (W, K.kpad(k)), generator=g, device="cuda", dtype=torch.int8)
+    xs = torch.rand((T,), generator=g, device="cuda") * 1e-3 + 1e-4
+    ws = torch.rand((W,), generator=g, device="cuda") * 1e-3 + 1e-4
+    st = torch.cuda.current_stream().cuda_stream
+
+    def outputs():
+        return dict(q8=torch.empty((T, Hq * 128), dtype=torch.int8, device="cuda"),
+                    k8=torch.empty((T, Hkv * 128), dtype=torch.int8, device="cuda"),
+                    v8=torch.empty((T, Hkv * 128), dtype=torch.int8, device="cuda"),
+                    qs=torch.empty((B, Hq, S), device="cuda"),
+                    ks=torch.empty((B, Hkv, S), device="cuda"),
+                    vs=torch.empty((B, Hkv, S), device="cuda"),
+                    vt=torch.empty((B, Hkv, 128, S), dtype=torch.float16, device="cuda"))
+
+    y = K.gemm_w8a8(xq, xs, w, ws, in_features=k)
+    ref = outputs()
+    _lib.call("reef_b200_rope_qkv_quant", B, S, Hq, Hkv, 10000.0, y.data_ptr(),
+              ref["q8"].data_ptr(), ref["k8"].data_ptr(), ref["v8"].data_ptr(),
+              ref["qs"].data_ptr(), ref["ks"].data_ptr(), ref["vs"].data_ptr(),
+              ref["vt"].data_ptr(), st)
+    rope = torch.empty((S, 64, 2), device="cuda")
+    for with_v in (True, False):
+        got = outputs()
+        _lib.call("reef_b200_linear_w8a8_qkv_rope", B, S, k, Hq, Hkv, 10000.0, xq.data_ptr(),
+                  xs.data_ptr(), w.data_ptr(), ws.data_ptr(), got["q8"].data_ptr(),
+                  got["k8"].data_ptr(), got["v8"].data_ptr() if with_v else None,
+                  got["qs"].data_ptr(), got["ks"].data_ptr(),
+                  got["vs"].data_ptr() if with_v else None, got["vt"].data_ptr(),
+                  rope.data_ptr(), st)
+        torch.cuda.synchronize()
+        names = ["q8", "k8", "qs", "ks", "vt"] + (["v8", "vs"] if with_v else [])
+        for name in names:
+            a, b = got[name].cpu(), ref[name].cpu()
+            if a.dtype in (torch.float32, torch.float16):
+                a, b = a.view(torch.int32 if a.dtype == torch.float32 else torch.int16), \
+                    b.view(torch.int32 if b.dtype == torch.float32 else torch.int16)
+            assert torch.equal(a, b), (name, with_v)
