@@ -109,6 +109,21 @@ int reef_b200_gemm_w8a8(size_t rows, size_t in, size_t out, const int8_t* x_q,
                         const float* x_scale, const int8_t* w, const float* w_scale,
                         const float* bias, float* y, reef_b200_stream_t stream);
 
+/* Llama pre-norm then int8 (no counterpart in reef, whose GPT-Neo block uses
+ * LayerNorm): y = x * gain * r, r = 1 / sqrt(sum(x^2) / width + eps), then
+ * reef's quantiser per row (quant.hpp:112-133 on y).  The sum of squares has
+ * a fixed order that a tensor-parallel shard reproduces: 8 chunks of width/8
+ * columns; in chunk c, 128 partial sums p_i (i < 128) over the float4s
+ * i, i + 128, ... of the chunk, each float4 adding ((x0^2 + x1^2) + x2^2) +
+ * x3^2; the partials of i in [32w, 32w + 32) reduced by an xor butterfly
+ * (offsets 16, 8, 4, 2, 1) to w_w; chunk = ((w_0 + w_1) + w_2) + w_3; total =
+ * ((c0 + c1) + (c2 + c3)) + ((c4 + c5) + (c6 + c7)).  max |y| is taken as
+ * max |x * gain| * r.  x [rows][width] fp32 (width a multiple of 32),
+ * gain [width]; x_q [rows][width] int8, x_scale [rows]. */
+int reef_b200_rmsnorm_quant(size_t rows, size_t width, float eps, const float* x,
+                            const float* gain, int8_t* x_q, float* x_scale,
+                            reef_b200_stream_t stream);
+
 /* Gate/up projection of a SwiGLU MLP with the activation in the GEMM
  * epilogue (no counterpart in reef, whose GPT-Neo MLP is GELU; the Llama
  * layer's MLP uses it):

@@ -112,6 +112,18 @@ int reef_b200_linear_w8a8_bias(size_t rows, size_t in, size_t out, const float* 
   return reef_b200_gemm_w8a8(rows, in, out, x_q, x_scale, w, w_scale, bias, y, stream);
 }
 
+int reef_b200_rmsnorm_quant(size_t rows, size_t width, float eps, const float* x,
+                            const float* gain, int8_t* x_q, float* x_scale,
+                            reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (width == 0 || width > 16384 || rows > kMaxDim || !x || !gain || !x_q || !x_scale)
+    return REEF_B200_ERR_INVALID;
+  if (width % 32 != 0) return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  return rmsnorm_quant(static_cast<long long>(rows), static_cast<int>(width), eps, x, gain, x_q,
+                       x_scale, S(stream));
+}
+
 int reef_b200_linear_w8a8_swiglu(size_t rows, size_t in, size_t ffn, const int8_t* x_q,
                                  const float* x_scale, const int8_t* w_gu,
                                  const float* w_scale, float* h, float* row_max,

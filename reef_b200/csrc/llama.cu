@@ -112,96 +112,128 @@ __device__ __forceinline__ float4 scale4(float4 a, float r) {
   return make_float4(a.x * r, a.y * r, a.z * r, a.w * r);
 }
 
-// TP=1: one CTA of 8 x 128 threads per row; P float4 per thread.
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One warp computes a chunk's sum exactly as the 128-thread definition above
+// does: lane l plays threads l, 32 + l, 64 + l and 96 + l (the chunk's four
+// warps), each summing its float4s l + 32 w + 128 k (k < P) in order, then
+// runs each of those warps' xor-shuffle trees (an xor butterfly leaves the
+// same sum in every lane) and adds ((w0 + w1) + w2) + w3.  v (when given)
+// keeps x * gain, m the max of |x * gain|.
+template <int P, bool kKeep>
+__device__ __forceinline__ float chunk_sum(const float4* __restrict__ xr,
+                                           const float4* __restrict__ gr, int n4, int l,
+                                           float4 (&v)[4][P], float& m) {
+  float ws[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const int idx = l + 32 * w + kChunkThreads * k;
+      if (idx < n4) {
+        const float4 x4 = __ldg(xr + idx);
+        s = s + sumsq4(x4);
+        const float4 y4 = mul4(x4, __ldg(gr + idx));
+        m = fmaxf(m, amax4(y4));
+        if (kKeep) v[w][k] = y4;
+      }
+    }
+    ws[w] = warp_sum_tree(s);
+  }
+  return ((ws[0] + ws[1]) + ws[2]) + ws[3];
+}
+
+// TP=1: one CTA of 8 warps per row, warp c the chunk c; P float4 per lane
+// and virtual thread.
 template <int P>
-__global__ void __launch_bounds__(kChunks * kChunkThreads)
+__global__ void __launch_bounds__(kChunks * 32)
     rmsnorm_quant_kernel(int width, float eps, const float* __restrict__ x,
                          const float* __restrict__ gain, int8_t* __restrict__ xq,
                          long long ldq, float* __restrict__ xs) {
-  __shared__ float wsum[kChunks * 4];
   __shared__ float csum[kChunks];
-  __shared__ float red[32];
+  __shared__ float cmax[kChunks];
   const long long row = blockIdx.x;
-  const int t = threadIdx.x, c = t / kChunkThreads, i = t % kChunkThreads;
+  const int c = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int n4 = width / (4 * kChunks);  // float4 per chunk
   const float4* xr = reinterpret_cast<const float4*>(x + row * width) + c * n4;
   const float4* gr = reinterpret_cast<const float4*>(gain) + c * n4;
-  float4 v[P];
-  float s = 0.0f, m = 0.0f;
-#pragma unroll
-  for (int k = 0; k < P; ++k) {
-    const int idx = i + k * kChunkThreads;
-    if (idx < n4) {
-      v[k] = __ldg(xr + idx);
-      s = s + sumsq4(v[k]);
-      v[k] = mul4(v[k], __ldg(gr + idx));
-      m = fmaxf(m, amax4(v[k]));
-    }
+  float4 v[4][P];
+  float m = 0.0f;
+  const float cs = chunk_sum<P, true>(xr, gr, n4, l, v, m);
+  m = warp_max(m);
+  if (l == 0) {
+    csum[c] = cs;
+    cmax[c] = m;
   }
-  s = warp_sum_tree(s);
-  if ((t & 31) == 0) wsum[t >> 5] = s;
-  m = block_max(m, red);  // syncs: wsum is visible after this
-  if (t < kChunks) csum[t] = ((wsum[4 * t] + wsum[4 * t + 1]) + wsum[4 * t + 2]) + wsum[4 * t + 3];
   __syncthreads();
   const float r = 1.0f / sqrtf(chunk_tree(csum) / static_cast<float>(width) + eps);
-  const float mx = m * r;
+  float mm = cmax[0];
+#pragma unroll
+  for (int j = 1; j < kChunks; ++j) mm = fmaxf(mm, cmax[j]);
+  const float mx = mm * r;
   const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
-  if (t == 0) xs[row] = scale;
+  if (threadIdx.x == 0) xs[row] = scale;
   char4* out = reinterpret_cast<char4*>(xq + row * ldq) + c * n4;
 #pragma unroll
-  for (int k = 0; k < P; ++k) {
-    const int idx = i + k * kChunkThreads;
-    if (idx < n4) out[idx] = q8x4(scale4(v[k], r), scale);
+  for (int w = 0; w < 4; ++w) {
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const int idx = l + 32 * w + kChunkThreads * k;
+      if (idx < n4) out[idx] = q8x4(scale4(v[w][k], r), scale);
+    }
   }
 }
 
 // TP>1, pass 1: this rank's chunk sums and max|x * gain| over its columns.
 // x [rows][width_local], width_local = (chunks_local / 8) * width; stats
-// [rows][chunks_local + 1].  One CTA of chunks_local x 128 threads per row.
+// [rows][chunks_local + 1].  One CTA of chunks_local warps per row.
 template <int P>
-__global__ void rms_stats_kernel(int width, int chunks_local, const float* __restrict__ x,
-                                 const float* __restrict__ gain, float* __restrict__ stats) {
-  __shared__ float wsum[kChunks * 4];
-  __shared__ float red[32];
+__global__ void __launch_bounds__(kChunks * 32)
+    rms_stats_kernel(int width, int chunks_local, const float* __restrict__ x,
+                     const float* __restrict__ gain, float* __restrict__ stats) {
+  __shared__ float cmax[kChunks];
   const long long row = blockIdx.x;
-  const int t = threadIdx.x, c = t / kChunkThreads, i = t % kChunkThreads;
+  const int c = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int n4 = width / (4 * kChunks);
   const int wl = chunks_local * (width / kChunks);
   const float4* xr = reinterpret_cast<const float4*>(x + row * wl) + c * n4;
   const float4* gr = reinterpret_cast<const float4*>(gain) + c * n4;
-  float s = 0.0f, m = 0.0f;
-#pragma unroll
-  for (int k = 0; k < P; ++k) {
-    const int idx = i + k * kChunkThreads;
-    if (idx < n4) {
-      const float4 v = __ldg(xr + idx);
-      s = s + sumsq4(v);
-      m = fmaxf(m, amax4(mul4(v, __ldg(gr + idx))));
-    }
-  }
-  s = warp_sum_tree(s);
-  if ((t & 31) == 0) wsum[t >> 5] = s;
-  m = block_max(m, red);
+  float4 unused[4][P];
+  float m = 0.0f;
+  const float cs = chunk_sum<P, false>(xr, gr, n4, l, unused, m);
+  m = warp_max(m);
   float* st = stats + row * (chunks_local + 1);
-  if (t < chunks_local)
-    st[t] = ((wsum[4 * t] + wsum[4 * t + 1]) + wsum[4 * t + 2]) + wsum[4 * t + 3];
-  if (t == 0) st[chunks_local] = m;
+  if (l == 0) {
+    st[c] = cs;
+    cmax[c] = m;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = cmax[0];
+    for (int j = 1; j < chunks_local; ++j) mm = fmaxf(mm, cmax[j]);
+    st[chunks_local] = mm;
+  }
 }
 
 // TP>1, pass 2: from the all-gathered stats [ranks][rows][chunks_local + 1],
 // the row's r and scale (identical on every rank and to TP=1), then this
-// rank's columns quantised.
+// rank's columns quantised.  One CTA of chunks_local warps per row.
 template <int P>
-__global__ void rms_apply_kernel(int width, int chunks_local, int ranks, long long rows,
-                                 float eps, const float* __restrict__ x,
-                                 const float* __restrict__ gain,
-                                 const float* __restrict__ stats_all, int8_t* __restrict__ xq,
-                                 float* __restrict__ xs) {
+__global__ void __launch_bounds__(kChunks * 32)
+    rms_apply_kernel(int width, int chunks_local, int ranks, long long rows, float eps,
+                     const float* __restrict__ x, const float* __restrict__ gain,
+                     const float* __restrict__ stats_all, int8_t* __restrict__ xq,
+                     float* __restrict__ xs) {
   __shared__ float rs[2];
   const long long row = blockIdx.x;
-  const int t = threadIdx.x, c = t / kChunkThreads, i = t % kChunkThreads;
+  const int c = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int S = chunks_local + 1;
-  if (t == 0) {
+  if (threadIdx.x == 0) {
     float cs[kChunks];
     float mx = 0.0f;
     for (int g = 0; g < ranks; ++g) {
@@ -223,8 +255,8 @@ __global__ void rms_apply_kernel(int width, int chunks_local, int ranks, long lo
   const float4* gr = reinterpret_cast<const float4*>(gain) + c * n4;
   char4* out = reinterpret_cast<char4*>(xq + row * wl) + c * n4;
 #pragma unroll
-  for (int k = 0; k < P; ++k) {
-    const int idx = i + k * kChunkThreads;
+  for (int k = 0; k < 4 * P; ++k) {
+    const int idx = l + 32 * k;
     if (idx < n4) out[idx] = q8x4(scale4(mul4(__ldg(xr + idx), __ldg(gr + idx)), r), scale);
   }
 }
@@ -307,7 +339,7 @@ int rmsnorm_quant(long long rows, int width, float eps, const float* x, const fl
   if (width <= 0 || width % (4 * kChunks) != 0) return kErrInvalid;
   const unsigned grid = static_cast<unsigned>(rows);
   const int P = per_thread(width);
-  const int T = kChunks * kChunkThreads;
+  const int T = kChunks * 32;
   const long long ld = width;
   if (P <= 1) rmsnorm_quant_kernel<1><<<grid, T, 0, stream>>>(width, eps, x, gain, x_q, ld, x_scale);
   else if (P <= 2) rmsnorm_quant_kernel<2><<<grid, T, 0, stream>>>(width, eps, x, gain, x_q, ld, x_scale);
@@ -322,7 +354,7 @@ int rms_stats(long long rows, int width, int ranks, const float* x_local, const 
   if (width % (4 * kChunks) != 0 || kChunks % ranks != 0) return kErrInvalid;
   const int cl = kChunks / ranks, P = per_thread(width);
   const unsigned grid = static_cast<unsigned>(rows);
-  const int T = cl * kChunkThreads;
+  const int T = cl * 32;
   if (P <= 1) rms_stats_kernel<1><<<grid, T, 0, stream>>>(width, cl, x_local, gain_local, stats);
   else if (P <= 2) rms_stats_kernel<2><<<grid, T, 0, stream>>>(width, cl, x_local, gain_local, stats);
   else if (P <= 4) rms_stats_kernel<4><<<grid, T, 0, stream>>>(width, cl, x_local, gain_local, stats);
@@ -337,7 +369,7 @@ int rms_apply_quant(long long rows, int width, int ranks, float eps, const float
   if (width % (4 * kChunks) != 0 || kChunks % ranks != 0) return kErrInvalid;
   const int cl = kChunks / ranks, P = per_thread(width);
   const unsigned grid = static_cast<unsigned>(rows);
-  const int T = cl * kChunkThreads;
+  const int T = cl * 32;
   if (P <= 1)
     rms_apply_kernel<1><<<grid, T, 0, stream>>>(width, cl, ranks, rows, eps, x_local, gain_local, stats_all, x_q, x_scale);
   else if (P <= 2)
