@@ -293,6 +293,11 @@ __device__ __forceinline__ void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Arrive on hardware barrier `id` (expecting `count` threads) without waiting.
+__device__ __forceinline__ void named_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
 // 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart
 // (stride byte offset), leading byte offset unused for this layout,

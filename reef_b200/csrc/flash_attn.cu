@@ -29,8 +29,11 @@
 //               P_x(j) only after the product has read it, and S_x(j+1)
 //               complete means O_x holds every P.V up to j.
 //   warps 4..7  softmax of query tile A, warps 8..11 of query tile B: each
-//               thread owns one row (its TMEM lane).  While one group waits
-//               for its P.V and next scores, the other computes.
+//               thread owns one row (its TMEM lane).  The two groups take turns
+//               at the exponentials (the MUFU-bound phase): A's k-th turn
+//               follows B's (k-1)-th, B's k-th follows A's k-th, through two
+//               named barriers, so one group loads scores and takes its
+//               maxima while the other exponentiates.
 // Per score: int32 -> fp32 exactly by adding the bit pattern of 1.5 * 2^23
 // (|q.k| < 2^22 for 128 int8 products) and subtracting 1.5 * 2^23, times the
 // key's scale, a 3-input max, and one ex2; masks run only on the diagonal and
@@ -300,6 +303,16 @@ __global__ void __launch_bounds__(kFThreads, 1)
     float* ksw = reinterpret_cast<float*>(smem + FL::kScales) + (warp - 4) * 256;
     float m = 0.0f, l = 0.0f;
     bool ok = true;
+    // Turn-taking (hardware barriers 3 and 4, 256 threads: one group syncs,
+    // the other arrives).  A syncs on 3 before each of its n_a turns and
+    // arrives on 4 after; B arrives on 3 once up front and after each turn j
+    // with j + 1 < n_a, and syncs on 4 before its turns j < n_a (its extra
+    // causal tile runs alone).  Both barriers then see n_a completions with
+    // at most one outstanding, for n_b >= n_a; otherwise the groups do not
+    // take turns.  The sequence is walked whether or not a wait timed out.
+    const bool turns = n_b >= n_a && n_b > 0;
+    constexpr int kTurnA = 3, kTurnB = 4;
+    if (turns && x == 1) named_arrive(kTurnA, 256);
     // lane l stages keys [4l, 4l+4) of each tile, loaded a tile ahead (seq is
     // a multiple of 8, so four keys are all in range or all past the end)
     const float4* ks4 = reinterpret_cast<const float4*>(a.k_scale + kv_base);
@@ -372,6 +385,13 @@ __global__ void __launch_bounds__(kFThreads, 1)
         m = m_new;
         rescale = true;
       }
+      if (turns) {
+        if (x == 0) {
+          named_barrier(kTurnA, 256);
+        } else if (j < n_a) {
+          named_barrier(kTurnB, 256);
+        }
+      }
       // P = 2^(score - m) as f16 pairs, packed into r[0..63] (each pair
       // overwrites scores already consumed)
       const float nm = -m;
@@ -387,6 +407,13 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
         const __half2 hv = __floats2half2_rn(p0, p1);
         r[k0 >> 1] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+      if (turns) {
+        if (x == 0) {
+          named_arrive(kTurnB, 256);
+        } else if (j + 1 < n_a) {
+          named_arrive(kTurnA, 256);
+        }
       }
       l = __fmaf_rn(l, alpha, ps0 + ps1);
       tmem_st_32x32b_x32(tSx, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
