@@ -204,7 +204,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.index)],
+                 "-lms", "50", "-i", str(self.index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -300,32 +300,39 @@ def run_reef(args) -> int:
         if world > 1:
             dist.barrier()
 
-    for _ in range(max(args.warmup, 3)):
+    w_evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    warm = max(args.warmup, 3)
+    for i in range(warm):
+        if i == warm - 1:
+            w_evs[0].record(stream)
         L.forward(x, y)
+    w_evs[1].record(stream)
     torch.cuda.synchronize(dev)
     K.check_device_error()
+    step_s = w_evs[0].elapsed_time(w_evs[1]) * 1e-3
+    n_pre = max(1, int(1.0 / max(step_s, 1e-4)))
+    if world > 1:  # every rank runs the same number of forwards (collectives)
+        t_pre = torch.tensor([n_pre], device=dev)
+        dist.all_reduce(t_pre, op=dist.ReduceOp.MAX)
+        n_pre = int(t_pre.item())
 
-    # events: 10 per step around the GEMMs and the flash kernel
+    # The timed region: K forwards through the public entry point.  A second
+    # of the same forward runs just before it, so that the clock samples
+    # (one per 50 ms) cover sustained load even when the region is short.
     K_steps = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(10)] for _ in range(K_steps)]
-    for row in evs:
-        for e in row:
-            e.record(stream)
-    torch.cuda.synchronize(dev)
-    handles = [(C.c_void_p * 10)(*[e.cuda_event for e in row]) for row in evs]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     clocks = Clocks(local)
     clocks.start()
-    time.sleep(0.6)  # the sampler is up before the timed region
+    time.sleep(0.6)  # the sampler is up before the load starts
     barrier()
     torch.cuda.synchronize(dev)
     w0 = time.time()
+    for _ in range(n_pre):
+        L.forward(x, y)
     t_start.record(stream)
     for k in range(K_steps):
-        _lib.call("reef_b200_llama_layer_forward_events", C.byref(L.desc), x.data_ptr(),
-                  y.data_ptr(), L.workspace.data_ptr(), L.workspace.numel(), handles[k],
-                  stream.cuda_stream)
+        L.forward(x, y)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
     w1 = time.time()
@@ -334,6 +341,22 @@ def run_reef(args) -> int:
     clocks.stop()
     K.check_device_error()
     ms = t_start.elapsed_time(t_end) / K_steps
+
+    # per-kernel spans (QKV, flash, o-proj, gate/up, down) from the
+    # instrumented forward, which runs its steps in sequence
+    n_inst = max(3, min(K_steps, 10))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(10)] for _ in range(n_inst)]
+    for row in evs:
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize(dev)
+    handles = [(C.c_void_p * 10)(*[e.cuda_event for e in row]) for row in evs]
+    for k in range(n_inst):
+        _lib.call("reef_b200_llama_layer_forward_events", C.byref(L.desc), x.data_ptr(),
+                  y.data_ptr(), L.workspace.data_ptr(), L.workspace.numel(), handles[k],
+                  stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    K.check_device_error()
     spans = [[row[2 * i].elapsed_time(row[2 * i + 1]) for i in range(5)] for row in evs]
     gemm_ms = statistics.mean(sum(r[i] for i in (0, 2, 3, 4)) for r in spans)
     flash_ms = statistics.mean(r[1] for r in spans)
@@ -409,7 +432,8 @@ def run_reef(args) -> int:
                 "h2d_bytes_per_step": x.numel() * 4, "d2h_bytes_per_step": y.numel() * 4,
                 "ms_per_step": e2e_ms},
         "gpu_launches": int(launches) * K_steps,
-        "clocks": clocks.summary(w0, w1),
+        "clocks": dict(clocks.summary(w0, w1),
+                       window="the timed region and the 1 s of the same forward just before it"),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(s, host_threads())

@@ -394,7 +394,11 @@ typedef struct reef_b200_llama_layer {
  *    [hidden/world][hidden_q] and w_down [hidden/world][ffn_total] are this
  *    rank's OUTPUT rows over the full K.  Moves int8 activations instead of
  *    int32 partial sums (about a third of the bytes) and shards every
- *    element-wise step.  world must divide 8. */
+ *    element-wise step.  world must divide 8.  When the batch splits into 2
+ *    or 4 groups of whole sequences, the forward pipelines over them: the
+ *    collectives of one group run on the communicator's own stream while the
+ *    other groups compute on `stream` (same result; the stream still orders
+ *    everything before the call's last kernel). */
 #define REEF_B200_TP_ALLREDUCE 0
 #define REEF_B200_TP_ALLGATHER 1
 
@@ -407,12 +411,13 @@ int reef_b200_llama_layer_forward(const reef_b200_llama_layer* layer, const floa
                                   float* y, void* workspace, size_t workspace_bytes,
                                   reef_b200_stream_t stream);
 
-/* Kernels one forward launches (for launch accounting). */
+/* Kernels one reef_b200_llama_layer_forward launches (for launch accounting). */
 size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* layer);
 /* reef_b200_llama_layer_forward that also records 10 caller-created CUDA
  * events (cudaEvent_t, timing enabled) on `stream`: begin/end of the QKV
  * GEMM, the flash kernel, the o-proj GEMM, the gate/up GEMM and the down
- * GEMM, in that order (for per-kernel timing in a live run). */
+ * GEMM, in that order (for per-kernel timing in a live run).  The steps run
+ * in sequence on `stream` (the all-gather plan is not pipelined here). */
 int reef_b200_llama_layer_forward_events(const reef_b200_llama_layer* layer, const float* x,
                                          float* y, void* workspace, size_t workspace_bytes,
                                          void* const* events, reef_b200_stream_t stream);

@@ -16,8 +16,11 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <thread>
+#include <vector>
 
 namespace reef {
 
@@ -26,12 +29,24 @@ struct Comm {
   int rank = 0;
   int world = 1;
   double timeout_s = 60.0;
+  cudaStream_t stream = nullptr;  // collectives that overlap compute
+  cudaStream_t compute[kComputeStreams] = {};  // the pipelined chunks' kernels
+  int ctas = 0;                   // NCCL's CTA budget
+  // symmetric arena
+  uint8_t* arena = nullptr;        // this rank's (cudaMalloc)
+  std::vector<uint8_t*> peer;      // every rank's, mapped here (peer[rank] = arena)
+  size_t arena_data = 0;           // data bytes
+  int arena_slots = 0;
+  uint32_t round = 0;
 };
 
 namespace {
 
 // Drive a non-blocking NCCL operation to completion, or give up at the
 // deadline (abort the communicator: the caller's ranks are out of step).
+// Enqueuing a collective usually settles within microseconds, so the first
+// 2 ms poll without sleeping (a sleep per collective would make the host,
+// not the GPU, set the pace); after that, every 200 us.
 int settle(Comm* c, ncclResult_t r) {
   if (r == ncclSuccess) return kOk;
   if (r != ncclInProgress) return kErrNccl;
@@ -44,8 +59,49 @@ int settle(Comm* c, ncclResult_t r) {
     const double waited =
         std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
     if (waited > c->timeout_s) return kErrTimeout;
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    if (waited > 2e-3) {
+      std::this_thread::sleep_for(std::chrono::microseconds(200));
+    } else {
+      std::this_thread::yield();
+    }
   }
+}
+
+// Stream memory operations (driver entry points, no link-time libcuda).
+using WaitValue32 = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+using WriteValue32 = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+struct StreamOps {
+  WaitValue32 wait = nullptr;
+  WriteValue32 write = nullptr;
+};
+const StreamOps& stream_ops() {
+  static StreamOps ops;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWaitValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      ops.wait = reinterpret_cast<WaitValue32>(p);
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      ops.write = reinterpret_cast<WriteValue32>(p);
+  });
+  return ops;
+}
+
+void arena_free(Comm* c) {
+  for (int r = 0; r < static_cast<int>(c->peer.size()); ++r)
+    if (r != c->rank && c->peer[r] != nullptr) cudaIpcCloseMemHandle(c->peer[r]);
+  c->peer.clear();
+  if (c->arena != nullptr) cudaFree(c->arena);
+  c->arena = nullptr;
+  c->arena_data = 0;
+  c->arena_slots = 0;
+}
+
+size_t flag_bytes(int slots, int world) {
+  return (static_cast<size_t>(slots) * world * sizeof(uint32_t) + 255) & ~static_cast<size_t>(255);
 }
 
 }  // namespace
@@ -69,10 +125,28 @@ int comm_init(int rank, int world, const void* id_bytes, double timeout_s, Comm*
   c->timeout_s = timeout_s > 0 ? timeout_s : 60.0;
   ncclUniqueId id;
   std::memcpy(&id, id_bytes, sizeof id);
+  // NCCL's kernels share the GPU with the layer's: cap their CTAs (a
+  // persistent GEMM running beside a collective leaves this many SMs free).
+  // REEF_B200_NCCL_CTAS overrides the default of 8 (2 ranks) / 16 (more).
+  c->ctas = world <= 2 ? 8 : 16;
+  if (const char* e = std::getenv("REEF_B200_NCCL_CTAS")) {
+    const int v = std::atoi(e);
+    if (v >= 1 && v <= 64) c->ctas = v;
+  }
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
+  cfg.maxCTAs = c->ctas;
   ncclResult_t r = ncclCommInitRankConfig(&c->nccl, world, id, rank, &cfg);
   int rc = (c->nccl == nullptr && r != ncclSuccess) ? kErrNccl : settle(c, r);
+  if (rc == kOk) {
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    if (cudaStreamCreateWithPriority(&c->stream, cudaStreamNonBlocking, hi) != cudaSuccess)
+      rc = kErrCuda;
+    for (auto& s : c->compute)
+      if (rc == kOk && cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
+        rc = kErrCuda;
+  }
   if (rc != kOk) {
     if (c->nccl != nullptr) ncclCommAbort(c->nccl);
     delete c;
@@ -85,6 +159,19 @@ int comm_init(int rank, int world, const void* id_bytes, double timeout_s, Comm*
 int comm_destroy(Comm* c) {
   if (c == nullptr) return kOk;
   int rc = kOk;
+  if (c->arena != nullptr) {
+    cudaDeviceSynchronize();
+    arena_free(c);
+  }
+  if (c->stream != nullptr) {
+    cudaStreamSynchronize(c->stream);
+    cudaStreamDestroy(c->stream);
+  }
+  for (auto s : c->compute)
+    if (s != nullptr) {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
   if (c->nccl != nullptr) {
     ncclResult_t r = ncclCommFinalize(c->nccl);
     rc = settle(c, r);
@@ -100,13 +187,22 @@ int comm_destroy(Comm* c) {
 
 int comm_abort(Comm* c) {
   if (c == nullptr) return kOk;
+  arena_free(c);
   if (c->nccl != nullptr) ncclCommAbort(c->nccl);
+  if (c->stream != nullptr) cudaStreamDestroy(c->stream);
+  for (auto s : c->compute)
+    if (s != nullptr) cudaStreamDestroy(s);
   delete c;
   return kOk;
 }
 
 int comm_rank(const Comm* c) { return c ? c->rank : 0; }
 int comm_world(const Comm* c) { return c ? c->world : 1; }
+cudaStream_t comm_stream(const Comm* c) { return c ? c->stream : nullptr; }
+cudaStream_t comm_compute_stream(const Comm* c, int i) {
+  return (c && i >= 0 && i < kComputeStreams) ? c->compute[i] : nullptr;
+}
+int comm_ctas(const Comm* c) { return c ? c->ctas : 0; }
 
 int allreduce_max_f32(Comm* c, float* buf, size_t n, cudaStream_t stream) {
   if (c == nullptr || c->world == 1 || n == 0) return kOk;
@@ -129,5 +225,96 @@ int allgather_bytes(Comm* c, const void* send, void* recv, size_t bytes, cudaStr
   if (bytes == 0) return kOk;
   return settle(c, ncclAllGather(send, recv, bytes, ncclInt8, c->nccl, stream));
 }
+
+
+int comm_arena_reserve(Comm* c, size_t data_bytes, int slots) {
+  if (c == nullptr || c->world < 2 || slots < 1) return kErrInvalid;
+  if (c->arena != nullptr && c->arena_data >= data_bytes && c->arena_slots >= slots) return kOk;
+  const StreamOps& ops = stream_ops();
+  if (ops.wait == nullptr || ops.write == nullptr) return kErrUnsupported;
+  // every rank reaches this point with the same sizes; drain before replacing
+  if (cudaDeviceSynchronize() != cudaSuccess) return kErrCuda;
+  arena_free(c);
+  const size_t fb = flag_bytes(slots, c->world);
+  const size_t total = fb + ((data_bytes + 255) & ~static_cast<size_t>(255));
+  if (cudaMalloc(&c->arena, total) != cudaSuccess) return kErrCuda;
+  if (cudaMemset(c->arena, 0, fb) != cudaSuccess) return kErrCuda;
+  // exchange IPC handles (an all-gather through NCCL, which also orders the
+  // zeroed flags before any peer can signal)
+  cudaIpcMemHandle_t mine;
+  if (cudaIpcGetMemHandle(&mine, c->arena) != cudaSuccess) return kErrCuda;
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  uint8_t* dev = nullptr;
+  if (cudaMalloc(&dev, hb * (c->world + 1)) != cudaSuccess) return kErrCuda;
+  std::vector<cudaIpcMemHandle_t> all(c->world);
+  int rc = kOk;
+  if (cudaMemcpy(dev + hb * c->world, &mine, hb, cudaMemcpyHostToDevice) != cudaSuccess) rc = kErrCuda;
+  if (rc == kOk) rc = allgather_bytes(c, dev + hb * c->world, dev, hb, c->stream);
+  if (rc == kOk && cudaStreamSynchronize(c->stream) != cudaSuccess) rc = kErrCuda;
+  if (rc == kOk && cudaMemcpy(all.data(), dev, hb * c->world, cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = kErrCuda;
+  cudaFree(dev);
+  if (rc != kOk) return rc;
+  c->peer.assign(c->world, nullptr);
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) {
+      c->peer[r] = c->arena;
+      continue;
+    }
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+      return kErrCuda;
+    c->peer[r] = static_cast<uint8_t*>(p);
+  }
+  c->arena_data = data_bytes;
+  c->arena_slots = slots;
+  return kOk;
+}
+
+uint8_t* comm_arena_data(Comm* c) {
+  return c && c->arena ? c->arena + flag_bytes(c->arena_slots, c->world) : nullptr;
+}
+
+int comm_put(Comm* c, const void* src, size_t data_off, size_t bytes, cudaStream_t s) {
+  if (c == nullptr || c->arena == nullptr || data_off + bytes > c->arena_data) return kErrInvalid;
+  const size_t fb = flag_bytes(c->arena_slots, c->world);
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) continue;
+    if (cudaMemcpyAsync(c->peer[r] + fb + data_off, src, bytes, cudaMemcpyDeviceToDevice, s) !=
+        cudaSuccess)
+      return kErrCuda;
+  }
+  return kOk;
+}
+
+int comm_signal(Comm* c, int slot, uint32_t value, cudaStream_t s) {
+  if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots) return kErrInvalid;
+  const StreamOps& ops = stream_ops();
+  const size_t off = (static_cast<size_t>(slot) * c->world + c->rank) * sizeof(uint32_t);
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) continue;
+    // the default flags order the write after the stream's earlier work
+    // (its copies included) with a memory barrier
+    if (ops.write(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(c->peer[r] + off),
+                  value, 0) != CUDA_SUCCESS)
+      return kErrCuda;
+  }
+  return kOk;
+}
+
+int comm_wait(Comm* c, int slot, uint32_t value, cudaStream_t s) {
+  if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots) return kErrInvalid;
+  const StreamOps& ops = stream_ops();
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) continue;
+    const size_t off = (static_cast<size_t>(slot) * c->world + r) * sizeof(uint32_t);
+    if (ops.wait(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(c->arena + off), value,
+                 CU_STREAM_WAIT_VALUE_GEQ) != CUDA_SUCCESS)
+      return kErrCuda;
+  }
+  return kOk;
+}
+
+uint32_t comm_next_round(Comm* c) { return c ? ++c->round : 0; }
 
 }  // namespace reef

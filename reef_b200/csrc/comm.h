@@ -14,6 +14,35 @@ int comm_destroy(Comm* c);
 int comm_abort(Comm* c);
 int comm_rank(const Comm* c);
 int comm_world(const Comm* c);
+// The communicator's own stream (high priority) for collectives that overlap
+// compute, and the SMs its kernels may occupy (NCCL's maxCTAs): a compute
+// kernel meant to run beside them leaves that many SMs free.
+cudaStream_t comm_stream(const Comm* c);
+int comm_ctas(const Comm* c);
+// Compute streams for work pipelined against the collectives (kComputeStreams).
+constexpr int kComputeStreams = 4;
+cudaStream_t comm_compute_stream(const Comm* c, int i);
+
+// ---- Symmetric arena: copy-engine transfers over NVLink, stream-ordered flags
+//
+// Every rank holds an arena of the same size, mapped into every peer's
+// address space (CUDA IPC), laid out alike: `slots` x world uint32 flags, then
+// data.  comm_put copies local bytes to the same data offset in every peer's
+// arena with the copy engines (no SMs); comm_signal writes a flag
+// (slot, this rank) in every peer's arena after the stream's earlier work;
+// comm_wait makes a stream wait, in the stream's front end, until every
+// peer's flag (slot, peer) in the local arena reaches a value.  Values only
+// grow, so a flag never needs resetting.
+// (Re)creates the arena when it is smaller than asked; collective (every rank
+// calls it with the same sizes in the same order).
+int comm_arena_reserve(Comm* c, size_t data_bytes, int slots);
+uint8_t* comm_arena_data(Comm* c);  // this rank's data region
+int comm_put(Comm* c, const void* src, size_t data_off, size_t bytes, cudaStream_t s);
+int comm_signal(Comm* c, int slot, uint32_t value, cudaStream_t s);
+int comm_wait(Comm* c, int slot, uint32_t value, cudaStream_t s);
+// A counter the pipelined forward advances once per call (identical on all
+// ranks, which make the same calls), from which flag values derive.
+uint32_t comm_next_round(Comm* c);
 int allreduce_max_f32(Comm* c, float* buf, size_t n, cudaStream_t stream);
 int allreduce_sum_i32(Comm* c, int32_t* buf, size_t n, cudaStream_t stream);
 // rank-major all-gather: recv = [world][bytes] (send may not alias recv)

@@ -656,7 +656,8 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
   constexpr int kOut = EPI == kEpiSwiGLU ? BN / 2 : BN;
   const int num_tiles = ((p.M + kBM - 1) / kBM) * ((p.N + kOut - 1) / kOut);
   const int splits = p.args.k_splits > 1 ? p.args.k_splits : 1;
-  const int grid = std::min(num_tiles * splits, num_sms());
+  const int ctas = p.args.max_ctas > 0 ? std::min(p.args.max_ctas, num_sms()) : num_sms();
+  const int grid = std::min(num_tiles * splits, ctas);
   GemmArgs args = p.args;
   args.M = p.M;
   args.N = p.N;

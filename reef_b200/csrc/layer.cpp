@@ -20,6 +20,8 @@
 #include "ops.h"
 
 #include <algorithm>
+#include <cstdlib>
+#include <vector>
 #include <cstdint>
 
 namespace reef {
@@ -231,6 +233,14 @@ size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
   b->acc = c.take<int32_t>(L->comm != nullptr ? T * H : 0);
   b->rope = c.take<float>(L->seq * 64 * 2);
   return c.used + 256;
+}
+
+// Chunks of whole sequences the all-gather plan pipelines over: 4 (or 2)
+// when the batch divides, else 1 (no pipelining).
+int ag_chunks(const reef_b200_llama_layer* L) {
+  for (int c : {4, 2})
+    if (L->batch % static_cast<size_t>(c) == 0) return c;
+  return 1;
 }
 
 bool llama_allgather(const reef_b200_llama_layer* L) {
@@ -478,7 +488,9 @@ size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* L) {
   // plan: a row-parallel linear adds an absmax pass and an int32 epilogue pass
   // (the MLP's absmax comes from the gate/up GEMM); all-gather plan: each
   // RMSNorm is two passes (stats, apply) and the o-proj input an absmax pass.
-  if (llama_allgather(L)) return 13;
+  // The all-gather plan pipelined over k chunks of sequences runs each of its
+  // 12 per-token kernels once per chunk (the RoPE table once).
+  if (llama_allgather(L)) return ag_chunks(L) > 1 ? 12 * ag_chunks(L) + 1 : 13;
   return L->comm != nullptr ? 13 : 10;
 }
 
@@ -504,6 +516,248 @@ int reef_b200_llama_layer_forward_events(const reef_b200_llama_layer* L, const f
   return llama_forward(L, x, y, workspace, workspace_bytes, ev, stream);
 }
 
+// Events of the pipelined forward, destroyed on every exit (a pending event
+// may be destroyed; its resources go when it completes).
+struct EventSet {
+  std::vector<cudaEvent_t> ev;
+  explicit EventSet(int n) : ev(n, nullptr) {}
+  int create() {
+    for (auto& e : ev)
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return kErrCuda;
+    return kOk;
+  }
+  ~EventSet() {
+    for (auto e : ev)
+      if (e != nullptr) cudaEventDestroy(e);
+  }
+};
+
+// The all-gather plan, pipelined over chunks of whole sequences, with every
+// transfer on the copy engines.  Chunk k's kernels run on the communicator's
+// compute stream k.  The data a step gathers lives in the communicator's
+// symmetric arena, one region per chunk and kind (int8 activations, RMSNorm
+// chunk sums, row maxima), laid out [rank][rows][...]: each rank's kernel
+// writes its own segment, and the collective stream copies it into every
+// peer's arena (cudaMemcpyAsync over NVLink: no SMs, so it overlaps the
+// persistent GEMMs) and then raises the (region, rank) data flag there.  The
+// consuming kernel's stream waits for every peer's data flag; after it ran,
+// the stream raises the region's "consumed" flag in every peer's arena, and a
+// rank copies into a peer's region only once that peer has consumed the
+// previous contents.  Flag values are (forward round, use) counters that only
+// grow.  Steps are issued wavefront-wise so that every rank issues the same
+// sequence; each wait depends only on copies issued earlier in it, so the
+// pipeline cannot deadlock.  Each chunk computes exactly what the unpipelined
+// plan computes for its rows, so the result is identical.
+static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const float* x, float* y,
+                                      const LlamaAgBufs& b, int chunks, cudaStream_t st) {
+  Comm* c = C(L->comm);
+  const int N = comm_world(c), rank = comm_rank(c);
+  cudaStream_t cs = comm_stream(c);
+  if (cs == nullptr || chunks > kComputeStreams) return REEF_B200_ERR_INVALID;
+  const int H = static_cast<int>(L->hidden), hq = static_cast<int>(L->heads_q),
+            hkv = static_cast<int>(L->heads_kv), F = static_cast<int>(L->ffn), D = 128;
+  const int seq = static_cast<int>(L->seq);
+  const int Hl = H / N, S = 8 / N + 1, qkv_w = (hq + 2 * hkv) * D;
+  const long long kmax = std::max({Hl, hq * D, F});
+  const int bc = static_cast<int>(L->batch) / chunks;  // sequences per chunk
+  const long long Tc = static_cast<long long>(bc) * seq;
+  const float* g1 = L->attn_norm + static_cast<long long>(rank) * Hl;
+  const float* g2 = L->mlp_norm + static_cast<long long>(rank) * Hl;
+
+  // arena: per chunk [XQ: N*Tc*kmax B][ST: N*Tc*S f32][MX: N*Tc f32], 256-B aligned
+  auto al = [](long long v) { return (v + 255) & ~255ll; };
+  const long long xq_bytes = al(N * Tc * kmax), st_bytes = al(N * Tc * S * 4),
+                  mx_bytes = al(N * Tc * 4);
+  const long long chunk_bytes = xq_bytes + st_bytes + mx_bytes;
+  enum Kind { kXq = 0, kSt = 1, kMx = 2 };
+  constexpr int kUses[3] = {4, 2, 2};  // per forward
+  REEF_TRY(comm_arena_reserve(c, static_cast<size_t>(chunk_bytes * chunks), 6 * chunks));
+  uint8_t* arena = comm_arena_data(c);
+  const uint32_t round = comm_next_round(c);
+  auto region_off = [&](int k, Kind kind) {
+    return k * chunk_bytes + (kind == kXq ? 0 : kind == kSt ? xq_bytes : xq_bytes + st_bytes);
+  };
+  auto data_slot = [&](int k, Kind kind) { return 6 * k + 2 * kind; };
+  auto cons_slot = [&](int k, Kind kind) { return 6 * k + 2 * kind + 1; };
+  auto epoch = [&](Kind kind, int use) {
+    return static_cast<uint32_t>((round - 1) * kUses[kind] + use + 1);
+  };
+  auto xq_all = [&](int k) { return reinterpret_cast<int8_t*>(arena + region_off(k, kXq)); };
+  auto st_all = [&](int k) { return reinterpret_cast<float*>(arena + region_off(k, kSt)); };
+  auto mx_all = [&](int k) { return reinterpret_cast<float*>(arena + region_off(k, kMx)); };
+  // this rank's segment of a region (the [N][Tc][w] layout of the step's width w)
+  auto xq_mine = [&](int k, long long kl) { return xq_all(k) + rank * Tc * kl; };
+  auto st_mine = [&](int k) { return st_all(k) + rank * Tc * S; };
+  auto mx_mine = [&](int k) { return mx_all(k) + rank * Tc; };
+
+  EventSet done(chunks), pushed(chunks), fork(1);
+  REEF_TRY(done.create());
+  REEF_TRY(pushed.create());
+  REEF_TRY(fork.create());
+  auto sk = [&](int k) { return comm_compute_stream(c, k); };
+  REEF_TRY(rope_table(seq, L->rope_base, b.rope, st));
+  if (cudaEventRecord(fork.ev[0], st) != cudaSuccess) return REEF_B200_ERR_CUDA;
+  for (int k = 0; k < chunks; ++k)
+    if (cudaStreamWaitEvent(sk(k), fork.ev[0], 0) != cudaSuccess) return REEF_B200_ERR_CUDA;
+
+  // a compute step of chunk k: wait for the gathered inputs it consumes, run,
+  // mark them consumed, and mark the step done (for the collective stream)
+  struct In {
+    Kind kind;
+    int use;
+  };
+  // (it also waits for chunk k's last outgoing copy, which may still read the
+  // segment this step overwrites)
+  auto compute = [&](int k, std::initializer_list<In> ins, auto&& fn) -> int {
+    if (cudaStreamWaitEvent(sk(k), pushed.ev[k], 0) != cudaSuccess) return kErrCuda;
+    for (const In& i : ins) REEF_TRY(comm_wait(c, data_slot(k, i.kind), epoch(i.kind, i.use), sk(k)));
+    REEF_TRY(fn(sk(k)));
+    for (const In& i : ins) REEF_TRY(comm_signal(c, cons_slot(k, i.kind), epoch(i.kind, i.use), sk(k)));
+    return cudaEventRecord(done.ev[k], sk(k)) == cudaSuccess ? kOk : kErrCuda;
+  };
+  // the collective step: once chunk k's producing kernel is done and every
+  // peer has consumed the region's previous contents, copy this rank's
+  // segment into every peer's arena and raise the data flag there
+  auto gather = [&](int k, Kind kind, int use, const void* mine, size_t bytes) -> int {
+    if (cudaStreamWaitEvent(cs, done.ev[k], 0) != cudaSuccess) return kErrCuda;
+    const uint32_t e = epoch(kind, use);
+    REEF_TRY(comm_wait(c, cons_slot(k, kind), e - 1, cs));
+    const size_t off = static_cast<const uint8_t*>(mine) - arena;
+    REEF_TRY(comm_put(c, mine, off, bytes, cs));
+    REEF_TRY(comm_signal(c, data_slot(k, kind), e, cs));
+    return cudaEventRecord(pushed.ev[k], cs) == cudaSuccess ? kOk : kErrCuda;
+  };
+  // per-chunk views of the workspace
+  auto xk = [&](int k) { return x + k * Tc * Hl; };
+  auto hk = [&](int k) { return b.h + k * Tc * Hl; };
+  auto xsk = [&](int k) { return b.xs + k * Tc; };
+  auto rmk = [&](int k) { return b.row_max + k * Tc; };
+  auto attnk = [&](int k) { return b.attn + k * Tc * hq * D; };
+  auto bigk = [&](int k) { return b.big + k * Tc * F; };
+  // the gathered activation [N][Tc][kl] of chunk k times this rank's rows of W
+  auto problem_k = [&](int k, int kl, const int8_t* w, int n, const float* ws, float* out) {
+    GemmProblem p{};
+    p.M = static_cast<int>(Tc);
+    p.N = n;
+    p.K = kl;
+    p.a = xq_all(k);
+    p.lda = kl;
+    p.a_seg = Tc * kl;
+    p.b = w;
+    p.ldb = static_cast<long long>(kl) * N;
+    p.b_seg = kl;
+    p.args.k_segments = N;
+    p.args.x_scale = xsk(k);
+    p.args.w_scale = ws;
+    p.args.y = out;
+    p.args.ldy = n;
+    return p;
+  };
+  auto gather_xq = [&](int k, int use, long long kl) {
+    return gather(k, kXq, use, xq_mine(k, kl), static_cast<size_t>(Tc * kl));
+  };
+  auto gather_st = [&](int k, int use) {
+    return gather(k, kSt, use, st_mine(k), static_cast<size_t>(Tc * S * 4));
+  };
+  auto gather_mx = [&](int k, int use) {
+    return gather(k, kMx, use, mx_mine(k), static_cast<size_t>(Tc * 4));
+  };
+
+  // ---- attention block
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {}, [&](cudaStream_t s) {
+      return rms_stats(Tc, H, N, xk(k), g1, st_mine(k), s);
+    }));
+  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_st(k, 0));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {{kSt, 0}}, [&](cudaStream_t s) {
+      return rms_apply_quant(Tc, H, N, L->rms_eps, xk(k), g1, st_all(k), xq_mine(k, Hl), xsk(k), s);
+    }));
+  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_xq(k, 0, Hl));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {{kXq, 0}}, [&](cudaStream_t s) {
+      uint16_t* vt = static_cast<uint16_t*>(b.vt) + static_cast<long long>(k) * bc * hkv * D * seq;
+      GemmProblem p = problem_k(k, Hl, L->w_qkv, qkv_w, L->s_qkv, nullptr);
+      p.args.qkv = qkv_out(L, hq, hkv, b.q8 + k * Tc * hq * D, b.k8 + k * Tc * hkv * D,
+                           b.qs + static_cast<long long>(k) * bc * hq * seq,
+                           b.ks + static_cast<long long>(k) * bc * hkv * seq, vt, b.rope);
+      return gemm_i8(p, kEpiQkvRope, s);
+    }));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {}, [&](cudaStream_t s) {
+      FlashProblem fp{};
+      fp.batch = bc;
+      fp.heads_q = hq;
+      fp.heads_kv = hkv;
+      fp.seq = seq;
+      fp.head_dim = D;
+      fp.causal = 1;
+      fp.sm_scale = 0.08838834764831845f;
+      fp.q8 = b.q8 + k * Tc * hq * D;
+      fp.k8 = b.k8 + k * Tc * hkv * D;
+      fp.vt = static_cast<uint16_t*>(b.vt) + static_cast<long long>(k) * bc * hkv * D * seq;
+      fp.q_scale = b.qs + static_cast<long long>(k) * bc * hq * seq;
+      fp.k_scale = b.ks + static_cast<long long>(k) * bc * hkv * seq;
+      fp.out = attnk(k);
+      fp.out_ld = static_cast<long long>(hq) * D;
+      REEF_TRY(flash_prefill_i8(fp, s));
+      return row_absmax(Tc, hq * D, attnk(k), mx_mine(k), s);
+    }));
+  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_mx(k, 0));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {{kMx, 0}}, [&](cudaStream_t s) {
+      REEF_TRY(max_segments(N, Tc, mx_all(k), rmk(k), s));
+      return quantize_rows(Tc, hq * D, attnk(k), xq_mine(k, hq * D), hq * D, xsk(k), rmk(k), s);
+    }));
+  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_xq(k, 1, hq * D));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {{kXq, 1}}, [&](cudaStream_t s) {
+      GemmProblem p = problem_k(k, hq * D, L->w_o, Hl, L->s_o, hk(k));
+      p.args.residual = xk(k);
+      return gemm_i8(p, kEpiF32W8A8, s);
+    }));
+  // ---- MLP block
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {}, [&](cudaStream_t s) {
+      return rms_stats(Tc, H, N, hk(k), g2, st_mine(k), s);
+    }));
+  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_st(k, 1));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {{kSt, 1}}, [&](cudaStream_t s) {
+      return rms_apply_quant(Tc, H, N, L->rms_eps, hk(k), g2, st_all(k), xq_mine(k, Hl), xsk(k), s);
+    }));
+  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_xq(k, 2, Hl));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {{kXq, 2}}, [&](cudaStream_t s) {
+      if (cudaMemsetAsync(mx_mine(k), 0, static_cast<size_t>(Tc) * sizeof(float), s) != cudaSuccess)
+        return static_cast<int>(kErrCuda);
+      GemmProblem p = problem_k(k, Hl, L->w_gu, F, L->s_gu, bigk(k));
+      p.args.b_up = F;
+      p.args.row_max = mx_mine(k);
+      return gemm_i8(p, kEpiSwiGLU, s);
+    }));
+  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_mx(k, 1));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {{kMx, 1}}, [&](cudaStream_t s) {
+      REEF_TRY(max_segments(N, Tc, mx_all(k), rmk(k), s));
+      return quantize_rows(Tc, F, bigk(k), xq_mine(k, F), F, xsk(k), rmk(k), s);
+    }));
+  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_xq(k, 3, F));
+  for (int k = 0; k < chunks; ++k)
+    REEF_TRY(compute(k, {{kXq, 3}}, [&](cudaStream_t s) {
+      GemmProblem p = problem_k(k, F, L->w_down, Hl, L->s_down, y + k * Tc * Hl);
+      p.args.residual = hk(k);
+      return gemm_i8(p, kEpiF32W8A8, s);
+    }));
+  // join: the caller's stream waits for every chunk's last kernel and last
+  // outgoing copy
+  for (int k = 0; k < chunks; ++k)
+    if (cudaStreamWaitEvent(st, done.ev[k], 0) != cudaSuccess ||
+        cudaStreamWaitEvent(st, pushed.ev[k], 0) != cudaSuccess)
+      return REEF_B200_ERR_CUDA;
+  return REEF_B200_OK;
+}
+
 // The all-gather plan (REEF_B200_TP_ALLGATHER): x, y and the residual are
 // this rank's hidden/world columns; every projection reads the all-gathered
 // int8 activation (rank-major [world][tokens][K/world], consumed as K
@@ -515,6 +769,9 @@ static int llama_forward_ag(const reef_b200_llama_layer* L, const float* x, floa
   const int N = comm_world(c), rank = comm_rank(c);
   LlamaAgBufs b;
   if (llama_ag_carve(L, N, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
+  // the instrumented forward (per-kernel spans) runs the steps in sequence
+  if (ev == nullptr && ag_chunks(L) > 1)
+    return llama_forward_ag_pipelined(L, x, y, b, ag_chunks(L), st);
   const long long T = static_cast<long long>(L->batch * L->seq);
   const int H = static_cast<int>(L->hidden), hq = static_cast<int>(L->heads_q),
             hkv = static_cast<int>(L->heads_kv), F = static_cast<int>(L->ffn), D = 128;

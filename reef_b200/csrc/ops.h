@@ -71,6 +71,7 @@ struct GemmArgs {
   QkvOut qkv;             // kEpiQkvRope
   long long split_stride; // elements between the partial outputs of two splits
   int vec_ok;             // 16-byte (int8: 4-byte) output stores allowed (launcher)
+  int max_ctas;           // > 0: at most this many persistent CTAs (SMs left to others)
   int* err;               // device error word (set by the launcher)
 };
 
@@ -131,6 +132,8 @@ int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int ep
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q,
                   long long ldq, float* x_scale, const float* row_max,
                   cudaStream_t stream);
+// out[r] = max_s in[s][r] for in [segs][rows]
+int max_segments(int segs, long long rows, const float* in, float* out, cudaStream_t stream);
 int row_absmax(long long rows, long long in, const float* x, float* row_max,
                cudaStream_t stream);
 int pack_weight_i8(long long in, long long out, const int8_t* wt, int8_t* w,

@@ -121,6 +121,16 @@ __global__ void __launch_bounds__(kQuantThreads)
   if (threadIdx.x == 0) out[blockIdx.x] = m;
 }
 
+// out[r] = max over s of in[s][r] (row maxima gathered from `segs` ranks).
+__global__ void max_segments_kernel(int segs, long long rows, const float* __restrict__ in,
+                                    float* __restrict__ out) {
+  const long long r = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float m = in[r];
+  for (int s = 1; s < segs; ++s) m = fmaxf(m, in[s * rows + r]);
+  out[r] = m;
+}
+
 // [in][out] (Coral's transposed layout, kernels.hpp:15-16) -> [out][ldw].
 __global__ void pack_weight_kernel(int in, int out, const int8_t* __restrict__ wt,
                                    int8_t* __restrict__ w, long long ldw) {
@@ -200,6 +210,14 @@ int row_absmax(long long rows, long long in, const float* x, float* row_max,
   if (in <= 0 || x == nullptr || row_max == nullptr) return kErrInvalid;
   row_absmax_kernel<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
       static_cast<int>(in), x, row_max);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int max_segments(int segs, long long rows, const float* in, float* out, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (segs < 1 || in == nullptr || out == nullptr) return kErrInvalid;
+  max_segments_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, stream>>>(segs, rows,
+                                                                                     in, out);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
