@@ -284,6 +284,15 @@ int reef_b200_linear_w8a8_qkv_rope(size_t batch, size_t seq, size_t in, size_t h
                                    float* q_scale, float* k_scale, float* v_scale, void* vt,
                                    void* rope_table, reef_b200_stream_t stream);
 
+/* Failure-detection self-test (no counterpart in reef): launches one thread
+ * that waits, with the library's bounded mbarrier wait but a limit of
+ * limit_us microseconds (1 .. 2e6), on a barrier nothing completes.  The wait
+ * gives up, records its timeout code (0x101) in the device error word that
+ * reef_b200_device_error returns, and the kernel exits normally; *done
+ * (device int) becomes 2 (1 would mean the wait was satisfied).  The device
+ * stays usable. */
+int reef_b200_selftest_wait_timeout(unsigned limit_us, int* done, reef_b200_stream_t stream);
+
 /* Flash attention over int8 q / k and f16 v (attend_head,
  * attention.hpp:117-123, on the dequantised values, with score scale
  * sm_scale and GQA: query head h reads kv head h / (heads_q / heads_kv)).

@@ -287,6 +287,12 @@ int reef_b200_rope_qkv_quant(size_t batch, size_t seq, size_t heads_q, size_t he
                         S(stream));
 }
 
+int reef_b200_selftest_wait_timeout(unsigned limit_us, int* done, reef_b200_stream_t stream) {
+  if (done == nullptr || limit_us == 0 || limit_us > 2000000u) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return selftest_wait_timeout(1000ull * limit_us, done, S(stream));
+}
+
 int reef_b200_linear_w8a8_qkv_rope(size_t batch, size_t seq, size_t in, size_t heads_q,
                                    size_t heads_kv, float rope_base, const int8_t* x_q,
                                    const float* x_scale, const int8_t* w_qkv,

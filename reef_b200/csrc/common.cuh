@@ -85,14 +85,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns
-// false (after recording `code`) when the deadline passes.
+// false (after recording `code`) when `limit_ns` of %globaltimer pass.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          int* err, int code) {
+                                          int* err, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = globaltimer();
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 255u) == 0 && globaltimer() - start > kWaitLimitNs) {
+    if ((spin & 255u) == 0 && globaltimer() - start > limit_ns) {
       record_error(err, code);
       return false;
     }

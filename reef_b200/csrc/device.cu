@@ -1,6 +1,7 @@
 // device.cu -- per-device plumbing: SM count, the device error word, the
 // architecture check and TMA tensor-map encoding (through the driver entry
 // point, so the library needs no link-time libcuda).
+#include "common.cuh"
 #include "ops.h"
 
 #include <mutex>
@@ -88,6 +89,27 @@ int read_device_error(int* code) {
     return kErrCuda;
   *code = v;
   return kOk;
+}
+
+namespace {
+// One thread initialises an mbarrier that expects one arrival nobody makes and
+// waits on it with the bounded wait: the wait must give up after `limit_ns`,
+// record kDevTimeoutFull and return.
+__global__ void wait_timeout_kernel(unsigned long long limit_ns, int* err, int* done) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    const bool ok = mbar_wait(&bar, 0, err, kDevTimeoutFull, limit_ns);
+    *done = ok ? 1 : 2;
+  }
+}
+}  // namespace
+
+int selftest_wait_timeout(unsigned long long limit_ns, int* done, cudaStream_t stream) {
+  if (done == nullptr || limit_ns == 0 || limit_ns > kWaitLimitNs) return kErrInvalid;
+  wait_timeout_kernel<<<1, 32, 0, stream>>>(limit_ns, device_error_ptr(), done);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int make_tma_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes,

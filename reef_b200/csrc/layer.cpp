@@ -236,10 +236,13 @@ size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
 }
 
 // Chunks of whole sequences the all-gather plan pipelines over: 4 (or 2)
-// when the batch divides, else 1 (no pipelining).
+// when the batch divides, else 1 (no pipelining).  REEF_B200_TP_CHUNKS (1, 2
+// or 4) caps it.
 int ag_chunks(const reef_b200_llama_layer* L) {
+  int cap = 4;
+  if (const char* e = std::getenv("REEF_B200_TP_CHUNKS")) cap = std::max(1, std::min(4, std::atoi(e)));
   for (int c : {4, 2})
-    if (L->batch % static_cast<size_t>(c) == 0) return c;
+    if (c <= cap && L->batch % static_cast<size_t>(c) == 0) return c;
   return 1;
 }
 

@@ -89,7 +89,9 @@ struct GemmProblem {
 // ---- device plumbing (device.cu) ----------------------------------------------
 int num_sms();
 int* device_error_ptr();               // this device's error word
-int check_device();                    // kOk on sm_100, else kErrUnsupported
+int check_device();
+// Failure-detection self-test: a bounded wait that nothing satisfies (see device.cu).
+int selftest_wait_timeout(unsigned long long limit_ns, int* done, cudaStream_t stream);                    // kOk on sm_100, else kErrUnsupported
 int read_device_error(int* code);      // synchronizes, returns and clears
 int make_tma_2d_i8(CUtensorMap* map, const void* base, long long rows,
                    long long cols, long long ld_bytes, int box_cols, int box_rows);

@@ -1,0 +1,40 @@
+"""Failure detection on the GPU without a fault: a bounded mbarrier wait that
+nothing satisfies gives up after its limit, records its code in the device
+error word and returns; the context stays usable (a W8A8 linear right after
+is still bit-exact with the oracle).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as ro
+from reef_b200 import _lib
+from reef_b200 import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+
+def device_error() -> int:
+    code = C.c_int(0)
+    _lib.call("reef_b200_device_error", C.addressof(code))
+    return code.value
+
+
+def test_bounded_wait_times_out_and_context_survives():
+    assert device_error() == 0  # clean before
+    done = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.call("reef_b200_selftest_wait_timeout", 2000, done.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(done.item()) == 2          # the wait gave up
+    assert device_error() == 0x101        # kDevTimeoutFull, read and cleared
+    assert device_error() == 0
+    # the device still computes correctly
+    x = ro.normal(11, (64, 256))
+    w, ws = ro.quantize_rows(ro.normal(12, (96, 256), 0, 0.02))
+    y = K.linear_w8a8(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(),
+                      torch.from_numpy(ws).cuda())
+    want = ro.linear_w8a8(x, w, ws)
+    np.testing.assert_array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
