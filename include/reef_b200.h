@@ -316,8 +316,10 @@ int reef_b200_flash_attn_i8(size_t batch, size_t seq, size_t heads_q, size_t hea
  * q8 [batch][heads_q][128] + q_scale [batch][heads_q]; k_cache / v_cache
  * [batch][heads_kv][max_len][128] int8 (16-byte aligned) + k_scale / v_scale
  * [batch][heads_kv][max_len] fp32; lens [batch] int32 on the device (each in
- * [1, max_len]) or NULL for `len` keys in every sequence.  Split across CTAs
- * along the keys (flash-decoding); the partial results need
+ * [1, max_len]) or NULL for `len` keys in every sequence.  max_len must be
+ * a multiple of 4 and the caches and scales 16-byte aligned (they are read
+ * by bulk copies).  Split across CTAs along the keys (flash-decoding); the
+ * partial results need
  * reef_b200_decode_attn_workspace_bytes() of scratch.  out
  * [batch][heads_q][128] fp32.  Within 1e-2 of the float head. */
 size_t reef_b200_decode_attn_workspace_bytes(size_t batch, size_t heads_q, size_t max_len);

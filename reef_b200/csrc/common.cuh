@@ -121,6 +121,17 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Global -> shared bulk copy (not a tensor map, no multicast): `bytes` (a
+// multiple of 16; both addresses 16-byte aligned), completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Shared -> global tile store (bulk-group completion).  The tensor map
 // clips rows outside its extent.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0,

@@ -3,6 +3,7 @@
     python -m reef_b200.profile_cases gemm  [--m 16384 --n 12288 --k 4096]
     python -m reef_b200.profile_cases flash [--batch 8 --seq 2048 --heads 32]
     python -m reef_b200.profile_cases qkv   [--batch 8 --seq 2048 --heads 32]
+    python -m reef_b200.profile_cases decode [--batch 64 --heads 8 --kv-heads 1 --seq 4096]
 
 Each case allocates its seeded inputs once, launches the kernel twice (a
 warm-up launch, then the one to capture: ``ncu -k regex:<name> -s 1 -c 1``)
@@ -73,9 +74,31 @@ def qkv(batch: int, seq: int, heads: int, kv_heads: int, hidden: int = 4096) -> 
     torch.cuda.synchronize()
 
 
+def decode(batch: int, heads: int, kv_heads: int, cache_len: int) -> None:
+    """Decode attention over a full int8 KV cache (config 4's TP=8 shard by default)."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q8 = torch.randint(-127, 128, (batch, heads, 128), generator=g, device="cuda", dtype=torch.int8)
+    qs = torch.rand((batch, heads), generator=g, device="cuda") * 0.02
+    shp = (batch, kv_heads, cache_len)
+    k8 = torch.randint(-127, 128, shp + (128,), generator=g, device="cuda", dtype=torch.int8)
+    v8 = torch.randint(-127, 128, shp + (128,), generator=g, device="cuda", dtype=torch.int8)
+    ks = torch.rand(shp, generator=g, device="cuda") * 0.02
+    vs = torch.rand(shp, generator=g, device="cuda") * 0.02
+    out = torch.empty((batch, heads, 128), device="cuda")
+    n = _lib.lib().reef_b200_decode_attn_workspace_bytes(batch, heads, cache_len)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        _lib.call("reef_b200_decode_attn_i8", batch, heads, kv_heads, 128, cache_len, None,
+                  cache_len, 1.0 / math.sqrt(128), q8.data_ptr(), qs.data_ptr(), k8.data_ptr(),
+                  ks.data_ptr(), v8.data_ptr(), vs.data_ptr(), ws.data_ptr(), n, out.data_ptr(),
+                  st)
+    torch.cuda.synchronize()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "flash", "qkv"])
+    ap.add_argument("case", choices=["gemm", "flash", "qkv", "decode"])
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=4096)
@@ -88,6 +111,8 @@ def main() -> None:
         gemm(a.m, a.n, a.k)
     elif a.case == "qkv":
         qkv(a.batch, a.seq, a.heads, a.kv_heads)
+    elif a.case == "decode":
+        decode(a.batch, a.heads, a.kv_heads, a.seq)
     else:
         flash(a.batch, a.seq, a.heads, a.kv_heads)
     K.check_device_error()
