@@ -10,24 +10,30 @@
 //
 // HBM-bound by design, and built so that the per-byte instruction count is
 // small enough for the copies to set the pace:
-//   * a CTA streams its split of one (sequence, KV head) in 128-key tiles
-//     through a 3-stage ring: K and V by TMA (128-byte swizzle, so the
-//     tensor-core fragment loads below hit every bank once), their scales by
-//     bulk copies, all completing on one mbarrier per stage; thread 0
-//     refills a stage once the eight warps have released it (a second
-//     mbarrier per stage), so there is no CTA-wide barrier per tile;
-//   * warp w owns keys [16w, 16w + 16) of every tile and keeps its own
-//     online-softmax state: S = q . K^T for the G heads (padded to 16 rows)
-//     by int8 mma.sync m16n8k32 with q resident in registers; the scores,
-//     the running max and the exponentials stay in the accumulator
-//     registers, whose layout is the A operand of the P . V mma (f16
-//     m16n8k16), so P never goes through shared memory;
-//   * V reaches the P . V mma from the int8 tile with ldmatrix .trans on
-//     byte pairs: a thread receives two dims of two keys and splits them into
-//     two f16 pairs (exact, by byte permutes under the 0x64 exponent), so the
-//     warp's 16 n-tiles are the even and odd dims of each 16-dim chunk;
-//   * at the end the eight warps' (max, sum, O) merge through shared memory
-//     into the split's partial; a second kernel merges the splits.
+//   * work is cut into units of (sequence x KV head, 128-key tile) and
+//     spread evenly over one wave of CTAs; a CTA may end one sequence and
+//     start the next, writing one partial (max, sum, O) per sequence it
+//     touched;
+//   * a CTA streams its units through a 3-stage ring: K and V by TMA
+//     (128-byte swizzle, so the fragment loads below hit every bank once),
+//     their scales by bulk copies, completing on one mbarrier per stage;
+//     thread 0 refills a stage once the eight warps have released it (a
+//     second mbarrier per stage), so there is no CTA-wide barrier per tile;
+//   * warp w owns keys [16w, 16w + 16) of every tile with its own
+//     online-softmax state.  Both products run transposed so the heads are
+//     the n = 8 side of the mma and no row is padding: S^T = K . q^T by int8
+//     mma.sync m16n8k32 (q resident in registers), O^T = V^T . P^T by f16
+//     m16n8k16, P^T reaching the B operand through movmatrix;
+//   * V^T comes from the int8 tile by ldmatrix .trans on byte pairs: a
+//     thread receives dims (d, d + 1) of keys (k, k + 1) and permutes them
+//     into the f16 pairs {(d, k), (d, k + 1)} and {(d + 1, k), (d + 1, k + 1)}
+//     under the exponent byte 0x64, i.e. the exact values v + 1152; the
+//     offset is removed at the end with the column sums of P, which one more
+//     mma (A = ones) accumulates alongside;
+//   * the running max is raised only when a tile exceeds it by more than
+//     2^kLazy, so the accumulators are rarely rescaled (P stays below
+//     2^kLazy times the key's V scale).
+//   A second kernel merges the partials of each sequence.
 #include "common.cuh"
 #include "ops.h"
 
@@ -41,18 +47,23 @@ namespace {
 
 constexpr int kDThreads = 256;   // eight warps
 constexpr int kDWarps = kDThreads / 32;
-constexpr int kChunk = 256;      // sizing unit of the partial buffer (keys)
-constexpr int kTileKeys = 128;   // keys per tile
+constexpr int kTileKeys = 128;   // keys per unit of work
 constexpr int kWarpKeys = kTileKeys / kDWarps;  // 16 keys per warp per tile
 constexpr int kStages = 3;
 constexpr int kMaxGroup = 16;    // query heads per KV head
-constexpr int kORow = 132;       // floats per head row of the merge area
+constexpr int kPartRow = 132;    // floats per head of a partial: m, l, 2 unused, O[128]
+constexpr int kMaxCtasPerSm = 4; // bound used to size the partial buffer
+constexpr int kMaxRowsPerPair = 64;  // CTAs sharing one (sequence, KV head) at most
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLazy = 4.0f;    // log2 of the largest P / v_scale
+constexpr float kVBias = 1152.0f;
 static_assert(kWarpKeys == 16, "one m16n8k16 k-step of keys per warp");
 
 struct DecodeArgs {
-  int batch, heads_q, heads_kv, group, max_len, chunks;
-  int keys_per_split;
+  int batch, heads_q, heads_kv, max_len;
+  int tiles;         // units per (sequence, KV head): ceil(max_len / 128)
+  int ctas;          // CTAs launched
+  long long units;   // batch * heads_kv * tiles
   float sm_scale;
   const int8_t* q8;        // [B][Hq][128]
   const float* q_scale;    // [B][Hq]
@@ -60,39 +71,45 @@ struct DecodeArgs {
   const float* v_scale;
   const int* lens;         // [B] keys per sequence, or null
   int len;                 // keys per sequence when lens is null
-  float* part;             // [chunks][B][Hq][2 + 128]
+  float* part;             // [ctas + B*Hkv][G][kPartRow]: row c + pair
   float* out;              // [B][Hq][128]
   int* err;
 };
 
 struct DL {  // shared memory layout (bytes from a 1024-aligned base)
-  static constexpr int kStageK = 0;                         // int8 [128][128], SW128
-  static constexpr int kStageV = kTileKeys * 128;           // int8 [128][128], SW128
-  static constexpr int kStageKs = 2 * kTileKeys * 128;      // f32 [128]
-  static constexpr int kStageVs = kStageKs + kTileKeys * 4; // f32 [128]
-  static constexpr int kStage = 34 * 1024;                  // 33 KB used, 1024-aligned
-  static constexpr int kBars = kStages * kStage;            // full[kStages], empty[kStages]
+  static constexpr int kKV = 2 * kTileKeys * 128;            // K then V, int8 [128][128] SW128
+  static constexpr int kScales = kStages * kKV;              // per stage ks[128], vs[128]
+  static constexpr int kWarpM = kScales + kStages * 1024;    // m[8][16], then l[8][16]
+  static constexpr int kBars = kWarpM + 2 * kDWarps * kMaxGroup * 4;  // full[], empty[]
   static constexpr int kEnd = kBars + 2 * kStages * 8;
-  static constexpr int kBytes = kEnd + 1024;                // + alignment slack
-  // after the last tile: per warp m[16], l[16], O[16][kORow] (reuses the stages)
-  static constexpr int kMergeWarp = (32 + kMaxGroup * kORow) * 4;
+  // The merge of the eight warps' O ([8][G][128] fp32) reuses the K / V
+  // buffers of the stage just consumed when it fits there (G <= 8); G = 16
+  // has its own area after kEnd.
+  __host__ __device__ static constexpr int merge_bytes(int g) { return kDWarps * g * 128 * 4; }
+  __host__ __device__ static constexpr int bytes(int g) {
+    return (merge_bytes(g) <= kKV ? kEnd : kEnd + merge_bytes(g)) + 1024;  // + alignment slack
+  }
 };
-static_assert(DL::kStageVs + kTileKeys * 4 <= DL::kStage, "stage fits");
-static_assert(kDWarps * DL::kMergeWarp <= DL::kBars, "merge area fits in the stages");
-static_assert(DL::kBytes <= 232448 / 2 - 1024, "two CTAs per SM");
+static_assert(DL::merge_bytes(8) <= DL::kKV, "G <= 8 merges inside a stage");
+static_assert(DL::bytes(8) <= 232448 / 2 - 1024, "two CTAs per SM up to G = 8");
+static_assert(DL::bytes(16) <= 232448 - 1024, "one CTA per SM at G = 16");
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
 
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
 // D (16x8 s32) += A (16x32 s8, row) x B (32x8 s8, col)
@@ -115,20 +132,21 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// A word of an ldmatrix .trans over int8 pairs holds bytes (k0, d), (k0, d+1),
-// (k1, d), (k1, d+1) for keys k0 < k1 and dims d, d + 1.  Split it into the
-// f16 pairs {(k0, d), (k1, d)} and {(k0, d+1), (k1, d+1)}, exactly: byte b
-// becomes the f16 1024 + (b + 128) by placing b ^ 0x80 under the exponent
-// byte 0x64, and 1152 is subtracted.
-__device__ __forceinline__ void split_i8_pairs(uint32_t w, uint32_t& even, uint32_t& odd) {
+// A word of an ldmatrix .trans over int8 pairs: bytes (k, d), (k, d+1),
+// (k+1, d), (k+1, d+1).  Out: the f16 pairs {(k, d), (k+1, d)} and
+// {(k, d+1), (k+1, d+1)}, each value v + 1152 exactly (byte v ^ 0x80 = v +
+// 128 as the mantissa under the exponent byte 0x64, i.e. 1024 + v + 128).
+__device__ __forceinline__ void split_biased(uint32_t w, uint32_t& even, uint32_t& odd) {
   const uint32_t u = w ^ 0x80808080u;
-  const uint32_t e = __byte_perm(u, 0x64646464u, 0x4240);
-  const uint32_t o = __byte_perm(u, 0x64646464u, 0x4341);
-  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
-  const __half2 x = __hsub2(*reinterpret_cast<const __half2*>(&e), bias);
-  const __half2 y = __hsub2(*reinterpret_cast<const __half2*>(&o), bias);
-  even = *reinterpret_cast<const uint32_t*>(&x);
-  odd = *reinterpret_cast<const uint32_t*>(&y);
+  even = __byte_perm(u, 0x64646464u, 0x4240);
+  odd = __byte_perm(u, 0x64646464u, 0x4341);
+}
+
+// 2^x (ex2.approx.ftz: 2 ulp; -inf -> 0, results below 2^-126 flush to 0)
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // int32 -> fp32, exact for |v| < 2^22 (an int8 dot over 128 dims is at most
@@ -143,32 +161,35 @@ __device__ __forceinline__ uint32_t sw128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+__device__ __forceinline__ int seq_len(const DecodeArgs& a, int b) {
+  return a.lens != nullptr ? a.lens[b] : a.len;
+}
+
+// the CTA whose units include unit x
+__device__ __forceinline__ int cta_of(const DecodeArgs& a, long long x) {
+  return static_cast<int>(((x + 1) * a.ctas - 1) / a.units);
+}
+
+// G query heads per KV head; NT = n-tiles of 8 heads
 template <int G>
-__global__ void __launch_bounds__(kDThreads, 2)
+__global__ void __launch_bounds__(kDThreads, G > 8 ? 1 : 2)  // 16 heads: twice the accumulators
     decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, DecodeArgs a) {
+  constexpr int NT = (G + 7) / 8;
   extern __shared__ uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + DL::kBars);
   uint64_t* empty = full + kStages;
+  float* warp_m = reinterpret_cast<float*>(sm + DL::kWarpM);    // [8][16]
+  float* warp_l = warp_m + kDWarps * kMaxGroup;                 // [8][16]
 
-  const int split = blockIdx.x;
-  const int bk = blockIdx.y;  // b * Hkv + hkv
-  const int b = bk / a.heads_kv, hkv = bk % a.heads_kv;
-  const int len = a.lens != nullptr ? a.lens[b] : a.len;
-  const int k_begin = split * a.keys_per_split;
-  const int k_end = min(len, k_begin + a.keys_per_split);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tig = lane & 3;
-  const int h0 = hkv * G;  // first query head of this KV head
-  float* part = a.part + ((static_cast<long long>(split) * a.batch + b) * a.heads_q + h0) * 130;
-  if (k_end <= k_begin) {  // split past this sequence's end: an empty partial
-    for (int i = tid; i < G * 130; i += kDThreads) part[i] = (i % 130 == 0) ? -INFINITY : 0.0f;
-    return;
-  }
-  const int ntiles = (k_end - k_begin + kTileKeys - 1) / kTileKeys;
-  const long long srow0 = static_cast<long long>(bk) * a.max_len + k_begin;  // scale index
+  const int cta = blockIdx.x;
+  const long long u0 = static_cast<long long>(cta) * a.units / a.ctas;
+  const long long u1 = static_cast<long long>(cta + 1) * a.units / a.ctas;
+  const int nunits = static_cast<int>(u1 - u0);
 
   if (tid == 0) {
     prefetch_tensormap(&kmap);
@@ -179,287 +200,345 @@ __global__ void __launch_bounds__(kDThreads, 2)
     }
     fence_barrier_init();
   }
+  // the combine kernel may be scheduled now; it waits for this grid's
+  // completion (and its memory) before reading the partials
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
 
-  // tile t into stage t % kStages (thread 0).  The TMA boxes are always
+  // unit j of this CTA into stage j % kStages (thread 0).  The TMA boxes are
   // whole (rows past max_len arrive as zeros); the scales cover the tile's
   // keys inside the sequence, rounded up to whole 16-byte groups (max_len is
-  // a multiple of 4, so the groups stay inside the row of scales).
-  auto issue = [&](int t) {
-    const int s = t % kStages;
-    uint8_t* st = sm + s * DL::kStage;
-    const int key0 = t * kTileKeys;
-    const int n = min(kTileKeys, k_end - k_begin - key0);
-    const int n4 = (n + 3) & ~3;
-    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(2 * kTileKeys * 128 + 2 * n4 * 4));
-    tma_load_3d(st + DL::kStageK, &kmap, &full[s], 0, k_begin + key0, bk);
-    tma_load_3d(st + DL::kStageV, &vmap, &full[s], 0, k_begin + key0, bk);
-    bulk_load(st + DL::kStageKs, a.k_scale + srow0 + key0, n4 * 4, &full[s]);
-    bulk_load(st + DL::kStageVs, a.v_scale + srow0 + key0, n4 * 4, &full[s]);
-  };
-  int issued = 0;  // tiles issued (thread 0)
-  if (tid == 0)
-    for (; issued < kStages && issued < ntiles; ++issued) issue(issued);
-
-  // q as the A operand of the score mma: rows g and g + 8 (heads; rows at or
-  // past G are zero), k-step s covering dims [32 s, 32 s + 32)
-  uint32_t qa[4][4];
-  {
-    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(
-        a.q8 + (static_cast<long long>(b) * a.heads_q + h0) * 128);
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      qa[s][0] = g < G ? q32[g * 32 + 8 * s + tig] : 0u;
-      qa[s][1] = g + 8 < G ? q32[(g + 8) * 32 + 8 * s + tig] : 0u;
-      qa[s][2] = g < G ? q32[g * 32 + 8 * s + 4 + tig] : 0u;
-      qa[s][3] = g + 8 < G ? q32[(g + 8) * 32 + 8 * s + 4 + tig] : 0u;
+  // a multiple of 4, so they stay inside the sequence's row of scales).  A
+  // tile wholly past the sequence's end loads nothing.
+  const int pair0 = static_cast<int>(u0 / a.tiles), tile0 = static_cast<int>(u0 % a.tiles);
+  int ipair = pair0, itile = tile0;  // next unit to issue (thread 0)
+  auto issue = [&](int j) {
+    const int s = j % kStages;
+    const int pair = ipair;
+    const int key0 = itile * kTileKeys;
+    if (++itile == a.tiles) {
+      itile = 0;
+      ++ipair;
     }
-  }
+    const int n = min(kTileKeys, seq_len(a, pair / a.heads_kv) - key0);
+    if (n <= 0) {
+      mbar_arrive(&full[s]);
+      return;
+    }
+    const int n4 = (n + 3) & ~3;
+    const long long srow = static_cast<long long>(pair) * a.max_len + key0;
+    uint8_t* kv = sm + s * DL::kKV;
+    float* sc = reinterpret_cast<float*>(sm + DL::kScales + s * 1024);
+    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(2 * kTileKeys * 128 + 2 * n4 * 4));
+    tma_load_3d(kv, &kmap, &full[s], 0, key0, pair);
+    tma_load_3d(kv + kTileKeys * 128, &vmap, &full[s], 0, key0, pair);
+    bulk_load(sc, a.k_scale + srow, n4 * 4, &full[s]);
+    bulk_load(sc + kTileKeys, a.v_scale + srow, n4 * 4, &full[s]);
+  };
+  int issued = 0;  // units issued (thread 0)
+  if (tid == 0)
+    for (; issued < kStages && issued < nunits; ++issued) issue(issued);
+
   const float base = a.sm_scale * kLog2e;
-  const float qs_lo = g < G ? a.q_scale[static_cast<long long>(b) * a.heads_q + h0 + g] * base : 0.0f;
-  const float qs_hi =
-      g + 8 < G ? a.q_scale[static_cast<long long>(b) * a.heads_q + h0 + g + 8] * base : 0.0f;
-
-  // O for rows g (e 0, 1) and g + 8 (e 2, 3): n-tile 4c + 2p + q covers the
-  // dims of 16-dim chunk 2c + p with parity q
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[i][e] = 0.0f;
-  float m_lo = -INFINITY, m_hi = -INFINITY;  // running max (log2 units) of rows g, g + 8
-  float l_lo = 0.0f, l_hi = 0.0f;            // this thread's share of the running sums
-  bool ok = true;
-  int waited = 0;  // tiles whose stage thread 0 saw complete
-
   const int wk = warp * kWarpKeys;  // this warp's first key in a tile
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % kStages;
-    uint8_t* st = sm + s * DL::kStage;
-    if (ok) ok = mbar_wait(&full[s], (t / kStages) & 1, a.err, kDevTimeoutFull);
-    if (ok && tid == 0) waited = t + 1;
-    const int n = min(kTileKeys, k_end - k_begin - t * kTileKeys);  // keys of the tile
+  // fragment rows of this lane in the ldmatrix loads (keys wk + [0, 16))
+  const int frow = wk + ((lane >> 3) & 1) * 8 + (lane & 7);
+  const uint32_t ones = 0x3C003C00u;  // f16 pair (1, 1)
+  const uint32_t ones_a[4] = {ones, ones, ones, ones};
+
+  // per-sequence state: q as the B operand of S^T (dims x heads, k-step s =
+  // dims [32 s, 32 s + 32)); the score scale of heads nt*8 + 2 tig + {0, 1};
+  // O^T accumulators o[c][nt] for 16-dim chunk c (rows g: dim 16c + 2g,
+  // rows g + 8: dim 16c + 2g + 1; columns: heads nt*8 + 2 tig + {0, 1}); the
+  // column sums of P (os); the running max and this thread's share of the
+  // sums per head column
+  uint32_t qb[4][NT][2];
+  float qsc[NT][2];
+  float o[8][NT][4];
+  float os[NT][4];
+  float m[NT][2], l[NT][2];
+  int pair = pair0, tile = tile0, len = 0;  // the unit being consumed
+  bool ok = true;
+  int waited = 0;  // units whose stage thread 0 saw complete
+
+  for (int j = 0; j < nunits; ++j) {
+    const int s = j % kStages;
+    if (j == 0 || tile == 0) {  // a new (sequence, KV head): load q, reset the state
+      const int b = pair / a.heads_kv, hkv = pair % a.heads_kv;
+      len = seq_len(a, b);
+      const long long qrow = static_cast<long long>(b) * a.heads_q + hkv * G;
+      const uint32_t* q32 = reinterpret_cast<const uint32_t*>(a.q8 + qrow * 128);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int h = nt * 8 + g;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          qb[ks][nt][0] = h < G ? q32[h * 32 + 8 * ks + tig] : 0u;
+          qb[ks][nt][1] = h < G ? q32[h * 32 + 8 * ks + 4 + tig] : 0u;
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int hc = nt * 8 + 2 * tig + e;
+          qsc[nt][e] = hc < G ? a.q_scale[qrow + hc] * base : 0.0f;
+          m[nt][e] = -INFINITY;
+          l[nt][e] = 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) os[nt][e] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[c][nt][e] = 0.0f;
+      }
+    }
+    if (ok) ok = mbar_wait(&full[s], (j / kStages) & 1, a.err, kDevTimeoutFull);
+    if (ok && tid == 0) waited = j + 1;
+    const int n = min(kTileKeys, len - tile * kTileKeys);  // keys of the tile
     if (ok && wk < n) {
-      // ---- S = q . K^T over this warp's 16 keys: n-tile j = keys wk + 8 j + [0, 8)
-      int c[2][4];
+      const uint8_t* kv = sm + s * DL::kKV;
+      const float* ksc = reinterpret_cast<const float*>(sm + DL::kScales + s * 1024);
+      // ---- S^T = K . q^T: rows keys wk + g (c 0, 1), wk + g + 8 (c 2, 3)
+      int c[NT][4], c2[NT][4];  // k-steps 0, 2 and 1, 3: two independent mma chains
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) c[j][e] = 0;
+        for (int e = 0; e < 4; ++e) c[nt][e] = c2[nt][e] = 0;
+      const uint32_t kb = smem_u32(kv);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t ka[4];
+        ldsm_x4(kb + sw128(frow, 2 * ks + (lane >> 4)), ka);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          mma_s8_16832((ks & 1) ? c2[nt] : c[nt], ka, qb[ks][nt][0], qb[ks][nt][1]);
       }
-      const uint32_t kb = smem_u32(st + DL::kStageK);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int row = wk + 8 * j + (lane & 7);
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {  // dims [64 hh, 64 hh + 64): chunks 4 hh + (lane >> 3)
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(kb + sw128(row, 4 * hh + (lane >> 3)), b0, b1, b2, b3);
-          mma_s8_16832(c[j], qa[2 * hh], b0, b1);
-          mma_s8_16832(c[j], qa[2 * hh + 1], b2, b3);
-        }
+        for (int e = 0; e < 4; ++e) c[nt][e] += c2[nt][e];
+      // ---- scores in log2 units; keys past the tile's end masked
+      const bool val_lo = wk + g < n, val_hi = wk + g + 8 < n;
+      const float ks_lo = ksc[wk + g], ks_hi = ksc[wk + g + 8];
+      const float vs_lo = val_lo ? ksc[kTileKeys + wk + g] : 0.0f;
+      const float vs_hi = val_hi ? ksc[kTileKeys + wk + g + 8] : 0.0f;
+      float sc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        sc[nt][0] = val_lo ? small_i2f(c[nt][0]) * qsc[nt][0] * ks_lo : -INFINITY;
+        sc[nt][1] = val_lo ? small_i2f(c[nt][1]) * qsc[nt][1] * ks_lo : -INFINITY;
+        sc[nt][2] = val_hi ? small_i2f(c[nt][2]) * qsc[nt][0] * ks_hi : -INFINITY;
+        sc[nt][3] = val_hi ? small_i2f(c[nt][3]) * qsc[nt][1] * ks_hi : -INFINITY;
       }
-      // ---- scores (log2 units), masked past the tile's keys
-      const float2* ks2 = reinterpret_cast<const float2*>(st + DL::kStageKs);
-      const float2* vs2 = reinterpret_cast<const float2*>(st + DL::kStageVs);
-      float sc[2][4];
-      float2 vsc[2];
+      // ---- the running max per head column stays while no score passes it
+      // by more than 2^kLazy (one vote); otherwise the tile's max over the
+      // warp's 16 keys (the eight lanes of one tig) replaces it where it
+      // passed, and the accumulators are rescaled
+      bool need = false;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int k0 = wk + 8 * j + 2 * tig;  // keys k0, k0 + 1
-        const float2 ks = ks2[k0 >> 1];
-        vsc[j] = vs2[k0 >> 1];
-        const bool v0 = k0 < n, v1 = k0 + 1 < n;
-        sc[j][0] = v0 ? small_i2f(c[j][0]) * qs_lo * ks.x : -INFINITY;
-        sc[j][1] = v1 ? small_i2f(c[j][1]) * qs_lo * ks.y : -INFINITY;
-        sc[j][2] = v0 ? small_i2f(c[j][2]) * qs_hi * ks.x : -INFINITY;
-        sc[j][3] = v1 ? small_i2f(c[j][3]) * qs_hi * ks.y : -INFINITY;
-        if (!v0) vsc[j].x = 0.0f;
-        if (!v1) vsc[j].y = 0.0f;
-      }
-      // ---- online softmax per row over the warp's keys (the four lanes of a
-      // row hold its 16 keys)
-      float t_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-      float t_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-      t_lo = fmaxf(t_lo, __shfl_xor_sync(0xffffffffu, t_lo, 1));
-      t_lo = fmaxf(t_lo, __shfl_xor_sync(0xffffffffu, t_lo, 2));
-      if (G > 8) {
-        t_hi = fmaxf(t_hi, __shfl_xor_sync(0xffffffffu, t_hi, 1));
-        t_hi = fmaxf(t_hi, __shfl_xor_sync(0xffffffffu, t_hi, 2));
-      }
-      const float mn_lo = fmaxf(m_lo, t_lo), mn_hi = fmaxf(m_hi, t_hi);
-      // reference points: a row with no visible key yet keeps 0 (its p are 0)
-      const float r_lo = mn_lo == -INFINITY ? 0.0f : mn_lo;
-      const float r_hi = mn_hi == -INFINITY ? 0.0f : mn_hi;
-      if (__any_sync(0xffffffffu, mn_lo != m_lo || (G > 8 && mn_hi != m_hi))) {
-        const float al_lo = exp2f(m_lo - r_lo);  // 0 while the row was empty
-        const float al_hi = G > 8 ? exp2f(m_hi - r_hi) : 1.0f;
-        l_lo *= al_lo;
-        l_hi *= al_hi;
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          o[i][0] *= al_lo;
-          o[i][1] *= al_lo;
-          if (G > 8) {
-            o[i][2] *= al_hi;
-            o[i][3] *= al_hi;
+        for (int e = 0; e < 2; ++e) need |= fmaxf(sc[nt][e], sc[nt][e + 2]) > m[nt][e] + kLazy;
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float x = fmaxf(sc[nt][e], sc[nt][e + 2]);
+            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
+            x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 16));
+            const bool up = x > m[nt][e] + kLazy;
+            const float al = up ? fast_exp2(m[nt][e] - x) : 1.0f;  // 0 from -inf
+            if (up) m[nt][e] = x;
+            l[nt][e] *= al;
+            os[nt][e] *= al;
+            os[nt][e + 2] *= al;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+              o[cc][nt][e] *= al;
+              o[cc][nt][e + 2] *= al;
+            }
           }
-        }
-        m_lo = mn_lo;
-        m_hi = mn_hi;
       }
-      // P = 2^(s - max) (summed unscaled), times the key's V scale, as the
-      // f16 A operand of P . V: a0 / a1 keys wk + 2 tig (+1) rows g / g + 8,
-      // a2 / a3 the same 8 keys on
-      uint32_t pa[4];
+      // ---- P = 2^(s - m) (summed unscaled), times the key's V scale, as
+      // f16 pairs (key; heads 2 tig, 2 tig + 1), transposed into the B
+      // operand (keys 2 tig, 2 tig + 1; head g)
+      uint32_t pb[NT][2];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float p0 = exp2f(sc[j][0] - r_lo), p1 = exp2f(sc[j][1] - r_lo);
-        l_lo += p0 + p1;
-        const __half2 lo = __floats2half2_rn(p0 * vsc[j].x, p1 * vsc[j].y);
-        pa[2 * j] = *reinterpret_cast<const uint32_t*>(&lo);
-        if (G > 8) {
-          const float p2 = exp2f(sc[j][2] - r_hi), p3 = exp2f(sc[j][3] - r_hi);
-          l_hi += p2 + p3;
-          const __half2 hi = __floats2half2_rn(p2 * vsc[j].x, p3 * vsc[j].y);
-          pa[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&hi);
-        } else {
-          pa[2 * j + 1] = 0u;
-        }
+      for (int nt = 0; nt < NT; ++nt) {
+        const float r0 = m[nt][0] == -INFINITY ? 0.0f : m[nt][0];
+        const float r1 = m[nt][1] == -INFINITY ? 0.0f : m[nt][1];
+        const float p0 = fast_exp2(sc[nt][0] - r0), p1 = fast_exp2(sc[nt][1] - r1);
+        const float p2 = fast_exp2(sc[nt][2] - r0), p3 = fast_exp2(sc[nt][3] - r1);
+        l[nt][0] += p0 + p2;
+        l[nt][1] += p1 + p3;
+        const __half2 x0 = __floats2half2_rn(p0 * vs_lo, p1 * vs_lo);
+        const __half2 x1 = __floats2half2_rn(p2 * vs_hi, p3 * vs_hi);
+        pb[nt][0] = movmatrix_t(*reinterpret_cast<const uint32_t*>(&x0));
+        pb[nt][1] = movmatrix_t(*reinterpret_cast<const uint32_t*>(&x1));
       }
-      // ---- O += P . V over the warp's 16 keys: ldmatrix .trans of int8
-      // pairs; matrices (keys wk + [0, 8), chunk 2c), (keys wk + [8, 16),
-      // chunk 2c), then chunk 2c + 1
-      const uint32_t vb = smem_u32(st + DL::kStageV);
-      const int vrow = wk + ((lane >> 3) & 1) * 8 + (lane & 7);
+      // ---- O^T += (V + 1152)^T . P^T; ldmatrix .trans matrices (keys
+      // wk + [0, 8), chunk 2cc), (keys wk + [8, 16), chunk 2cc), then 2cc + 1
+      const uint32_t vb = smem_u32(kv + kTileKeys * 128);
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4_t(vb + sw128(vrow, 2 * cc + (lane >> 4)), r0, r1, r2, r3);
-        uint32_t e0, d0, e1, d1, e2, d2, e3, d3;
-        split_i8_pairs(r0, e0, d0);
-        split_i8_pairs(r1, e1, d1);
-        split_i8_pairs(r2, e2, d2);
-        split_i8_pairs(r3, e3, d3);
-        mma_f16_16816(o[4 * cc + 0], pa, e0, e1);
-        mma_f16_16816(o[4 * cc + 1], pa, d0, d1);
-        mma_f16_16816(o[4 * cc + 2], pa, e2, e3);
-        mma_f16_16816(o[4 * cc + 3], pa, d2, d3);
+        uint32_t r[4];
+        ldsm_x4_t(vb + sw128(frow, 2 * cc + (lane >> 4)), r);
+        uint32_t va[4], vc[4];
+        split_biased(r[0], va[0], va[1]);
+        split_biased(r[1], va[2], va[3]);
+        split_biased(r[2], vc[0], vc[1]);
+        split_biased(r[3], vc[2], vc[3]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_f16_16816(o[2 * cc][nt], va, pb[nt][0], pb[nt][1]);
+          mma_f16_16816(o[2 * cc + 1][nt], vc, pb[nt][0], pb[nt][1]);
+        }
       }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma_f16_16816(os[nt], ones_a, pb[nt][0], pb[nt][1]);
     }
-    // ---- release the stage; thread 0 refills it once every warp has
+    // ---- release the stage; thread 0 refills it once every warp has (after
+    // the merge below when this unit ends a sequence: the merge uses it)
+    const bool last = j + 1 == nunits || tile + 1 == a.tiles;
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (tid == 0 && ok && t + kStages < ntiles) {
-      ok = mbar_wait(&empty[s], (t / kStages) & 1, a.err, kDevTimeoutEmpty);
+    if (tid == 0 && ok && !last && j + kStages < nunits) {
+      ok = mbar_wait(&empty[s], (j / kStages) & 1, a.err, kDevTimeoutEmpty);
       if (ok) issue(issued++);
     }
-  }
-  // copies still in flight land before the stages are reused (only after a
-  // timeout can any remain)
-  if (tid == 0 && !ok) {
-    for (int t = waited; t < issued; ++t)
-      mbar_wait(&full[t % kStages], (t / kStages) & 1, a.err, kDevTimeoutDrain);
-  }
-  __syncthreads();  // every warp is done with the stages
 
-  // ---- merge the eight warps' states: per warp m[16], l[16], O[16][kORow]
-  float* mw = reinterpret_cast<float*>(sm + warp * DL::kMergeWarp);
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
-  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
-  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-  if (tig == 0) {
-    if (g < G) {
-      mw[g] = m_lo;
-      mw[16 + g] = l_lo;
+    // ---- end of this (sequence, KV head) in this CTA: merge the eight
+    // warps into the partial row cta + pair.  Each warp weighs its state by
+    // 2^(m_w - max) and writes it to its own slot; the slots are then summed
+    // in warp order (a fixed order for every dim).
+    if (last) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float x = l[nt][e];
+          x += __shfl_xor_sync(0xffffffffu, x, 4);
+          x += __shfl_xor_sync(0xffffffffu, x, 8);
+          x += __shfl_xor_sync(0xffffffffu, x, 16);
+          l[nt][e] = x;
+          const int h = nt * 8 + 2 * tig + e;
+          if (g == 0 && h < G) warp_m[warp * kMaxGroup + h] = m[nt][e];
+        }
+      __syncthreads();  // every warp's m is in, and every warp is done with stage s
+      float* mrg = reinterpret_cast<float*>(DL::merge_bytes(G) <= DL::kKV ? sm + s * DL::kKV
+                                                                        : sm + DL::kEnd);
+      float* mine = mrg + warp * G * 128;  // [G][128]
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int h = nt * 8 + 2 * tig + e;
+          if (h >= G) continue;
+          float mx = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < kDWarps; ++w) mx = fmaxf(mx, warp_m[w * kMaxGroup + h]);
+          const float ws = m[nt][e] == -INFINITY ? 0.0f : exp2f(m[nt][e] - mx);
+          if (g == 0) warp_l[warp * kMaxGroup + h] = l[nt][e] * ws;
+          const float bias = kVBias * os[nt][e];
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc)
+            *reinterpret_cast<float2*>(mine + h * 128 + 16 * cc + 2 * g) =
+                make_float2((o[cc][nt][e] - bias) * ws, (o[cc][nt][e + 2] - bias) * ws);
+        }
+      __syncthreads();
+      float* prow = a.part + (static_cast<long long>(cta) + pair) * G * kPartRow;
+      for (int i = tid; i < G * 128; i += kDThreads) {
+        const int h = i >> 7, d = i & 127;
+        float acc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kDWarps; ++w) acc += mrg[w * G * 128 + i];
+        prow[h * kPartRow + 4 + d] = acc;
+      }
+      if (tid < G) {
+        float mx = -INFINITY, ls = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kDWarps; ++w) {
+          mx = fmaxf(mx, warp_m[w * kMaxGroup + tid]);
+          ls += warp_l[w * kMaxGroup + tid];
+        }
+        prow[tid * kPartRow] = mx;
+        prow[tid * kPartRow + 1] = ls;
+      }
+      __syncthreads();  // the merge area and warp_m / warp_l are free again
+      if (tid == 0 && ok && j + kStages < nunits) {  // the refill held back above
+        fence_proxy_async_smem();  // the merge's stores before the copy's writes
+        ok = mbar_wait(&empty[s], (j / kStages) & 1, a.err, kDevTimeoutEmpty);
+        if (ok) issue(issued++);
+      }
     }
-    if (g + 8 < G) {
-      mw[8 + g] = m_hi;
-      mw[24 + g] = l_hi;
+    if (++tile == a.tiles) {
+      tile = 0;
+      ++pair;
     }
   }
-#pragma unroll
-  for (int cc = 0; cc < 4; ++cc) {
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {  // chunk 2 cc + p: dims 32 cc + 16 p + 4 tig + [0, 4)
-      const int d = 32 * cc + 16 * p + 4 * tig;
-      const float* ev = o[4 * cc + 2 * p];
-      const float* od = o[4 * cc + 2 * p + 1];
-      if (g < G)
-        *reinterpret_cast<float4*>(mw + 32 + g * kORow + d) = make_float4(ev[0], od[0], ev[1], od[1]);
-      if (g + 8 < G)
-        *reinterpret_cast<float4*>(mw + 32 + (g + 8) * kORow + d) =
-            make_float4(ev[2], od[2], ev[3], od[3]);
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < G * 128; i += kDThreads) {
-    const int h = i >> 7, d = i & 127;
-    float m = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kDWarps; ++w)
-      m = fmaxf(m, reinterpret_cast<const float*>(sm + w * DL::kMergeWarp)[h]);
-    float l = 0.0f, acc = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kDWarps; ++w) {
-      const float* ww = reinterpret_cast<const float*>(sm + w * DL::kMergeWarp);
-      const float mw_h = ww[h];
-      if (mw_h == -INFINITY) continue;  // the warp saw no key of this split
-      const float sc = exp2f(mw_h - m);
-      l += sc * ww[16 + h];
-      acc += sc * ww[32 + h * kORow + d];
-    }
-    part[h * 130 + 2 + d] = acc;
-    if (d == 0) {
-      part[h * 130] = m;
-      part[h * 130 + 1] = l;
-    }
+  // copies still in flight land before exit (only after a timeout can any
+  // remain)
+  if (tid == 0 && !ok) {
+    for (int j = waited; j < issued; ++j)
+      mbar_wait(&full[j % kStages], (j / kStages) & 1, a.err, kDevTimeoutDrain);
   }
 }
 
-// Merge the splits of one (sequence, query head): weights 2^(m_c - max) per
-// split, computed once per block of 128 splits in shared memory.
-__global__ void __launch_bounds__(128) decode_combine_kernel(DecodeArgs a) {
-  __shared__ float wsm[128];
-  __shared__ float red[4];
+
+// Merge the partials of one (sequence, query head): rows cta + pair for the
+// CTAs that worked on the pair.  Warp w takes rows w, w + 8, ... (a lane
+// holds 4 dims); the eight warp sums are added in a fixed order.
+template <int G>
+__global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a) {
+  __shared__ float4 osm[kDWarps][32];
+  __shared__ float lsm[kDWarps], red[kDWarps];
   const int bh = blockIdx.x;  // b * Hq + h
-  const int d = threadIdx.x;  // 128
-  const long long stride = static_cast<long long>(a.batch) * a.heads_q * 130;
-  const float* pb = a.part + static_cast<long long>(bh) * 130;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = bh / a.heads_q, h = bh % a.heads_q;
+  const int pair = b * a.heads_kv + h / G, hg = h % G;
+  const int c0 = cta_of(a, static_cast<long long>(pair) * a.tiles);
+  const int nc = cta_of(a, static_cast<long long>(pair + 1) * a.tiles - 1) - c0 + 1;
+  const long long stride = static_cast<long long>(G) * kPartRow;  // one row
+  const float* pb = a.part + (static_cast<long long>(c0) + pair) * stride + hg * kPartRow;
+  // launched early (programmatic dependent launch): wait for the main
+  // kernel's completion and memory before reading its partials
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   float m = -INFINITY;
-  for (int c = d; c < a.chunks; c += 128) m = fmaxf(m, pb[c * stride]);
+  for (int c = tid; c < nc; c += kDThreads) m = fmaxf(m, pb[c * stride]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if ((d & 31) == 0) red[d >> 5] = m;
+  if (lane == 0) red[warp] = m;
   __syncthreads();
-  m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  float lp = 0.0f, o = 0.0f;
-  for (int c0 = 0; c0 < a.chunks; c0 += 128) {
-    __syncthreads();
-    const int c = c0 + d;
-    float w = 0.0f;
-    if (c < a.chunks) {
-      const float mc = pb[c * stride];
-      if (mc != -INFINITY) {
-        w = exp2f(mc - m);
-        lp += w * pb[c * stride + 1];
-      }
-    }
-    wsm[d] = w;
-    __syncthreads();
-    const int nc = min(128, a.chunks - c0);
-    const float* pc = pb + c0 * stride + 2 + d;
-#pragma unroll 4
-    for (int i = 0; i < nc; ++i) o += wsm[i] * pc[i * stride];
-  }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) lp += __shfl_xor_sync(0xffffffffu, lp, off);
+  for (int w = 0; w < kDWarps; ++w) m = fmaxf(m, red[w]);
+  float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float l = 0.0f;
+#pragma unroll 2
+  for (int c = warp; c < nc; c += kDWarps) {
+    const float* pr = pb + c * stride;
+    const float mc = pr[0];
+    if (mc == -INFINITY) continue;  // a CTA whose tiles all lay past the sequence's end
+    const float w = exp2f(mc - m);
+    l += w * pr[1];
+    const float4 v = reinterpret_cast<const float4*>(pr + 4)[lane];
+    o.x += w * v.x;
+    o.y += w * v.y;
+    o.z += w * v.z;
+    o.w += w * v.w;
+  }
+  osm[warp][lane] = o;
+  if (lane == 0) lsm[warp] = l;
   __syncthreads();
-  if ((d & 31) == 0) red[d >> 5] = lp;
-  __syncthreads();
-  const float l = (red[0] + red[1]) + (red[2] + red[3]);
-  a.out[static_cast<long long>(bh) * 128 + d] = o / l;
+  if (tid < 128) {
+    float acc = 0.0f, ls = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kDWarps; ++w) {
+      acc += reinterpret_cast<const float*>(&osm[w][0])[tid];
+      ls += lsm[w];
+    }
+    a.out[static_cast<long long>(bh) * 128 + tid] = acc / ls;
+  }
 }
 
 // CTAs of decode_mma_kernel<G> resident per SM (0 on an error); the shared
@@ -472,20 +551,38 @@ int tile_ctas_per_sm() {
   if (per_sm[dev] == 0) {
     int n = 0;
     if (cudaFuncSetAttribute(decode_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             DL::kBytes) != cudaSuccess ||
+                             DL::bytes(G)) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<G>, kDThreads,
-                                                      DL::kBytes) != cudaSuccess)
+                                                      DL::bytes(G)) != cudaSuccess)
       return 0;
-    per_sm[dev] = n;
+    per_sm[dev] = std::min(n, kMaxCtasPerSm);
   }
   return per_sm[dev];
 }
 
 template <int G>
-int launch_tiles(const CUtensorMap& km, const CUtensorMap& vm, const DecodeArgs& a, int splits,
-                 cudaStream_t st) {
-  dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(a.batch * a.heads_kv));
-  decode_mma_kernel<G><<<grid, kDThreads, DL::kBytes, st>>>(km, vm, a);
+int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodeArgs& a, cudaStream_t st) {
+  const int per_sm = tile_ctas_per_sm<G>();
+  if (per_sm <= 0) return kErrCuda;
+  // one wave, and at most kMaxRowsPerPair CTAs on any (sequence, KV head)
+  const long long pairs = static_cast<long long>(a.batch) * a.heads_kv;
+  a.ctas = static_cast<int>(std::min({static_cast<long long>(per_sm) * num_sms(), a.units,
+                                      pairs * (kMaxRowsPerPair - 1)}));
+  decode_mma_kernel<G><<<static_cast<unsigned>(a.ctas), kDThreads, DL::bytes(G), st>>>(km, vm, a);
+  if (cudaGetLastError() != cudaSuccess) return kErrCuda;
+  // the combine launches as a programmatic dependent of the main kernel, so
+  // its launch overlaps the main kernel's tail
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.batch * a.heads_q));
+  cfg.blockDim = dim3(kDThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, decode_combine_kernel<G>, a) != cudaSuccess) return kErrCuda;
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -563,28 +660,32 @@ int decode_rope_append(int batch, int heads_q, int heads_kv, int max_len, float 
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
+
+// the partial rows cta + pair of G heads each: at most (ctas + pairs) * G
+// <= (ctas + batch) * heads_q head rows
 size_t decode_attn_partial_floats(int batch, int heads_q, int max_len) {
-  const int chunks = (max_len + kChunk - 1) / kChunk;
-  return static_cast<size_t>(chunks) * batch * heads_q * 130;
+  (void)max_len;
+  return static_cast<size_t>(kMaxCtasPerSm * num_sms() + batch) * heads_q * kPartRow;
 }
 
 int decode_attn_i8(const DecodeProblem& p, cudaStream_t st) {
   if (p.batch <= 0 || p.heads_q <= 0 || p.heads_kv <= 0 || p.max_len <= 0) return kErrInvalid;
   if (p.heads_q % p.heads_kv != 0) return kErrInvalid;
-  // the bulk copies read cache rows and scale groups of 16 bytes
+  // the bulk copies read scale groups of 16 bytes; TMA wants 16-byte bases
   if (p.max_len % 4 != 0 ||
       ((reinterpret_cast<uintptr_t>(p.k_cache) | reinterpret_cast<uintptr_t>(p.v_cache) |
         reinterpret_cast<uintptr_t>(p.k_scale) | reinterpret_cast<uintptr_t>(p.v_scale)) & 15u) != 0)
     return kErrAlignment;
   const int G = p.heads_q / p.heads_kv;
   if (G > kMaxGroup) return kErrInvalid;
+  const int pairs = p.batch * p.heads_kv;
   DecodeArgs a{};
   a.batch = p.batch;
   a.heads_q = p.heads_q;
   a.heads_kv = p.heads_kv;
-  a.group = G;
   a.max_len = p.max_len;
-  a.chunks = (p.max_len + kChunk - 1) / kChunk;
+  a.tiles = (p.max_len + kTileKeys - 1) / kTileKeys;
+  a.units = static_cast<long long>(pairs) * a.tiles;
   a.sm_scale = p.sm_scale;
   a.q8 = p.q8;
   a.q_scale = p.q_scale;
@@ -595,21 +696,6 @@ int decode_attn_i8(const DecodeProblem& p, cudaStream_t st) {
   a.part = p.partial;
   a.out = p.out;
   a.err = device_error_ptr();
-  // Splits along the keys: at most one wave of CTAs (every CTA resident at
-  // once, so none waits for a second wave), each split a whole number of
-  // tiles; never more splits than the partial buffer holds (one per 256
-  // keys).
-  int per_sm = 0;
-  switch (G) {
-    case 1: per_sm = tile_ctas_per_sm<1>(); break;
-    case 2: per_sm = tile_ctas_per_sm<2>(); break;
-    case 4: per_sm = tile_ctas_per_sm<4>(); break;
-    case 8: per_sm = tile_ctas_per_sm<8>(); break;
-    case 16: per_sm = tile_ctas_per_sm<16>(); break;
-    default: return kErrInvalid;
-  }
-  if (per_sm <= 0) return kErrCuda;
-  const int pairs = p.batch * p.heads_kv;
   // K and V as [pairs][max_len][128] int8, 128-key boxes with the 128-byte
   // swizzle (rows past max_len read as zeros)
   CUtensorMap km, vm;
@@ -618,25 +704,14 @@ int decode_attn_i8(const DecodeProblem& p, cudaStream_t st) {
     return rc;
   if (int rc = make_tma_3d_i8(&vm, p.v_cache, p.max_len, 128, 128, pairs, seg, 128, kTileKeys))
     return rc;
-  const int tiles = (p.max_len + kTileKeys - 1) / kTileKeys;
-  int splits = std::max(1, per_sm * num_sms() / pairs);
-  splits = std::min({splits, tiles, a.chunks});
-  const int tiles_per = (tiles + splits - 1) / splits;
-  a.keys_per_split = tiles_per * kTileKeys;
-  splits = (tiles + tiles_per - 1) / tiles_per;
-  a.chunks = splits;
-  int rc;
   switch (G) {
-    case 1: rc = launch_tiles<1>(km, vm, a, splits, st); break;
-    case 2: rc = launch_tiles<2>(km, vm, a, splits, st); break;
-    case 4: rc = launch_tiles<4>(km, vm, a, splits, st); break;
-    case 8: rc = launch_tiles<8>(km, vm, a, splits, st); break;
-    case 16: rc = launch_tiles<16>(km, vm, a, splits, st); break;
+    case 1: return launch_decode<1>(km, vm, a, st);
+    case 2: return launch_decode<2>(km, vm, a, st);
+    case 4: return launch_decode<4>(km, vm, a, st);
+    case 8: return launch_decode<8>(km, vm, a, st);
+    case 16: return launch_decode<16>(km, vm, a, st);
     default: return kErrInvalid;
   }
-  if (rc) return rc;
-  decode_combine_kernel<<<static_cast<unsigned>(p.batch * p.heads_q), 128, 0, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 }  // namespace reef

@@ -60,7 +60,11 @@ def run(B, Hq, Hkv, L, lens, sm, t):
 
 @pytest.mark.parametrize("B,Hq,Hkv,L,lens", [(2, 4, 4, 300, None), (3, 8, 1, 1000, [1000, 257, 1]),
                                              (2, 16, 1, 520, [513, 256]),
-                                             (1, 4, 2, 4096, None)])
+                                             (1, 4, 2, 4096, None),
+                                             # more (sequence, KV head) pairs than CTAs:
+                                             # CTAs that end one sequence and start the next
+                                             (300, 4, 2, 256, [1 + (37 * i) % 256 for i in range(300)]),
+                                             (5, 32, 2, 1024, [1024, 129, 128, 700, 3])])
 def test_decode_matches_reef_float_head(B, Hq, Hkv, L, lens):
     sm = 1.0 / math.sqrt(128)
     t = make(B, Hq, Hkv, L, seed=B + Hq + L)
