@@ -504,28 +504,40 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a) {
   // launched early (programmatic dependent launch): wait for the main
   // kernel's completion and memory before reading its partials
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // one pass over the rows: warp w holds rows w, w + 8, ... (m, l and a
+  // float4 of O per lane) in registers while the block finds the max
+  constexpr int kRows = (kMaxRowsPerPair + kDWarps - 1) / kDWarps;
+  float mr[kRows], lr[kRows];
+  float4 vr[kRows];
   float m = -INFINITY;
-  for (int c = tid; c < nc; c += kDThreads) m = fmaxf(m, pb[c * stride]);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  for (int i = 0; i < kRows; ++i) {
+    const int c = warp + i * kDWarps;
+    mr[i] = -INFINITY;
+    if (c < nc) {
+      const float* pr = pb + c * stride;
+      mr[i] = pr[0];
+      lr[i] = pr[1];
+      vr[i] = reinterpret_cast<const float4*>(pr + 4)[lane];
+      m = fmaxf(m, mr[i]);
+    }
+  }
   if (lane == 0) red[warp] = m;
   __syncthreads();
 #pragma unroll
   for (int w = 0; w < kDWarps; ++w) m = fmaxf(m, red[w]);
   float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   float l = 0.0f;
-#pragma unroll 2
-  for (int c = warp; c < nc; c += kDWarps) {
-    const float* pr = pb + c * stride;
-    const float mc = pr[0];
-    if (mc == -INFINITY) continue;  // a CTA whose tiles all lay past the sequence's end
-    const float w = exp2f(mc - m);
-    l += w * pr[1];
-    const float4 v = reinterpret_cast<const float4*>(pr + 4)[lane];
-    o.x += w * v.x;
-    o.y += w * v.y;
-    o.z += w * v.z;
-    o.w += w * v.w;
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    // a CTA whose tiles all lay past the sequence's end has m = -inf
+    if (mr[i] == -INFINITY) continue;
+    const float w = exp2f(mr[i] - m);
+    l += w * lr[i];
+    o.x += w * vr[i].x;
+    o.y += w * vr[i].y;
+    o.z += w * vr[i].z;
+    o.w += w * vr[i].w;
   }
   osm[warp][lane] = o;
   if (lane == 0) lsm[warp] = l;
