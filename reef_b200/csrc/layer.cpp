@@ -235,15 +235,30 @@ size_t llama_carve(const reef_b200_llama_layer* L, void* ws, LlamaBufs* b) {
   return c.used + 256;
 }
 
-// Chunks of whole sequences the all-gather plan pipelines over: 4 (or 2)
-// when the batch divides, else 1 (no pipelining).  REEF_B200_TP_CHUNKS (1, 2
-// or 4) caps it.
+// Chunks of whole sequences the all-gather plan pipelines over: 2 when the
+// batch divides (measured on config 3 at TP=2 and TP=4: 2.04 / 1.55 ms per
+// layer against 2.11 / 1.68 with 4), else 1 (no pipelining).
+// REEF_B200_TP_CHUNKS (1, 2 or 4) sets the cap.
 int ag_chunks(const reef_b200_llama_layer* L) {
-  int cap = 4;
+  int cap = 2;
   if (const char* e = std::getenv("REEF_B200_TP_CHUNKS")) cap = std::max(1, std::min(4, std::atoi(e)));
   for (int c : {4, 2})
     if (c <= cap && L->batch % static_cast<size_t>(c) == 0) return c;
   return 1;
+}
+
+// SMs the pipelined all-gather plan's GEMMs may occupy (0: all): the rest
+// stay free for the neighbouring chunk's NVLink-writing kernels, which would
+// otherwise wait for the persistent GEMM to leave the SMs.
+// REEF_B200_TP_GEMM_SMS overrides the default.
+int ag_gemm_sms() {
+  static int v = -1;
+  if (v < 0) {
+    int x = 0;
+    if (const char* e = std::getenv("REEF_B200_TP_GEMM_SMS")) x = std::max(0, std::atoi(e));
+    v = x;
+  }
+  return v;
 }
 
 bool llama_allgather(const reef_b200_llama_layer* L) {
@@ -492,8 +507,9 @@ size_t reef_b200_llama_layer_kernel_launches(const reef_b200_llama_layer* L) {
   // (the MLP's absmax comes from the gate/up GEMM); all-gather plan: each
   // RMSNorm is two passes (stats, apply) and the o-proj input an absmax pass.
   // The all-gather plan pipelined over k chunks of sequences runs each of its
-  // 12 per-token kernels once per chunk (the RoPE table once).
-  if (llama_allgather(L)) return ag_chunks(L) > 1 ? 12 * ag_chunks(L) + 1 : 13;
+  // 12 per-token kernels once per chunk, plus the push of the SwiGLU row
+  // maxima (the RoPE table once).
+  if (llama_allgather(L)) return ag_chunks(L) > 1 ? 13 * ag_chunks(L) + 1 : 13;
   return L->comm != nullptr ? 13 : 10;
 }
 
@@ -535,28 +551,31 @@ struct EventSet {
   }
 };
 
-// The all-gather plan, pipelined over chunks of whole sequences, with every
-// transfer on the copy engines.  Chunk k's kernels run on the communicator's
-// compute stream k.  The data a step gathers lives in the communicator's
-// symmetric arena, one region per chunk and kind (int8 activations, RMSNorm
-// chunk sums, row maxima), laid out [rank][rows][...]: each rank's kernel
-// writes its own segment, and the collective stream copies it into every
-// peer's arena (cudaMemcpyAsync over NVLink: no SMs, so it overlaps the
-// persistent GEMMs) and then raises the (region, rank) data flag there.  The
-// consuming kernel's stream waits for every peer's data flag; after it ran,
-// the stream raises the region's "consumed" flag in every peer's arena, and a
-// rank copies into a peer's region only once that peer has consumed the
-// previous contents.  Flag values are (forward round, use) counters that only
-// grow.  Steps are issued wavefront-wise so that every rank issues the same
-// sequence; each wait depends only on copies issued earlier in it, so the
-// pipeline cannot deadlock.  Each chunk computes exactly what the unpipelined
-// plan computes for its rows, so the result is identical.
+// The all-gather plan, pipelined over chunks of whole sequences.  Chunk k's
+// kernels run on the communicator's compute stream k.  The data a step
+// exchanges lives in the communicator's symmetric arena, one region per chunk
+// and kind (int8 activations, RMSNorm chunk sums, row maxima), laid out
+// [rank][rows][...]: the kernel that produces a rank's segment writes it
+// straight into every rank's arena over NVLink (its stores go to the peers'
+// mapped arenas; on 4 GPUs that moves ~550-620 GB/s per GPU against
+// ~300-350 GB/s for copy-engine copies, and no separate transfer step waits
+// in between).  The gate/up GEMM takes its row maxima with atomics locally,
+// and a small kernel pushes them.  After a producing step the stream raises
+// the region's data flag (region, rank) in every peer's arena (the stream
+// write fences the kernel's stores first); a consuming step's stream waits
+// for every peer's data flag, and afterwards raises the region's "consumed"
+// flag in every peer's arena; a producing step writes a region only once
+// every peer has consumed its previous contents.  Flag values are (forward
+// round, use) counters that only grow.  Steps are issued wavefront-wise so
+// that every rank issues the same sequence; each wait depends only on steps
+// issued earlier on some rank, so the pipeline cannot deadlock.  Each chunk
+// computes exactly what the unpipelined plan computes for its rows, so the
+// result is identical.
 static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const float* x, float* y,
                                       const LlamaAgBufs& b, int chunks, cudaStream_t st) {
   Comm* c = C(L->comm);
   const int N = comm_world(c), rank = comm_rank(c);
-  cudaStream_t cs = comm_stream(c);
-  if (cs == nullptr || chunks > kComputeStreams) return REEF_B200_ERR_INVALID;
+  if (chunks > kComputeStreams) return REEF_B200_ERR_INVALID;
   const int H = static_cast<int>(L->hidden), hq = static_cast<int>(L->heads_q),
             hkv = static_cast<int>(L->heads_kv), F = static_cast<int>(L->ffn), D = 128;
   const int seq = static_cast<int>(L->seq);
@@ -588,14 +607,11 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
   auto xq_all = [&](int k) { return reinterpret_cast<int8_t*>(arena + region_off(k, kXq)); };
   auto st_all = [&](int k) { return reinterpret_cast<float*>(arena + region_off(k, kSt)); };
   auto mx_all = [&](int k) { return reinterpret_cast<float*>(arena + region_off(k, kMx)); };
-  // this rank's segment of a region (the [N][Tc][w] layout of the step's width w)
-  auto xq_mine = [&](int k, long long kl) { return xq_all(k) + rank * Tc * kl; };
-  auto st_mine = [&](int k) { return st_all(k) + rank * Tc * S; };
+  // this rank's segment of the row-max region here
   auto mx_mine = [&](int k) { return mx_all(k) + rank * Tc; };
 
-  EventSet done(chunks), pushed(chunks), fork(1);
+  EventSet done(chunks), fork(1);
   REEF_TRY(done.create());
-  REEF_TRY(pushed.create());
   REEF_TRY(fork.create());
   auto sk = [&](int k) { return comm_compute_stream(c, k); };
   REEF_TRY(rope_table(seq, L->rope_base, b.rope, st));
@@ -603,33 +619,44 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
   for (int k = 0; k < chunks; ++k)
     if (cudaStreamWaitEvent(sk(k), fork.ev[0], 0) != cudaSuccess) return REEF_B200_ERR_CUDA;
 
-  // a compute step of chunk k: wait for the gathered inputs it consumes, run,
-  // mark them consumed, and mark the step done (for the collective stream)
-  struct In {
+  // A step of chunk k on its own stream.  It waits until every peer has
+  // delivered the uses of the regions it reads (`ins`) and has consumed the
+  // previous use of the regions it writes (`outs`: it writes them into every
+  // rank's arena, its own included); after the kernels it marks its inputs
+  // consumed and its outputs delivered, on every peer.  Chunk k's step also
+  // waits for chunk k - 1's same step, so the chunks run one step apart: the
+  // NVLink-bound steps (the quantisers that write to every peer) of one
+  // chunk overlap the tensor-bound steps (GEMMs, flash) of its neighbour
+  // instead of running beside their own kind.
+  struct Use {
     Kind kind;
     int use;
   };
-  // (it also waits for chunk k's last outgoing copy, which may still read the
-  // segment this step overwrites)
-  auto compute = [&](int k, std::initializer_list<In> ins, auto&& fn) -> int {
-    if (cudaStreamWaitEvent(sk(k), pushed.ev[k], 0) != cudaSuccess) return kErrCuda;
-    for (const In& i : ins) REEF_TRY(comm_wait(c, data_slot(k, i.kind), epoch(i.kind, i.use), sk(k)));
+  auto step = [&](int k, std::initializer_list<Use> ins, std::initializer_list<Use> outs,
+                  auto&& fn) -> int {
+    if (k > 0 && cudaStreamWaitEvent(sk(k), done.ev[k - 1], 0) != cudaSuccess) return kErrCuda;
+    for (const Use& i : ins) REEF_TRY(comm_wait(c, data_slot(k, i.kind), epoch(i.kind, i.use), sk(k)));
+    for (const Use& o : outs)
+      REEF_TRY(comm_wait(c, cons_slot(k, o.kind), epoch(o.kind, o.use) - 1, sk(k)));
     REEF_TRY(fn(sk(k)));
-    for (const In& i : ins) REEF_TRY(comm_signal(c, cons_slot(k, i.kind), epoch(i.kind, i.use), sk(k)));
+    for (const Use& i : ins) REEF_TRY(comm_signal(c, cons_slot(k, i.kind), epoch(i.kind, i.use), sk(k)));
+    for (const Use& o : outs)
+      REEF_TRY(comm_signal(c, data_slot(k, o.kind), epoch(o.kind, o.use), sk(k)));
     return cudaEventRecord(done.ev[k], sk(k)) == cudaSuccess ? kOk : kErrCuda;
   };
-  // the collective step: once chunk k's producing kernel is done and every
-  // peer has consumed the region's previous contents, copy this rank's
-  // segment into every peer's arena and raise the data flag there
-  auto gather = [&](int k, Kind kind, int use, const void* mine, size_t bytes) -> int {
-    if (cudaStreamWaitEvent(cs, done.ev[k], 0) != cudaSuccess) return kErrCuda;
-    const uint32_t e = epoch(kind, use);
-    REEF_TRY(comm_wait(c, cons_slot(k, kind), e - 1, cs));
-    const size_t off = static_cast<const uint8_t*>(mine) - arena;
-    REEF_TRY(comm_put(c, mine, off, bytes, cs));
-    REEF_TRY(comm_signal(c, data_slot(k, kind), e, cs));
-    return cudaEventRecord(pushed.ev[k], cs) == cudaSuccess ? kOk : kErrCuda;
+  // this rank's segment of region (k, kind) in every rank's arena (the [N][Tc][w]
+  // layout of the step's width w, bytes per row given)
+  auto everywhere = [&](int k, Kind kind, long long row_bytes, bool self) {
+    PeerDst d;
+    for (int r = 0; r < N; ++r) {
+      if (r == rank && !self) continue;
+      d.p[d.n++] = comm_peer_data(c, r) + region_off(k, kind) + rank * Tc * row_bytes;
+    }
+    return d;
   };
+  auto xq_to = [&](int k, long long kl) { return everywhere(k, kXq, kl, true); };
+  auto st_to = [&](int k) { return everywhere(k, kSt, S * 4, true); };
+  auto mx_to = [&](int k, bool self) { return everywhere(k, kMx, 4, self); };
   // per-chunk views of the workspace
   auto xk = [&](int k) { return x + k * Tc * Hl; };
   auto hk = [&](int k) { return b.h + k * Tc * Hl; };
@@ -654,31 +681,21 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
     p.args.w_scale = ws;
     p.args.y = out;
     p.args.ldy = n;
+    p.args.max_ctas = ag_gemm_sms();
     return p;
-  };
-  auto gather_xq = [&](int k, int use, long long kl) {
-    return gather(k, kXq, use, xq_mine(k, kl), static_cast<size_t>(Tc * kl));
-  };
-  auto gather_st = [&](int k, int use) {
-    return gather(k, kSt, use, st_mine(k), static_cast<size_t>(Tc * S * 4));
-  };
-  auto gather_mx = [&](int k, int use) {
-    return gather(k, kMx, use, mx_mine(k), static_cast<size_t>(Tc * 4));
   };
 
   // ---- attention block
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {}, [&](cudaStream_t s) {
-      return rms_stats(Tc, H, N, xk(k), g1, st_mine(k), s);
+    REEF_TRY(step(k, {}, {{kSt, 0}}, [&](cudaStream_t s) {
+      return rms_stats(Tc, H, N, xk(k), g1, st_to(k), s);
     }));
-  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_st(k, 0));
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {{kSt, 0}}, [&](cudaStream_t s) {
-      return rms_apply_quant(Tc, H, N, L->rms_eps, xk(k), g1, st_all(k), xq_mine(k, Hl), xsk(k), s);
+    REEF_TRY(step(k, {{kSt, 0}}, {{kXq, 0}}, [&](cudaStream_t s) {
+      return rms_apply_quant(Tc, H, N, L->rms_eps, xk(k), g1, st_all(k), xq_to(k, Hl), xsk(k), s);
     }));
-  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_xq(k, 0, Hl));
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {{kXq, 0}}, [&](cudaStream_t s) {
+    REEF_TRY(step(k, {{kXq, 0}}, {}, [&](cudaStream_t s) {
       uint16_t* vt = static_cast<uint16_t*>(b.vt) + static_cast<long long>(k) * bc * hkv * D * seq;
       GemmProblem p = problem_k(k, Hl, L->w_qkv, qkv_w, L->s_qkv, nullptr);
       p.args.qkv = qkv_out(L, hq, hkv, b.q8 + k * Tc * hq * D, b.k8 + k * Tc * hkv * D,
@@ -687,7 +704,7 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
       return gemm_i8(p, kEpiQkvRope, s);
     }));
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {}, [&](cudaStream_t s) {
+    REEF_TRY(step(k, {}, {{kMx, 0}}, [&](cudaStream_t s) {
       FlashProblem fp{};
       fp.batch = bc;
       fp.heads_q = hq;
@@ -704,60 +721,54 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
       fp.out = attnk(k);
       fp.out_ld = static_cast<long long>(hq) * D;
       REEF_TRY(flash_prefill_i8(fp, s));
-      return row_absmax(Tc, hq * D, attnk(k), mx_mine(k), s);
+      return row_absmax_to(Tc, hq * D, attnk(k), mx_to(k, true), s);
     }));
-  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_mx(k, 0));
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {{kMx, 0}}, [&](cudaStream_t s) {
+    REEF_TRY(step(k, {{kMx, 0}}, {{kXq, 1}}, [&](cudaStream_t s) {
       REEF_TRY(max_segments(N, Tc, mx_all(k), rmk(k), s));
-      return quantize_rows(Tc, hq * D, attnk(k), xq_mine(k, hq * D), hq * D, xsk(k), rmk(k), s);
+      return quantize_rows_to(Tc, hq * D, attnk(k), xq_to(k, hq * D), hq * D, xsk(k), rmk(k), s);
     }));
-  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_xq(k, 1, hq * D));
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {{kXq, 1}}, [&](cudaStream_t s) {
+    REEF_TRY(step(k, {{kXq, 1}}, {}, [&](cudaStream_t s) {
       GemmProblem p = problem_k(k, hq * D, L->w_o, Hl, L->s_o, hk(k));
       p.args.residual = xk(k);
       return gemm_i8(p, kEpiF32W8A8, s);
     }));
   // ---- MLP block
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {}, [&](cudaStream_t s) {
-      return rms_stats(Tc, H, N, hk(k), g2, st_mine(k), s);
+    REEF_TRY(step(k, {}, {{kSt, 1}}, [&](cudaStream_t s) {
+      return rms_stats(Tc, H, N, hk(k), g2, st_to(k), s);
     }));
-  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_st(k, 1));
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {{kSt, 1}}, [&](cudaStream_t s) {
-      return rms_apply_quant(Tc, H, N, L->rms_eps, hk(k), g2, st_all(k), xq_mine(k, Hl), xsk(k), s);
+    REEF_TRY(step(k, {{kSt, 1}}, {{kXq, 2}}, [&](cudaStream_t s) {
+      return rms_apply_quant(Tc, H, N, L->rms_eps, hk(k), g2, st_all(k), xq_to(k, Hl), xsk(k), s);
     }));
-  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_xq(k, 2, Hl));
+  // gate/up: the SwiGLU epilogue takes each row's max with atomics into this
+  // rank's segment here; it is then pushed to the peers
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {{kXq, 2}}, [&](cudaStream_t s) {
+    REEF_TRY(step(k, {{kXq, 2}}, {{kMx, 1}}, [&](cudaStream_t s) {
       if (cudaMemsetAsync(mx_mine(k), 0, static_cast<size_t>(Tc) * sizeof(float), s) != cudaSuccess)
         return static_cast<int>(kErrCuda);
       GemmProblem p = problem_k(k, Hl, L->w_gu, F, L->s_gu, bigk(k));
       p.args.b_up = F;
       p.args.row_max = mx_mine(k);
-      return gemm_i8(p, kEpiSwiGLU, s);
+      REEF_TRY(gemm_i8(p, kEpiSwiGLU, s));
+      return push_f32(Tc, mx_mine(k), mx_to(k, false), s);
     }));
-  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_mx(k, 1));
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {{kMx, 1}}, [&](cudaStream_t s) {
+    REEF_TRY(step(k, {{kMx, 1}}, {{kXq, 3}}, [&](cudaStream_t s) {
       REEF_TRY(max_segments(N, Tc, mx_all(k), rmk(k), s));
-      return quantize_rows(Tc, F, bigk(k), xq_mine(k, F), F, xsk(k), rmk(k), s);
+      return quantize_rows_to(Tc, F, bigk(k), xq_to(k, F), F, xsk(k), rmk(k), s);
     }));
-  for (int k = 0; k < chunks; ++k) REEF_TRY(gather_xq(k, 3, F));
   for (int k = 0; k < chunks; ++k)
-    REEF_TRY(compute(k, {{kXq, 3}}, [&](cudaStream_t s) {
+    REEF_TRY(step(k, {{kXq, 3}}, {}, [&](cudaStream_t s) {
       GemmProblem p = problem_k(k, F, L->w_down, Hl, L->s_down, y + k * Tc * Hl);
       p.args.residual = hk(k);
       return gemm_i8(p, kEpiF32W8A8, s);
     }));
-  // join: the caller's stream waits for every chunk's last kernel and last
-  // outgoing copy
+  // join: the caller's stream waits for every chunk's last kernel
   for (int k = 0; k < chunks; ++k)
-    if (cudaStreamWaitEvent(st, done.ev[k], 0) != cudaSuccess ||
-        cudaStreamWaitEvent(st, pushed.ev[k], 0) != cudaSuccess)
-      return REEF_B200_ERR_CUDA;
+    if (cudaStreamWaitEvent(st, done.ev[k], 0) != cudaSuccess) return REEF_B200_ERR_CUDA;
   return REEF_B200_OK;
 }
 
@@ -809,9 +820,9 @@ static int llama_forward_ag(const reef_b200_llama_layer* L, const float* x, floa
     return gemm_i8(p, kEpiF32W8A8, st);
   };
   auto rms = [&](const float* xin, const float* g) -> int {
-    REEF_TRY(rms_stats(T, H, N, xin, g, b.stats, st));
+    REEF_TRY(rms_stats(T, H, N, xin, g, one_dst(b.stats), st));
     REEF_TRY(allgather_bytes(c, b.stats, b.stats_all, static_cast<size_t>(T) * S * 4, st));
-    REEF_TRY(rms_apply_quant(T, H, N, L->rms_eps, xin, g, b.stats_all, b.xq, b.xs, st));
+    REEF_TRY(rms_apply_quant(T, H, N, L->rms_eps, xin, g, b.stats_all, one_dst(b.xq), b.xs, st));
     return allgather_bytes(c, b.xq, b.xq_all, static_cast<size_t>(T) * Hl, st);
   };
 

@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kChunks * 32)
 template <int P>
 __global__ void __launch_bounds__(kChunks * 32)
     rms_stats_kernel(int width, int chunks_local, const float* __restrict__ x,
-                     const float* __restrict__ gain, float* __restrict__ stats) {
+                     const float* __restrict__ gain, PeerDst stats) {
   __shared__ float cmax[kChunks];
   const long long row = blockIdx.x;
   const int c = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -207,16 +207,16 @@ __global__ void __launch_bounds__(kChunks * 32)
   float m = 0.0f;
   const float cs = chunk_sum<P, false>(xr, gr, n4, l, unused, m);
   m = warp_max(m);
-  float* st = stats + row * (chunks_local + 1);
+  const long long off = row * (chunks_local + 1);
   if (l == 0) {
-    st[c] = cs;
+    for (int d = 0; d < stats.n; ++d) static_cast<float*>(stats.p[d])[off + c] = cs;
     cmax[c] = m;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     float mm = cmax[0];
     for (int j = 1; j < chunks_local; ++j) mm = fmaxf(mm, cmax[j]);
-    st[chunks_local] = mm;
+    for (int d = 0; d < stats.n; ++d) static_cast<float*>(stats.p[d])[off + chunks_local] = mm;
   }
 }
 
@@ -227,8 +227,7 @@ template <int P>
 __global__ void __launch_bounds__(kChunks * 32)
     rms_apply_kernel(int width, int chunks_local, int ranks, long long rows, float eps,
                      const float* __restrict__ x, const float* __restrict__ gain,
-                     const float* __restrict__ stats_all, int8_t* __restrict__ xq,
-                     float* __restrict__ xs) {
+                     const float* __restrict__ stats_all, PeerDst xq, float* __restrict__ xs) {
   __shared__ float rs[2];
   const long long row = blockIdx.x;
   const int c = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -253,11 +252,15 @@ __global__ void __launch_bounds__(kChunks * 32)
   const int wl = chunks_local * (width / kChunks);
   const float4* xr = reinterpret_cast<const float4*>(x + row * wl) + c * n4;
   const float4* gr = reinterpret_cast<const float4*>(gain) + c * n4;
-  char4* out = reinterpret_cast<char4*>(xq + row * wl) + c * n4;
+  const long long off = row * wl + static_cast<long long>(c) * n4 * 4;  // bytes
 #pragma unroll
   for (int k = 0; k < 4 * P; ++k) {
     const int idx = l + 32 * k;
-    if (idx < n4) out[idx] = q8x4(scale4(mul4(__ldg(xr + idx), __ldg(gr + idx)), r), scale);
+    if (idx < n4) {
+      const char4 q = q8x4(scale4(mul4(__ldg(xr + idx), __ldg(gr + idx)), r), scale);
+      for (int d = 0; d < xq.n; ++d)
+        reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + off)[idx] = q;
+    }
   }
 }
 
@@ -349,7 +352,7 @@ int rmsnorm_quant(long long rows, int width, float eps, const float* x, const fl
 }
 
 int rms_stats(long long rows, int width, int ranks, const float* x_local, const float* gain_local,
-              float* stats, cudaStream_t stream) {
+              const PeerDst& stats, cudaStream_t stream) {
   if (rows == 0) return kOk;
   if (width % (4 * kChunks) != 0 || kChunks % ranks != 0) return kErrInvalid;
   const int cl = kChunks / ranks, P = per_thread(width);
@@ -363,8 +366,8 @@ int rms_stats(long long rows, int width, int ranks, const float* x_local, const 
 }
 
 int rms_apply_quant(long long rows, int width, int ranks, float eps, const float* x_local,
-                    const float* gain_local, const float* stats_all, int8_t* x_q, float* x_scale,
-                    cudaStream_t stream) {
+                    const float* gain_local, const float* stats_all, const PeerDst& x_q,
+                    float* x_scale, cudaStream_t stream) {
   if (rows == 0) return kOk;
   if (width % (4 * kChunks) != 0 || kChunks % ranks != 0) return kErrInvalid;
   const int cl = kChunks / ranks, P = per_thread(width);

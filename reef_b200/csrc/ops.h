@@ -130,14 +130,37 @@ int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int ep
                    const float* x_scale, const float* w_scale, const float* bias,
                    const float* residual, void* y, void* partial, cudaStream_t stream);
 
+// One output written alike to up to kMaxDst places: the same offset in every
+// rank's symmetric arena, so an exchanged activation goes from the kernel that
+// produces it straight into every peer's memory over NVLink (no separate copy).
+constexpr int kMaxDst = 8;
+struct PeerDst {
+  int n = 0;
+  void* p[kMaxDst] = {};
+};
+inline PeerDst one_dst(void* p) {
+  PeerDst d;
+  d.n = 1;
+  d.p[0] = p;
+  return d;
+}
+
 // quant.cu
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q,
                   long long ldq, float* x_scale, const float* row_max,
                   cudaStream_t stream);
+// quantize_rows with the int8 rows written to every destination (in and ldq
+// multiples of 4, x 16-byte aligned; x_scale local)
+int quantize_rows_to(long long rows, long long in, const float* x, const PeerDst& x_q,
+                     long long ldq, float* x_scale, const float* row_max, cudaStream_t stream);
+// src [n] fp32 copied to every destination by SM stores
+int push_f32(long long n, const float* src, const PeerDst& dst, cudaStream_t stream);
 // out[r] = max_s in[s][r] for in [segs][rows]
 int max_segments(int segs, long long rows, const float* in, float* out, cudaStream_t stream);
 int row_absmax(long long rows, long long in, const float* x, float* row_max,
                cudaStream_t stream);
+int row_absmax_to(long long rows, long long in, const float* x, const PeerDst& row_max,
+                  cudaStream_t stream);
 int pack_weight_i8(long long in, long long out, const int8_t* wt, int8_t* w,
                    long long ldw, cudaStream_t stream);
 int pad_rows_i8(long long rows, long long in, const int8_t* x, long long ldx,
@@ -155,11 +178,12 @@ int swiglu_absmax(long long rows, int ffn, const float* gu, float* row_max,
                   cudaStream_t stream);
 // TP-sharded RMSNorm (columns split over `ranks`): per-rank stats, all-gather,
 // then quantise this rank's columns with the full row's scale.
+// stats and x_q go to every destination of their PeerDst (x_scale is local).
 int rms_stats(long long rows, int width, int ranks, const float* x_local, const float* gain_local,
-              float* stats, cudaStream_t stream);
+              const PeerDst& stats, cudaStream_t stream);
 int rms_apply_quant(long long rows, int width, int ranks, float eps, const float* x_local,
-                    const float* gain_local, const float* stats_all, int8_t* x_q, float* x_scale,
-                    cudaStream_t stream);
+                    const float* gain_local, const float* stats_all, const PeerDst& x_q,
+                    float* x_scale, cudaStream_t stream);
 
 // attention_exact.cu -- reef's integer and float heads, bit for bit.
 // Scores stay in shared memory, which bounds the key length.

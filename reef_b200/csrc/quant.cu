@@ -47,9 +47,8 @@ __device__ __forceinline__ int8_t q8(float x, float scale) {
 // registers and occupancy follow the width); longer rows re-read the rest.
 template <int CACHE>
 __global__ void __launch_bounds__(kQuantThreads)
-    quantize_rows_vec4(int in, const float* __restrict__ x, int8_t* __restrict__ xq,
-                       long long ldq, float* __restrict__ xs,
-                       const float* __restrict__ row_max) {
+    quantize_rows_vec4(int in, const float* __restrict__ x, PeerDst xq, long long ldq,
+                       float* __restrict__ xs, const float* __restrict__ row_max) {
   __shared__ float red[32];
   const long long row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * in);
@@ -77,21 +76,26 @@ __global__ void __launch_bounds__(kQuantThreads)
   }
   const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
   if (threadIdx.x == 0) xs[row] = scale;
-  char4* out = reinterpret_cast<char4*>(xq + row * ldq);
+  // each int8 row goes to every destination
 #pragma unroll
   for (int i = 0; i < CACHE; ++i) {
     const int idx = threadIdx.x + i * kQuantThreads;
     if (idx < n4) {
       const float4 v = cache[i];
-      out[idx] = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
+      const char4 q = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
+      for (int d = 0; d < xq.n; ++d)
+        reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + row * ldq)[idx] = q;
     }
   }
   for (int idx = threadIdx.x + CACHE * kQuantThreads; idx < n4; idx += kQuantThreads) {
     const float4 v = __ldg(xr + idx);
-    out[idx] = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
+    const char4 q = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
+    for (int d = 0; d < xq.n; ++d)
+      reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + row * ldq)[idx] = q;
   }
   // zero the stride padding [in, ldq)
-  for (long long c = in + threadIdx.x; c < ldq; c += kQuantThreads) xq[row * ldq + c] = 0;
+  for (long long c = in + threadIdx.x; c < ldq; c += kQuantThreads)
+    for (int d = 0; d < xq.n; ++d) static_cast<int8_t*>(xq.p[d])[row * ldq + c] = 0;
 }
 
 // Any width / alignment.
@@ -112,13 +116,21 @@ __global__ void __launch_bounds__(kQuantThreads)
 }
 
 __global__ void __launch_bounds__(kQuantThreads)
-    row_absmax_kernel(int in, const float* __restrict__ x, float* __restrict__ out) {
+    row_absmax_kernel(int in, const float* __restrict__ x, PeerDst out) {
   __shared__ float red[32];
   const float* xr = x + static_cast<long long>(blockIdx.x) * in;
   float m = 0.0f;
   for (int c = threadIdx.x; c < in; c += kQuantThreads) m = fmaxf(m, fabsf(xr[c]));
   m = block_max(m, red);
-  if (threadIdx.x == 0) out[blockIdx.x] = m;
+  if (threadIdx.x == 0)
+    for (int d = 0; d < out.n; ++d) static_cast<float*>(out.p[d])[blockIdx.x] = m;
+}
+
+__global__ void push_f32_kernel(long long n, const float* __restrict__ src, PeerDst dst) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = src[i];
+  for (int d = 0; d < dst.n; ++d) static_cast<float*>(dst.p[d])[i] = v;
 }
 
 // out[r] = max over s of in[s][r] (row maxima gathered from `segs` ranks).
@@ -172,6 +184,28 @@ __global__ void w8a8_epilogue_kernel(long long rows, int out, const int32_t* __r
 
 }  // namespace
 
+static int quantize_vec4(long long rows, long long in, const float* x, const PeerDst& x_q,
+                         long long ldq, float* x_scale, const float* row_max,
+                         cudaStream_t stream) {
+  const int per = static_cast<int>((in / 4 + kQuantThreads - 1) / kQuantThreads);
+  const unsigned grid = static_cast<unsigned>(rows);
+  const int ii = static_cast<int>(in);
+  if (per <= 1) {
+    quantize_rows_vec4<1><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+  } else if (per <= 2) {
+    quantize_rows_vec4<2><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+  } else if (per <= 4) {
+    quantize_rows_vec4<4><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+  } else if (per <= 8) {
+    quantize_rows_vec4<8><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+  } else if (per <= 12) {
+    quantize_rows_vec4<12><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+  } else {
+    quantize_rows_vec4<16><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q, long long ldq,
                   float* x_scale, const float* row_max, cudaStream_t stream) {
   if (rows == 0) return kOk;
@@ -180,37 +214,43 @@ int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q, lon
   const bool vec = (in % 4 == 0) && (ldq % 4 == 0) &&
                    (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(x_q) % 4 == 0);
-  if (vec) {
-    const int per = static_cast<int>((in / 4 + kQuantThreads - 1) / kQuantThreads);
-    const unsigned grid = static_cast<unsigned>(rows);
-    const int ii = static_cast<int>(in);
-    if (per <= 1) {
-      quantize_rows_vec4<1><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-    } else if (per <= 2) {
-      quantize_rows_vec4<2><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-    } else if (per <= 4) {
-      quantize_rows_vec4<4><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-    } else if (per <= 8) {
-      quantize_rows_vec4<8><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-    } else if (per <= 12) {
-      quantize_rows_vec4<12><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-    } else {
-      quantize_rows_vec4<16><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-    }
-  } else {
-    quantize_rows_scalar<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
-        static_cast<int>(in), x, x_q, ldq, x_scale, row_max);
-  }
+  if (vec) return quantize_vec4(rows, in, x, one_dst(x_q), ldq, x_scale, row_max, stream);
+  quantize_rows_scalar<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
+      static_cast<int>(in), x, x_q, ldq, x_scale, row_max);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int quantize_rows_to(long long rows, long long in, const float* x, const PeerDst& x_q,
+                     long long ldq, float* x_scale, const float* row_max, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (in <= 0 || ldq < in || in % 4 != 0 || ldq % 4 != 0 || x == nullptr || x_scale == nullptr ||
+      x_q.n < 1 || x_q.n > kMaxDst || reinterpret_cast<uintptr_t>(x) % 16 != 0)
+    return kErrInvalid;
+  for (int d = 0; d < x_q.n; ++d)
+    if (x_q.p[d] == nullptr || reinterpret_cast<uintptr_t>(x_q.p[d]) % 4 != 0) return kErrInvalid;
+  return quantize_vec4(rows, in, x, x_q, ldq, x_scale, row_max, stream);
+}
+
+int push_f32(long long n, const float* src, const PeerDst& dst, cudaStream_t stream) {
+  if (n == 0) return kOk;
+  if (n < 0 || src == nullptr || dst.n < 1 || dst.n > kMaxDst) return kErrInvalid;
+  push_f32_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(n, src, dst);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int row_absmax_to(long long rows, long long in, const float* x, const PeerDst& row_max,
+                  cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (in <= 0 || x == nullptr || row_max.n < 1 || row_max.n > kMaxDst) return kErrInvalid;
+  row_absmax_kernel<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
+      static_cast<int>(in), x, row_max);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int row_absmax(long long rows, long long in, const float* x, float* row_max,
                cudaStream_t stream) {
-  if (rows == 0) return kOk;
-  if (in <= 0 || x == nullptr || row_max == nullptr) return kErrInvalid;
-  row_absmax_kernel<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
-      static_cast<int>(in), x, row_max);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  if (row_max == nullptr) return kErrInvalid;
+  return row_absmax_to(rows, in, x, one_dst(row_max), stream);
 }
 
 int max_segments(int segs, long long rows, const float* in, float* out, cudaStream_t stream) {

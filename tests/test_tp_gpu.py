@@ -1,12 +1,13 @@
-"""Tensor parallelism on two B200s (NCCL over NVLink): every rank's output is
-bit-identical to TP=1.
+"""Tensor parallelism on two and on four B200s (NCCL and copy-engine
+transfers over NVLink): every rank's output is bit-identical to TP=1.
 
 * reef_b200_linear_w8a8_rowpar (all-reduce MAX of row maxima, int32 partial
   GEMM, all-reduce SUM, dequant + bias) == reef_b200_linear_w8a8_bias;
-* the Llama-shape layer at TP=2 == the same layer at TP=1 (same seed);
-* reef's GPT-Neo block at TP=2 (config 2's shape) == the oracle, i.e.
+* the Llama-shape layer at TP=N == the same layer at TP=1 (same seed), with
+  the all-reduce plan and with the pipelined all-gather plan;
+* reef's GPT-Neo block at TP=N (config 2's shape) == the oracle, i.e.
   Block<float>::forward.
-Skipped when fewer than two GPUs are visible.
+Each world size is skipped when fewer GPUs are visible.
 """
 import datetime
 import os
@@ -105,18 +106,21 @@ def _worker(rank, world, port, q):
 
 
 @needs2
-def test_tp2_bit_identical_to_tp1():
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_bit_identical_to_tp1(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict(q.get(timeout=600) for _ in procs)
     for p in procs:
         p.join(timeout=60)
-    for r in range(2):
+    for r in range(world):
         status, res = out[r]
         assert status == "ok", res
         assert res == {"rowpar": True, "llama": True, "llama_allgather": True,
