@@ -38,11 +38,6 @@ struct Comm {
   size_t arena_data = 0;           // data bytes
   int arena_slots = 0;
   uint32_t round = 0;
-  // per-peer copy streams (so the copies to different peers run on several
-  // copy engines at once), the fork event and one join event per peer
-  std::vector<cudaStream_t> put_stream;
-  std::vector<cudaEvent_t> put_join;
-  cudaEvent_t put_fork = nullptr;
 };
 
 namespace {
@@ -93,20 +88,6 @@ const StreamOps& stream_ops() {
       ops.write = reinterpret_cast<WriteValue32>(p);
   });
   return ops;
-}
-
-void put_streams_free(Comm* c) {
-  for (auto s : c->put_stream)
-    if (s != nullptr) {
-      cudaStreamSynchronize(s);
-      cudaStreamDestroy(s);
-    }
-  for (auto e : c->put_join)
-    if (e != nullptr) cudaEventDestroy(e);
-  if (c->put_fork != nullptr) cudaEventDestroy(c->put_fork);
-  c->put_stream.clear();
-  c->put_join.clear();
-  c->put_fork = nullptr;
 }
 
 void arena_free(Comm* c) {
@@ -182,7 +163,6 @@ int comm_destroy(Comm* c) {
     cudaDeviceSynchronize();
     arena_free(c);
   }
-  put_streams_free(c);
   if (c->stream != nullptr) {
     cudaStreamSynchronize(c->stream);
     cudaStreamDestroy(c->stream);
@@ -208,7 +188,6 @@ int comm_destroy(Comm* c) {
 int comm_abort(Comm* c) {
   if (c == nullptr) return kOk;
   arena_free(c);
-  put_streams_free(c);
   if (c->nccl != nullptr) ncclCommAbort(c->nccl);
   if (c->stream != nullptr) cudaStreamDestroy(c->stream);
   for (auto s : c->compute)
@@ -301,18 +280,6 @@ uint8_t* comm_peer_data(Comm* c, int r) {
   return c->peer[r] + flag_bytes(c->arena_slots, c->world);
 }
 
-int comm_put(Comm* c, const void* src, size_t data_off, size_t bytes, cudaStream_t s) {
-  if (c == nullptr || c->arena == nullptr || data_off + bytes > c->arena_data) return kErrInvalid;
-  const size_t fb = flag_bytes(c->arena_slots, c->world);
-  for (int r = 0; r < c->world; ++r) {
-    if (r == c->rank) continue;
-    if (cudaMemcpyAsync(c->peer[r] + fb + data_off, src, bytes, cudaMemcpyDeviceToDevice, s) !=
-        cudaSuccess)
-      return kErrCuda;
-  }
-  return kOk;
-}
-
 int comm_signal(Comm* c, int slot, uint32_t value, cudaStream_t s) {
   if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots) return kErrInvalid;
   const StreamOps& ops = stream_ops();
@@ -336,48 +303,6 @@ int comm_wait(Comm* c, int slot, uint32_t value, cudaStream_t s) {
     const size_t off = (static_cast<size_t>(slot) * c->world + r) * sizeof(uint32_t);
     if (ops.wait(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(c->arena + off), value,
                  CU_STREAM_WAIT_VALUE_GEQ) != CUDA_SUCCESS)
-      return kErrCuda;
-  }
-  return kOk;
-}
-
-int comm_gather_put(Comm* c, cudaStream_t s, const void* src, size_t data_off, size_t bytes,
-                    int data_slot, uint32_t value, int cons_slot, uint32_t cons_min) {
-  if (c == nullptr || c->arena == nullptr || data_off + bytes > c->arena_data || data_slot < 0 ||
-      data_slot >= c->arena_slots || cons_slot < 0 || cons_slot >= c->arena_slots)
-    return kErrInvalid;
-  if (c->put_stream.empty()) {  // first use: one high-priority stream and join event per peer
-    int lo = 0, hi = 0;
-    cudaDeviceGetStreamPriorityRange(&lo, &hi);
-    c->put_stream.assign(c->world, nullptr);
-    c->put_join.assign(c->world, nullptr);
-    if (cudaEventCreateWithFlags(&c->put_fork, cudaEventDisableTiming) != cudaSuccess)
-      return kErrCuda;
-    for (int r = 0; r < c->world; ++r) {
-      if (r == c->rank) continue;
-      if (cudaStreamCreateWithPriority(&c->put_stream[r], cudaStreamNonBlocking, hi) !=
-              cudaSuccess ||
-          cudaEventCreateWithFlags(&c->put_join[r], cudaEventDisableTiming) != cudaSuccess)
-        return kErrCuda;
-    }
-  }
-  const StreamOps& ops = stream_ops();
-  const size_t fb = flag_bytes(c->arena_slots, c->world);
-  const size_t data_flag = (static_cast<size_t>(data_slot) * c->world + c->rank) * sizeof(uint32_t);
-  if (cudaEventRecord(c->put_fork, s) != cudaSuccess) return kErrCuda;
-  for (int r = 0; r < c->world; ++r) {
-    if (r == c->rank) continue;
-    cudaStream_t ps = c->put_stream[r];
-    const size_t cons_flag = (static_cast<size_t>(cons_slot) * c->world + r) * sizeof(uint32_t);
-    if (cudaStreamWaitEvent(ps, c->put_fork, 0) != cudaSuccess ||
-        ops.wait(reinterpret_cast<CUstream>(ps), reinterpret_cast<CUdeviceptr>(c->arena + cons_flag),
-                 cons_min, CU_STREAM_WAIT_VALUE_GEQ) != CUDA_SUCCESS ||
-        cudaMemcpyAsync(c->peer[r] + fb + data_off, src, bytes, cudaMemcpyDeviceToDevice, ps) !=
-            cudaSuccess ||
-        ops.write(reinterpret_cast<CUstream>(ps), reinterpret_cast<CUdeviceptr>(c->peer[r] + data_flag),
-                  value, 0) != CUDA_SUCCESS ||
-        cudaEventRecord(c->put_join[r], ps) != cudaSuccess ||
-        cudaStreamWaitEvent(s, c->put_join[r], 0) != cudaSuccess)
       return kErrCuda;
   }
   return kOk;

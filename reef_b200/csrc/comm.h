@@ -23,13 +23,13 @@ int comm_ctas(const Comm* c);
 constexpr int kComputeStreams = 4;
 cudaStream_t comm_compute_stream(const Comm* c, int i);
 
-// ---- Symmetric arena: copy-engine transfers over NVLink, stream-ordered flags
+// ---- Symmetric arena: peer stores over NVLink, stream-ordered flags
 //
 // Every rank holds an arena of the same size, mapped into every peer's
 // address space (CUDA IPC), laid out alike: `slots` x world uint32 flags, then
-// data.  comm_put copies local bytes to the same data offset in every peer's
-// arena with the copy engines (no SMs); comm_signal writes a flag
-// (slot, this rank) in every peer's arena after the stream's earlier work;
+// data.  Kernels write into peers' data regions directly (comm_peer_data);
+// comm_signal writes a flag (slot, this rank) in every peer's arena after the
+// stream's earlier work (the write fences that work's stores first);
 // comm_wait makes a stream wait, in the stream's front end, until every
 // peer's flag (slot, peer) in the local arena reaches a value.  Values only
 // grow, so a flag never needs resetting.
@@ -39,16 +39,8 @@ int comm_arena_reserve(Comm* c, size_t data_bytes, int slots);
 uint8_t* comm_arena_data(Comm* c);  // this rank's data region
 // rank r's data region as mapped here (r = this rank: comm_arena_data)
 uint8_t* comm_peer_data(Comm* c, int r);
-int comm_put(Comm* c, const void* src, size_t data_off, size_t bytes, cudaStream_t s);
 int comm_signal(Comm* c, int slot, uint32_t value, cudaStream_t s);
 int comm_wait(Comm* c, int slot, uint32_t value, cudaStream_t s);
-// The three above for one all-gather segment, with the peers in parallel:
-// after the work already on `s`, one stream per peer waits until that peer's
-// flag (cons_slot, peer) here reaches cons_min (it has consumed what the copy
-// overwrites), copies `bytes` at data_off into its arena and raises (data_slot,
-// this rank) there to `value`; `s` then waits for every peer's copy.
-int comm_gather_put(Comm* c, cudaStream_t s, const void* src, size_t data_off, size_t bytes,
-                    int data_slot, uint32_t value, int cons_slot, uint32_t cons_min);
 // A counter the pipelined forward advances once per call (identical on all
 // ranks, which make the same calls), from which flag values derive.
 uint32_t comm_next_round(Comm* c);
