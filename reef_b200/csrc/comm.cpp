@@ -308,6 +308,24 @@ int comm_wait(Comm* c, int slot, uint32_t value, cudaStream_t s) {
   return kOk;
 }
 
+unsigned int* comm_counter(Comm* c, int slot, int r) {
+  if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots || r < 0 ||
+      r >= c->world)
+    return nullptr;
+  return reinterpret_cast<unsigned int*>(c->peer[r] + static_cast<size_t>(slot) * c->world *
+                                                           sizeof(uint32_t));
+}
+
+int comm_wait_count(Comm* c, int slot, uint32_t value, cudaStream_t s) {
+  if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots) return kErrInvalid;
+  const StreamOps& ops = stream_ops();
+  const size_t off = static_cast<size_t>(slot) * c->world * sizeof(uint32_t);
+  return ops.wait(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(c->arena + off), value,
+                  CU_STREAM_WAIT_VALUE_GEQ) == CUDA_SUCCESS
+             ? kOk
+             : kErrCuda;
+}
+
 uint32_t comm_next_round(Comm* c) { return c ? ++c->round : 0; }
 
 }  // namespace reef

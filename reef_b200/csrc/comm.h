@@ -41,6 +41,11 @@ uint8_t* comm_arena_data(Comm* c);  // this rank's data region
 uint8_t* comm_peer_data(Comm* c, int r);
 int comm_signal(Comm* c, int slot, uint32_t value, cudaStream_t s);
 int comm_wait(Comm* c, int slot, uint32_t value, cudaStream_t s);
+// Counting form: a slot's counter (its first flag word) that every peer
+// increments.  comm_counter is the counter in rank r's arena (for
+// signal_peers); comm_wait_count waits until the local counter reaches value.
+unsigned int* comm_counter(Comm* c, int slot, int r);
+int comm_wait_count(Comm* c, int slot, uint32_t value, cudaStream_t s);
 // A counter the pipelined forward advances once per call (identical on all
 // ranks, which make the same calls), from which flag values derive.
 uint32_t comm_next_round(Comm* c);

@@ -623,7 +623,12 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
   // delivered the uses of the regions it reads (`ins`) and has consumed the
   // previous use of the regions it writes (`outs`: it writes them into every
   // rank's arena, its own included); after the kernels it marks its inputs
-  // consumed and its outputs delivered, on every peer.  Chunk k's step also
+  // consumed and its outputs delivered, on every peer: each region has a
+  // "delivered" and a "consumed" counter that every peer increments once per
+  // use (one warp's system-scope atomics after the step), so a step waits on
+  // one counter per region instead of one flag per peer.  A peer cannot run
+  // two uses ahead (producing use e + 1 needs this rank's consumption of use
+  // e), so a counter never passes a target early.  Chunk k's step also
   // waits for chunk k - 1's same step, so the chunks run one step apart: the
   // NVLink-bound steps (the quantisers that write to every peer) of one
   // chunk overlap the tensor-bound steps (GEMMs, flash) of its neighbour
@@ -635,13 +640,19 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
   auto step = [&](int k, std::initializer_list<Use> ins, std::initializer_list<Use> outs,
                   auto&& fn) -> int {
     if (k > 0 && cudaStreamWaitEvent(sk(k), done.ev[k - 1], 0) != cudaSuccess) return kErrCuda;
-    for (const Use& i : ins) REEF_TRY(comm_wait(c, data_slot(k, i.kind), epoch(i.kind, i.use), sk(k)));
+    const uint32_t peers = static_cast<uint32_t>(N - 1);
+    for (const Use& i : ins)
+      REEF_TRY(comm_wait_count(c, data_slot(k, i.kind), epoch(i.kind, i.use) * peers, sk(k)));
     for (const Use& o : outs)
-      REEF_TRY(comm_wait(c, cons_slot(k, o.kind), epoch(o.kind, o.use) - 1, sk(k)));
+      REEF_TRY(comm_wait_count(c, cons_slot(k, o.kind), (epoch(o.kind, o.use) - 1) * peers, sk(k)));
     REEF_TRY(fn(sk(k)));
-    for (const Use& i : ins) REEF_TRY(comm_signal(c, cons_slot(k, i.kind), epoch(i.kind, i.use), sk(k)));
-    for (const Use& o : outs)
-      REEF_TRY(comm_signal(c, data_slot(k, o.kind), epoch(o.kind, o.use), sk(k)));
+    PeerFlags f;
+    for (int r = 0; r < N; ++r) {
+      if (r == rank) continue;
+      for (const Use& i : ins) f.p[f.n++] = comm_counter(c, cons_slot(k, i.kind), r);
+      for (const Use& o : outs) f.p[f.n++] = comm_counter(c, data_slot(k, o.kind), r);
+    }
+    REEF_TRY(signal_peers(f, sk(k)));
     return cudaEventRecord(done.ev[k], sk(k)) == cudaSuccess ? kOk : kErrCuda;
   };
   // this rank's segment of region (k, kind) in every rank's arena (the [N][Tc][w]

@@ -145,6 +145,15 @@ inline PeerDst one_dst(void* p) {
   return d;
 }
 
+// Counters in peers' memory that one warp increments (system-scope atomics,
+// after a system-wide fence): a step's "delivered" / "consumed" signals.
+constexpr int kMaxFlags = 32;
+struct PeerFlags {
+  int n = 0;
+  unsigned int* p[kMaxFlags] = {};
+};
+int signal_peers(const PeerFlags& f, cudaStream_t stream);
+
 // quant.cu
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q,
                   long long ldq, float* x_scale, const float* row_max,

@@ -126,6 +126,13 @@ __global__ void __launch_bounds__(kQuantThreads)
     for (int d = 0; d < out.n; ++d) static_cast<float*>(out.p[d])[blockIdx.x] = m;
 }
 
+// Every earlier kernel on the stream has finished; the fence orders their
+// stores (peer stores included) before the increments.
+__global__ void signal_peers_kernel(PeerFlags f) {
+  __threadfence_system();
+  for (int i = threadIdx.x; i < f.n; i += blockDim.x) atomicAdd_system(f.p[i], 1u);
+}
+
 __global__ void push_f32_kernel(long long n, const float* __restrict__ src, PeerDst dst) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -229,6 +236,13 @@ int quantize_rows_to(long long rows, long long in, const float* x, const PeerDst
   for (int d = 0; d < x_q.n; ++d)
     if (x_q.p[d] == nullptr || reinterpret_cast<uintptr_t>(x_q.p[d]) % 4 != 0) return kErrInvalid;
   return quantize_vec4(rows, in, x, x_q, ldq, x_scale, row_max, stream);
+}
+
+int signal_peers(const PeerFlags& f, cudaStream_t stream) {
+  if (f.n == 0) return kOk;
+  if (f.n < 0 || f.n > kMaxFlags) return kErrInvalid;
+  signal_peers_kernel<<<1, 32, 0, stream>>>(f);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int push_f32(long long n, const float* src, const PeerDst& dst, cudaStream_t stream) {
