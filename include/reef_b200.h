@@ -406,9 +406,11 @@ typedef struct reef_b200_llama_layer {
  *    rank's OUTPUT rows over the full K.  Moves int8 activations instead of
  *    int32 partial sums (about a third of the bytes) and shards every
  *    element-wise step.  world must divide 8.  When the batch splits into 2
- *    or 4 groups of whole sequences, the forward pipelines over them: the
- *    collectives of one group run on the communicator's own stream while the
- *    other groups compute on `stream` (same result; the stream still orders
+ *    groups of whole sequences, the forward pipelines over them on the
+ *    communicator's compute streams, one group a step behind the other; the
+ *    kernels that produce exchanged data write it into every rank's memory
+ *    over NVLink, and stream-ordered counters in a symmetric arena say when it
+ *    has arrived and been consumed (same result; `stream` still orders
  *    everything before the call's last kernel). */
 #define REEF_B200_TP_ALLREDUCE 0
 #define REEF_B200_TP_ALLGATHER 1
