@@ -280,34 +280,6 @@ uint8_t* comm_peer_data(Comm* c, int r) {
   return c->peer[r] + flag_bytes(c->arena_slots, c->world);
 }
 
-int comm_signal(Comm* c, int slot, uint32_t value, cudaStream_t s) {
-  if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots) return kErrInvalid;
-  const StreamOps& ops = stream_ops();
-  const size_t off = (static_cast<size_t>(slot) * c->world + c->rank) * sizeof(uint32_t);
-  for (int r = 0; r < c->world; ++r) {
-    if (r == c->rank) continue;
-    // the default flags order the write after the stream's earlier work
-    // (its copies included) with a memory barrier
-    if (ops.write(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(c->peer[r] + off),
-                  value, 0) != CUDA_SUCCESS)
-      return kErrCuda;
-  }
-  return kOk;
-}
-
-int comm_wait(Comm* c, int slot, uint32_t value, cudaStream_t s) {
-  if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots) return kErrInvalid;
-  const StreamOps& ops = stream_ops();
-  for (int r = 0; r < c->world; ++r) {
-    if (r == c->rank) continue;
-    const size_t off = (static_cast<size_t>(slot) * c->world + r) * sizeof(uint32_t);
-    if (ops.wait(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(c->arena + off), value,
-                 CU_STREAM_WAIT_VALUE_GEQ) != CUDA_SUCCESS)
-      return kErrCuda;
-  }
-  return kOk;
-}
-
 unsigned int* comm_counter(Comm* c, int slot, int r) {
   if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots || r < 0 ||
       r >= c->world)

@@ -27,23 +27,19 @@ cudaStream_t comm_compute_stream(const Comm* c, int i);
 //
 // Every rank holds an arena of the same size, mapped into every peer's
 // address space (CUDA IPC), laid out alike: `slots` x world uint32 flags, then
-// data.  Kernels write into peers' data regions directly (comm_peer_data);
-// comm_signal writes a flag (slot, this rank) in every peer's arena after the
-// stream's earlier work (the write fences that work's stores first);
-// comm_wait makes a stream wait, in the stream's front end, until every
-// peer's flag (slot, peer) in the local arena reaches a value.  Values only
-// grow, so a flag never needs resetting.
+// data.  Kernels write into peers' data regions directly (comm_peer_data).
+// A slot's first flag word is a counter that peers increment with
+// signal_peers (ops.h) after their kernels; comm_wait_count makes a stream
+// wait, in its front end, until the local counter reaches a value.  Counts
+// only grow, so a counter never needs resetting.
 // (Re)creates the arena when it is smaller than asked; collective (every rank
 // calls it with the same sizes in the same order).
 int comm_arena_reserve(Comm* c, size_t data_bytes, int slots);
 uint8_t* comm_arena_data(Comm* c);  // this rank's data region
 // rank r's data region as mapped here (r = this rank: comm_arena_data)
 uint8_t* comm_peer_data(Comm* c, int r);
-int comm_signal(Comm* c, int slot, uint32_t value, cudaStream_t s);
-int comm_wait(Comm* c, int slot, uint32_t value, cudaStream_t s);
-// Counting form: a slot's counter (its first flag word) that every peer
-// increments.  comm_counter is the counter in rank r's arena (for
-// signal_peers); comm_wait_count waits until the local counter reaches value.
+// The counter of `slot` in rank r's arena (for signal_peers), and a stream
+// wait until the local counter of `slot` reaches `value`.
 unsigned int* comm_counter(Comm* c, int slot, int r);
 int comm_wait_count(Comm* c, int slot, uint32_t value, cudaStream_t s);
 // A counter the pipelined forward advances once per call (identical on all

@@ -1,4 +1,4 @@
-"""Tensor-parallel host logic on CPU ranks (gloo, world size 2).
+"""Tensor-parallel host logic on CPU ranks (gloo, world sizes 2 and 4).
 
 The GPU path shards with reef_b200.tp and runs the row-parallel algebra in
 layer.cpp over NCCL.  Here the same shard functions and the same algebra run
@@ -96,7 +96,7 @@ def _rowpar_case(rank, world):
 
 
 def _colpar_case(rank, world):
-    hq, hkv, hd, hidden, ffn = 4, 2, 16, 64, 96
+    hq, hkv, hd, hidden, ffn = 8, 4, 16, 64, 96
     x = ro.normal(5, (7, hidden))
     wqkv, sqkv = ro.quantize_rows(ro.normal(6, ((hq + 2 * hkv) * hd, hidden), 0, 0.02))
     rows = tp.qkv_rows(hq, hkv, hd, world, rank)
@@ -111,7 +111,7 @@ def _colpar_case(rank, world):
 
 
 def _gptneo_tp_case(rank, world):
-    """Config 2: the 256-d, 4-head, FFN-1024 block, TP=2, against TP=1."""
+    """Config 2: the 256-d, 4-head, FFN-1024 block, TP=world, against TP=1."""
     seq, d, heads, ffn = 32, 256, 4, 1024
     fw = block_float_weights(d, ffn, seed=80)
     p = ro.quantize_block(fw)
@@ -152,19 +152,22 @@ def _dead_peer_case(rank, world):
     return "no error"
 
 
-def test_rowpar_linear_bit_identical_to_tp1():
-    r = _run(_rowpar_case)
-    assert all(v == ("ok", True) for v in r.values()), r
+@pytest.mark.parametrize("world", [2, 4])
+def test_rowpar_linear_bit_identical_to_tp1(world):
+    r = _run(_rowpar_case, world=world)
+    assert len(r) == world and all(v == ("ok", True) for v in r.values()), r
 
 
-def test_colpar_rows_are_the_tp1_columns():
-    r = _run(_colpar_case)
-    assert all(v == ("ok", True) for v in r.values()), r
+@pytest.mark.parametrize("world", [2, 4])
+def test_colpar_rows_are_the_tp1_columns(world):
+    r = _run(_colpar_case, world=world)
+    assert len(r) == world and all(v == ("ok", True) for v in r.values()), r
 
 
-def test_gptneo_block_tp2_bit_identical_to_tp1():
-    r = _run(_gptneo_tp_case)
-    assert all(v == ("ok", True) for v in r.values()), r
+@pytest.mark.parametrize("world", [2, 4])
+def test_gptneo_block_tp_bit_identical_to_tp1(world):
+    r = _run(_gptneo_tp_case, world=world)
+    assert len(r) == world and all(v == ("ok", True) for v in r.values()), r
 
 
 def test_dead_peer_surfaces_as_error():
