@@ -47,6 +47,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace reef {
 
@@ -630,6 +631,29 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
   }
 }
 
+// M-blocks per raster group when the caller leaves it open.  A group walks
+// all n-blocks together, so B is streamed from DRAM once per group while
+// the group's A rows stay in L2: the largest power of two from 8 to 64 whose
+// A rows (group x 128 x K bytes) fit in 32 MiB.  Measured on config 3 under
+// the power cap: group 8 -> 64 takes the gate/up GEMM (B 90 MB) from 1.09 to
+// 1.00 ms, while the down GEMM (K 11008) is best at 16.
+// REEF_B200_GEMM_GROUP fixes it instead.
+int default_group_m(int K) {
+  static int fixed = -1;
+  if (fixed < 0) {
+    int x = 0;
+    if (const char* e = std::getenv("REEF_B200_GEMM_GROUP")) {
+      const int y = std::atoi(e);
+      if (y >= 1 && y <= 1024) x = y;
+    }
+    fixed = x;
+  }
+  if (fixed > 0) return fixed;
+  int g = 64;
+  while (g > 8 && static_cast<long long>(g) * kBM * K > (32ll << 20)) g /= 2;
+  return g;
+}
+
 template <int BN, int STAGES, int EPI>
 int launch(const GemmProblem& p, cudaStream_t stream) {
   using L = Layout<BN, STAGES>;
@@ -662,7 +686,8 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
   args.M = p.M;
   args.N = p.N;
   args.K = p.K;
-  if (args.group_m <= 0) args.group_m = 8;
+  // A's K spans every segment of an all-gathered operand
+  if (args.group_m <= 0) args.group_m = default_group_m(p.K * std::max(1, p.args.k_segments));
   args.err = device_error_ptr();
   {
     const uintptr_t y = reinterpret_cast<uintptr_t>(args.y);
