@@ -13,7 +13,10 @@ projections, plus the causal q.k and p.v of attention) over the device-timed
 steps (CUDA events, max over ranks), inputs resident in HBM (x is 256 MiB,
 the weights 200 MiB: both larger than L2, so no flush is needed between
 steps).  `e2e` is the same metric through the C ABI with host buffers: each
-step copies x from pinned host memory and y back inside the timed region.
+step copies x from pinned host memory and y back inside the timed region;
+as in a serving loop, one step's copies overlap its neighbours' forwards
+(a copy-in stream, the compute stream and a copy-out stream, two device
+buffers of each, ordered by events).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -362,24 +365,50 @@ def run_reef(args) -> int:
     flash_ms = statistics.mean(r[1] for r in spans)
     per_gemm = [statistics.mean(r[i] for r in spans) for i in (0, 2, 3, 4)]
 
-    # end to end through the C ABI with host buffers
+    # end to end through the C ABI with host buffers: step i copies x in on
+    # s_in, runs the forward on `stream` and reads y back on s_out; buffers
+    # alternate, so step i's copy-in overlaps step i - 1's forward and its
+    # copy-out overlaps step i + 1's forward (events order each reuse)
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
-    xd = torch.empty_like(x)
+    xd = [torch.empty_like(x) for _ in range(2)]
+    yd = [torch.empty_like(y) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event()
+    in_done = [ev(), ev()]
+    fwd_done = [ev(), ev()]
+    out_done = [ev(), ev()]
+
+    def e2e_step(i):
+        b = i % 2
+        if i >= 2:
+            s_in.wait_event(fwd_done[b])  # step i - 2's forward has read xd[b]
+        with torch.cuda.stream(s_in):
+            xd[b].copy_(xh, non_blocking=True)
+        in_done[b].record(s_in)
+        stream.wait_event(in_done[b])
+        if i >= 2:
+            stream.wait_event(out_done[b])  # step i - 2's y has left yd[b]
+        L.forward(xd[b], yd[b])
+        fwd_done[b].record(stream)
+        s_out.wait_event(fwd_done[b])
+        with torch.cuda.stream(s_out):
+            yh.copy_(yd[b], non_blocking=True)
+        out_done[b].record(s_out)
+
     e_steps = max(3, min(K_steps, 20))
-    for _ in range(2):
-        xd.copy_(xh, non_blocking=True)
-        L.forward(xd, y)
-        yh.copy_(y, non_blocking=True)
+    for i in range(2):
+        e2e_step(i)
     torch.cuda.synchronize(dev)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e_steps):
-        xd.copy_(xh, non_blocking=True)
-        L.forward(xd, y)
-        yh.copy_(y, non_blocking=True)
+    s_in.wait_event(e0)
+    for i in range(e_steps):
+        e2e_step(i)
+    stream.wait_event(out_done[(e_steps - 1) % 2])
+    stream.wait_event(out_done[e_steps % 2])
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1) / e_steps
