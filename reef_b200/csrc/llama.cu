@@ -354,7 +354,7 @@ int rmsnorm_quant(long long rows, int width, float eps, const float* x, const fl
 int rms_stats(long long rows, int width, int ranks, const float* x_local, const float* gain_local,
               const PeerDst& stats, cudaStream_t stream) {
   if (rows == 0) return kOk;
-  if (width % (4 * kChunks) != 0 || kChunks % ranks != 0) return kErrInvalid;
+  if (width % (4 * kChunks) != 0 || kChunks % ranks != 0 || !dst_ok(stats)) return kErrInvalid;
   const int cl = kChunks / ranks, P = per_thread(width);
   const unsigned grid = static_cast<unsigned>(rows);
   const int T = cl * 32;
@@ -369,7 +369,7 @@ int rms_apply_quant(long long rows, int width, int ranks, float eps, const float
                     const float* gain_local, const float* stats_all, const PeerDst& x_q,
                     float* x_scale, cudaStream_t stream) {
   if (rows == 0) return kOk;
-  if (width % (4 * kChunks) != 0 || kChunks % ranks != 0) return kErrInvalid;
+  if (width % (4 * kChunks) != 0 || kChunks % ranks != 0 || !dst_ok(x_q)) return kErrInvalid;
   const int cl = kChunks / ranks, P = per_thread(width);
   const unsigned grid = static_cast<unsigned>(rows);
   const int T = cl * 32;

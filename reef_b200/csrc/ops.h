@@ -144,6 +144,13 @@ inline PeerDst one_dst(void* p) {
   d.p[0] = p;
   return d;
 }
+// 1..kMaxDst destinations, none null
+inline bool dst_ok(const PeerDst& d) {
+  if (d.n < 1 || d.n > kMaxDst) return false;
+  for (int i = 0; i < d.n; ++i)
+    if (d.p[i] == nullptr) return false;
+  return true;
+}
 
 // Counters in peers' memory that one warp increments (system-scope atomics,
 // after a system-wide fence): a step's "delivered" / "consumed" signals.

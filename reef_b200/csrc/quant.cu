@@ -231,23 +231,25 @@ int quantize_rows_to(long long rows, long long in, const float* x, const PeerDst
                      long long ldq, float* x_scale, const float* row_max, cudaStream_t stream) {
   if (rows == 0) return kOk;
   if (in <= 0 || ldq < in || in % 4 != 0 || ldq % 4 != 0 || x == nullptr || x_scale == nullptr ||
-      x_q.n < 1 || x_q.n > kMaxDst || reinterpret_cast<uintptr_t>(x) % 16 != 0)
+      !dst_ok(x_q) || reinterpret_cast<uintptr_t>(x) % 16 != 0)
     return kErrInvalid;
   for (int d = 0; d < x_q.n; ++d)
-    if (x_q.p[d] == nullptr || reinterpret_cast<uintptr_t>(x_q.p[d]) % 4 != 0) return kErrInvalid;
+    if (reinterpret_cast<uintptr_t>(x_q.p[d]) % 4 != 0) return kErrInvalid;
   return quantize_vec4(rows, in, x, x_q, ldq, x_scale, row_max, stream);
 }
 
 int signal_peers(const PeerFlags& f, cudaStream_t stream) {
   if (f.n == 0) return kOk;
   if (f.n < 0 || f.n > kMaxFlags) return kErrInvalid;
+  for (int i = 0; i < f.n; ++i)
+    if (f.p[i] == nullptr) return kErrInvalid;
   signal_peers_kernel<<<1, 32, 0, stream>>>(f);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int push_f32(long long n, const float* src, const PeerDst& dst, cudaStream_t stream) {
   if (n == 0) return kOk;
-  if (n < 0 || src == nullptr || dst.n < 1 || dst.n > kMaxDst) return kErrInvalid;
+  if (n < 0 || src == nullptr || !dst_ok(dst)) return kErrInvalid;
   push_f32_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(n, src, dst);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
@@ -255,7 +257,7 @@ int push_f32(long long n, const float* src, const PeerDst& dst, cudaStream_t str
 int row_absmax_to(long long rows, long long in, const float* x, const PeerDst& row_max,
                   cudaStream_t stream) {
   if (rows == 0) return kOk;
-  if (in <= 0 || x == nullptr || row_max.n < 1 || row_max.n > kMaxDst) return kErrInvalid;
+  if (in <= 0 || x == nullptr || !dst_ok(row_max)) return kErrInvalid;
   row_absmax_kernel<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
       static_cast<int>(in), x, row_max);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
