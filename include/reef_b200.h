@@ -251,6 +251,24 @@ int reef_b200_attention_heads_int8(size_t heads, size_t query_len, size_t key_le
                                    size_t out_stride, size_t out_head,
                                    reef_b200_stream_t stream);
 
+/* ---- output projection and greedy choice (model.hpp:86-112, 32-42) ------ */
+
+/* matvec_rows_f32 (kernels.hpp:48-52): y[c] = sum over k, in order, of
+ * x[k] * w[c][k], for w [out][in] fp32 in its natural layout (GPT-Neo's
+ * lm_head reuses the token embedding table this way); reef's float linear
+ * (operator/linear.hpp:75-84, tensor.hpp:179-192): each sum starts at 0 and
+ * every product and sum is rounded on its own, so y is bit-identical.  A
+ * product or sum that is infinite or NaN (the engine throws
+ * std::overflow_error, util.hpp:81-131) records 0x301 in the device error
+ * word (reef_b200_device_error).  x [in], y [out] fp32. */
+int reef_b200_matvec_rows_f32(size_t out, size_t in, const float* w, const float* x, float* y,
+                              reef_b200_stream_t stream);
+/* argmax_f32 (kernels.hpp:89-90; the engine's argmax, model.hpp:32-42): the
+ * index of the first largest of x [n] fp32, written to *index (device
+ * uint32).  Ties give the lowest index; a NaN never wins unless it is x[0]
+ * (the engine's scan then keeps 0).  n in [1, 2^32 - 1]. */
+int reef_b200_argmax_f32(size_t n, const float* x, uint32_t* index, reef_b200_stream_t stream);
+
 /* ---- int8 flash attention (the fast head) ------------------------------- */
 
 /* Packs one QKV projection output for the flash head.  qkv [batch*seq]

@@ -90,6 +90,10 @@ def lib() -> C.CDLL:
         L.ro_layernorm_f32.argtypes = [_sz, _sz, _f32p, _f32p, _f32p, C.c_float,
                                        _f32p]
         L.ro_gelu_f32.argtypes = [_sz, _f32p, _f32p]
+        L.ro_matvec_rows_f32.argtypes = [_sz, _sz, _f32p, _f32p, _f32p]
+        L.ro_matvec_rows_f32.restype = C.c_int
+        L.ro_argmax_f32.argtypes = [_sz, _f32p]
+        L.ro_argmax_f32.restype = _sz
         L.ro_gptneo_block_w8a8.argtypes = (
             [_sz, _sz, _sz, _sz, _sz, C.c_float, _f32p, _f32p, _f32p]
             + [_i8p, _f32p] * 3 + [_i8p, _f32p, _f32p, _f32p, _f32p]
@@ -126,6 +130,8 @@ def ref() -> C.CDLL:
                                           _f32p, _f32p, _f32p]
         R.ref_block_w8a8.argtypes = ([_sz, _sz, _sz, _sz, _sz, C.c_int,
                                       C.c_float] + [_f32p] * 15)
+        R.ref_matvec_rows_f32.argtypes = [_sz, _sz, _f32p, _f32p, _f32p]
+        R.ref_argmax_f32.argtypes = [_sz, _f32p, C.POINTER(_sz)]
     return _ref
 
 
@@ -302,6 +308,23 @@ def layernorm(x, gain, shift, eps: float = 1e-5) -> np.ndarray:
                            _p(np.ascontiguousarray(shift, np.float32), _f32p),
                            eps, _p(y, _f32p))
     return y
+
+
+def matvec_rows_f32(w, x):
+    """reef's lm_head row, linear(x, w) with w [out][in] (model.hpp:107-110):
+    returns (y [out] fp32, ok) -- ok False where the engine would throw."""
+    w = np.ascontiguousarray(w, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    out, n = w.shape
+    y = np.empty(out, np.float32)
+    bad = lib().ro_matvec_rows_f32(out, n, _p(w, _f32p), _p(x, _f32p), _p(y, _f32p))
+    return y, bad == 0
+
+
+def argmax_f32(x) -> int:
+    """argmax (model.hpp:32-42): the first index of the largest value."""
+    x = np.ascontiguousarray(x, np.float32)
+    return int(lib().ro_argmax_f32(x.size, _p(x, _f32p)))
 
 
 def gelu(x) -> np.ndarray:

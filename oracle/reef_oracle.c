@@ -460,6 +460,37 @@ void ro_add_f32(size_t n, const float* a, const float* b, float* y) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* lm_head and greedy choice: model.hpp:86-112, 32-42                        */
+/* ------------------------------------------------------------------------ */
+
+int ro_matvec_rows_f32(size_t out, size_t in, const float* w, const float* x, float* y) {
+    /* linear(row, w) for one row: operator/linear.hpp:75-84 through
+       tensor.hpp:179-192 -- the sum starts at 0 and adds each product in k
+       order; util.hpp:81-131 reject a non-finite product or sum (1 here) */
+    int bad = 0;
+    for (size_t c = 0; c < out; ++c) {
+        const float* wr = w + c * in;
+        float sum = 0.0f;
+        for (size_t k = 0; k < in; ++k) {
+            const float p = x[k] * wr[k];
+            if (!isfinite(p)) bad = 1;
+            sum = sum + p;
+            if (!isfinite(sum)) bad = 1;
+        }
+        y[c] = sum;
+    }
+    return bad;
+}
+
+size_t ro_argmax_f32(size_t n, const float* x) {
+    /* model.hpp:32-42: the best index moves only on a strictly greater value */
+    size_t best = 0;
+    for (size_t i = 1; i < n; ++i)
+        if (x[i] > x[best]) best = i;
+    return best;
+}
+
+/* ------------------------------------------------------------------------ */
 /* GPT-Neo W8A8 block, operator/block.hpp:97-108                             */
 /* ------------------------------------------------------------------------ */
 

@@ -142,6 +142,9 @@ void ro_layernorm_f32(size_t rows, size_t width, const float* x,
 void ro_gelu_f32(size_t n, const float* x, float* y);
 /* residual_add, operator/block.hpp:27-39. */
 void ro_add_f32(size_t n, const float* a, const float* b, float* y);
+/* GPT-Neo's lm_head row (linear with w [out][in]) and argmax */
+int ro_matvec_rows_f32(size_t out, size_t in, const float* w, const float* x, float* y);
+size_t ro_argmax_f32(size_t n, const float* x);
 
 /* ---- GPT-Neo W8A8 block (operator/block.hpp:97-108) ------------------- */
 

@@ -12,6 +12,7 @@
 // "reference").  Every wrapper catches the engine's exceptions and returns
 // -1 (std::invalid_argument / length_error) or -2 (std::overflow_error).
 #include "inference_engine/int8.hpp"
+#include "inference_engine/model.hpp"
 #include "inference_engine/operator/attention.hpp"
 #include "inference_engine/operator/block.hpp"
 #include "inference_engine/operator/linear.hpp"
@@ -236,6 +237,20 @@ int ref_block_w8a8(std::size_t seq, std::size_t d, std::size_t heads,
         const ie::Tensor<float> r = block.forward(matrix(seq, d, x));
         std::memcpy(y, r.values.data(), seq * d * sizeof(float));
     });
+}
+
+// GPT-Neo's lm_head for one row: linear<float>(row, wte) (model.hpp:107-110).
+int ref_matvec_rows_f32(std::size_t out, std::size_t in, const float* w, const float* x,
+                        float* y) {
+    return guarded([&] {
+        const ie::Tensor<float> r = ie::linear<float>(matrix(1, in, x), matrix(out, in, w));
+        std::memcpy(y, r.values.data(), out * sizeof(float));
+    });
+}
+
+// argmax (model.hpp:32-42).
+int ref_argmax_f32(std::size_t n, const float* x, std::size_t* index) {
+    return guarded([&] { *index = ie::argmax(vector1(n, x)); });
 }
 
 } // extern "C"

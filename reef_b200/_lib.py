@@ -29,6 +29,8 @@ SIGNATURES = {
     "reef_b200_check_device": ([], _i),
     "reef_b200_device_error": ([_p], _i),
     "reef_b200_quantize_rows": ([_sz, _sz, _p, _p, _p, _p], _i),
+    "reef_b200_matvec_rows_f32": ([_sz, _sz, _p, _p, _p, _p], _i),
+    "reef_b200_argmax_f32": ([_sz, _p, _p, _p], _i),
     "reef_b200_pack_weight_i8": ([_sz, _sz, _p, _p, _p], _i),
     "reef_b200_pad_rows_i8": ([_sz, _sz, _p, _p, _p], _i),
     "reef_b200_linear_w8a8": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p], _i),

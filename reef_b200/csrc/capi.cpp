@@ -66,6 +66,23 @@ int reef_b200_device_error(int* code) {
   return read_device_error(code);
 }
 
+int reef_b200_matvec_rows_f32(size_t out, size_t in, const float* w, const float* x, float* y,
+                              reef_b200_stream_t stream) {
+  if (out == 0 || in == 0 || !w || !x || !y) return REEF_B200_ERR_INVALID;
+  if (out > (1ull << 40) || in > (1ull << 40) || out > (1ull << 62) / in)
+    return REEF_B200_ERR_TOO_LARGE;
+  if (int rc = check_device()) return rc;
+  return matvec_rows_f32(static_cast<long long>(out), static_cast<long long>(in), w, x, y,
+                         S(stream));
+}
+
+int reef_b200_argmax_f32(size_t n, const float* x, uint32_t* index, reef_b200_stream_t stream) {
+  if (n == 0 || !x || !index) return REEF_B200_ERR_INVALID;
+  if (n > 0xffffffffull) return REEF_B200_ERR_TOO_LARGE;
+  if (int rc = check_device()) return rc;
+  return argmax_f32(static_cast<long long>(n), x, index, S(stream));
+}
+
 int reef_b200_quantize_rows(size_t rows, size_t in, const float* x, int8_t* x_q,
                             float* x_scale, reef_b200_stream_t stream) {
   if (rows == 0) return REEF_B200_OK;

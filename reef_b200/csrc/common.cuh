@@ -22,6 +22,8 @@ enum DeviceError : int {
   kDevTimeoutAccEmpty = 0x104, // MMA waited too long for the epilogue
   kDevTimeoutDrain = 0x105,    // final drain of the MMA pipe
   kDevTimeoutPeer = 0x106,     // a peer flag never arrived
+  kDevBadPosition = 0x201,     // a decode position outside the cache
+  kDevNonFinite = 0x301,       // a float product or sum the engine would reject
 };
 
 // A wait gives up after this long (ns of %globaltimer).

@@ -618,7 +618,7 @@ __global__ void decode_rope_append_kernel(int batch, int hq, int hkv, int max_le
   const int b = gw / heads, hh = gw % heads;
   const int pos = positions[b];
   if (pos < 0 || pos >= max_len) {
-    if (lane == 0 && hh == 0) record_error(err, 0x201);
+    if (lane == 0 && hh == 0) record_error(err, kDevBadPosition);
     return;
   }
   if (hh == 0 && lane == 0) lens[b] = pos + 1;

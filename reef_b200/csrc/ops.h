@@ -161,6 +161,11 @@ struct PeerFlags {
 };
 int signal_peers(const PeerFlags& f, cudaStream_t stream);
 
+// lm_head.cu -- reef's float linear(x, w) for one row (bit-identical) and argmax
+int matvec_rows_f32(long long out, long long in, const float* w, const float* x, float* y,
+                    cudaStream_t stream);
+int argmax_f32(long long n, const float* x, uint32_t* index, cudaStream_t stream);
+
 // quant.cu
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q,
                   long long ldq, float* x_scale, const float* row_max,

@@ -52,6 +52,23 @@ def quantize_rows(x: torch.Tensor):
     return x_q, xs
 
 
+def matvec_rows_f32(w: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """reef_kernels::matvec_rows_f32 (kernels.hpp:48-52): y[c] = sum over k, in
+    order, of x[k] * w[c][k] (GPT-Neo's lm_head), bit-identical to the engine."""
+    out, k = w.shape
+    y = torch.empty((out,), dtype=torch.float32, device=w.device)
+    _lib.call("reef_b200_matvec_rows_f32", out, k, _ptr(w), _ptr(x), _ptr(y), _stream())
+    return y
+
+
+def argmax_f32(x: torch.Tensor) -> torch.Tensor:
+    """reef_kernels::argmax_f32 (kernels.hpp:89-90): index of the first largest
+    value, as one device int32 element holding the uint32 index."""
+    idx = torch.empty((1,), dtype=torch.int32, device=x.device)
+    _lib.call("reef_b200_argmax_f32", x.numel(), _ptr(x), _ptr(idx), _stream())
+    return idx
+
+
 def pack_weight_i8(wt: torch.Tensor) -> torch.Tensor:
     """Coral weight [in][out] -> K-major [out][kpad(in)]."""
     k, n = wt.shape

@@ -8,9 +8,10 @@ C++17, ``-ffp-contract=off``; the reference's CMake is not run), runs it into a
 temporary directory, parses the headers and stores every array and case table
 as ``tests/golden/<test>.npz`` plus ``tests/golden/<test>_cases.json``.
 
-Only the headers on the W8A8 / int8 / attention path are kept: ``linear``,
-``int8``, ``attention``, ``math`` (exp_nonpositive) and ``layernorm`` (used by
-the GPT-Neo block).  The committed fixtures are what the tests read; this
+Only the headers on the W8A8 / int8 / attention path and its lm_head are
+kept: ``linear`` (matvec_rows_f32 included), ``int8``, ``attention``, ``math``
+(exp_nonpositive), ``layernorm`` (used by the GPT-Neo block) and
+``elementwise`` (argmax).  The committed fixtures are what the tests read; this
 script needs the reference checkout and runs here, never on a GPU box.
 
 Usage:  python tests/golden/make_golden.py [--reference /root/reference]
@@ -28,7 +29,7 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-KEEP = ("linear", "int8", "attention", "math", "layernorm")
+KEEP = ("linear", "int8", "attention", "math", "layernorm", "elementwise")
 
 _DTYPES = {
     "float": np.float32,

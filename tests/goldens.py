@@ -31,6 +31,8 @@ FIELDS = {
     "kTanh": ("n", "x", "y"),
     "kGelu": ("n", "x", "y"),
     "kLayerNorm": ("rows", "width", "eps", "x", "gain", "shift", "y"),
+    "kMatvec": ("out", "in", "w", "x", "y"),
+    "kArgmax": ("n", "x", "index"),
 }
 
 

@@ -67,6 +67,20 @@ def test_attention_f32_matches_reef_goldens():
         np.testing.assert_array_equal(bits(y.ravel()), bits(c["y"]))
 
 
+def test_matvec_matches_reef_goldens():
+    for c in goldens.cases("linear", "kMatvec"):
+        y, ok = ro.matvec_rows_f32(c["w"].reshape(c["out"], c["in"]), c["x"])
+        assert ok
+        np.testing.assert_array_equal(bits(y), bits(c["y"]))
+
+
+def test_argmax_matches_reef_goldens():
+    cs = goldens.cases("elementwise", "kArgmax")
+    assert len(cs) == 3  # random, ties (first of two maxima), signed zeros
+    for c in cs:
+        assert ro.argmax_f32(c["x"]) == c["index"]
+
+
 def test_exp_tanh_gelu_match_reef_goldens():
     (e,) = goldens.cases("math", "kExp")
     np.testing.assert_array_equal(bits(ro.exp_nonpositive(e["x"])), bits(e["y"]))
@@ -209,3 +223,36 @@ def block_float_weights(d, ffn, seed):
         "wproj": ro.normal(seed + 8, (d, ffn), 0, 0.02),
         "bproj": ro.normal(seed + 9, (d,), 0, 0.02),
     }
+
+
+@needs_ref
+def test_lm_head_and_argmax_match_engine():
+    R = ro.ref()
+    rng = np.random.default_rng(11)
+    for out, n in [(1, 1), (129, 33), (500, 256)]:
+        w = rng.uniform(-0.5, 0.5, (out, n)).astype(np.float32)
+        x = rng.uniform(-2.0, 2.0, n).astype(np.float32)
+        y, ok = ro.matvec_rows_f32(w, x)
+        want = np.empty(out, np.float32)
+        rc = R.ref_matvec_rows_f32(out, n, ro._p(w, ro._f32p), ro._p(x, ro._f32p),
+                                   ro._p(want, ro._f32p))
+        assert ok and rc == 0
+        np.testing.assert_array_equal(bits(y), bits(want))
+    # a product that overflows: the engine throws, the restatement says so
+    w = np.full((3, 4), 1e30, np.float32)
+    x = np.full(4, 1e30, np.float32)
+    _, ok = ro.matvec_rows_f32(w, x)
+    want = np.empty(3, np.float32)
+    rc = R.ref_matvec_rows_f32(3, 4, ro._p(w, ro._f32p), ro._p(x, ro._f32p), ro._p(want, ro._f32p))
+    assert not ok and rc == -2
+    import ctypes as C
+    cases = [rng.uniform(-10, 10, 1000).astype(np.float32),
+             np.array([1.0, 3.0, 3.0, 2.0], np.float32),
+             np.array([np.nan, 5.0, 1.0], np.float32),
+             np.array([1.0, np.nan, 5.0, np.nan], np.float32),
+             np.array([-np.inf, -np.inf], np.float32),
+             np.array([0.0, -0.0], np.float32), np.array([-0.0, 0.0], np.float32)]
+    for v in cases:
+        idx = C.c_size_t()
+        assert R.ref_argmax_f32(v.size, ro._p(v, ro._f32p), C.byref(idx)) == 0
+        assert ro.argmax_f32(v) == idx.value, v
