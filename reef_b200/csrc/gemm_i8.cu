@@ -42,6 +42,7 @@
 // Double-buffered accumulators let the epilogue of tile i overlap the MMAs of
 // tile i+1.  No TMA multicast anywhere.
 #include "common.cuh"
+#include "exact_math.cuh"
 #include "ops.h"
 
 #include <cuda_fp16.h>
@@ -579,6 +580,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
                   o[e] = __fmul_rn(__int2float_rn(static_cast<int32_t>(av[e])),
                                    __fmul_rn(rsv, ws[e]));
                   if (args.bias_f != nullptr) o[e] = __fadd_rn(o[e], bf[e]);
+                  if (args.gelu) o[e] = gelu_dev(o[e]);  // MLP c_fc + gelu, mlp.hpp:108-133
                 }
                 if (args.residual != nullptr) {  // residual_add(input, sublayer), block.hpp:27-39
                   o[0] = __fadd_rn(res[it].x, o[0]);
@@ -689,6 +691,8 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
   // A's K spans every segment of an all-gathered operand
   if (args.group_m <= 0) args.group_m = default_group_m(p.K * std::max(1, p.args.k_segments));
   args.err = device_error_ptr();
+  // gelu is an option of the fp32 epilogue of whole (unsplit) outputs only
+  if (args.gelu && (EPI != kEpiF32W8A8 || splits > 1)) return kErrInvalid;
   {
     const uintptr_t y = reinterpret_cast<uintptr_t>(args.y);
     const int align = EPI == kEpiI8Shift ? 4 : 16;

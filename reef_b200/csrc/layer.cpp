@@ -68,7 +68,7 @@ GemmProblem problem(long long rows, int in, int out, const int8_t* a, const int8
 
 int gemm_w8a8_f32(long long rows, int in, int out, const int8_t* xq, const float* xs,
                   const int8_t* w, const float* ws, const float* bias, const float* residual,
-                  float* y, cudaStream_t st) {
+                  float* y, cudaStream_t st, bool gelu = false) {
   GemmProblem p = problem(rows, in, out, xq, w);
   p.args.x_scale = xs;
   p.args.w_scale = ws;
@@ -76,6 +76,7 @@ int gemm_w8a8_f32(long long rows, int in, int out, const int8_t* xq, const float
   p.args.residual = residual;
   p.args.y = y;
   p.args.ldy = out;
+  p.args.gelu = gelu ? 1 : 0;
   return gemm_i8(p, kEpiF32W8A8, st);
 }
 
@@ -1089,12 +1090,12 @@ int reef_b200_gptneo_block_forward(const reef_b200_gptneo_block* B, const float*
     REEF_TRY(rowpar_linear(c, T, dl, d, quant, absmax, B->wo, B->so, B->bo, x, b.xq, b.xs,
                            b.row_max, b.acc, b.a, st));
   }
-  // MLP::forward (mlp.hpp:108-133): ln_2, c_fc (column-parallel) + gelu,
-  // c_proj (row-parallel) with the second residual fused in.
+  // MLP::forward (mlp.hpp:108-133): ln_2, c_fc (column-parallel) with gelu
+  // in its epilogue, c_proj (row-parallel) with the second residual fused in.
   REEF_TRY(layernorm_exact(T, d, B->eps, b.a, B->ln2_g, B->ln2_b, b.h, st));
   REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
-  REEF_TRY(gemm_w8a8_f32(T, d, F, b.xq, b.xs, B->wfc, B->sfc, B->bfc, nullptr, b.f, st));
-  REEF_TRY(gelu_exact(T * F, b.f, b.f, st));
+  REEF_TRY(gemm_w8a8_f32(T, d, F, b.xq, b.xs, B->wfc, B->sfc, B->bfc, nullptr, b.f, st,
+                         /*gelu=*/true));
   {
     auto quant = [&](const float* rm) {
       return quantize_rows(T, F, b.f, b.xq, static_cast<long long>(kpad(F)), b.xs, rm, st);

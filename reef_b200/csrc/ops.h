@@ -72,6 +72,7 @@ struct GemmArgs {
   long long split_stride; // elements between the partial outputs of two splits
   int vec_ok;             // 16-byte (int8: 4-byte) output stores allowed (launcher)
   int max_ctas;           // > 0: at most this many persistent CTAs (SMs left to others)
+  int gelu;               // kEpiF32W8A8: y = gelu(dequant + bias), reef's tanh form, before any residual
   int* err;               // device error word (set by the launcher)
 };
 
