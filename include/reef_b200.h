@@ -497,6 +497,37 @@ int reef_b200_gptneo_block_forward(const reef_b200_gptneo_block* block, const fl
                                    float* y, void* workspace, size_t workspace_bytes,
                                    reef_b200_stream_t stream);
 
+/* ---- reef's packed model ("REEF" blob v1, model_blob.hpp:18-66) --------- */
+
+/* The header of a blob written by reef's packer (coral/host/pack_model.hpp:
+ * 88-160).  precision: 0 float, 1 W8A8 (model_blob.hpp:23-26); wte, wpe,
+ * ln_f_weight, ln_f_bias: byte offsets of those float arrays in the blob
+ * ([vocab][hidden], [max_positions][hidden], [hidden], [hidden]); the token
+ * embedding rows are also the tied lm_head (reef_b200_matvec_rows_f32). */
+typedef struct reef_b200_blob_info {
+  uint32_t precision;
+  size_t vocab, max_positions, hidden, layers, heads, inner, window;
+  float eps;
+  size_t wte, wpe, ln_f_weight, ln_f_bias;
+} reef_b200_blob_info;
+/* Validates a blob in HOST memory (magic "REEF", version 1, every array
+ * inside total_bytes <= bytes and 16-byte aligned) and reads its header.
+ * Needs no GPU.  REEF_B200_ERR_INVALID for a malformed blob. */
+int reef_b200_blob_read_info(const void* blob, size_t bytes, reef_b200_blob_info* info);
+/* Device bytes one layer takes in reef_b200_blob_load_layer's arena. */
+size_t reef_b200_blob_layer_bytes(const reef_b200_blob_info* info);
+/* Copies layer `layer` of a W8A8 blob (host memory) into `arena` (device,
+ * 256-byte aligned, >= reef_b200_blob_layer_bytes), repacking every [in][out]
+ * int8 weight into the K-major [out][kpad(in)] layout, and fills the
+ * block's weights and shape (heads, head_dim, ffn, window: the blob's window
+ * for a local layer, 0 for a global one; eps); seq and comm are the
+ * caller's.  A float blob is REEF_B200_ERR_UNSUPPORTED (these kernels run
+ * W8A8 blocks).  Asynchronous on `stream`; the blob may be reused once the
+ * call returns. */
+int reef_b200_blob_load_layer(const void* blob, size_t bytes, size_t layer, void* arena,
+                              size_t arena_bytes, reef_b200_gptneo_block* block,
+                              reef_b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

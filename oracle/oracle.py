@@ -132,6 +132,8 @@ def ref() -> C.CDLL:
                                       C.c_float] + [_f32p] * 15)
         R.ref_matvec_rows_f32.argtypes = [_sz, _sz, _f32p, _f32p, _f32p]
         R.ref_argmax_f32.argtypes = [_sz, _f32p, C.POINTER(_sz)]
+        R.ref_pack_random_gpt_neo.argtypes = ([_sz] * 7 + [C.c_uint32, C.POINTER(C.c_uint8), _sz,
+                                               C.POINTER(_sz)])
     return _ref
 
 

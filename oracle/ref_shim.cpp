@@ -19,6 +19,7 @@
 #include "inference_engine/quant.hpp"
 #include "inference_engine/tensor.hpp"
 #include "inference_engine/weights.hpp"
+#include "pack_model.hpp"
 
 #include <cstddef>
 #include <cstdint>
@@ -245,6 +246,31 @@ int ref_matvec_rows_f32(std::size_t out, std::size_t in, const float* w, const f
     return guarded([&] {
         const ie::Tensor<float> r = ie::linear<float>(matrix(1, in, x), matrix(out, in, w));
         std::memcpy(y, r.values.data(), out * sizeof(float));
+    });
+}
+
+// A random GPT-Neo (weights.hpp:407), quantize_w8a8 (weights.hpp:460), then
+// reef's packer for the firmware, W8A8 (coral/host/pack_model.hpp:88-160):
+// the "REEF" v1 blob.  *size gets its length; cap bytes at out are filled.
+int ref_pack_random_gpt_neo(std::size_t vocab, std::size_t positions, std::size_t hidden,
+                            std::size_t layers, std::size_t heads, std::size_t inner,
+                            std::size_t window, std::uint32_t seed, std::uint8_t* out,
+                            std::size_t cap, std::size_t* size) {
+    return guarded([&] {
+        ie::GptNeoConfig config;
+        config.vocab_size = vocab;
+        config.max_positions = positions;
+        config.hidden_size = hidden;
+        config.num_layers = layers;
+        config.num_heads = heads;
+        config.inner_size = inner;
+        config.window_size = window;
+        ie::ModelWeights<float> weights = ie::random_gpt_neo(config, seed);
+        ie::quantize_w8a8(weights);
+        const std::vector<std::uint8_t> blob =
+            coral_host::pack_gpt_neo(weights, reef_kernels::Precision::kW8A8);
+        *size = blob.size();
+        if (blob.size() <= cap) std::memcpy(out, blob.data(), blob.size());
     });
 }
 

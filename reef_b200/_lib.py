@@ -31,6 +31,9 @@ SIGNATURES = {
     "reef_b200_quantize_rows": ([_sz, _sz, _p, _p, _p, _p], _i),
     "reef_b200_matvec_rows_f32": ([_sz, _sz, _p, _p, _p, _p], _i),
     "reef_b200_argmax_f32": ([_sz, _p, _p, _p], _i),
+    "reef_b200_blob_read_info": ([_p, _sz, _p], _i),
+    "reef_b200_blob_layer_bytes": ([_p], _sz),
+    "reef_b200_blob_load_layer": ([_p, _sz, _sz, _p, _sz, _p, _p], _i),
     "reef_b200_pack_weight_i8": ([_sz, _sz, _p, _p, _p], _i),
     "reef_b200_pad_rows_i8": ([_sz, _sz, _p, _p, _p], _i),
     "reef_b200_linear_w8a8": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p], _i),
@@ -94,6 +97,14 @@ class GptNeoBlockDesc(C.Structure):
                 ("wo", _p), ("so", _p), ("bo", _p), ("ln2_g", _p), ("ln2_b", _p),
                 ("wfc", _p), ("sfc", _p), ("bfc", _p), ("wproj", _p), ("sproj", _p),
                 ("bproj", _p), ("comm", _p)]
+
+
+class BlobInfo(C.Structure):
+    """reef_b200_blob_info (include/reef_b200.h)."""
+    _fields_ = [("precision", C.c_uint32), ("vocab", _sz), ("max_positions", _sz),
+                ("hidden", _sz), ("layers", _sz), ("heads", _sz), ("inner", _sz),
+                ("window", _sz), ("eps", C.c_float), ("wte", _sz), ("wpe", _sz),
+                ("ln_f_weight", _sz), ("ln_f_bias", _sz)]
 
 
 class ReefError(RuntimeError):

@@ -1,0 +1,63 @@
+"""reef's packed model ("REEF" blob v1) read through the C ABI, on the CPU.
+
+The fixture was written by reef's own packer (tests/golden/make_blob.py).
+reef_b200_blob_read_info must return its header; malformed blobs (wrong
+magic or version, truncated, an array running past the end or off its
+16-byte alignment) must be refused.  Reading needs no GPU.
+"""
+import ctypes as C
+
+from reef_b200 import _lib
+from tests import blob_fixture as BF
+
+
+def read(b: bytes):
+    info = _lib.BlobInfo()
+    buf = C.create_string_buffer(b, len(b))
+    rc = _lib.lib().reef_b200_blob_read_info(buf, len(b), C.byref(info))
+    return rc, info
+
+
+def test_header_of_reef_packed_blob():
+    b = BF.data()
+    cfg = BF.config()
+    h = BF.header(b)
+    rc, info = read(b)
+    assert rc == 0
+    assert h["magic"] == 0x46454552 and h["version"] == 1 and h["total_bytes"] == len(b)
+    assert info.precision == 1  # W8A8
+    assert (info.vocab, info.max_positions, info.hidden, info.layers, info.heads, info.inner,
+            info.window) == (cfg["vocab"], cfg["positions"], cfg["hidden"], cfg["layers"],
+                             cfg["heads"], cfg["inner"], cfg["window"])
+    assert abs(info.eps - 1e-5) < 1e-12
+    assert (info.wte, info.wpe, info.ln_f_weight, info.ln_f_bias) == (
+        h["wte"], h["wpe"], h["ln_f_weight"], h["ln_f_bias"])
+    need = _lib.lib().reef_b200_blob_layer_bytes(C.byref(info))
+    d, f = cfg["hidden"], cfg["inner"]
+    assert need >= 4 * d * d + 2 * d * f + 4 * (11 * d + 2 * f)
+
+
+def test_malformed_blobs_are_refused():
+    b = bytearray(BF.data())
+    h = BF.header(bytes(b))
+    bad = []
+    x = bytearray(b)
+    x[0] ^= 1  # magic
+    bad.append(bytes(x))
+    x = bytearray(b)
+    x[4] = 2  # version
+    bad.append(bytes(x))
+    bad.append(bytes(b[: len(b) - 16]))  # shorter than total_bytes
+    bad.append(bytes(b[:40]))  # shorter than the header
+    x = bytearray(b)
+    x[44:48] = (h["wte"] + 4).to_bytes(4, "little")  # wte off its 16-byte alignment
+    bad.append(bytes(x))
+    x = bytearray(b)
+    x[48:52] = (len(b) - 16).to_bytes(4, "little")  # wpe runs past the end
+    bad.append(bytes(x))
+    x = bytearray(b)
+    x[24:28] = (0).to_bytes(4, "little")  # no layers
+    bad.append(bytes(x))
+    for blob in bad:
+        rc, _ = read(blob)
+        assert rc == 1, rc  # REEF_B200_ERR_INVALID
