@@ -1,7 +1,8 @@
 // blob.cpp -- loading reef's packed GPT-Neo model ("REEF" blob v1).
 //
 // The layout is reef's firmware format (coral/include/reef_kernels/
-// model_blob.hpp:18-66; written by coral/host/pack_model.hpp:88-160):
+// model_blob.hpp:18-66, read in place by coral/firmware/gpt_neo.cc:61-97;
+// written by coral/host/pack_model.hpp:88-160):
 // little-endian, a fixed header, every array at a 16-byte-aligned byte offset,
 // linear weights stored transposed ([in][out]) with float row scales for
 // W8A8, and a table of per-layer records.  The structs below restate that
