@@ -152,6 +152,9 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // a programmatic dependent (the split-K reduce) may be scheduled now; it
+  // waits for this grid's completion and memory before reading the outputs
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -715,6 +718,9 @@ __global__ void splitk_reduce_kernel(int splits, int M, int N, const int32_t* __
   __shared__ int32_t tile[32][33];
   const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  // launched early (programmatic dependent launch): wait for the split-K
+  // GEMM's completion and memory before reading its partials
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int n = n0 + ty + 8 * i, m = m0 + tx;
@@ -747,8 +753,11 @@ __global__ void splitk_reduce_kernel(int splits, int M, int N, const int32_t* __
 int skinny_splits(int n, int k) {
   const int tiles = (n + kBM - 1) / kBM;
   const int nk = (k + kBK - 1) / kBK;
-  const int want = (num_sms() + tiles - 1) / tiles;
-  return std::max(1, std::min(want, std::max(1, nk / 2)));
+  // one wave: tiles x splits <= SMs.  A second, partial wave would give some
+  // CTAs two items, doubling the slowest CTA's share; at least two k-blocks
+  // per split.
+  const int fit = num_sms() / tiles;
+  return std::max(1, std::min(fit, std::max(1, nk / 2)));
 }
 
 }  // namespace
@@ -778,15 +787,29 @@ int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int ep
   p.args.ldy = m;
   const int rc = m <= 64 ? launch<64, 8, kEpiI32>(p, stream) : launch<128, 6, kEpiI32>(p, stream);
   if (rc) return rc;
-  dim3 grid(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>((m + 31) / 32));
-  if (epilogue == kEpiF32W8A8) {
-    splitk_reduce_kernel<kEpiF32W8A8><<<grid, dim3(32, 8), 0, stream>>>(
-        splits, m, n, static_cast<const int32_t*>(partial), x_scale, w_scale, bias, residual, y);
-  } else {
-    splitk_reduce_kernel<kEpiI32><<<grid, dim3(32, 8), 0, stream>>>(
-        splits, m, n, static_cast<const int32_t*>(partial), nullptr, nullptr, nullptr, nullptr, y);
-  }
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  // the reduce launches as a programmatic dependent of the GEMM, so its launch
+  // overlaps the GEMM's tail
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>((m + 31) / 32));
+  cfg.blockDim = dim3(32, 8);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int32_t* part = static_cast<const int32_t*>(partial);
+  const cudaError_t e =
+      epilogue == kEpiF32W8A8
+          ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<kEpiF32W8A8>, splits, m, n, part,
+                               x_scale, w_scale, bias, residual, y)
+          : cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<kEpiI32>, splits, m, n, part,
+                               static_cast<const float*>(nullptr),
+                               static_cast<const float*>(nullptr),
+                               static_cast<const float*>(nullptr),
+                               static_cast<const float*>(nullptr), y);
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream) {
