@@ -4,17 +4,29 @@
     python -m reef_b200.profile_cases flash [--batch 8 --seq 2048 --heads 32]
     python -m reef_b200.profile_cases qkv   [--batch 8 --seq 2048 --heads 32]
     python -m reef_b200.profile_cases decode [--batch 64 --heads 8 --kv-heads 1 --seq 4096]
+    python -m reef_b200.profile_cases sweep [--out gpurun_out/sweep.json]
 
 Each case allocates its seeded inputs once, launches the kernel twice (a
 warm-up launch, then the one to capture: ``ncu -k regex:<name> -s 1 -c 1``)
 and synchronises.  The default GEMM is the config-3 QKV projection
 (A 64 MiB + B 48 MiB of int8 and an 768 MiB fp32 output: larger than L2,
 about 1 GiB on the device); the default flash case is config 3's attention.
+
+``sweep`` is not a capture case: it times the W8A8 GEMM at every point of the
+config-5 sweep (M in {1, 16, 128, 1024, 8192, 16384} x five (N, K) shapes)
+through the C ABI -- ``reef_b200_gemm_w8a8`` for M > 128, the swap-AB split-K
+``reef_b200_gemm_w8a8_skinny`` for M <= 128 -- with CUDA events, and prints
+one JSON line per point with its roofline fraction (tensor-bound against twice
+the measured burst bf16 rate for M >= 1024, HBM-bound against the measured
+copy bandwidth below).  Operands rotate through enough copies that every call
+reads them from DRAM, not L2.
 """
 from __future__ import annotations
 
 import argparse
+import json
 import math
+import os
 
 import torch
 
@@ -96,9 +108,85 @@ def decode(batch: int, heads: int, kv_heads: int, cache_len: int) -> None:
     torch.cuda.synchronize()
 
 
+SWEEP_M = (1, 16, 128, 1024, 8192, 16384)
+SWEEP_NK = ((4096, 4096), (11008, 4096), (4096, 11008), (28672, 8192), (8192, 28672))
+L2_BYTES = 126 << 20
+
+
+def _peaks() -> dict:
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    try:
+        with open(os.path.join(root, "MEASURED_PEAKS.json")) as fh:
+            m = json.load(fh)
+        return {"int8_tops": 2.0 * m["bf16_tflops"], "hbm_gbs": m["hbm_gbs"], "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"int8_tops": 2.0 * 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def sweep(out: str | None, iters: int = 20) -> None:
+    peaks = _peaks()
+    st = torch.cuda.current_stream().cuda_stream
+    lib = _lib.lib()
+    rows = []
+    for (n, k) in SWEEP_NK:
+        kp = K.kpad(k)
+        for m in SWEEP_M:
+            g = torch.Generator(device="cuda").manual_seed(m + n + k)
+            per_copy = (m + n) * kp
+            copies = max(1, min(16, -(-2 * L2_BYTES // per_copy)))
+            a = [torch.randint(-127, 128, (m, kp), generator=g, device="cuda", dtype=torch.int8)
+                 for _ in range(copies)]
+            b = [torch.randint(-127, 128, (n, kp), generator=g, device="cuda", dtype=torch.int8)
+                 for _ in range(copies)]
+            xs = torch.rand(m, generator=g, device="cuda") * 1e-3 + 1e-3
+            ws = torch.rand(n, generator=g, device="cuda") * 1e-3 + 1e-3
+            y = torch.empty((m, n), device="cuda")
+            skinny = m <= 128
+            wsb = lib.reef_b200_gemm_skinny_workspace_bytes(m, k, n) if skinny else 0
+            work = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
+
+            def call(i: int) -> None:
+                c = i % copies
+                if skinny:
+                    _lib.call("reef_b200_gemm_w8a8_skinny", m, k, n, a[c].data_ptr(), xs.data_ptr(),
+                              b[c].data_ptr(), ws.data_ptr(), None, work.data_ptr(), work.numel(),
+                              y.data_ptr(), st)
+                else:
+                    _lib.call("reef_b200_gemm_w8a8", m, k, n, a[c].data_ptr(), xs.data_ptr(),
+                              b[c].data_ptr(), ws.data_ptr(), None, y.data_ptr(), st)
+
+            for i in range(3):
+                call(i)
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(iters):
+                call(i)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / iters
+            ops = 2.0 * m * n * k
+            moved = m * k + n * k + 4.0 * m * n  # int8 A and B, fp32 y
+            tops = ops / (ms * 1e-3) / 1e12
+            gbs = moved / (ms * 1e-3) / 1e9
+            tensor = m >= 1024
+            r = {"m": m, "n": n, "k": k, "path": "skinny split-K" if skinny else "tcgen05 persistent",
+                 "ms": ms, "tops": tops, "gbs": gbs, "bound": "tensor" if tensor else "hbm",
+                 "frac": tops / peaks["int8_tops"] if tensor else gbs / peaks["hbm_gbs"],
+                 "peak_source": peaks["source"], "operand_copies": copies}
+            rows.append(r)
+            print(json.dumps(r), flush=True)
+            del a, b, y, work
+            torch.cuda.empty_cache()
+    if out:
+        with open(out, "w") as fh:
+            json.dump(rows, fh, indent=1)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "flash", "qkv", "decode"])
+    ap.add_argument("case", choices=["gemm", "flash", "qkv", "decode", "sweep"])
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=4096)
@@ -106,8 +194,11 @@ def main() -> None:
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--kv-heads", type=int, default=32)
+    ap.add_argument("--out", default=None)
     a = ap.parse_args()
-    if a.case == "gemm":
+    if a.case == "sweep":
+        sweep(a.out)
+    elif a.case == "gemm":
         gemm(a.m, a.n, a.k)
     elif a.case == "qkv":
         qkv(a.batch, a.seq, a.heads, a.kv_heads)
