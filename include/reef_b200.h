@@ -268,6 +268,19 @@ int reef_b200_matvec_rows_f32(size_t out, size_t in, const float* w, const float
  * uint32).  Ties give the lowest index; a NaN never wins unless it is x[0]
  * (the engine's scan then keeps 0).  n in [1, 2^32 - 1]. */
 int reef_b200_argmax_f32(size_t n, const float* x, uint32_t* index, reef_b200_stream_t stream);
+/* embedding_f32 (kernels.hpp:81-84; the engine's lookup_token_embeddings +
+ * add_position_embeddings, embedding.hpp:31-66) for `count` tokens:
+ * y[t][c] = wte[ids[t]][c] + wpe[first_position + t][c], one rounded float
+ * add.  ids [count] uint32 on the DEVICE (so a decode loop can feed the
+ * previous argmax back without a host round trip); wte [vocab][width], wpe
+ * [max_positions][width], y [count][width] fp32.  first_position + count
+ * must not pass max_positions (REEF_B200_ERR_INVALID).  An id >= vocab
+ * records 0x202 in the device error word and writes that row as zeros; a
+ * non-finite sum records 0x301. */
+int reef_b200_embedding_f32(size_t width, size_t count, const uint32_t* ids,
+                            size_t first_position, size_t vocab, size_t max_positions,
+                            const float* wte, const float* wpe, float* y,
+                            reef_b200_stream_t stream);
 
 /* ---- int8 flash attention (the fast head) ------------------------------- */
 
@@ -496,6 +509,55 @@ size_t reef_b200_gptneo_block_workspace_bytes(const reef_b200_gptneo_block* bloc
 int reef_b200_gptneo_block_forward(const reef_b200_gptneo_block* block, const float* x,
                                    float* y, void* workspace, size_t workspace_bytes,
                                    reef_b200_stream_t stream);
+/* The same block on `seq` new positions [position, position + seq) of a
+ * cache that holds the earlier ones (Attention::forward with a KV cache,
+ * attention.hpp:290-372; the firmware's per-layer step, gpt_neo.cc:136-176):
+ * the projected keys and values are written into k_cache / v_cache rows
+ * [position, position + seq) and every query attends over cache rows
+ * [0, position + its offset] (window as the block's).  The caches are this
+ * layer's [max_tokens][heads*head_dim] fp32, token-major (a projection's
+ * output rows land in place).  position + seq <= max_tokens.  Prefill and
+ * decode give the same bits (a prompt run at once or one token at a time).
+ * Workspace: reef_b200_gptneo_block_workspace_bytes. */
+int reef_b200_gptneo_block_forward_cached(const reef_b200_gptneo_block* block, const float* x,
+                                          float* y, size_t position, float* k_cache,
+                                          float* v_cache, size_t max_tokens, void* workspace,
+                                          size_t workspace_bytes, reef_b200_stream_t stream);
+
+/* ---- GPT-Neo decode loop (the firmware's GptNeo::step) ------------------ */
+
+/* A whole W8A8 GPT-Neo model: the token and position tables, the final
+ * LayerNorm and `layers` blocks (a HOST array; each block's seq is
+ * ignored).  wte doubles as the tied lm_head. */
+typedef struct reef_b200_gptneo_model {
+  size_t vocab, max_positions, hidden, layers;
+  float eps;
+  const float* wte;      /* [vocab][hidden] */
+  const float* wpe;      /* [max_positions][hidden] */
+  const float* ln_f_g;   /* [hidden] */
+  const float* ln_f_b;
+  const reef_b200_gptneo_block* blocks;
+} reef_b200_gptneo_model;
+
+/* Workspace for reef_b200_gptneo_step on up to `count` tokens at once. */
+size_t reef_b200_gptneo_step_workspace_bytes(const reef_b200_gptneo_model* model, size_t count);
+/* GptNeo::step (coral/firmware/gpt_neo.cc:123-188) for `count` tokens at
+ * once: ids [count] (device uint32) at positions [position, position +
+ * count) go through the embedding and every block, appending their keys and
+ * values to the caches; then, for the last token, ln_f, the tied lm_head
+ * (logits [vocab], when not NULL) and the greedy choice (*next_id, device
+ * uint32, when not NULL).  With both NULL only the caches advance (the
+ * firmware's want_logits = false).  k_cache and v_cache are [layers]
+ * [max_tokens][heads*head_dim] fp32; position + count <= max_tokens <=
+ * max_positions.  A prompt may go in at once (count = its length) or a
+ * token at a time: the logits are the same bits, and equal the engine's
+ * GPTNeo<float> forward.  Feeding next_id back as the next call's ids
+ * makes a generation loop with no host round trip (capturable in a CUDA
+ * graph for a fixed position). */
+int reef_b200_gptneo_step(const reef_b200_gptneo_model* model, const uint32_t* ids,
+                          size_t count, size_t position, float* k_cache, float* v_cache,
+                          size_t max_tokens, float* logits, uint32_t* next_id, void* workspace,
+                          size_t workspace_bytes, reef_b200_stream_t stream);
 
 /* ---- reef's packed model ("REEF" blob v1, model_blob.hpp:18-66) --------- */
 
@@ -522,10 +584,22 @@ size_t reef_b200_blob_layer_bytes(const reef_b200_blob_info* info);
  * block's weights and shape (heads, head_dim, ffn, window: the blob's window
  * for a local layer, 0 for a global one; eps); seq and comm are the
  * caller's.  A float blob is REEF_B200_ERR_UNSUPPORTED (these kernels run
- * W8A8 blocks).  Asynchronous on `stream`; the blob may be reused once the
- * call returns. */
+ * W8A8 blocks).  Asynchronous on `stream`: a blob in page-locked memory must
+ * stay unchanged until the stream has passed this call (pageable memory is
+ * staged before the call returns). */
 int reef_b200_blob_load_layer(const void* blob, size_t bytes, size_t layer, void* arena,
                               size_t arena_bytes, reef_b200_gptneo_block* block,
+                              reef_b200_stream_t stream);
+/* Device bytes a whole model takes in reef_b200_blob_load_model's arena. */
+size_t reef_b200_blob_model_bytes(const reef_b200_blob_info* info);
+/* Loads a whole W8A8 blob (the firmware's GptNeo constructor, gpt_neo.cc:
+ * 61-97, which reads the blob in place): the tables, ln_f and every layer
+ * into `arena` (device, 256-byte aligned, >= reef_b200_blob_model_bytes),
+ * filling `blocks` (a host array of info.layers) and `model` (whose blocks
+ * pointer is set to `blocks`).  Errors and asynchrony as
+ * reef_b200_blob_load_layer. */
+int reef_b200_blob_load_model(const void* blob, size_t bytes, void* arena, size_t arena_bytes,
+                              reef_b200_gptneo_model* model, reef_b200_gptneo_block* blocks,
                               reef_b200_stream_t stream);
 
 #ifdef __cplusplus

@@ -34,6 +34,12 @@ SIGNATURES = {
     "reef_b200_blob_read_info": ([_p, _sz, _p], _i),
     "reef_b200_blob_layer_bytes": ([_p], _sz),
     "reef_b200_blob_load_layer": ([_p, _sz, _sz, _p, _sz, _p, _p], _i),
+    "reef_b200_blob_model_bytes": ([_p], _sz),
+    "reef_b200_blob_load_model": ([_p, _sz, _p, _sz, _p, _p, _p], _i),
+    "reef_b200_embedding_f32": ([_sz, _sz, _p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
+    "reef_b200_gptneo_block_forward_cached": ([_p, _p, _p, _sz, _p, _p, _sz, _p, _sz, _p], _i),
+    "reef_b200_gptneo_step_workspace_bytes": ([_p, _sz], _sz),
+    "reef_b200_gptneo_step": ([_p, _p, _sz, _sz, _p, _p, _sz, _p, _p, _p, _sz, _p], _i),
     "reef_b200_pack_weight_i8": ([_sz, _sz, _p, _p, _p], _i),
     "reef_b200_pad_rows_i8": ([_sz, _sz, _p, _p, _p], _i),
     "reef_b200_linear_w8a8": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p], _i),
@@ -97,6 +103,13 @@ class GptNeoBlockDesc(C.Structure):
                 ("wo", _p), ("so", _p), ("bo", _p), ("ln2_g", _p), ("ln2_b", _p),
                 ("wfc", _p), ("sfc", _p), ("bfc", _p), ("wproj", _p), ("sproj", _p),
                 ("bproj", _p), ("comm", _p)]
+
+
+class GptNeoModelDesc(C.Structure):
+    """reef_b200_gptneo_model (include/reef_b200.h)."""
+    _fields_ = [("vocab", _sz), ("max_positions", _sz), ("hidden", _sz), ("layers", _sz),
+                ("eps", C.c_float), ("wte", _p), ("wpe", _p), ("ln_f_g", _p), ("ln_f_b", _p),
+                ("blocks", _p)]
 
 
 class BlobInfo(C.Structure):

@@ -12,7 +12,10 @@
 // caller-provided device arena and repacks each [in][out] int8 weight into
 // the K-major [out][kpad(in)] layout the tcgen05 GEMM reads (pack_weight_i8,
 // through a staging area in the same arena), then fills a GPT-Neo block
-// descriptor with the pointers.
+// descriptor with the pointers.  Loading a model puts the token and position
+// tables and ln_f first, then one such layer arena per layer, and fills a
+// model descriptor (the firmware's GptNeo constructor reads the blob in
+// place instead).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -111,6 +114,33 @@ Arena arena_layout(size_t d, size_t f) {
   a.bfc = take(f * 4);
   a.end = at;
   return a;
+}
+
+struct ModelArena {  // byte offsets of the model-level arrays, then the layers
+  size_t wte, wpe, ln_f_g, ln_f_b, layers, layer_bytes, end;
+};
+
+ModelArena model_layout(size_t vocab, size_t positions, size_t d, size_t layers, size_t f) {
+  ModelArena m{};
+  size_t at = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = at;
+    at += al256(bytes);
+    return o;
+  };
+  m.wte = take(vocab * d * 4);
+  m.wpe = take(positions * d * 4);
+  m.ln_f_g = take(d * 4);
+  m.ln_f_b = take(d * 4);
+  m.layer_bytes = arena_layout(d, f).end;
+  m.layers = at;
+  m.end = at + layers * m.layer_bytes;
+  return m;
+}
+
+bool model_size_ok(size_t vocab, size_t positions, size_t d, size_t layers, size_t f) {
+  return d > 0 && f > 0 && d <= (1u << 20) && f <= (1u << 22) && vocab <= (1u << 24) &&
+         positions <= (1u << 24) && layers <= 4096;
 }
 
 }  // namespace
@@ -254,6 +284,61 @@ int reef_b200_blob_load_layer(const void* blob, size_t bytes, size_t layer, void
   block->wproj = i8(a.wproj);
   block->sproj = f32(a.sproj);
   block->bproj = f32(a.bproj);
+  return REEF_B200_OK;
+}
+
+size_t reef_b200_blob_model_bytes(const reef_b200_blob_info* info) {
+  if (info == nullptr ||
+      !model_size_ok(info->vocab, info->max_positions, info->hidden, info->layers, info->inner))
+    return 0;
+  return model_layout(info->vocab, info->max_positions, info->hidden, info->layers, info->inner)
+      .end;
+}
+
+int reef_b200_blob_load_model(const void* blob, size_t bytes, void* arena, size_t arena_bytes,
+                              reef_b200_gptneo_model* model, reef_b200_gptneo_block* blocks,
+                              reef_b200_stream_t stream) {
+  if (arena == nullptr || model == nullptr || blocks == nullptr) return REEF_B200_ERR_INVALID;
+  Header h;
+  if (int rc = read_header(blob, bytes, &h)) return rc;
+  if (h.precision != kPrecisionW8A8) return REEF_B200_ERR_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(arena) % 256 != 0) return REEF_B200_ERR_ALIGNMENT;
+  const size_t v = h.vocab_size, n = h.max_positions, d = h.hidden_size, f = h.inner_size;
+  if (!model_size_ok(v, n, d, h.num_layers, f)) return REEF_B200_ERR_TOO_LARGE;
+  const ModelArena ma = model_layout(v, n, d, h.num_layers, f);
+  if (arena_bytes < ma.end) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  const auto* src = static_cast<const uint8_t*>(blob);
+  auto* dst = static_cast<uint8_t*>(arena);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the tables and ln_f (read_header checked their spans)
+  const struct {
+    uint32_t off;
+    size_t bytes, to;
+  } arrays[] = {{h.wte, v * d * 4, ma.wte},
+                {h.wpe, n * d * 4, ma.wpe},
+                {h.ln_f_weight, d * 4, ma.ln_f_g},
+                {h.ln_f_bias, d * 4, ma.ln_f_b}};
+  for (const auto& a : arrays)
+    if (cudaMemcpyAsync(dst + a.to, src + a.off, a.bytes, cudaMemcpyHostToDevice, st) !=
+        cudaSuccess)
+      return REEF_B200_ERR_CUDA;
+  for (size_t l = 0; l < h.num_layers; ++l) {
+    if (int rc = reef_b200_blob_load_layer(blob, bytes, l, dst + ma.layers + l * ma.layer_bytes,
+                                           ma.layer_bytes, &blocks[l], stream))
+      return rc;
+  }
+  auto f32 = [&](size_t o) { return reinterpret_cast<const float*>(dst + o); };
+  model->vocab = v;
+  model->max_positions = n;
+  model->hidden = d;
+  model->layers = h.num_layers;
+  model->eps = h.layer_norm_eps;
+  model->wte = f32(ma.wte);
+  model->wpe = f32(ma.wpe);
+  model->ln_f_g = f32(ma.ln_f_g);
+  model->ln_f_b = f32(ma.ln_f_b);
+  model->blocks = blocks;
   return REEF_B200_OK;
 }
 

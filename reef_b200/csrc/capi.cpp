@@ -83,6 +83,21 @@ int reef_b200_argmax_f32(size_t n, const float* x, uint32_t* index, reef_b200_st
   return argmax_f32(static_cast<long long>(n), x, index, S(stream));
 }
 
+int reef_b200_embedding_f32(size_t width, size_t count, const uint32_t* ids,
+                            size_t first_position, size_t vocab, size_t max_positions,
+                            const float* wte, const float* wpe, float* y,
+                            reef_b200_stream_t stream) {
+  if (count == 0) return REEF_B200_OK;
+  if (width == 0 || width > kMaxDim || count > kMaxDim || vocab == 0 || max_positions == 0 ||
+      first_position > max_positions || count > max_positions - first_position || !ids ||
+      !wte || !wpe || !y)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return embedding_f32(static_cast<int>(width), static_cast<long long>(count), ids,
+                       static_cast<long long>(first_position), static_cast<long long>(vocab),
+                       static_cast<long long>(max_positions), wte, wpe, y, S(stream));
+}
+
 int reef_b200_quantize_rows(size_t rows, size_t in, const float* x, int8_t* x_q,
                             float* x_scale, reef_b200_stream_t stream) {
   if (rows == 0) return REEF_B200_OK;

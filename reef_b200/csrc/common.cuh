@@ -23,6 +23,7 @@ enum DeviceError : int {
   kDevTimeoutDrain = 0x105,    // final drain of the MMA pipe
   kDevTimeoutPeer = 0x106,     // a peer flag never arrived
   kDevBadPosition = 0x201,     // a decode position outside the cache
+  kDevBadToken = 0x202,        // a token id outside the vocabulary
   kDevNonFinite = 0x301,       // a float product or sum the engine would reject
 };
 

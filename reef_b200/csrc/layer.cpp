@@ -435,6 +435,122 @@ int neo_check(const reef_b200_gptneo_block* B) {
   return REEF_B200_OK;
 }
 
+
+// This layer's KV cache for a cached block: [max_tokens][heads*head_dim]
+// rows, token-major; the block's `seq` new rows go at `position`.
+struct NeoCache {
+  float* k;
+  float* v;
+  size_t position;
+};
+
+int neo_forward(const reef_b200_gptneo_block* B, const float* x, float* y, const NeoCache* kv,
+                void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  if (int rc = neo_check(B)) return rc;
+  if (!x || !y || !workspace) return REEF_B200_ERR_INVALID;
+  NeoBufs b;
+  if (neo_carve(B, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  Comm* c = C(B->comm);
+  const long long T = static_cast<long long>(B->seq);
+  const int d = static_cast<int>(B->hidden), dl = static_cast<int>(B->heads * B->head_dim),
+            F = static_cast<int>(B->ffn);
+  const long long ld = static_cast<long long>(kpad(d));
+
+  // Attention::forward (attention.hpp:354-372): ln_1, q/k/v projections
+  // (column-parallel by heads), every local head, o_proj (row-parallel) with
+  // the residual of Block::forward (block.hpp:99-102) fused in.
+  REEF_TRY(layernorm_exact(T, d, B->eps, x, B->ln1_g, B->ln1_b, b.h, st));
+  REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
+  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wq, B->sq, nullptr, nullptr, b.q, st));
+  // with a cache the key and value rows go straight into it
+  const size_t past = kv != nullptr ? kv->position : 0;
+  float* kr = kv != nullptr ? kv->k + past * dl : b.k;
+  float* vr = kv != nullptr ? kv->v + past * dl : b.v;
+  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wk, B->sk, nullptr, nullptr, kr, st));
+  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wv, B->sv, nullptr, nullptr, vr, st));
+  AttnHeadArgs aa{};
+  aa.heads = static_cast<int>(B->heads);
+  aa.query_len = static_cast<int>(T);
+  aa.key_len = static_cast<int>(past + T);
+  aa.head_dim = static_cast<int>(B->head_dim);
+  aa.window = static_cast<int>(B->window);
+  aa.query_start = static_cast<long long>(past);
+  aa.q_stride = aa.kv_stride = aa.out_stride = dl;
+  aa.q_head = aa.kv_head = aa.out_head = static_cast<long long>(B->head_dim);
+  REEF_TRY(attention_head_f32(aa, b.q, kv != nullptr ? kv->k : b.k, kv != nullptr ? kv->v : b.v,
+                              b.ctx, st));
+  {
+    auto quant = [&](const float* rm) {
+      return quantize_rows(T, dl, b.ctx, b.xq, static_cast<long long>(kpad(dl)), b.xs, rm, st);
+    };
+    auto absmax = [&](float* rm) { return row_absmax(T, dl, b.ctx, rm, st); };
+    REEF_TRY(rowpar_linear(c, T, dl, d, quant, absmax, B->wo, B->so, B->bo, x, b.xq, b.xs,
+                           b.row_max, b.acc, b.a, st));
+  }
+  // MLP::forward (mlp.hpp:108-133): ln_2, c_fc (column-parallel) with gelu
+  // in its epilogue, c_proj (row-parallel) with the second residual fused in.
+  REEF_TRY(layernorm_exact(T, d, B->eps, b.a, B->ln2_g, B->ln2_b, b.h, st));
+  REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
+  REEF_TRY(gemm_w8a8_f32(T, d, F, b.xq, b.xs, B->wfc, B->sfc, B->bfc, nullptr, b.f, st,
+                         /*gelu=*/true));
+  {
+    auto quant = [&](const float* rm) {
+      return quantize_rows(T, F, b.f, b.xq, static_cast<long long>(kpad(F)), b.xs, rm, st);
+    };
+    auto absmax = [&](float* rm) { return row_absmax(T, F, b.f, rm, st); };
+    REEF_TRY(rowpar_linear(c, T, F, d, quant, absmax, B->wproj, B->sproj, B->bproj, b.a, b.xq,
+                           b.xs, b.row_max, b.acc, y, st));
+  }
+  return REEF_B200_OK;
+}
+
+
+// ---- GPT-Neo model step ------------------------------------------------------------------
+
+int model_check(const reef_b200_gptneo_model* m, size_t count) {
+  if (m == nullptr || m->blocks == nullptr || m->layers == 0 || m->vocab == 0 ||
+      m->max_positions == 0 || m->hidden == 0 || count == 0 ||
+      count > static_cast<size_t>(kMaxKeysExact) || !m->wte || !m->wpe || !m->ln_f_g ||
+      !m->ln_f_b || m->vocab > 0xffffffffull)
+    return REEF_B200_ERR_INVALID;
+  const size_t dl = m->blocks[0].heads * m->blocks[0].head_dim;
+  for (size_t l = 0; l < m->layers; ++l) {
+    reef_b200_gptneo_block blk = m->blocks[l];
+    blk.seq = count;
+    if (blk.hidden != m->hidden || blk.heads * blk.head_dim != dl || neo_check(&blk) != REEF_B200_OK)
+      return REEF_B200_ERR_INVALID;
+  }
+  return REEF_B200_OK;
+}
+
+struct StepBufs {
+  float* x[2];       // [count][hidden], ping-pong between blocks
+  float* normed;     // [hidden]
+  float* logits;     // [vocab] when the caller wants only the token
+  void* block_ws;    // one block's workspace for `count` rows
+  size_t block_bytes;
+};
+
+size_t step_carve(const reef_b200_gptneo_model* m, size_t count, void* ws, StepBufs* b) {
+  Carve c(ws, ~static_cast<size_t>(0));
+  b->x[0] = c.take<float>(count * m->hidden);
+  b->x[1] = c.take<float>(count * m->hidden);
+  b->normed = c.take<float>(m->hidden);
+  b->logits = c.take<float>(m->vocab);
+  size_t need = 0;
+  for (size_t l = 0; l < m->layers; ++l) {
+    reef_b200_gptneo_block blk = m->blocks[l];
+    blk.seq = count;
+    NeoBufs nb;
+    need = std::max(need, neo_carve(&blk, nullptr, &nb));
+  }
+  b->block_bytes = need;
+  b->block_ws = c.take<uint8_t>(need);
+  return c.used + 256;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1051,59 +1167,68 @@ size_t reef_b200_gptneo_block_workspace_bytes(const reef_b200_gptneo_block* B) {
 int reef_b200_gptneo_block_forward(const reef_b200_gptneo_block* B, const float* x, float* y,
                                    void* workspace, size_t workspace_bytes,
                                    reef_b200_stream_t stream) {
-  if (int rc = neo_check(B)) return rc;
-  if (!x || !y || !workspace) return REEF_B200_ERR_INVALID;
-  NeoBufs b;
-  if (neo_carve(B, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
+  return neo_forward(B, x, y, nullptr, workspace, workspace_bytes, S(stream));
+}
+
+int reef_b200_gptneo_block_forward_cached(const reef_b200_gptneo_block* B, const float* x,
+                                          float* y, size_t position, float* k_cache,
+                                          float* v_cache, size_t max_tokens, void* workspace,
+                                          size_t workspace_bytes, reef_b200_stream_t stream) {
+  if (!k_cache || !v_cache || B == nullptr || max_tokens > static_cast<size_t>(kMaxKeysExact) ||
+      position > max_tokens || B->seq > max_tokens - position)
+    return REEF_B200_ERR_INVALID;
+  const NeoCache kv{k_cache, v_cache, position};
+  return neo_forward(B, x, y, &kv, workspace, workspace_bytes, S(stream));
+}
+
+// ---- GPT-Neo decode loop ---------------------------------------------------------------
+
+size_t reef_b200_gptneo_step_workspace_bytes(const reef_b200_gptneo_model* m, size_t count) {
+  if (model_check(m, count) != REEF_B200_OK) return 0;
+  StepBufs b;
+  return step_carve(m, count, nullptr, &b);
+}
+
+int reef_b200_gptneo_step(const reef_b200_gptneo_model* m, const uint32_t* ids, size_t count,
+                          size_t position, float* k_cache, float* v_cache, size_t max_tokens,
+                          float* logits, uint32_t* next_id, void* workspace,
+                          size_t workspace_bytes, reef_b200_stream_t stream) {
+  if (int rc = model_check(m, count)) return rc;
+  if (!ids || !k_cache || !v_cache || !workspace || max_tokens > m->max_positions ||
+      max_tokens > static_cast<size_t>(kMaxKeysExact) || position > max_tokens ||
+      count > max_tokens - position)
+    return REEF_B200_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return REEF_B200_ERR_ALIGNMENT;
+  StepBufs b;
+  if (step_carve(m, count, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
   if (int rc = check_device()) return rc;
   cudaStream_t st = S(stream);
-  Comm* c = C(B->comm);
-  const long long T = static_cast<long long>(B->seq);
-  const int d = static_cast<int>(B->hidden), dl = static_cast<int>(B->heads * B->head_dim),
-            F = static_cast<int>(B->ffn);
-  const long long ld = static_cast<long long>(kpad(d));
-
-  // Attention::forward (attention.hpp:354-372): ln_1, q/k/v projections
-  // (column-parallel by heads), every local head, o_proj (row-parallel) with
-  // the residual of Block::forward (block.hpp:99-102) fused in.
-  REEF_TRY(layernorm_exact(T, d, B->eps, x, B->ln1_g, B->ln1_b, b.h, st));
-  REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
-  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wq, B->sq, nullptr, nullptr, b.q, st));
-  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wk, B->sk, nullptr, nullptr, b.k, st));
-  REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wv, B->sv, nullptr, nullptr, b.v, st));
-  AttnHeadArgs aa{};
-  aa.heads = static_cast<int>(B->heads);
-  aa.query_len = static_cast<int>(T);
-  aa.key_len = static_cast<int>(T);
-  aa.head_dim = static_cast<int>(B->head_dim);
-  aa.window = static_cast<int>(B->window);
-  aa.query_start = 0;
-  aa.q_stride = aa.kv_stride = aa.out_stride = dl;
-  aa.q_head = aa.kv_head = aa.out_head = static_cast<long long>(B->head_dim);
-  REEF_TRY(attention_head_f32(aa, b.q, b.k, b.v, b.ctx, st));
-  {
-    auto quant = [&](const float* rm) {
-      return quantize_rows(T, dl, b.ctx, b.xq, static_cast<long long>(kpad(dl)), b.xs, rm, st);
-    };
-    auto absmax = [&](float* rm) { return row_absmax(T, dl, b.ctx, rm, st); };
-    REEF_TRY(rowpar_linear(c, T, dl, d, quant, absmax, B->wo, B->so, B->bo, x, b.xq, b.xs,
-                           b.row_max, b.acc, b.a, st));
+  const size_t d = m->hidden;
+  const size_t dl = m->blocks[0].heads * m->blocks[0].head_dim;
+  // x = wte[id] + wpe[position] (gpt_neo.cc:130-133)
+  REEF_TRY(embedding_f32(static_cast<int>(d), static_cast<long long>(count), ids,
+                         static_cast<long long>(position), static_cast<long long>(m->vocab),
+                         static_cast<long long>(m->max_positions), m->wte, m->wpe, b.x[0], st));
+  // every block on this layer's cache (gpt_neo.cc:135-177)
+  int cur = 0;
+  for (size_t l = 0; l < m->layers; ++l) {
+    reef_b200_gptneo_block blk = m->blocks[l];
+    blk.seq = count;
+    const size_t layer_off = l * max_tokens * dl;
+    const NeoCache kv{k_cache + layer_off, v_cache + layer_off, position};
+    REEF_TRY(neo_forward(&blk, b.x[cur], b.x[cur ^ 1], &kv, b.block_ws, b.block_bytes, st));
+    cur ^= 1;
   }
-  // MLP::forward (mlp.hpp:108-133): ln_2, c_fc (column-parallel) with gelu
-  // in its epilogue, c_proj (row-parallel) with the second residual fused in.
-  REEF_TRY(layernorm_exact(T, d, B->eps, b.a, B->ln2_g, B->ln2_b, b.h, st));
-  REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
-  REEF_TRY(gemm_w8a8_f32(T, d, F, b.xq, b.xs, B->wfc, B->sfc, B->bfc, nullptr, b.f, st,
-                         /*gelu=*/true));
-  {
-    auto quant = [&](const float* rm) {
-      return quantize_rows(T, F, b.f, b.xq, static_cast<long long>(kpad(F)), b.xs, rm, st);
-    };
-    auto absmax = [&](float* rm) { return row_absmax(T, F, b.f, rm, st); };
-    REEF_TRY(rowpar_linear(c, T, F, d, quant, absmax, B->wproj, B->sproj, B->bproj, b.a, b.xq,
-                           b.xs, b.row_max, b.acc, y, st));
-  }
+  if (logits == nullptr && next_id == nullptr) return REEF_B200_OK;
+  // logits = ln_f(x) . wte^T for the last token, then the greedy choice
+  // (gpt_neo.cc:179-187)
+  float* lg = logits != nullptr ? logits : b.logits;
+  REEF_TRY(layernorm_exact(1, static_cast<int>(d), m->eps, b.x[cur] + (count - 1) * d, m->ln_f_g,
+                           m->ln_f_b, b.normed, st));
+  REEF_TRY(matvec_rows_f32(static_cast<long long>(m->vocab), static_cast<long long>(d), m->wte,
+                           b.normed, lg, st));
+  if (next_id != nullptr)
+    REEF_TRY(argmax_f32(static_cast<long long>(m->vocab), lg, next_id, st));
   return REEF_B200_OK;
 }
 

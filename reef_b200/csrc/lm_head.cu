@@ -1,4 +1,13 @@
-// lm_head.cu -- GPT-Neo's output projection and greedy token choice.
+// lm_head.cu -- GPT-Neo's token input, output projection and greedy token
+// choice.
+//
+// embedding_f32 is reef's embedding (embedding.hpp:31-66 lookup_token_embeddings
+// then add_position_embeddings; the firmware's embedding_f32, kernels.hpp:81-84):
+// y[t][c] = wte[id_t][c] + wpe[first_position + t][c], one rounded float add.
+// The ids are read on the device (the previous step's argmax), so a decode
+// loop needs no host round trip.  The engine throws on an id outside the
+// vocabulary or a non-finite sum; here the first records kDevBadToken (and
+// the row is written as zeros) and the second kDevNonFinite.
 //
 // matvec_rows_f32 is reef's float linear(x, wte) for one row
 // (operator/linear.hpp:75-84 through tensor.hpp:179-192): every logit starts
@@ -109,7 +118,44 @@ __global__ void __launch_bounds__(kArgThreads)
   }
 }
 
+__global__ void embedding_f32_kernel(int width, const uint32_t* __restrict__ ids,
+                                     long long first_position, long long vocab,
+                                     long long positions, const float* __restrict__ wte,
+                                     const float* __restrict__ wpe, float* __restrict__ y,
+                                     int* err) {
+  const long long t = blockIdx.x;
+  const uint32_t id = ids[t];
+  const long long pos = first_position + t;
+  float* yr = y + t * width;
+  if (id >= vocab || pos >= positions) {
+    if (threadIdx.x == 0) record_error(err, id >= vocab ? kDevBadToken : kDevBadPosition);
+    for (int c = threadIdx.x; c < width; c += blockDim.x) yr[c] = 0.0f;
+    return;
+  }
+  const float* a = wte + static_cast<long long>(id) * width;
+  const float* b = wpe + pos * width;
+  bool finite = true;
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    const float v = __fadd_rn(a[c], b[c]);
+    finite = finite && isfinite(v);
+    yr[c] = v;
+  }
+  if (!finite) record_error(err, kDevNonFinite);
+}
+
 }  // namespace
+
+int embedding_f32(int width, long long count, const uint32_t* ids, long long first_position,
+                  long long vocab, long long positions, const float* wte, const float* wpe,
+                  float* y, cudaStream_t stream) {
+  if (width <= 0 || count <= 0 || vocab <= 0 || positions <= 0 || first_position < 0 ||
+      ids == nullptr || wte == nullptr || wpe == nullptr || y == nullptr)
+    return kErrInvalid;
+  if (count > 0x7fffffffLL) return kErrTooLarge;
+  embedding_f32_kernel<<<static_cast<unsigned>(count), 128, 0, stream>>>(
+      width, ids, first_position, vocab, positions, wte, wpe, y, device_error_ptr());
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
 
 int matvec_rows_f32(long long out, long long in, const float* w, const float* x, float* y,
                     cudaStream_t stream) {

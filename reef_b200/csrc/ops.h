@@ -162,7 +162,11 @@ struct PeerFlags {
 };
 int signal_peers(const PeerFlags& f, cudaStream_t stream);
 
-// lm_head.cu -- reef's float linear(x, w) for one row (bit-identical) and argmax
+// lm_head.cu -- the token embedding, reef's float linear(x, w) for one row
+// (bit-identical) and argmax
+int embedding_f32(int width, long long count, const uint32_t* ids, long long first_position,
+                  long long vocab, long long positions, const float* wte, const float* wpe,
+                  float* y, cudaStream_t stream);
 int matvec_rows_f32(long long out, long long in, const float* w, const float* x, float* y,
                     cudaStream_t stream);
 int argmax_f32(long long n, const float* x, uint32_t* index, cudaStream_t stream);

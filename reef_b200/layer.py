@@ -225,3 +225,70 @@ class GptNeoBlock:
                   y.data_ptr(), self.workspace.data_ptr(), self.workspace.numel(),
                   torch.cuda.current_stream().cuda_stream)
         return y
+
+
+class GptNeoModel:
+    """A whole W8A8 GPT-Neo from reef's packed blob, generating on the GPU: the
+    firmware's GptNeo (coral/firmware/gpt_neo.cc:61-188) over the C ABI.
+
+    ``reef_b200_blob_load_model`` puts the blob's tables and layers in one
+    device arena; ``step`` runs ``reef_b200_gptneo_step`` on ids already on
+    the device, appending to the fp32 KV caches ([layers][max_tokens]
+    [hidden] each); ``generate`` feeds each chosen id back on the device, so
+    the loop reads nothing back until it ends.
+    """
+
+    def __init__(self, blob: bytes, max_tokens: int, device: str | torch.device = "cuda"):
+        dev = torch.device(device)
+        self._blob = C.create_string_buffer(bytes(blob), len(blob))
+        self.info = _lib.BlobInfo()
+        _lib.call("reef_b200_blob_read_info", self._blob, len(blob), C.byref(self.info))
+        lib = _lib.lib()
+        nbytes = lib.reef_b200_blob_model_bytes(C.byref(self.info))
+        if nbytes == 0:
+            raise ValueError("blob shape out of range")
+        self.arena = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.blocks = (_lib.GptNeoBlockDesc * self.info.layers)()
+        self.desc = _lib.GptNeoModelDesc()
+        st = torch.cuda.current_stream(dev).cuda_stream
+        _lib.call("reef_b200_blob_load_model", self._blob, len(blob), self.arena.data_ptr(),
+                  nbytes, C.byref(self.desc), self.blocks, st)
+        if max_tokens > self.info.max_positions:
+            raise ValueError("max_tokens past the position table")
+        width = self.blocks[0].heads * self.blocks[0].head_dim
+        shape = (self.info.layers, max_tokens, width)
+        self.k_cache = torch.zeros(shape, dtype=torch.float32, device=dev)
+        self.v_cache = torch.zeros(shape, dtype=torch.float32, device=dev)
+        self.max_tokens = max_tokens
+        wbytes = lib.reef_b200_gptneo_step_workspace_bytes(C.byref(self.desc), max_tokens)
+        if wbytes == 0:
+            raise ValueError("invalid model description")
+        self.workspace = torch.empty(wbytes, dtype=torch.uint8, device=dev)
+        self.position = 0
+        self.device = dev
+
+    def step(self, ids: torch.Tensor, logits: torch.Tensor | None = None,
+             next_id: torch.Tensor | None = None) -> None:
+        """Runs ``ids`` (device uint32/int32 [count]) at the next positions;
+        writes the last one's logits and greedy id where given."""
+        count = ids.numel()
+        _lib.call("reef_b200_gptneo_step", C.byref(self.desc), ids.data_ptr(), count,
+                  self.position, self.k_cache.data_ptr(), self.v_cache.data_ptr(),
+                  self.max_tokens, logits.data_ptr() if logits is not None else None,
+                  next_id.data_ptr() if next_id is not None else None,
+                  self.workspace.data_ptr(), self.workspace.numel(),
+                  torch.cuda.current_stream(self.device).cuda_stream)
+        self.position += count
+
+    def generate(self, prompt, new_tokens: int):
+        """Greedy generation (GPTNeo::generate): the prompt at once, then one
+        token a time.  Returns (tokens [new_tokens] int64, logits
+        [new_tokens][vocab]), the logits behind each token."""
+        dev = self.device
+        ids = torch.tensor(list(prompt), dtype=torch.int32, device=dev)
+        tokens = torch.empty(new_tokens, dtype=torch.int32, device=dev)
+        logits = torch.empty((new_tokens, self.info.vocab), dtype=torch.float32, device=dev)
+        self.step(ids, logits[0], tokens[0:1])
+        for i in range(1, new_tokens):
+            self.step(tokens[i - 1:i], logits[i], tokens[i:i + 1])
+        return tokens.to(torch.int64).cpu(), logits.cpu()

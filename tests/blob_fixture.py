@@ -1,9 +1,14 @@
-"""The committed "REEF" blob fixture (tests/golden/gptneo_w8a8.blob, written
-by reef's packer: tests/golden/make_blob.py), parsed here with numpy alone,
+"""reef's packed "REEF" v1 model blobs, parsed here with numpy alone,
 independently of the library's C++ reader: the header and layer records of
-coral/include/reef_kernels/model_blob.hpp:18-66 and each layer's arrays in
-the engine's [out][in] layout, keyed as the oracle's GPT-Neo block takes
-them."""
+coral/include/reef_kernels/model_blob.hpp:18-66, each layer's arrays in the
+engine's [out][in] layout keyed as the oracle's GPT-Neo block takes them, and
+the model-level arrays (wte, wpe, ln_f).
+
+Two blobs are committed, both written by reef's own packer: the layer fixture
+tests/golden/gptneo_w8a8.blob (tests/golden/make_blob.py) and the W8A8 model
+of reef's kGptNeo golden (gen_golden.cpp:755-805, in tests/golden/gpt_neo.npz
+with its prompt, generated tokens and the logits behind each token).  An
+oracle forward of a whole model over a token sequence is here too."""
 from __future__ import annotations
 
 import json
@@ -35,6 +40,52 @@ def config() -> dict:
 
 def header(b: bytes) -> dict:
     return dict(zip(HEADER_FIELDS, struct.unpack_from("<10If6I", b, 0)))
+
+
+def golden_model(precision: str = "w8a8"):
+    """(blob bytes, prompt, tokens, logits [tokens][vocab]) of reef's kGptNeo
+    golden case for ``precision`` ("fp32" or "w8a8")."""
+    from tests import goldens
+    (c,) = [c for c in goldens.cases("gpt_neo", "kGptNeo")
+            if header(c["blob"].astype("<u4").tobytes())["precision"] == (precision == "w8a8")]
+    blob = c["blob"].astype("<u4").tobytes()
+    assert c["prompt"].size == c["prompt_length"] and c["tokens"].size == c["new_tokens"]
+    logits = c["logits"].reshape(c["new_tokens"], c["vocab_size"])
+    return blob, c["prompt"].astype(np.uint32), c["tokens"].astype(np.uint32), logits
+
+
+def model_arrays(b: bytes) -> dict:
+    """wte [vocab][hidden], wpe [positions][hidden], ln_f gain and shift."""
+    h = header(b)
+    v, n, d = h["vocab"], h["max_positions"], h["hidden"]
+
+    def floats(off, count):
+        return np.frombuffer(b, np.float32, count, off).copy()
+
+    return {"wte": floats(h["wte"], v * d).reshape(v, d),
+            "wpe": floats(h["wpe"], n * d).reshape(n, d),
+            "ln_f_g": floats(h["ln_f_weight"], d), "ln_f_b": floats(h["ln_f_bias"], d)}
+
+
+def oracle_logits(b: bytes, tokens) -> np.ndarray:
+    """The engine's GPTNeo forward over ``tokens`` at positions 0.. (W8A8
+    blocks; model.hpp's embedding add, final layernorm and tied lm_head),
+    restated with the oracle: logits [len(tokens)][vocab]."""
+    from oracle import oracle as ro
+    h = header(b)
+    m = model_arrays(b)
+    ids = np.asarray(tokens, np.int64)
+    x = (m["wte"][ids] + m["wpe"][np.arange(ids.size)]).astype(np.float32)
+    for i in range(h["layers"]):
+        p, local = layer(b, i)
+        x = ro.gptneo_block_w8a8(x, p, h["heads"], window=h["window"] if local else 0,
+                                 eps=h["eps"])
+    normed = ro.layernorm(x, m["ln_f_g"], m["ln_f_b"], h["eps"])
+    out = np.empty((ids.size, h["vocab"]), np.float32)
+    for t in range(ids.size):
+        out[t], ok = ro.matvec_rows_f32(m["wte"], normed[t])
+        assert ok
+    return out
 
 
 def layer(b: bytes, index: int):

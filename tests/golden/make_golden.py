@@ -29,7 +29,7 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-KEEP = ("linear", "int8", "attention", "math", "layernorm", "elementwise")
+KEEP = ("linear", "int8", "attention", "math", "layernorm", "elementwise", "gpt_neo")
 
 _DTYPES = {
     "float": np.float32,

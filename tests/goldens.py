@@ -33,6 +33,10 @@ FIELDS = {
     "kLayerNorm": ("rows", "width", "eps", "x", "gain", "shift", "y"),
     "kMatvec": ("out", "in", "w", "x", "y"),
     "kArgmax": ("n", "x", "index"),
+    "kAdd": ("n", "a", "b", "y"),
+    "kEmbedding": ("width", "id", "position", "wte", "wpe", "y"),
+    "kGptNeo": ("blob", "prompt_length", "prompt", "new_tokens", "tokens", "vocab_size",
+                "logits"),
 }
 
 

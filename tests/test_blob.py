@@ -7,6 +7,8 @@ magic or version, truncated, an array running past the end or off its
 """
 import ctypes as C
 
+import numpy as np
+
 from reef_b200 import _lib
 from tests import blob_fixture as BF
 
@@ -61,3 +63,19 @@ def test_malformed_blobs_are_refused():
     for blob in bad:
         rc, _ = read(blob)
         assert rc == 1, rc  # REEF_B200_ERR_INVALID
+
+
+def test_oracle_model_reproduces_reef_generation():
+    """reef's kGptNeo golden (gen_golden.cpp:755-805): the W8A8 model generates
+    20 tokens greedily from a 5-token prompt.  The oracle's blocks, final
+    layernorm, tied lm_head and argmax over the whole sequence reproduce
+    every logit bit for bit and every token -- the whole-model check the
+    GPU decode loop is held to."""
+    from oracle import oracle as ro
+    blob, prompt, tokens, logits = BF.golden_model("w8a8")
+    h = BF.header(blob)
+    assert h["precision"] == 1 and h["total_bytes"] == len(blob)
+    seq = np.concatenate([prompt, tokens[:-1]])
+    got = BF.oracle_logits(blob, seq)[prompt.size - 1:]
+    np.testing.assert_array_equal(got.view(np.uint32), logits.view(np.uint32))
+    assert [ro.argmax_f32(r) for r in got] == list(tokens)

@@ -256,3 +256,14 @@ def test_lm_head_and_argmax_match_engine():
         idx = C.c_size_t()
         assert R.ref_argmax_f32(v.size, ro._p(v, ro._f32p), C.byref(idx)) == 0
         assert ro.argmax_f32(v) == idx.value, v
+
+
+def test_embedding_and_add_match_reef_goldens():
+    """kEmbedding / kAdd (gen_golden.cpp:464-503): wte[id] + wpe[position] and
+    the residual add are one rounded float add each, as numpy's float32 add."""
+    for c in goldens.cases("elementwise", "kEmbedding"):
+        w = c["width"]
+        y = c["wte"].reshape(-1, w)[c["id"]] + c["wpe"].reshape(-1, w)[c["position"]]
+        np.testing.assert_array_equal(y.view(np.uint32), c["y"].view(np.uint32))
+    for c in goldens.cases("elementwise", "kAdd"):
+        np.testing.assert_array_equal((c["a"] + c["b"]).view(np.uint32), c["y"].view(np.uint32))
