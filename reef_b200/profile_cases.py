@@ -15,7 +15,8 @@ about 1 GiB on the device); the default flash case is config 3's attention.
 ``sweep`` is not a capture case: it times the W8A8 GEMM at every point of the
 config-5 sweep (M in {1, 16, 128, 1024, 8192, 16384} x five (N, K) shapes)
 through the C ABI -- ``reef_b200_gemm_w8a8`` for M > 128, the swap-AB split-K
-``reef_b200_gemm_w8a8_skinny`` for M <= 128 -- with CUDA events, and prints
+``reef_b200_gemm_w8a8_skinny`` for M <= 128 -- replayed from a CUDA graph and
+timed with CUDA events, and prints
 one JSON line per point with its roofline fraction (tensor-bound against twice
 the measured burst bf16 rate for M >= 1024, HBM-bound against the measured
 copy bandwidth below).  Operands rotate through enough copies that every call
@@ -123,9 +124,8 @@ def _peaks() -> dict:
         return {"int8_tops": 2.0 * 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def sweep(out: str | None, iters: int = 20) -> None:
+def sweep(out: str | None, iters: int = 20, reps: int = 3) -> None:
     peaks = _peaks()
-    st = torch.cuda.current_stream().cuda_stream
     lib = _lib.lib()
     rows = []
     for (n, k) in SWEEP_NK:
@@ -147,6 +147,7 @@ def sweep(out: str | None, iters: int = 20) -> None:
 
             def call(i: int) -> None:
                 c = i % copies
+                st = torch.cuda.current_stream().cuda_stream
                 if skinny:
                     _lib.call("reef_b200_gemm_w8a8_skinny", m, k, n, a[c].data_ptr(), xs.data_ptr(),
                               b[c].data_ptr(), ws.data_ptr(), None, work.data_ptr(), work.numel(),
@@ -158,14 +159,24 @@ def sweep(out: str | None, iters: int = 20) -> None:
             for i in range(3):
                 call(i)
             torch.cuda.synchronize()
+            # the timed calls replay from a CUDA graph, so the host's cost per
+            # call (ctypes, tensor-map encoding) is off the clock, as in a
+            # captured decode step
+            graph = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream()
+            with torch.cuda.stream(cap), torch.cuda.graph(graph, stream=cap):
+                for i in range(iters):
+                    call(i)
+            graph.replay()
+            torch.cuda.synchronize()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            for i in range(iters):
-                call(i)
+            for _ in range(reps):
+                graph.replay()
             e1.record()
             torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / iters
+            ms = e0.elapsed_time(e1) / (reps * iters)
             ops = 2.0 * m * n * k
             moved = m * k + n * k + 4.0 * m * n  # int8 A and B, fp32 y
             tops = ops / (ms * 1e-3) / 1e12
@@ -177,7 +188,7 @@ def sweep(out: str | None, iters: int = 20) -> None:
                  "peak_source": peaks["source"], "operand_copies": copies}
             rows.append(r)
             print(json.dumps(r), flush=True)
-            del a, b, y, work
+            del a, b, y, work, graph
             torch.cuda.empty_cache()
     if out:
         with open(out, "w") as fh:
