@@ -750,20 +750,40 @@ __global__ void splitk_reduce_kernel(int splits, int M, int N, const int32_t* __
   }
 }
 
-int skinny_splits(int n, int k) {
+// K splits for the skinny GEMM.  When the tiles fit on the SMs, split K so
+// that tiles x splits fills one wave without passing the SM count (at least
+// two k-blocks per split): a second, partial wave gives some CTAs two items,
+// and measured slower than one wave even with more, shorter items.  When
+// there are more tiles than SMs (a wide weight), the persistent grid deals
+// (tile, split) items round-robin, so the slowest CTA runs ceil(items / SMs)
+// items of ceil(k-blocks / splits) blocks (+1 for the per-item hand-off),
+// and the partials add splits * m * 4 bytes per weight row against k bytes of
+// weights: take the split count (<= 16) that minimises that product.
+int skinny_splits(int m, int n, int k) {
   const int tiles = (n + kBM - 1) / kBM;
   const int nk = (k + kBK - 1) / kBK;
-  // one wave: tiles x splits <= SMs.  A second, partial wave would give some
-  // CTAs two items, doubling the slowest CTA's share; at least two k-blocks
-  // per split.
-  const int fit = num_sms() / tiles;
-  return std::max(1, std::min(fit, std::max(1, nk / 2)));
+  const int sms = num_sms();
+  if (tiles <= sms) return std::max(1, std::min(sms / tiles, std::max(1, nk / 2)));
+  int best = 1;
+  double best_cost = 0.0;
+  for (int s = 1; s <= 16; ++s) {
+    if (s > 1 && nk / s < 2) break;
+    const long long items = static_cast<long long>(tiles) * s;
+    const long long waves = (items + sms - 1) / sms;
+    const double cost = static_cast<double>(waves) * ((nk + s - 1) / s + 1) *
+                        (1.0 + 4.0 * s * m / static_cast<double>(k));
+    if (s == 1 || cost < best_cost * (1.0 - 1e-9)) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 }  // namespace
 
 size_t skinny_partial_bytes(int m, int n, int k) {
-  return static_cast<size_t>(skinny_splits(n, k)) * n * m * sizeof(int32_t);
+  return static_cast<size_t>(skinny_splits(m, n, k)) * n * m * sizeof(int32_t);
 }
 
 int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int epilogue,
@@ -772,7 +792,7 @@ int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int ep
   if (m <= 0 || n <= 0 || k <= 0 || m > 128 || partial == nullptr || y == nullptr)
     return kErrInvalid;
   if (epilogue != kEpiF32W8A8 && epilogue != kEpiI32) return kErrInvalid;
-  const int splits = skinny_splits(n, k);
+  const int splits = skinny_splits(m, n, k);
   GemmProblem p{};
   p.M = n;  // weight rows on the MMA's M side (swap-AB)
   p.N = m;  // tokens on its N side

@@ -152,9 +152,11 @@ def test_sweep_shapes_sampled(m, n, k):
 
 # ---- skinny (decode) GEMM: swap-AB + split-K ---------------------------------------
 
+# the config-4 decode shapes (tiles fit one wave) and wide weights with more
+# 128-row tiles than SMs (the split chosen by the multi-wave cost)
 @pytest.mark.parametrize("m", [1, 16, 64, 100, 128])
 @pytest.mark.parametrize("n,k", [(1280, 8192), (8192, 1024), (7168, 8192), (8192, 3584),
-                                 (300, 200)])
+                                 (300, 200), (19000, 1024), (28672, 2048)])
 def test_skinny_gemm_matches_oracle(m, n, k):
     g = torch.Generator(device="cuda").manual_seed(m + n + k)
     a = torch.randint(-127, 128, (m, K.kpad(k)), generator=g, device="cuda", dtype=torch.int8)
