@@ -764,6 +764,7 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
       REEF_TRY(comm_wait_count(c, cons_slot(k, o.kind), (epoch(o.kind, o.use) - 1) * peers, sk(k)));
     REEF_TRY(fn(sk(k)));
     PeerFlags f;
+    if ((N - 1) * static_cast<int>(ins.size() + outs.size()) > kMaxFlags) return kErrInvalid;
     for (int r = 0; r < N; ++r) {
       if (r == rank) continue;
       for (const Use& i : ins) f.p[f.n++] = comm_counter(c, cons_slot(k, i.kind), r);
@@ -774,6 +775,7 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
   };
   // this rank's segment of region (k, kind) in every rank's arena (the [N][Tc][w]
   // layout of the step's width w, bytes per row given)
+  static_assert(kMaxDst >= 8, "the all-gather plan runs on up to 8 ranks");
   auto everywhere = [&](int k, Kind kind, long long row_bytes, bool self) {
     PeerDst d;
     for (int r = 0; r < N; ++r) {

@@ -79,3 +79,41 @@ def test_oracle_model_reproduces_reef_generation():
     got = BF.oracle_logits(blob, seq)[prompt.size - 1:]
     np.testing.assert_array_equal(got.view(np.uint32), logits.view(np.uint32))
     assert [ro.argmax_f32(r) for r in got] == list(tokens)
+
+
+def test_model_loading_and_step_refuse_bad_arguments():
+    """Argument checks that come before any device work (no GPU needed): the
+    whole-model loader, the decode step, the cached block and the embedding
+    refuse what the engine would throw on or what would run off a buffer."""
+    L = _lib.lib()
+    blob, prompt, _, _ = BF.golden_model("w8a8")
+    rc, info = read(blob)
+    assert rc == 0 and info.layers == 4
+    need = L.reef_b200_blob_model_bytes(C.byref(info))
+    assert need >= info.layers * L.reef_b200_blob_layer_bytes(C.byref(info))
+    buf = C.create_string_buffer(blob, len(blob))
+    model = _lib.GptNeoModelDesc()
+    blocks = (_lib.GptNeoBlockDesc * info.layers)()
+    fake = C.c_void_p(1 << 20)  # never dereferenced: each call fails its checks first
+    # arena too small
+    assert L.reef_b200_blob_load_model(buf, len(blob), fake, need - 256, C.byref(model), blocks,
+                                       None) == 1
+    # a float blob is reef's other mode
+    fblob, _, _, _ = BF.golden_model("fp32")
+    fbuf = C.create_string_buffer(fblob, len(fblob))
+    assert L.reef_b200_blob_load_model(fbuf, len(fblob), fake, 1 << 30, C.byref(model), blocks,
+                                       None) == 4
+    # the decode step: no model, no tokens, an empty model
+    assert L.reef_b200_gptneo_step_workspace_bytes(None, 1) == 0
+    assert L.reef_b200_gptneo_step(None, fake, 1, 0, fake, fake, 8, None, None, fake, 1 << 20,
+                                   None) == 1
+    empty = _lib.GptNeoModelDesc()
+    assert L.reef_b200_gptneo_step_workspace_bytes(C.byref(empty), 1) == 0
+    # the cached block: new rows past the cache
+    blk = _lib.GptNeoBlockDesc()
+    blk.seq = 4
+    assert L.reef_b200_gptneo_block_forward_cached(C.byref(blk), fake, fake, 6, fake, fake, 8,
+                                                   fake, 1 << 20, None) == 1
+    # the embedding: positions past the table; nothing to do is fine
+    assert L.reef_b200_embedding_f32(32, 4, fake, 30, 96, 32, fake, fake, fake, None) == 1
+    assert L.reef_b200_embedding_f32(32, 0, fake, 30, 96, 32, fake, fake, fake, None) == 0
