@@ -20,6 +20,9 @@ buffers of each, ordered by events).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
+At one GPU the line also carries `decode_attention`: config 4's int8 decode
+attention timed on its own against the measured HBM bandwidth.
+
 --impl reference times reef's own engine (inference-engine/reference/cpp,
 compiled in place into oracle/_ref) on the host cores, on a bounded sample of
 the same workload; rank 0 prints its line, other ranks exit without work.
@@ -267,6 +270,64 @@ def peaks() -> dict:
 
 # ---- the product ---------------------------------------------------------------
 
+def decode_attention(dev, pk: dict) -> dict:
+    """Config 4's decode attention (the Llama-70B TP=8 shard: 64 sequences, 8
+    query heads on 1 KV head, 4096 cached int8 keys each), timed on its own:
+    a CUDA graph of 12 calls over 4 rotating cache copies (277 MB, past L2, so
+    every call reads its 69 MB shard from DRAM), replayed 20 times."""
+    import torch
+    from reef_b200 import _lib
+    B, HQ, HKV, L, copies, calls, reps = 64, 8, 1, 4096, 4, 12, 20
+    g = torch.Generator(device=dev).manual_seed(4)
+    q8 = torch.randint(-127, 128, (B, HQ, 128), generator=g, device=dev, dtype=torch.int8)
+    qs = torch.rand((B, HQ), generator=g, device=dev) * 0.02
+    shp = (B, HKV, L)
+    caches = []
+    for _ in range(copies):
+        caches.append((torch.randint(-127, 128, shp + (128,), generator=g, device=dev,
+                                     dtype=torch.int8),
+                       torch.rand(shp, generator=g, device=dev) * 0.02,
+                       torch.randint(-127, 128, shp + (128,), generator=g, device=dev,
+                                     dtype=torch.int8),
+                       torch.rand(shp, generator=g, device=dev) * 0.02))
+    out = torch.empty((B, HQ, 128), device=dev)
+    n = _lib.lib().reef_b200_decode_attn_workspace_bytes(B, HQ, L)
+    ws = torch.empty(n, dtype=torch.uint8, device=dev)
+
+    def call(c: int) -> None:
+        k8, ks, v8, vs = caches[c % copies]
+        _lib.call("reef_b200_decode_attn_i8", B, HQ, HKV, 128, L, None, L, 1.0 / math.sqrt(128),
+                  q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), v8.data_ptr(),
+                  vs.data_ptr(), ws.data_ptr(), n, out.data_ptr(),
+                  torch.cuda.current_stream(dev).cuda_stream)
+
+    for c in range(copies):
+        call(c)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cap), torch.cuda.graph(graph, stream=cap):
+        for i in range(calls):
+            call(i)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+    nbytes = 2 * B * HKV * L * (128 + 4)  # int8 K and V rows + one fp32 scale each
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"kernel": "decode_mma + decode_combine (config 4, TP=8 shard)", "us": us,
+            "bytes": nbytes, "achieved_gbs": gbs, "peak_gbs": pk["hbm"],
+            "frac": gbs / pk["hbm"], "peak_source": pk["source"],
+            "timing": f"CUDA graph of {calls} calls over {copies} rotating cache copies, "
+                      f"{reps} replays"}
+
+
 def run_reef(args) -> int:
     import torch
     import torch.distributed as dist
@@ -464,6 +525,11 @@ def run_reef(args) -> int:
         "clocks": dict(clocks.summary(w0, w1),
                        window="the timed region and the 1 s of the same forward just before it"),
     }
+    if rank == 0 and world == 1:
+        try:  # after the measured line's own work; never lets it fail
+            out["decode_attention"] = decode_attention(dev, pk)
+        except Exception as e:  # noqa: BLE001
+            out["decode_attention"] = {"error": str(e)[:200]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(s, host_threads())
     if comm is not None:
