@@ -282,6 +282,58 @@ int reef_b200_embedding_f32(size_t width, size_t count, const uint32_t* ids,
                             const float* wte, const float* wpe, float* y,
                             reef_b200_stream_t stream);
 
+/* ---- the rest of reef's Coral operator set (kernels.hpp:26-146) ---------- */
+
+/* linear_f32 / linear_bias_f32 (kernels.hpp:26-33; the engine's float
+ * linear, operator/linear.hpp:75-84): y[r][c] = sum over k, in order from 0,
+ * of x[r][k] * wt[k][c], each product and sum rounded on its own, then
+ * + bias[c] (bias may be NULL).  wt is the float weight transposed, [in][out]
+ * (Coral's layout); x [rows][in], y [rows][out] fp32; rows <= 65535.  A
+ * non-finite product or sum records 0x301 in the device error word (the
+ * engine throws).  Bit-identical; written for exactness (the float GPT-Neo
+ * path), not speed. */
+int reef_b200_linear_f32(size_t rows, size_t in, size_t out, const float* x, const float* wt,
+                         float* y, reef_b200_stream_t stream);
+int reef_b200_linear_bias_f32(size_t rows, size_t in, size_t out, const float* x,
+                              const float* wt, const float* bias, float* y,
+                              reef_b200_stream_t stream);
+/* layernorm_f32 (kernels.hpp:55-56; operator/layernorm.hpp:62-80): per row,
+ * in-order mean and variance, y = ((x - mean) * inv_std) * gain + shift
+ * (shift may be NULL).  x, y [rows][width] fp32.  Bit-identical. */
+int reef_b200_layernorm_f32(size_t rows, size_t width, const float* x, const float* gain,
+                            const float* shift, float eps, float* y, reef_b200_stream_t stream);
+/* gelu_f32, exp_nonpositive_f32, tanh_f32 (kernels.hpp:59-64; activation.hpp:
+ * 78-90, math.hpp:34-81), elementwise over n floats.  Bit-identical. */
+int reef_b200_gelu_f32(size_t n, const float* x, float* y, reef_b200_stream_t stream);
+int reef_b200_exp_nonpositive_f32(size_t n, const float* x, float* y,
+                                  reef_b200_stream_t stream);
+int reef_b200_tanh_f32(size_t n, const float* x, float* y, reef_b200_stream_t stream);
+/* add_f32 (kernels.hpp:86-87): y = a + b, one rounded add per element; a
+ * non-finite sum records 0x301. */
+int reef_b200_add_f32(size_t n, const float* a, const float* b, float* y,
+                      reef_b200_stream_t stream);
+/* gelu_int8 (kernels.hpp:111-112; int8.hpp:135-147): y[i] = table[x[i] + 128]
+ * for a 256-entry int8 table (gelu_table) in device memory. */
+int reef_b200_gelu_int8(size_t n, const int8_t* x, const int8_t* table, int8_t* y,
+                        reef_b200_stream_t stream);
+/* layernorm_int8 (kernels.hpp:132-134; int8.hpp:319-374): per row mean =
+ * floor(sum / width), std = isqrt(sum((x - mean)^2) / width), inv = 2^20 /
+ * max(std, 1), y = sat8(rshift_rnu(((x - mean) * inv >> 16) * gain +
+ * shift * 32, 5)).  width <= 32767 (the engine's int32 sum of squares).
+ * Bit-identical. */
+int reef_b200_layernorm_int8(size_t rows, size_t width, const int8_t* x, const int8_t* gain,
+                             const int8_t* shift, int8_t* y, reef_b200_stream_t stream);
+/* add_int8 (kernels.hpp:137-138; int8.hpp:382-397): y = sat8(a + b). */
+int reef_b200_add_int8(size_t n, const int8_t* a, const int8_t* b, int8_t* y,
+                       reef_b200_stream_t stream);
+/* embedding_int8 (kernels.hpp:142-145) for `count` tokens: y[t][c] =
+ * sat8(wte[ids[t]][c] + wpe[first_position + t][c]); ids on the device, the
+ * same checks and error words as reef_b200_embedding_f32. */
+int reef_b200_embedding_int8(size_t width, size_t count, const uint32_t* ids,
+                             size_t first_position, size_t vocab, size_t max_positions,
+                             const int8_t* wte, const int8_t* wpe, int8_t* y,
+                             reef_b200_stream_t stream);
+
 /* ---- int8 flash attention (the fast head) ------------------------------- */
 
 /* Packs one QKV projection output for the flash head.  qkv [batch*seq]

@@ -323,6 +323,58 @@ def matvec_rows_f32(w, x):
     return y, bad == 0
 
 
+def linear_f32(x, wt, bias=None) -> np.ndarray:
+    """reef's float linear with Coral's transposed weight (kernels.hpp:26-33;
+    operator/linear.hpp:75-84): y[r][c] = sum over k, in order, of x[r][k] *
+    wt[k][c], then + bias[c] -- each row is matvec_rows_f32 of wt^T."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(np.asarray(wt, np.float32).T)
+    y = np.empty((x.shape[0], w.shape[0]), np.float32)
+    for r in range(x.shape[0]):
+        y[r], ok = matvec_rows_f32(w, x[r])
+        if not ok:
+            raise ValueError("non-finite product or sum")
+    if bias is not None:
+        y = (y + np.asarray(bias, np.float32)).astype(np.float32)
+    return y
+
+
+def gelu_int8(x, table) -> np.ndarray:
+    """gelu_int8 (int8.hpp:135-147): y = table[x + 128]."""
+    return np.asarray(table, np.int8)[np.asarray(x, np.int32) + 128]
+
+
+def add_int8(a, b) -> np.ndarray:
+    """add_int8 (int8.hpp:382-397): saturate(a + b)."""
+    return np.clip(np.asarray(a, np.int32) + np.asarray(b, np.int32), -128, 127).astype(np.int8)
+
+
+def embedding_int8(wte, wpe, ids, first_position: int = 0) -> np.ndarray:
+    """embedding_int8 (kernels.hpp:142-145): saturate(wte[id] + wpe[position])."""
+    ids = np.asarray(ids, np.int64)
+    pos = first_position + np.arange(ids.size)
+    return add_int8(np.asarray(wte)[ids], np.asarray(wpe)[pos])
+
+
+def layernorm_int8(x, gain, shift) -> np.ndarray:
+    """layernorm_int8 (int8.hpp:319-374): per row mean = floor(sum / width)
+    (floor_div, :311-316), std = isqrt(sum((x - mean)^2) / width) (isqrt,
+    :291-303, the floor of the square root), inv = 2^20 / max(std, 1), then
+    saturate(rounding_shift(((x - mean) * inv >> 16) * gain + shift * 32, 5))
+    with arithmetic right shifts."""
+    import math
+    x = np.asarray(x, np.int64)
+    rows, width = x.shape
+    mean = np.floor_divide(x.sum(axis=1), width)
+    c = x - mean[:, None]
+    dev = np.array([math.isqrt(int(v) // width) for v in (c * c).sum(axis=1)], np.int64)
+    inv = (1 << 20) // np.maximum(dev, 1)
+    normed = (c * inv[:, None]) >> 16
+    scaled = normed * np.asarray(gain, np.int64) + np.asarray(shift, np.int64) * 32
+    r = (scaled >> 5) + ((scaled >> 4) & 1)
+    return np.clip(r, -128, 127).astype(np.int8)
+
+
 def argmax_f32(x) -> int:
     """argmax (model.hpp:32-42): the first index of the largest value."""
     x = np.ascontiguousarray(x, np.float32)

@@ -37,6 +37,17 @@ SIGNATURES = {
     "reef_b200_blob_model_bytes": ([_p], _sz),
     "reef_b200_blob_load_model": ([_p, _sz, _p, _sz, _p, _p, _p], _i),
     "reef_b200_embedding_f32": ([_sz, _sz, _p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
+    "reef_b200_embedding_int8": ([_sz, _sz, _p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
+    "reef_b200_linear_f32": ([_sz, _sz, _sz, _p, _p, _p, _p], _i),
+    "reef_b200_linear_bias_f32": ([_sz, _sz, _sz, _p, _p, _p, _p, _p], _i),
+    "reef_b200_layernorm_f32": ([_sz, _sz, _p, _p, _p, C.c_float, _p, _p], _i),
+    "reef_b200_gelu_f32": ([_sz, _p, _p, _p], _i),
+    "reef_b200_exp_nonpositive_f32": ([_sz, _p, _p, _p], _i),
+    "reef_b200_tanh_f32": ([_sz, _p, _p, _p], _i),
+    "reef_b200_add_f32": ([_sz, _p, _p, _p, _p], _i),
+    "reef_b200_gelu_int8": ([_sz, _p, _p, _p, _p], _i),
+    "reef_b200_layernorm_int8": ([_sz, _sz, _p, _p, _p, _p, _p], _i),
+    "reef_b200_add_int8": ([_sz, _p, _p, _p, _p], _i),
     "reef_b200_gptneo_block_forward_cached": ([_p, _p, _p, _sz, _p, _p, _sz, _p, _sz, _p], _i),
     "reef_b200_gptneo_step_workspace_bytes": ([_p, _sz], _sz),
     "reef_b200_gptneo_step": ([_p, _p, _sz, _sz, _p, _p, _sz, _p, _p, _p, _sz, _p], _i),

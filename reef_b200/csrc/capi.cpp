@@ -98,6 +98,100 @@ int reef_b200_embedding_f32(size_t width, size_t count, const uint32_t* ids,
                        static_cast<long long>(max_positions), wte, wpe, y, S(stream));
 }
 
+int reef_b200_linear_bias_f32(size_t rows, size_t in, size_t out, const float* x,
+                              const float* wt, const float* bias, float* y,
+                              reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (!dims_ok(rows, in, out) || !x || !wt || !y) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return linear_f32(static_cast<long long>(rows), static_cast<int>(in), static_cast<int>(out), x,
+                    wt, bias, y, S(stream));
+}
+
+int reef_b200_linear_f32(size_t rows, size_t in, size_t out, const float* x, const float* wt,
+                         float* y, reef_b200_stream_t stream) {
+  return reef_b200_linear_bias_f32(rows, in, out, x, wt, nullptr, y, stream);
+}
+
+int reef_b200_layernorm_f32(size_t rows, size_t width, const float* x, const float* gain,
+                            const float* shift, float eps, float* y, reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (width == 0 || width > kMaxDim || rows > kMaxDim || !x || !gain || !y)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return layernorm_exact(static_cast<long long>(rows), static_cast<int>(width), eps, x, gain,
+                         shift, y, S(stream));
+}
+
+static int unary(int op, size_t n, const float* x, float* y, reef_b200_stream_t stream) {
+  if (n == 0) return REEF_B200_OK;
+  if (!x || !y) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return unary_exact(op, static_cast<long long>(n), x, y, S(stream));
+}
+
+int reef_b200_exp_nonpositive_f32(size_t n, const float* x, float* y,
+                                  reef_b200_stream_t stream) {
+  return unary(0, n, x, y, stream);
+}
+
+int reef_b200_tanh_f32(size_t n, const float* x, float* y, reef_b200_stream_t stream) {
+  return unary(1, n, x, y, stream);
+}
+
+int reef_b200_gelu_f32(size_t n, const float* x, float* y, reef_b200_stream_t stream) {
+  return unary(2, n, x, y, stream);
+}
+
+int reef_b200_add_f32(size_t n, const float* a, const float* b, float* y,
+                      reef_b200_stream_t stream) {
+  if (n == 0) return REEF_B200_OK;
+  if (!a || !b || !y) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return add_f32(static_cast<long long>(n), a, b, y, S(stream));
+}
+
+int reef_b200_gelu_int8(size_t n, const int8_t* x, const int8_t* table, int8_t* y,
+                        reef_b200_stream_t stream) {
+  if (n == 0) return REEF_B200_OK;
+  if (!x || !table || !y) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return gelu_int8(static_cast<long long>(n), x, table, y, S(stream));
+}
+
+int reef_b200_layernorm_int8(size_t rows, size_t width, const int8_t* x, const int8_t* gain,
+                             const int8_t* shift, int8_t* y, reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (width == 0 || width > 32767 || rows > kMaxDim || !x || !gain || !shift || !y)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return layernorm_int8(static_cast<long long>(rows), static_cast<int>(width), x, gain, shift, y,
+                        S(stream));
+}
+
+int reef_b200_add_int8(size_t n, const int8_t* a, const int8_t* b, int8_t* y,
+                       reef_b200_stream_t stream) {
+  if (n == 0) return REEF_B200_OK;
+  if (!a || !b || !y) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return add_int8(static_cast<long long>(n), a, b, y, S(stream));
+}
+
+int reef_b200_embedding_int8(size_t width, size_t count, const uint32_t* ids,
+                             size_t first_position, size_t vocab, size_t max_positions,
+                             const int8_t* wte, const int8_t* wpe, int8_t* y,
+                             reef_b200_stream_t stream) {
+  if (count == 0) return REEF_B200_OK;
+  if (width == 0 || width > kMaxDim || count > kMaxDim || vocab == 0 || max_positions == 0 ||
+      first_position > max_positions || count > max_positions - first_position || !ids ||
+      !wte || !wpe || !y)
+    return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  return embedding_int8(static_cast<int>(width), static_cast<long long>(count), ids,
+                        static_cast<long long>(first_position), static_cast<long long>(vocab),
+                        static_cast<long long>(max_positions), wte, wpe, y, S(stream));
+}
+
 int reef_b200_quantize_rows(size_t rows, size_t in, const float* x, int8_t* x_q,
                             float* x_scale, reef_b200_stream_t stream) {
   if (rows == 0) return REEF_B200_OK;

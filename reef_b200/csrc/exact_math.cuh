@@ -3,8 +3,8 @@
 // exp_nonpositive and tanh_float (math.hpp:34-81) and the tanh-form gelu
 // (operator/activation.hpp:78-90), each float operation rounded on its own
 // (__f*_rn: no fused multiply-add), in the engine's order, so every result
-// equals the engine's.  Shared by the GPT-Neo kernels and the GEMM epilogue
-// that fuses gelu into c_fc.
+// equals the engine's.  Shared by the element-wise kernels (elementwise.cu)
+// and the GEMM epilogue that fuses gelu into c_fc.
 #pragma once
 
 #include <cuda_runtime.h>

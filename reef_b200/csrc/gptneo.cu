@@ -1,17 +1,15 @@
-// gptneo.cu -- the float element-wise operators of reef's GPT-Neo block,
-// bit for bit, so a whole W8A8 block (operator/block.hpp:97-108) on the GPU
-// reproduces Block<float>::forward exactly.
+// gptneo.cu -- reef's float layernorm, bit for bit, so a whole W8A8 GPT-Neo
+// block (operator/block.hpp:97-108) on the GPU reproduces
+// Block<float>::forward exactly (its gelu runs in the c_fc GEMM's epilogue,
+// exact_math.cuh).
 //
 //   layernorm  operator/layernorm.hpp:62-80: mean and variance are in-order
 //              sums over the row (one thread), inv_std = 1 / sqrt(var + eps),
 //              y = ((x - mean) * inv_std) * gain + shift.
-//   gelu       operator/activation.hpp:78-90: the tanh form evaluated left to
-//              right, tanh_float from exp_nonpositive (math.hpp:34-81).
 // Every float step is one IEEE operation (__f*_rn, and the library is built
-// with -fmad=false).  These are tiny next to the GEMMs; they are written for
+// with -fmad=false).  It is tiny next to the GEMMs; it is written for
 // exactness, not speed.
 #include "common.cuh"
-#include "exact_math.cuh"
 #include "ops.h"
 
 namespace reef {
@@ -47,12 +45,6 @@ __global__ void layernorm_exact_kernel(int width, float eps, const float* __rest
   }
 }
 
-__global__ void gelu_exact_kernel(long long n, const float* __restrict__ x, float* __restrict__ y) {
-  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  y[i] = gelu_dev(x[i]);
-}
-
 }  // namespace
 
 int layernorm_exact(long long rows, int width, float eps, const float* x, const float* gain,
@@ -61,13 +53,6 @@ int layernorm_exact(long long rows, int width, float eps, const float* x, const 
   if (width <= 0 || !x || !gain || !y) return kErrInvalid;
   layernorm_exact_kernel<<<static_cast<unsigned>(rows), 128, 0, stream>>>(width, eps, x, gain,
                                                                           shift, y);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
-}
-
-int gelu_exact(long long n, const float* x, float* y, cudaStream_t stream) {
-  if (n == 0) return kOk;
-  if (!x || !y) return kErrInvalid;
-  gelu_exact_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(n, x, y);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -26,10 +26,6 @@
 
 namespace reef {
 
-int layernorm_exact(long long rows, int width, float eps, const float* x, const float* gain,
-                    const float* shift, float* y, cudaStream_t stream);
-int gelu_exact(long long n, const float* x, float* y, cudaStream_t stream);
-
 namespace {
 
 #define REEF_TRY(expr)            \

@@ -171,6 +171,23 @@ int matvec_rows_f32(long long out, long long in, const float* w, const float* x,
                     cudaStream_t stream);
 int argmax_f32(long long n, const float* x, uint32_t* index, cudaStream_t stream);
 
+// gptneo.cu -- reef's float layernorm, bit for bit (one row per CTA)
+int layernorm_exact(long long rows, int width, float eps, const float* x, const float* gain,
+                    const float* shift, float* y, cudaStream_t stream);
+
+// elementwise.cu -- the rest of reef's Coral operators, bit for bit
+int linear_f32(long long rows, int in, int out, const float* x, const float* wt,
+               const float* bias, float* y, cudaStream_t stream);
+int unary_exact(int op, long long n, const float* x, float* y, cudaStream_t stream);  // 0 exp, 1 tanh, 2 gelu
+int add_f32(long long n, const float* a, const float* b, float* y, cudaStream_t stream);
+int gelu_int8(long long n, const int8_t* x, const int8_t* table, int8_t* y, cudaStream_t stream);
+int add_int8(long long n, const int8_t* a, const int8_t* b, int8_t* y, cudaStream_t stream);
+int embedding_int8(int width, long long count, const uint32_t* ids, long long first_position,
+                   long long vocab, long long positions, const int8_t* wte, const int8_t* wpe,
+                   int8_t* y, cudaStream_t stream);
+int layernorm_int8(long long rows, int width, const int8_t* x, const int8_t* gain,
+                   const int8_t* shift, int8_t* y, cudaStream_t stream);
+
 // quant.cu
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q,
                   long long ldq, float* x_scale, const float* row_max,

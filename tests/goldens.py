@@ -34,6 +34,12 @@ FIELDS = {
     "kMatvec": ("out", "in", "w", "x", "y"),
     "kArgmax": ("n", "x", "index"),
     "kAdd": ("n", "a", "b", "y"),
+    "kLinear": ("rows", "in", "out", "x", "wt", "y"),
+    "kLinearBias": ("rows", "in", "out", "x", "wt", "bias", "y"),
+    "kInt8Gelu": ("n", "table", "x", "y"),
+    "kInt8LayerNorm": ("rows", "width", "x", "gain", "shift", "y"),
+    "kInt8Add": ("n", "a", "b", "y"),
+    "kInt8Embedding": ("width", "id", "position", "wte", "wpe", "y"),
     "kEmbedding": ("width", "id", "position", "wte", "wpe", "y"),
     "kGptNeo": ("blob", "prompt_length", "prompt", "new_tokens", "tokens", "vocab_size",
                 "logits"),

@@ -267,3 +267,33 @@ def test_embedding_and_add_match_reef_goldens():
         np.testing.assert_array_equal(y.view(np.uint32), c["y"].view(np.uint32))
     for c in goldens.cases("elementwise", "kAdd"):
         np.testing.assert_array_equal((c["a"] + c["b"]).view(np.uint32), c["y"].view(np.uint32))
+
+
+def test_coral_float_linear_matches_reef_goldens():
+    """kLinear / kLinearBias (gen_golden.cpp): the float linear with Coral's
+    [in][out] weight, bit for bit."""
+    for table in ("kLinear", "kLinearBias"):
+        for c in goldens.cases("linear", table):
+            x = c["x"].reshape(c["rows"], c["in"])
+            wt = c["wt"].reshape(c["in"], c["out"])
+            y = ro.linear_f32(x, wt, c.get("bias"))
+            np.testing.assert_array_equal(y.view(np.uint32).ravel(),
+                                          c["y"].view(np.uint32))
+
+
+def test_int8_elementwise_match_reef_goldens():
+    """kInt8Gelu, kInt8LayerNorm, kInt8Add, kInt8Embedding (gen_golden.cpp
+    write_int8): the integer-only operators, exactly."""
+    for c in goldens.cases("int8", "kInt8Gelu"):
+        np.testing.assert_array_equal(ro.gelu_int8(c["x"], c["table"]), c["y"])
+    for c in goldens.cases("int8", "kInt8LayerNorm"):
+        x = c["x"].reshape(c["rows"], c["width"])
+        np.testing.assert_array_equal(ro.layernorm_int8(x, c["gain"], c["shift"]).ravel(),
+                                      c["y"])
+    for c in goldens.cases("int8", "kInt8Add"):
+        np.testing.assert_array_equal(ro.add_int8(c["a"], c["b"]), c["y"])
+    for c in goldens.cases("int8", "kInt8Embedding"):
+        w = c["width"]
+        y = ro.embedding_int8(c["wte"].reshape(-1, w), c["wpe"].reshape(-1, w), [c["id"]],
+                              c["position"])
+        np.testing.assert_array_equal(y.ravel(), c["y"])
