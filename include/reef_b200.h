@@ -578,9 +578,25 @@ int reef_b200_gptneo_block_forward_cached(const reef_b200_gptneo_block* block, c
 
 /* ---- GPT-Neo decode loop (the firmware's GptNeo::step) ------------------ */
 
-/* A whole W8A8 GPT-Neo model: the token and position tables, the final
- * LayerNorm and `layers` blocks (a HOST array; each block's seq is
- * ignored).  wte doubles as the tied lm_head. */
+/* A float GPT-Neo block (the firmware's kFloat32 layers, gpt_neo.cc:100-121
+ * through linear_f32 / linear_bias_f32): weights in Coral's [in][out]
+ * layout, fp32; TP = 1.  Run by reef_b200_gptneo_step (every operator the
+ * engine's float Block<float>::forward uses, bit for bit). */
+typedef struct reef_b200_gptneo_block_f32 {
+  size_t seq, hidden, heads, head_dim, ffn, window;
+  float eps;
+  const float* ln1_g; const float* ln1_b;       /* [hidden] */
+  const float* wq; const float* wk; const float* wv;   /* [hidden][heads*head_dim] */
+  const float* wo; const float* bo;             /* [heads*head_dim][hidden], [hidden] */
+  const float* ln2_g; const float* ln2_b;
+  const float* wfc; const float* bfc;           /* [hidden][ffn], [ffn] */
+  const float* wproj; const float* bproj;       /* [ffn][hidden], [hidden] */
+} reef_b200_gptneo_block_f32;
+
+/* A whole GPT-Neo model: the token and position tables, the final LayerNorm
+ * and `layers` blocks -- W8A8 (`blocks`) or float (`blocks_f32`, the other
+ * NULL), a HOST array whose seq fields are ignored.  wte doubles as the tied
+ * lm_head. */
 typedef struct reef_b200_gptneo_model {
   size_t vocab, max_positions, hidden, layers;
   float eps;
@@ -589,12 +605,14 @@ typedef struct reef_b200_gptneo_model {
   const float* ln_f_g;   /* [hidden] */
   const float* ln_f_b;
   const reef_b200_gptneo_block* blocks;
+  const reef_b200_gptneo_block_f32* blocks_f32;
 } reef_b200_gptneo_model;
 
 /* Workspace for reef_b200_gptneo_step on up to `count` tokens at once. */
 size_t reef_b200_gptneo_step_workspace_bytes(const reef_b200_gptneo_model* model, size_t count);
-/* GptNeo::step (coral/firmware/gpt_neo.cc:123-188) for `count` tokens at
- * once: ids [count] (device uint32) at positions [position, position +
+/* GptNeo::step (coral/firmware/gpt_neo.cc:123-188), W8A8 or float, for
+ * `count` tokens at once: ids [count] (device uint32) at positions
+ * [position, position +
  * count) go through the embedding and every block, appending their keys and
  * values to the caches; then, for the last token, ln_f, the tied lm_head
  * (logits [vocab], when not NULL) and the greedy choice (*next_id, device
@@ -603,7 +621,7 @@ size_t reef_b200_gptneo_step_workspace_bytes(const reef_b200_gptneo_model* model
  * [max_tokens][heads*head_dim] fp32; position + count <= max_tokens <=
  * max_positions.  A prompt may go in at once (count = its length) or a
  * token at a time: the logits are the same bits, and equal the engine's
- * GPTNeo<float> forward.  Feeding next_id back as the next call's ids
+ * GPTNeo<float> forward at that precision.  Feeding next_id back as the next call's ids
  * makes a generation loop with no host round trip (capturable in a CUDA
  * graph for a fixed position). */
 int reef_b200_gptneo_step(const reef_b200_gptneo_model* model, const uint32_t* ids,
@@ -642,16 +660,19 @@ size_t reef_b200_blob_layer_bytes(const reef_b200_blob_info* info);
 int reef_b200_blob_load_layer(const void* blob, size_t bytes, size_t layer, void* arena,
                               size_t arena_bytes, reef_b200_gptneo_block* block,
                               reef_b200_stream_t stream);
-/* Device bytes a whole model takes in reef_b200_blob_load_model's arena. */
+/* Device bytes a whole model (either precision) takes in
+ * reef_b200_blob_load_model's arena. */
 size_t reef_b200_blob_model_bytes(const reef_b200_blob_info* info);
-/* Loads a whole W8A8 blob (the firmware's GptNeo constructor, gpt_neo.cc:
- * 61-97, which reads the blob in place): the tables, ln_f and every layer
- * into `arena` (device, 256-byte aligned, >= reef_b200_blob_model_bytes),
- * filling `blocks` (a host array of info.layers) and `model` (whose blocks
- * pointer is set to `blocks`).  Errors and asynchrony as
- * reef_b200_blob_load_layer. */
+/* Loads a whole blob (the firmware's GptNeo constructor, gpt_neo.cc:61-97,
+ * which reads the blob in place): the tables, ln_f and every layer into
+ * `arena` (device, 256-byte aligned, >= reef_b200_blob_model_bytes), and
+ * fills `model`.  A W8A8 blob fills `blocks` (a host array of info.layers;
+ * weights repacked K-major), a float blob `blocks_f32` (weights kept
+ * [in][out]); the array of the other precision may be NULL.  Errors and
+ * asynchrony as reef_b200_blob_load_layer. */
 int reef_b200_blob_load_model(const void* blob, size_t bytes, void* arena, size_t arena_bytes,
                               reef_b200_gptneo_model* model, reef_b200_gptneo_block* blocks,
+                              reef_b200_gptneo_block_f32* blocks_f32,
                               reef_b200_stream_t stream);
 
 #ifdef __cplusplus

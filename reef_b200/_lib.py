@@ -35,7 +35,7 @@ SIGNATURES = {
     "reef_b200_blob_layer_bytes": ([_p], _sz),
     "reef_b200_blob_load_layer": ([_p, _sz, _sz, _p, _sz, _p, _p], _i),
     "reef_b200_blob_model_bytes": ([_p], _sz),
-    "reef_b200_blob_load_model": ([_p, _sz, _p, _sz, _p, _p, _p], _i),
+    "reef_b200_blob_load_model": ([_p, _sz, _p, _sz, _p, _p, _p, _p], _i),
     "reef_b200_embedding_f32": ([_sz, _sz, _p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
     "reef_b200_embedding_int8": ([_sz, _sz, _p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
     "reef_b200_linear_f32": ([_sz, _sz, _sz, _p, _p, _p, _p], _i),
@@ -116,11 +116,19 @@ class GptNeoBlockDesc(C.Structure):
                 ("bproj", _p), ("comm", _p)]
 
 
+class GptNeoBlockF32Desc(C.Structure):
+    """reef_b200_gptneo_block_f32 (include/reef_b200.h)."""
+    _fields_ = [("seq", _sz), ("hidden", _sz), ("heads", _sz), ("head_dim", _sz), ("ffn", _sz),
+                ("window", _sz), ("eps", C.c_float), ("ln1_g", _p), ("ln1_b", _p),
+                ("wq", _p), ("wk", _p), ("wv", _p), ("wo", _p), ("bo", _p), ("ln2_g", _p),
+                ("ln2_b", _p), ("wfc", _p), ("bfc", _p), ("wproj", _p), ("bproj", _p)]
+
+
 class GptNeoModelDesc(C.Structure):
     """reef_b200_gptneo_model (include/reef_b200.h)."""
     _fields_ = [("vocab", _sz), ("max_positions", _sz), ("hidden", _sz), ("layers", _sz),
                 ("eps", C.c_float), ("wte", _p), ("wpe", _p), ("ln_f_g", _p), ("ln_f_b", _p),
-                ("blocks", _p)]
+                ("blocks", _p), ("blocks_f32", _p)]
 
 
 class BlobInfo(C.Structure):

@@ -15,7 +15,8 @@
 // descriptor with the pointers.  Loading a model puts the token and position
 // tables and ln_f first, then one such layer arena per layer, and fills a
 // model descriptor (the firmware's GptNeo constructor reads the blob in
-// place instead).
+// place instead).  A float blob's layers keep their [in][out] weights, which
+// the exact float linear reads as they are.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -116,11 +117,38 @@ Arena arena_layout(size_t d, size_t f) {
   return a;
 }
 
+struct ArenaF32 {  // byte offsets of one float layer's arrays (weights kept [in][out])
+  size_t wq, wk, wv, wo, wfc, wproj;
+  size_t bo, ln1g, ln1b, ln2g, ln2b, bproj, bfc;
+  size_t end;
+};
+
+ArenaF32 arena_layout_f32(size_t d, size_t f) {
+  ArenaF32 a{};
+  size_t at = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = at;
+    at += al256(bytes);
+    return o;
+  };
+  a.wq = take(d * d * 4);
+  a.wk = take(d * d * 4);
+  a.wv = take(d * d * 4);
+  a.wo = take(d * d * 4);
+  a.wfc = take(d * f * 4);
+  a.wproj = take(f * d * 4);
+  for (size_t* p : {&a.bo, &a.ln1g, &a.ln1b, &a.ln2g, &a.ln2b, &a.bproj}) *p = take(d * 4);
+  a.bfc = take(f * 4);
+  a.end = at;
+  return a;
+}
+
 struct ModelArena {  // byte offsets of the model-level arrays, then the layers
   size_t wte, wpe, ln_f_g, ln_f_b, layers, layer_bytes, end;
 };
 
-ModelArena model_layout(size_t vocab, size_t positions, size_t d, size_t layers, size_t f) {
+ModelArena model_layout(size_t vocab, size_t positions, size_t d, size_t layers, size_t f,
+                        bool w8a8) {
   ModelArena m{};
   size_t at = 0;
   auto take = [&](size_t bytes) {
@@ -132,10 +160,59 @@ ModelArena model_layout(size_t vocab, size_t positions, size_t d, size_t layers,
   m.wpe = take(positions * d * 4);
   m.ln_f_g = take(d * 4);
   m.ln_f_b = take(d * 4);
-  m.layer_bytes = arena_layout(d, f).end;
+  m.layer_bytes = w8a8 ? arena_layout(d, f).end : arena_layout_f32(d, f).end;
   m.layers = at;
   m.end = at + layers * m.layer_bytes;
   return m;
+}
+
+// Copies float layer `layer` of a validated float blob into `dst` (device)
+// and fills the block.  Every span is checked before anything is copied.
+int load_layer_f32(const Header& h, const uint8_t* src, size_t layer, uint8_t* dst,
+                   reef_b200_gptneo_block_f32* block, cudaStream_t st) {
+  Layer L;
+  std::memcpy(&L, src + h.layers + layer * sizeof(Layer), sizeof(Layer));
+  const uint64_t total = h.total_bytes, d = h.hidden_size, f = h.inner_size;
+  const ArenaF32 a = arena_layout_f32(d, f);
+  const struct {
+    uint32_t off;
+    uint64_t bytes;
+    size_t to;
+  } arrays[] = {{L.ln_1_weight, d * 4, a.ln1g},   {L.ln_1_bias, d * 4, a.ln1b},
+                {L.query.weight, d * d * 4, a.wq}, {L.key.weight, d * d * 4, a.wk},
+                {L.value.weight, d * d * 4, a.wv}, {L.output.weight, d * d * 4, a.wo},
+                {L.output_bias, d * 4, a.bo},      {L.ln_2_weight, d * 4, a.ln2g},
+                {L.ln_2_bias, d * 4, a.ln2b},      {L.fc.weight, d * f * 4, a.wfc},
+                {L.fc_bias, f * 4, a.bfc},         {L.proj.weight, f * d * 4, a.wproj},
+                {L.proj_bias, d * 4, a.bproj}};
+  for (const auto& r : arrays)
+    if (!span_ok(r.off, r.bytes, total)) return REEF_B200_ERR_INVALID;
+  for (const auto& r : arrays)
+    if (cudaMemcpyAsync(dst + r.to, src + r.off, r.bytes, cudaMemcpyHostToDevice, st) !=
+        cudaSuccess)
+      return REEF_B200_ERR_CUDA;
+  auto f32 = [&](size_t o) { return reinterpret_cast<const float*>(dst + o); };
+  block->seq = 0;
+  block->hidden = d;
+  block->heads = h.num_heads;
+  block->head_dim = d / h.num_heads;
+  block->ffn = f;
+  block->window = L.is_local ? h.window_size : 0;
+  block->eps = h.layer_norm_eps;
+  block->ln1_g = f32(a.ln1g);
+  block->ln1_b = f32(a.ln1b);
+  block->wq = f32(a.wq);
+  block->wk = f32(a.wk);
+  block->wv = f32(a.wv);
+  block->wo = f32(a.wo);
+  block->bo = f32(a.bo);
+  block->ln2_g = f32(a.ln2g);
+  block->ln2_b = f32(a.ln2b);
+  block->wfc = f32(a.wfc);
+  block->bfc = f32(a.bfc);
+  block->wproj = f32(a.wproj);
+  block->bproj = f32(a.bproj);
+  return REEF_B200_OK;
 }
 
 bool model_size_ok(size_t vocab, size_t positions, size_t d, size_t layers, size_t f) {
@@ -291,21 +368,25 @@ size_t reef_b200_blob_model_bytes(const reef_b200_blob_info* info) {
   if (info == nullptr ||
       !model_size_ok(info->vocab, info->max_positions, info->hidden, info->layers, info->inner))
     return 0;
-  return model_layout(info->vocab, info->max_positions, info->hidden, info->layers, info->inner)
+  return model_layout(info->vocab, info->max_positions, info->hidden, info->layers, info->inner,
+                      info->precision == kPrecisionW8A8)
       .end;
 }
 
 int reef_b200_blob_load_model(const void* blob, size_t bytes, void* arena, size_t arena_bytes,
                               reef_b200_gptneo_model* model, reef_b200_gptneo_block* blocks,
+                              reef_b200_gptneo_block_f32* blocks_f32,
                               reef_b200_stream_t stream) {
-  if (arena == nullptr || model == nullptr || blocks == nullptr) return REEF_B200_ERR_INVALID;
+  if (arena == nullptr || model == nullptr) return REEF_B200_ERR_INVALID;
   Header h;
   if (int rc = read_header(blob, bytes, &h)) return rc;
-  if (h.precision != kPrecisionW8A8) return REEF_B200_ERR_UNSUPPORTED;
+  const bool w8a8 = h.precision == kPrecisionW8A8;
+  if ((w8a8 && blocks == nullptr) || (!w8a8 && blocks_f32 == nullptr))
+    return REEF_B200_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(arena) % 256 != 0) return REEF_B200_ERR_ALIGNMENT;
   const size_t v = h.vocab_size, n = h.max_positions, d = h.hidden_size, f = h.inner_size;
   if (!model_size_ok(v, n, d, h.num_layers, f)) return REEF_B200_ERR_TOO_LARGE;
-  const ModelArena ma = model_layout(v, n, d, h.num_layers, f);
+  const ModelArena ma = model_layout(v, n, d, h.num_layers, f, w8a8);
   if (arena_bytes < ma.end) return REEF_B200_ERR_INVALID;
   if (int rc = check_device()) return rc;
   const auto* src = static_cast<const uint8_t*>(blob);
@@ -324,9 +405,11 @@ int reef_b200_blob_load_model(const void* blob, size_t bytes, void* arena, size_
         cudaSuccess)
       return REEF_B200_ERR_CUDA;
   for (size_t l = 0; l < h.num_layers; ++l) {
-    if (int rc = reef_b200_blob_load_layer(blob, bytes, l, dst + ma.layers + l * ma.layer_bytes,
-                                           ma.layer_bytes, &blocks[l], stream))
-      return rc;
+    uint8_t* at = dst + ma.layers + l * ma.layer_bytes;
+    const int rc = w8a8 ? reef_b200_blob_load_layer(blob, bytes, l, at, ma.layer_bytes,
+                                                    &blocks[l], stream)
+                        : load_layer_f32(h, src, l, at, &blocks_f32[l], st);
+    if (rc != REEF_B200_OK) return rc;
   }
   auto f32 = [&](size_t o) { return reinterpret_cast<const float*>(dst + o); };
   model->vocab = v;
@@ -338,7 +421,8 @@ int reef_b200_blob_load_model(const void* blob, size_t bytes, void* arena, size_
   model->wpe = f32(ma.wpe);
   model->ln_f_g = f32(ma.ln_f_g);
   model->ln_f_b = f32(ma.ln_f_b);
-  model->blocks = blocks;
+  model->blocks = w8a8 ? blocks : nullptr;
+  model->blocks_f32 = w8a8 ? nullptr : blocks_f32;
   return REEF_B200_OK;
 }
 

@@ -503,20 +503,103 @@ int neo_forward(const reef_b200_gptneo_block* B, const float* x, float* y, const
 }
 
 
+// ---- float GPT-Neo block ----------------------------------------------------------------
+
+int neo_f32_check(const reef_b200_gptneo_block_f32* B) {
+  if (B == nullptr || B->seq == 0 || B->hidden == 0 || B->heads == 0 || B->head_dim == 0 ||
+      B->ffn == 0 || B->seq > static_cast<size_t>(kMaxKeysExact) || B->seq > 65535 ||
+      !B->ln1_g || !B->wq || !B->wk || !B->wv || !B->wo || !B->ln2_g || !B->wfc || !B->wproj)
+    return REEF_B200_ERR_INVALID;
+  return REEF_B200_OK;
+}
+
+struct NeoF32Bufs {
+  float* h;    // layernormed rows [T][d]
+  float* q;    // [T][dl]
+  float* ctx;  // [T][dl]
+  float* t;    // a sublayer's output [T][d]
+  float* a;    // x + attention [T][d]
+  float* f;    // [T][ffn]
+};
+
+size_t neo_f32_carve(const reef_b200_gptneo_block_f32* B, void* ws, NeoF32Bufs* b) {
+  const size_t T = B->seq, d = B->hidden, dl = B->heads * B->head_dim;
+  Carve c(ws, ~static_cast<size_t>(0));
+  b->h = c.take<float>(T * d);
+  b->q = c.take<float>(T * dl);
+  b->ctx = c.take<float>(T * dl);
+  b->t = c.take<float>(T * d);
+  b->a = c.take<float>(T * d);
+  b->f = c.take<float>(T * B->ffn);
+  return c.used + 256;
+}
+
+// The firmware's float layer (gpt_neo.cc:136-176 with Precision::kFloat32)
+// on `seq` new positions of this layer's cache: every operator exact, so the
+// rows equal the engine's float Block<float>::forward.
+int neo_f32_forward(const reef_b200_gptneo_block_f32* B, const float* x, float* y,
+                    const NeoCache& kv, void* workspace, size_t workspace_bytes,
+                    cudaStream_t st) {
+  if (int rc = neo_f32_check(B)) return rc;
+  NeoF32Bufs b;
+  if (neo_f32_carve(B, workspace, &b) > workspace_bytes) return REEF_B200_ERR_INVALID;
+  const long long T = static_cast<long long>(B->seq);
+  const int d = static_cast<int>(B->hidden), dl = static_cast<int>(B->heads * B->head_dim),
+            F = static_cast<int>(B->ffn);
+  // x + attention(ln_1(x)): q/k/v without bias, the keys and values into the cache
+  REEF_TRY(layernorm_exact(T, d, B->eps, x, B->ln1_g, B->ln1_b, b.h, st));
+  REEF_TRY(linear_f32(T, d, dl, b.h, B->wq, nullptr, b.q, st));
+  REEF_TRY(linear_f32(T, d, dl, b.h, B->wk, nullptr, kv.k + kv.position * dl, st));
+  REEF_TRY(linear_f32(T, d, dl, b.h, B->wv, nullptr, kv.v + kv.position * dl, st));
+  AttnHeadArgs aa{};
+  aa.heads = static_cast<int>(B->heads);
+  aa.query_len = static_cast<int>(T);
+  aa.key_len = static_cast<int>(kv.position + T);
+  aa.head_dim = static_cast<int>(B->head_dim);
+  aa.window = static_cast<int>(B->window);
+  aa.query_start = static_cast<long long>(kv.position);
+  aa.q_stride = aa.kv_stride = aa.out_stride = dl;
+  aa.q_head = aa.kv_head = aa.out_head = static_cast<long long>(B->head_dim);
+  REEF_TRY(attention_head_f32(aa, b.q, kv.k, kv.v, b.ctx, st));
+  REEF_TRY(linear_f32(T, dl, d, b.ctx, B->wo, B->bo, b.t, st));
+  REEF_TRY(add_f32(T * d, x, b.t, b.a, st));
+  // + mlp(ln_2(.)): c_fc + bias, gelu, c_proj + bias
+  REEF_TRY(layernorm_exact(T, d, B->eps, b.a, B->ln2_g, B->ln2_b, b.h, st));
+  REEF_TRY(linear_f32(T, d, F, b.h, B->wfc, B->bfc, b.f, st));
+  REEF_TRY(unary_exact(2, T * F, b.f, b.f, st));
+  REEF_TRY(linear_f32(T, F, d, b.f, B->wproj, B->bproj, b.t, st));
+  return add_f32(T * d, b.a, b.t, y, st);
+}
+
 // ---- GPT-Neo model step ------------------------------------------------------------------
 
+// the cache row width (heads * head_dim) of a model's blocks
+size_t model_width(const reef_b200_gptneo_model* m) {
+  return m->blocks != nullptr ? m->blocks[0].heads * m->blocks[0].head_dim
+                              : m->blocks_f32[0].heads * m->blocks_f32[0].head_dim;
+}
+
 int model_check(const reef_b200_gptneo_model* m, size_t count) {
-  if (m == nullptr || m->blocks == nullptr || m->layers == 0 || m->vocab == 0 ||
-      m->max_positions == 0 || m->hidden == 0 || count == 0 ||
+  if (m == nullptr || (m->blocks == nullptr) == (m->blocks_f32 == nullptr) || m->layers == 0 ||
+      m->vocab == 0 || m->max_positions == 0 || m->hidden == 0 || count == 0 ||
       count > static_cast<size_t>(kMaxKeysExact) || !m->wte || !m->wpe || !m->ln_f_g ||
       !m->ln_f_b || m->vocab > 0xffffffffull)
     return REEF_B200_ERR_INVALID;
-  const size_t dl = m->blocks[0].heads * m->blocks[0].head_dim;
+  const size_t dl = model_width(m);
   for (size_t l = 0; l < m->layers; ++l) {
-    reef_b200_gptneo_block blk = m->blocks[l];
-    blk.seq = count;
-    if (blk.hidden != m->hidden || blk.heads * blk.head_dim != dl || neo_check(&blk) != REEF_B200_OK)
-      return REEF_B200_ERR_INVALID;
+    if (m->blocks != nullptr) {
+      reef_b200_gptneo_block blk = m->blocks[l];
+      blk.seq = count;
+      if (blk.hidden != m->hidden || blk.heads * blk.head_dim != dl ||
+          neo_check(&blk) != REEF_B200_OK)
+        return REEF_B200_ERR_INVALID;
+    } else {
+      reef_b200_gptneo_block_f32 blk = m->blocks_f32[l];
+      blk.seq = count;
+      if (blk.hidden != m->hidden || blk.heads * blk.head_dim != dl ||
+          neo_f32_check(&blk) != REEF_B200_OK)
+        return REEF_B200_ERR_INVALID;
+    }
   }
   return REEF_B200_OK;
 }
@@ -537,10 +620,17 @@ size_t step_carve(const reef_b200_gptneo_model* m, size_t count, void* ws, StepB
   b->logits = c.take<float>(m->vocab);
   size_t need = 0;
   for (size_t l = 0; l < m->layers; ++l) {
-    reef_b200_gptneo_block blk = m->blocks[l];
-    blk.seq = count;
-    NeoBufs nb;
-    need = std::max(need, neo_carve(&blk, nullptr, &nb));
+    if (m->blocks != nullptr) {
+      reef_b200_gptneo_block blk = m->blocks[l];
+      blk.seq = count;
+      NeoBufs nb;
+      need = std::max(need, neo_carve(&blk, nullptr, &nb));
+    } else {
+      reef_b200_gptneo_block_f32 blk = m->blocks_f32[l];
+      blk.seq = count;
+      NeoF32Bufs nb;
+      need = std::max(need, neo_f32_carve(&blk, nullptr, &nb));
+    }
   }
   b->block_bytes = need;
   b->block_ws = c.take<uint8_t>(need);
@@ -1202,7 +1292,7 @@ int reef_b200_gptneo_step(const reef_b200_gptneo_model* m, const uint32_t* ids, 
   if (int rc = check_device()) return rc;
   cudaStream_t st = S(stream);
   const size_t d = m->hidden;
-  const size_t dl = m->blocks[0].heads * m->blocks[0].head_dim;
+  const size_t dl = model_width(m);
   // x = wte[id] + wpe[position] (gpt_neo.cc:130-133)
   REEF_TRY(embedding_f32(static_cast<int>(d), static_cast<long long>(count), ids,
                          static_cast<long long>(position), static_cast<long long>(m->vocab),
@@ -1210,11 +1300,17 @@ int reef_b200_gptneo_step(const reef_b200_gptneo_model* m, const uint32_t* ids, 
   // every block on this layer's cache (gpt_neo.cc:135-177)
   int cur = 0;
   for (size_t l = 0; l < m->layers; ++l) {
-    reef_b200_gptneo_block blk = m->blocks[l];
-    blk.seq = count;
     const size_t layer_off = l * max_tokens * dl;
     const NeoCache kv{k_cache + layer_off, v_cache + layer_off, position};
-    REEF_TRY(neo_forward(&blk, b.x[cur], b.x[cur ^ 1], &kv, b.block_ws, b.block_bytes, st));
+    if (m->blocks != nullptr) {
+      reef_b200_gptneo_block blk = m->blocks[l];
+      blk.seq = count;
+      REEF_TRY(neo_forward(&blk, b.x[cur], b.x[cur ^ 1], &kv, b.block_ws, b.block_bytes, st));
+    } else {
+      reef_b200_gptneo_block_f32 blk = m->blocks_f32[l];
+      blk.seq = count;
+      REEF_TRY(neo_f32_forward(&blk, b.x[cur], b.x[cur ^ 1], kv, b.block_ws, b.block_bytes, st));
+    }
     cur ^= 1;
   }
   if (logits == nullptr && next_id == nullptr) return REEF_B200_OK;

@@ -228,8 +228,9 @@ class GptNeoBlock:
 
 
 class GptNeoModel:
-    """A whole W8A8 GPT-Neo from reef's packed blob, generating on the GPU: the
-    firmware's GptNeo (coral/firmware/gpt_neo.cc:61-188) over the C ABI.
+    """A whole GPT-Neo (W8A8 or float) from reef's packed blob, generating on
+    the GPU: the firmware's GptNeo (coral/firmware/gpt_neo.cc:61-188) over the
+    C ABI.
 
     ``reef_b200_blob_load_model`` puts the blob's tables and layers in one
     device arena; ``step`` runs ``reef_b200_gptneo_step`` on ids already on
@@ -248,11 +249,14 @@ class GptNeoModel:
         if nbytes == 0:
             raise ValueError("blob shape out of range")
         self.arena = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        self.blocks = (_lib.GptNeoBlockDesc * self.info.layers)()
+        w8a8 = self.info.precision == 1
+        kind = _lib.GptNeoBlockDesc if w8a8 else _lib.GptNeoBlockF32Desc
+        self.blocks = (kind * self.info.layers)()
         self.desc = _lib.GptNeoModelDesc()
         st = torch.cuda.current_stream(dev).cuda_stream
         _lib.call("reef_b200_blob_load_model", self._blob, len(blob), self.arena.data_ptr(),
-                  nbytes, C.byref(self.desc), self.blocks, st)
+                  nbytes, C.byref(self.desc), self.blocks if w8a8 else None,
+                  None if w8a8 else self.blocks, st)
         if max_tokens > self.info.max_positions:
             raise ValueError("max_tokens past the position table")
         width = self.blocks[0].heads * self.blocks[0].head_dim
@@ -265,12 +269,15 @@ class GptNeoModel:
             raise ValueError("invalid model description")
         self.workspace = torch.empty(wbytes, dtype=torch.uint8, device=dev)
         self.position = 0
-        self.device = dev
+        self.device = self.arena.device  # with its index
 
     def step(self, ids: torch.Tensor, logits: torch.Tensor | None = None,
              next_id: torch.Tensor | None = None) -> None:
         """Runs ``ids`` (device uint32/int32 [count]) at the next positions;
         writes the last one's logits and greedy id where given."""
+        if ids.dtype not in (torch.int32, torch.uint32) or not ids.is_contiguous() or \
+                ids.device != self.device:
+            raise TypeError("ids must be a contiguous 32-bit integer tensor on the model's device")
         count = ids.numel()
         _lib.call("reef_b200_gptneo_step", C.byref(self.desc), ids.data_ptr(), count,
                   self.position, self.k_cache.data_ptr(), self.v_cache.data_ptr(),

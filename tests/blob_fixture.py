@@ -88,6 +88,58 @@ def oracle_logits(b: bytes, tokens) -> np.ndarray:
     return out
 
 
+def layer_f32(b: bytes, index: int):
+    """(float layer arrays, is_local) of a float (precision 0) blob: weights
+    kept in the blob's [in][out] layout (Coral's linear_f32 takes them so)."""
+    h = header(b)
+    assert h["precision"] == 0
+    r = dict(zip(LAYER_FIELDS, struct.unpack_from("<20I", b, h["layer_table"] + 80 * index)))
+    d, f = h["hidden"], h["inner"]
+
+    def floats(off, *shape):
+        return np.frombuffer(b, np.float32, int(np.prod(shape)), off).reshape(shape).copy()
+
+    p = {"ln1_g": floats(r["ln_1_weight"], d), "ln1_b": floats(r["ln_1_bias"], d),
+         "wq": floats(r["q_w"], d, d), "wk": floats(r["k_w"], d, d), "wv": floats(r["v_w"], d, d),
+         "wo": floats(r["o_w"], d, d), "bo": floats(r["o_b"], d),
+         "ln2_g": floats(r["ln_2_weight"], d), "ln2_b": floats(r["ln_2_bias"], d),
+         "wfc": floats(r["fc_w"], d, f), "bfc": floats(r["fc_b"], f),
+         "wproj": floats(r["proj_w"], f, d), "bproj": floats(r["proj_b"], d)}
+    return p, bool(r["is_local"])
+
+
+def oracle_logits_f32(b: bytes, tokens) -> np.ndarray:
+    """The engine's float GPTNeo forward over ``tokens`` (the firmware's
+    kFloat32 step, gpt_neo.cc:123-188, on every position), restated with the
+    oracle's exact float operators: logits [len(tokens)][vocab]."""
+    from oracle import oracle as ro
+    h = header(b)
+    m = model_arrays(b)
+    ids = np.asarray(tokens, np.int64)
+    T, d, H = ids.size, h["hidden"], h["heads"]
+    hd = d // H
+    x = (m["wte"][ids] + m["wpe"][np.arange(T)]).astype(np.float32)
+    for i in range(h["layers"]):
+        p, local = layer_f32(b, i)
+        win = h["window"] if local else 0
+        n1 = ro.layernorm(x, p["ln1_g"], p["ln1_b"], h["eps"])
+        q, k, v = (ro.linear_f32(n1, p[w]) for w in ("wq", "wk", "wv"))
+        ctx = np.empty_like(q)
+        for j in range(H):
+            sl = slice(j * hd, (j + 1) * hd)
+            ctx[:, sl] = ro.attention_head_f32(q[:, sl], k[:, sl], v[:, sl], 0, win)
+        x = (x + ro.linear_f32(ctx, p["wo"], p["bo"])).astype(np.float32)
+        n2 = ro.layernorm(x, p["ln2_g"], p["ln2_b"], h["eps"])
+        f = ro.gelu(ro.linear_f32(n2, p["wfc"], p["bfc"]))
+        x = (x + ro.linear_f32(f, p["wproj"], p["bproj"])).astype(np.float32)
+    normed = ro.layernorm(x, m["ln_f_g"], m["ln_f_b"], h["eps"])
+    out = np.empty((T, h["vocab"]), np.float32)
+    for t in range(T):
+        out[t], ok = ro.matvec_rows_f32(m["wte"], normed[t])
+        assert ok
+    return out
+
+
 def layer(b: bytes, index: int):
     """(block weights for the oracle, is_local) of one layer."""
     h = header(b)

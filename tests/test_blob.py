@@ -97,12 +97,17 @@ def test_model_loading_and_step_refuse_bad_arguments():
     fake = C.c_void_p(1 << 20)  # never dereferenced: each call fails its checks first
     # arena too small
     assert L.reef_b200_blob_load_model(buf, len(blob), fake, need - 256, C.byref(model), blocks,
+                                       None, None) == 1
+    # a W8A8 blob needs W8A8 blocks, a float blob float blocks
+    assert L.reef_b200_blob_load_model(buf, len(blob), fake, need, C.byref(model), None, None,
                                        None) == 1
-    # a float blob is reef's other mode
     fblob, _, _, _ = BF.golden_model("fp32")
     fbuf = C.create_string_buffer(fblob, len(fblob))
+    rc, finfo = read(fblob)
+    assert rc == 0 and finfo.precision == 0
+    assert L.reef_b200_blob_model_bytes(C.byref(finfo)) > 0
     assert L.reef_b200_blob_load_model(fbuf, len(fblob), fake, 1 << 30, C.byref(model), blocks,
-                                       None) == 4
+                                       None, None) == 1
     # the decode step: no model, no tokens, an empty model
     assert L.reef_b200_gptneo_step_workspace_bytes(None, 1) == 0
     assert L.reef_b200_gptneo_step(None, fake, 1, 0, fake, fake, 8, None, None, fake, 1 << 20,
@@ -117,3 +122,15 @@ def test_model_loading_and_step_refuse_bad_arguments():
     # the embedding: positions past the table; nothing to do is fine
     assert L.reef_b200_embedding_f32(32, 4, fake, 30, 96, 32, fake, fake, fake, None) == 1
     assert L.reef_b200_embedding_f32(32, 0, fake, 30, 96, 32, fake, fake, fake, None) == 0
+
+
+def test_oracle_float_model_reproduces_reef_generation():
+    """The same kGptNeo golden at float precision: the oracle's exact float
+    operators (linear with Coral's [in][out] weights, layernorm, the float
+    head, gelu, residual adds, ln_f, lm_head) reproduce every logit and token."""
+    from oracle import oracle as ro
+    blob, prompt, tokens, logits = BF.golden_model("fp32")
+    seq = np.concatenate([prompt, tokens[:-1]])
+    got = BF.oracle_logits_f32(blob, seq)[prompt.size - 1:]
+    np.testing.assert_array_equal(got.view(np.uint32), logits.view(np.uint32))
+    assert [ro.argmax_f32(r) for r in got] == list(tokens)

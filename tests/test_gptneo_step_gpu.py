@@ -1,9 +1,10 @@
 """reef's GPT-Neo W8A8 model generating on the GPU, pinned to reef's golden.
 
-reef's kGptNeo golden (gen_golden.cpp:755-805) packs a small W8A8 GPT-Neo
-(4 layers, global and local, window 8, 4 heads, vocab 96), runs the engine's
-GPTNeo<float> on a 5-token prompt and greedily generates 20 tokens, keeping
-the logits behind each; the Coral firmware is held to it.  Here the blob is
+reef's kGptNeo golden (gen_golden.cpp:755-805) packs a small GPT-Neo (4
+layers, global and local, window 8, 4 heads, vocab 96) at W8A8 and at float
+precision, runs the engine's GPTNeo<float> on a 5-token prompt and greedily
+generates 20 tokens, keeping the logits behind each; the Coral firmware is
+held to it.  Here the blob is
 loaded by reef_b200_blob_load_model and run by reef_b200_gptneo_step: every
 logit must match bit for bit and every token, whether the prompt goes in at
 once or a token at a time (the firmware's way).  The pieces are checked on
@@ -38,6 +39,17 @@ def bits(a):
 
 def test_generation_matches_reef_golden():
     blob, prompt, tokens, logits = BF.golden_model("w8a8")
+    m = GptNeoModel(blob, max_tokens=prompt.size + tokens.size)
+    got_tokens, got_logits = m.generate(prompt, tokens.size)
+    torch.cuda.synchronize()
+    assert got_tokens.tolist() == tokens.tolist()
+    np.testing.assert_array_equal(bits(got_logits.numpy()), bits(logits))
+
+
+def test_float_generation_matches_reef_golden():
+    """The float (kFloat32) model of the same golden: a float blob loads with
+    its [in][out] weights and runs the exact float operators."""
+    blob, prompt, tokens, logits = BF.golden_model("fp32")
     m = GptNeoModel(blob, max_tokens=prompt.size + tokens.size)
     got_tokens, got_logits = m.generate(prompt, tokens.size)
     torch.cuda.synchronize()
