@@ -45,7 +45,7 @@ enum reef_b200_status {
   REEF_B200_ERR_INVALID = 1,     /* bad shape, null pointer or argument */
   REEF_B200_ERR_ALIGNMENT = 2,   /* pointer / stride breaks the 16-byte rule */
   REEF_B200_ERR_CUDA = 3,        /* a CUDA call failed */
-  REEF_B200_ERR_UNSUPPORTED = 4, /* current device is not sm_100 */
+  REEF_B200_ERR_UNSUPPORTED = 4, /* current device is not sm_100, or a mode the call does not run */
   REEF_B200_ERR_NCCL = 5,        /* a NCCL call failed */
   REEF_B200_ERR_TIMEOUT = 6,     /* a bounded device wait gave up */
   REEF_B200_ERR_TOO_LARGE = 7    /* a size exceeds a documented maximum */
@@ -62,8 +62,15 @@ int reef_b200_version(void);
 size_t reef_b200_kpad(size_t in);
 /* REEF_B200_OK when the current device is a B200 (sm_100). */
 int reef_b200_check_device(void);
-/* Synchronizes the current device, stores its device error word in *code
- * (0 = none; otherwise the bounded wait that gave up) and clears it. */
+/* Synchronizes the current device, stores its device error word in *code and
+ * clears it.  0 = none; otherwise the first error any kernel recorded since
+ * the last call:
+ *   0x101..0x106  a bounded wait gave up (TMA stage full / empty,
+ *                 accumulator full / empty, the MMA drain, a peer's flag);
+ *   0x201         a decode or embedding position outside the cache / table;
+ *   0x202         a token id outside the vocabulary;
+ *   0x301         a float product or sum that is not finite (the engine
+ *                 throws std::overflow_error there). */
 int reef_b200_device_error(int* code);
 
 /* ---- quantization (quant.hpp) ------------------------------------------- */

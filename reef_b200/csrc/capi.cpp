@@ -54,7 +54,7 @@ const char* reef_b200_status_string(int status) {
   }
 }
 
-int reef_b200_version(void) { return 100; }
+int reef_b200_version(void) { return 200; }
 
 size_t reef_b200_kpad(size_t in) { return kpad(in); }
 
