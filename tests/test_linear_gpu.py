@@ -99,9 +99,14 @@ def test_quantize_rows_matches_oracle():
     x = ro.normal(5, (37, 1000))
     x[3] = 0.0
     x[4, 7] = 127.0 * 3.0
+    # near-ties that a multiply by the reciprocal of the scale (128/127) rounds
+    # the other way: the quantiser's fast path must hand them to the division
+    x[5, :4] = [128.0, 5.543306827545166, 7.559054851531982, 88.18897247314453]
+    x[5, 4:] = 0.0
     q, s = K.quantize_rows(dev(x))
     wq, ws = ro.quantize_rows(x)
     np.testing.assert_array_equal(host(q)[:, :1000], wq)
+    assert list(host(q)[5, :4]) == [127, 6, 8, 88]
     assert not host(q)[:, 1000:].any()
     np.testing.assert_array_equal(bits(host(s)), bits(ws))
 
