@@ -221,3 +221,26 @@ def test_gptneo_window_off_by_one_is_caught():
     got = np.stack([ro.matvec_rows_f32(m["wte"], normed[t])[0]
                     for t in range(prompt.size - 1, seq.size)])
     assert not same_bits(got, logits)
+
+
+# ---- the Llama layer's own definitions (parity unpinned by reef) ----------------------
+
+def test_rmsnorm_sequential_sum_is_caught():
+    """The RMSNorm's sum of squares in plain left-to-right order instead of the
+    fixed 8-chunk tree that makes TP shards reproduce TP=1: the GPU test's
+    restatement of the tree tells the scales apart."""
+    from tests.test_rmsnorm_gpu import rmsnorm_quant_ref
+    f32 = np.float32
+    x = ro.normal(3, (4, 4096))
+    gain = (1.0 + 0.1 * ro.normal(4, (4096,))).astype(f32)
+    eps = f32(1e-5)
+    _, want = rmsnorm_quant_ref(x, gain, eps)
+    got = np.empty(4, f32)
+    for r in range(4):
+        total = f32(0)
+        for v in x[r]:
+            total = f32(total + f32(v * v))
+        rr = f32(f32(1) / np.sqrt(f32(f32(total / f32(4096)) + eps)))
+        mx = f32(np.abs((x[r] * gain).astype(f32)).max() * rr)
+        got[r] = f32(mx / f32(127))
+    assert not same_bits(got, want)
