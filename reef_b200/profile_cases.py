@@ -4,7 +4,7 @@
     python -m reef_b200.profile_cases flash [--batch 8 --seq 2048 --heads 32]
     python -m reef_b200.profile_cases qkv   [--batch 8 --seq 2048 --heads 32]
     python -m reef_b200.profile_cases decode [--batch 64 --heads 8 --kv-heads 1 --seq 4096]
-    python -m reef_b200.profile_cases sweep [--out gpurun_out/sweep.json]
+    python -m reef_b200.profile_cases sweep [--out sweep.json]
 
 Each case allocates its seeded inputs once, launches the kernel twice (a
 warm-up launch, then the one to capture: ``ncu -k regex:<name> -s 1 -c 1``)

@@ -14,7 +14,7 @@ kept: ``linear`` (matvec_rows_f32 included), ``int8``, ``attention``, ``math``
 ``elementwise`` (argmax).  The committed fixtures are what the tests read; this
 script needs the reference checkout and runs here, never on a GPU box.
 
-Usage:  python tests/golden/make_golden.py [--reference /root/reference]
+Usage:  python tests/golden/make_golden.py [--reference <reef checkout>]
 """
 from __future__ import annotations
 
