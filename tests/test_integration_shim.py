@@ -1,0 +1,36 @@
+"""The C++ binding a reef maintainer would add compiles against reef.
+
+INTEGRATION.md's first C++ block is the drop-in `kernels_b200.cc`: reef's
+own `reef_kernels` signatures (coral/include/reef_kernels/kernels.hpp) with
+bodies that forward to this library's C ABI (include/reef_b200.h).  This
+test extracts it and compiles it with g++ against both headers, so a change
+to either side that breaks the binding fails here.  It needs the reef
+checkout (REEF_REFERENCE) and the CUDA headers, and is skipped without them.
+"""
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.environ.get("REEF_REFERENCE", "/root/reference")
+CORAL_INC = os.path.join(REF, "inference-engine", "coral", "include")
+CUDA_INC = "/usr/local/cuda/include"
+
+
+def test_integration_shim_compiles_against_reef_kernels(tmp_path):
+    if not os.path.isfile(os.path.join(CORAL_INC, "reef_kernels", "kernels.hpp")):
+        pytest.skip("reef checkout not present")
+    if shutil.which("g++") is None or not os.path.isdir(CUDA_INC):
+        pytest.skip("g++ or the CUDA headers not present")
+    with open(os.path.join(ROOT, "INTEGRATION.md")) as fh:
+        blocks = re.findall(r"```cpp\n(.*?)```", fh.read(), re.S)
+    assert blocks and "namespace reef_kernels" in blocks[0]
+    src = tmp_path / "kernels_b200.cc"
+    src.write_text(blocks[0])
+    p = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-Wall", "-Werror",
+                        "-I", os.path.join(ROOT, "include"), "-I", CORAL_INC, "-I", CUDA_INC,
+                        str(src)], capture_output=True, text=True)
+    assert p.returncode == 0, p.stderr[-3000:]
