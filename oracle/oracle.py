@@ -134,6 +134,10 @@ def ref() -> C.CDLL:
         R.ref_argmax_f32.argtypes = [_sz, _f32p, C.POINTER(_sz)]
         R.ref_pack_random_gpt_neo.argtypes = ([_sz] * 7 + [C.c_uint32, C.POINTER(C.c_uint8), _sz,
                                                C.POINTER(_sz)])
+        R.ref_linear_f32.argtypes = [_sz, _sz, _sz, _f32p, _f32p, _f32p, _f32p]
+        R.ref_layernorm_int8.argtypes = [_sz, _sz, _i8p, _i8p, _i8p, _i8p]
+        R.ref_add_int8.argtypes = [_sz, _i8p, _i8p, _i8p]
+        R.ref_gelu_int8.argtypes = [_sz, _i8p, C.c_float, C.c_float, _i8p, _i8p]
     return _ref
 
 

@@ -279,4 +279,55 @@ int ref_argmax_f32(std::size_t n, const float* x, std::size_t* index) {
     return guarded([&] { *index = ie::argmax(vector1(n, x)); });
 }
 
+// The float linear of Coral's linear_f32 / linear_bias_f32: the engine's
+// linear<float> (operator/linear.hpp:75-84) on the weight wt [in][out]
+// transposed back to the engine's [out][in]; bias may be null.
+int ref_linear_f32(std::size_t rows, std::size_t in, std::size_t out, const float* x,
+                   const float* wt, const float* bias, float* y) {
+    return guarded([&] {
+        ie::Tensor<float> w{{out, in}, std::vector<float>(out * in)};
+        for (std::size_t k = 0; k < in; ++k)
+            for (std::size_t c = 0; c < out; ++c) w.values[c * in + k] = wt[k * out + c];
+        const ie::Tensor<float> x_t = matrix(rows, in, x);
+        ie::Tensor<float> r;
+        if (bias != nullptr) {
+            const ie::Tensor<float> b = vector1(out, bias);
+            r = ie::linear<float>(x_t, w, std::cref(b));
+        } else {
+            r = ie::linear<float>(x_t, w);
+        }
+        std::memcpy(y, r.values.data(), rows * out * sizeof(float));
+    });
+}
+
+// layernorm_int8 (int8.hpp:332-374).
+int ref_layernorm_int8(std::size_t rows, std::size_t width, const std::int8_t* x,
+                       const std::int8_t* gain, const std::int8_t* shift, std::int8_t* y) {
+    return guarded([&] {
+        const ie::Tensor<std::int8_t> r = ie::layernorm_int8(
+            matrix(rows, width, x), vector1(width, gain), vector1(width, shift));
+        std::memcpy(y, r.values.data(), rows * width);
+    });
+}
+
+// add_int8 (int8.hpp:382-397).
+int ref_add_int8(std::size_t n, const std::int8_t* a, const std::int8_t* b, std::int8_t* y) {
+    return guarded([&] {
+        const ie::Tensor<std::int8_t> r = ie::add_int8(vector1(n, a), vector1(n, b));
+        std::memcpy(y, r.values.data(), n);
+    });
+}
+
+// gelu_table then gelu_int8 (int8.hpp:112-147): the table for the given
+// scales into table[256], and x looked up through it into y.
+int ref_gelu_int8(std::size_t n, const std::int8_t* x, float in_scale, float out_scale,
+                  std::int8_t* table, std::int8_t* y) {
+    return guarded([&] {
+        const ie::Int8Table t = ie::gelu_table(in_scale, out_scale);
+        std::memcpy(table, t.data(), t.size());
+        const ie::Tensor<std::int8_t> r = ie::gelu_int8(vector1(n, x), t);
+        std::memcpy(y, r.values.data(), n);
+    });
+}
+
 } // extern "C"

@@ -297,3 +297,45 @@ def test_int8_elementwise_match_reef_goldens():
         y = ro.embedding_int8(c["wte"].reshape(-1, w), c["wpe"].reshape(-1, w), [c["id"]],
                               c["position"])
         np.testing.assert_array_equal(y.ravel(), c["y"])
+
+
+@needs_ref
+@pytest.mark.parametrize("rows,n_in,out,seed", [(3, 257, 300, 21), (1, 768, 96, 22)])
+def test_float_linear_matches_engine(rows, n_in, out, seed):
+    import ctypes as C
+    f = C.POINTER(C.c_float)
+    x = ro.normal(seed, (rows, n_in))
+    wt = ro.normal(seed + 1, (n_in, out), 0.0, 0.02)
+    b = ro.normal(seed + 2, (out,), 0.0, 0.02)
+    for bias in (None, b):
+        want = np.empty((rows, out), np.float32)
+        rc = ro.ref().ref_linear_f32(rows, n_in, out, _c(x, f), _c(wt, f),
+                                     None if bias is None else _c(bias, f), _c(want, f))
+        assert rc == 0
+        np.testing.assert_array_equal(bits(ro.linear_f32(x, wt, bias)), bits(want))
+
+
+@needs_ref
+def test_int8_elementwise_match_engine():
+    """layernorm_int8 (widths past a warp and odd ones, negative means), the
+    saturating add and the gelu table lookup against reef's engine."""
+    import ctypes as C
+    i8 = C.POINTER(C.c_int8)
+    rng = np.random.default_rng(23)
+    for rows, width in ((7, 768), (3, 37), (2, 4096)):
+        x = rng.integers(-128, 128, (rows, width), dtype=np.int8)
+        x[0] = -np.abs(x[0]) - 1  # a row with a negative, inexact mean
+        g = rng.integers(-128, 128, width, dtype=np.int8)
+        s = rng.integers(-128, 128, width, dtype=np.int8)
+        want = np.empty((rows, width), np.int8)
+        assert ro.ref().ref_layernorm_int8(rows, width, _c(x, i8), _c(g, i8), _c(s, i8),
+                                           _c(want, i8)) == 0
+        np.testing.assert_array_equal(ro.layernorm_int8(x, g, s), want)
+    a = rng.integers(-128, 128, 5000, dtype=np.int8)
+    b = rng.integers(-128, 128, 5000, dtype=np.int8)
+    want = np.empty(5000, np.int8)
+    assert ro.ref().ref_add_int8(5000, _c(a, i8), _c(b, i8), _c(want, i8)) == 0
+    np.testing.assert_array_equal(ro.add_int8(a, b), want)
+    table = np.empty(256, np.int8)
+    assert ro.ref().ref_gelu_int8(5000, _c(a, i8), 0.05, 0.02, _c(table, i8), _c(want, i8)) == 0
+    np.testing.assert_array_equal(ro.gelu_int8(a, table), want)
