@@ -132,15 +132,15 @@ static int unary(int op, size_t n, const float* x, float* y, reef_b200_stream_t 
 
 int reef_b200_exp_nonpositive_f32(size_t n, const float* x, float* y,
                                   reef_b200_stream_t stream) {
-  return unary(0, n, x, y, stream);
+  return unary(kUnaryExp, n, x, y, stream);
 }
 
 int reef_b200_tanh_f32(size_t n, const float* x, float* y, reef_b200_stream_t stream) {
-  return unary(1, n, x, y, stream);
+  return unary(kUnaryTanh, n, x, y, stream);
 }
 
 int reef_b200_gelu_f32(size_t n, const float* x, float* y, reef_b200_stream_t stream) {
-  return unary(2, n, x, y, stream);
+  return unary(kUnaryGelu, n, x, y, stream);
 }
 
 int reef_b200_add_f32(size_t n, const float* a, const float* b, float* y,

@@ -70,15 +70,15 @@ __global__ void __launch_bounds__(128)
   if (!finite) record_error(err, kDevNonFinite);
 }
 
-enum UnaryOp { kOpExp = 0, kOpTanh = 1, kOpGelu = 2 };
-
 template <int OP>
 __global__ void unary_exact_kernel(long long n, const float* __restrict__ x,
                                    float* __restrict__ y) {
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const float v = x[i];
-    y[i] = OP == kOpExp ? exp_nonpositive_dev(v) : OP == kOpTanh ? tanh_float_dev(v) : gelu_dev(v);
+    y[i] = OP == kUnaryExp    ? exp_nonpositive_dev(v)
+           : OP == kUnaryTanh ? tanh_float_dev(v)
+                              : gelu_dev(v);
   }
 }
 
@@ -211,12 +211,12 @@ int linear_f32(long long rows, int in, int out, const float* x, const float* wt,
 int unary_exact(int op, long long n, const float* x, float* y, cudaStream_t stream) {
   if (n <= 0 || !x || !y) return kErrInvalid;
   const unsigned g = grid_for(n, 256);
-  if (op == kOpExp)
-    unary_exact_kernel<kOpExp><<<g, 256, 0, stream>>>(n, x, y);
-  else if (op == kOpTanh)
-    unary_exact_kernel<kOpTanh><<<g, 256, 0, stream>>>(n, x, y);
-  else if (op == kOpGelu)
-    unary_exact_kernel<kOpGelu><<<g, 256, 0, stream>>>(n, x, y);
+  if (op == kUnaryExp)
+    unary_exact_kernel<kUnaryExp><<<g, 256, 0, stream>>>(n, x, y);
+  else if (op == kUnaryTanh)
+    unary_exact_kernel<kUnaryTanh><<<g, 256, 0, stream>>>(n, x, y);
+  else if (op == kUnaryGelu)
+    unary_exact_kernel<kUnaryGelu><<<g, 256, 0, stream>>>(n, x, y);
   else
     return kErrInvalid;
   return launched();

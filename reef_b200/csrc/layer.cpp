@@ -566,7 +566,7 @@ int neo_f32_forward(const reef_b200_gptneo_block_f32* B, const float* x, float* 
   // + mlp(ln_2(.)): c_fc + bias, gelu, c_proj + bias
   REEF_TRY(layernorm_exact(T, d, B->eps, b.a, B->ln2_g, B->ln2_b, b.h, st));
   REEF_TRY(linear_f32(T, d, F, b.h, B->wfc, B->bfc, b.f, st));
-  REEF_TRY(unary_exact(2, T * F, b.f, b.f, st));
+  REEF_TRY(unary_exact(kUnaryGelu, T * F, b.f, b.f, st));
   REEF_TRY(linear_f32(T, F, d, b.f, B->wproj, B->bproj, b.t, st));
   return add_f32(T * d, b.a, b.t, y, st);
 }

@@ -178,7 +178,8 @@ int layernorm_exact(long long rows, int width, float eps, const float* x, const 
 // elementwise.cu -- the rest of reef's Coral operators, bit for bit
 int linear_f32(long long rows, int in, int out, const float* x, const float* wt,
                const float* bias, float* y, cudaStream_t stream);
-int unary_exact(int op, long long n, const float* x, float* y, cudaStream_t stream);  // 0 exp, 1 tanh, 2 gelu
+enum UnaryExactOp { kUnaryExp = 0, kUnaryTanh = 1, kUnaryGelu = 2 };
+int unary_exact(int op, long long n, const float* x, float* y, cudaStream_t stream);
 int add_f32(long long n, const float* a, const float* b, float* y, cudaStream_t stream);
 int gelu_int8(long long n, const int8_t* x, const int8_t* table, int8_t* y, cudaStream_t stream);
 int add_int8(long long n, const int8_t* a, const int8_t* b, int8_t* y, cudaStream_t stream);
