@@ -4,6 +4,7 @@ CPU only: no call here reaches the GPU (only argument validation that returns
 before any CUDA call, and pure helpers).
 """
 import ctypes as C
+import os
 
 import pytest
 
@@ -84,3 +85,26 @@ def test_attention_validation_without_gpu(L):
                                            None, None, p, 8, None) == 7
     # empty query is a no-op
     assert L.reef_b200_attention_head_f32(0, 5, 8, 0, 0, p, 8, p, p, None, p, 8, None) == 0
+
+
+def test_header_is_c99_and_links_from_c(tmp_path):
+    """The boundary is a C ABI: a strict C99 program (the language cgo, JNI
+    and other FFI stubs bind through) includes the header, links the library
+    and calls an entry point that needs no GPU."""
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not present")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = tmp_path / "c_abi.c"
+    src.write_text('#include "reef_b200.h"\n'
+                   "int main(void) { return reef_b200_version() >= 200 && "
+                   "reef_b200_kpad(17) == 32 ? 0 : 1; }\n")
+    exe = tmp_path / "c_abi"
+    libdir = os.path.join(root, "reef_b200")
+    cc = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                         "-I", os.path.join(root, "include"), str(src), "-L", libdir,
+                         "-lreef_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                        capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr[-2000:]
+    assert subprocess.run([str(exe)]).returncode == 0
