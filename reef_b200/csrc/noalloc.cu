@@ -31,23 +31,84 @@ using namespace reef;
 constexpr size_t kScratchBytes = static_cast<size_t>(REEF_B200_NOALLOC_SCRATCH_BYTES);
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-void* g_scratch_dev[kMaxDevices] = {};
+// The device address of g_scratch belongs to one CUDA context: the module that
+// holds the array is loaded into each context separately, and a context that
+// is destroyed (cudaDeviceReset, or a caller's own cuCtxDestroy) takes the
+// array with it.  So the cache is keyed on the current context's unique id
+// (cuCtxGetId, never reused within a process), not on the device index alone:
+// a call made under a context the cache has not seen looks the address up
+// again, with that context current.
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+using CtxGetId = CUresult (*)(CUcontext, unsigned long long*);
+
+struct CtxFns {
+  CtxGetCurrent current = nullptr;
+  CtxGetId id = nullptr;
+};
+
+const CtxFns& ctx_fns() {
+  static CtxFns fns;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fns.current = reinterpret_cast<CtxGetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fns.id = reinterpret_cast<CtxGetId>(p);
+  });
+  return fns;
+}
+
+struct ScratchEntry {
+  bool used = false;
+  unsigned long long ctx_id = 0;
+  void* ptr = nullptr;
+};
+constexpr int kMaxEntries = 64;
+ScratchEntry g_scratch_dev[kMaxEntries];
+int g_scratch_next = 0;  // round-robin victim once every entry is taken
 std::mutex g_scratch_mu;
 
-// The device address of g_scratch on the current device.  In host code the
+// The device address of g_scratch in the current context.  In host code the
 // name g_scratch is only a stand-in for the symbol, never a device address,
-// so it is looked up once per device (with that device current) and cached.
+// so it is looked up with the context current and cached under that
+// context's id.
 int scratch_ptr(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kErrCuda;
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_dev[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || p == nullptr) return kErrCuda;
-    g_scratch_dev[dev] = p;
+  const CtxFns& f = ctx_fns();
+  if (f.current == nullptr || f.id == nullptr) return kErrCuda;
+  CUcontext ctx = nullptr;
+  if (f.current(&ctx) != CUDA_SUCCESS) return kErrCuda;
+  if (ctx == nullptr) {
+    // no context is current on this thread yet: make the runtime's primary
+    // context of the current device current (the one the kernels below
+    // launch in); a context the caller made current is never replaced
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess ||
+        f.current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+      return kErrCuda;
   }
-  *out = g_scratch_dev[dev];
+  unsigned long long id = 0;
+  if (f.id(ctx, &id) != CUDA_SUCCESS) return kErrCuda;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  for (const ScratchEntry& e : g_scratch_dev)
+    if (e.used && e.ctx_id == id) {
+      *out = e.ptr;
+      return kOk;
+    }
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || p == nullptr) return kErrCuda;
+  int slot = -1;
+  for (int i = 0; i < kMaxEntries; ++i)
+    if (!g_scratch_dev[i].used) {
+      slot = i;
+      break;
+    }
+  if (slot < 0) slot = g_scratch_next++ % kMaxEntries;
+  g_scratch_dev[slot] = ScratchEntry{true, id, p};
+  *out = p;
   return kOk;
 }
 

@@ -70,6 +70,10 @@ def test_argument_validation_without_gpu(L):
     # shifts above 31 are not a rounding_shift the engine defines
     assert L.reef_b200_linear_int8(4, 8, 8, p, p, 32, p, None) == 1
     assert L.reef_b200_quantize_rows(4, 0, p, p, p, None) == 1
+    # the no-allocation linear refuses, before any CUDA call, the first shape
+    # past its fixed scratch: 4093 rows of 4096 need 16,781,300 bytes of 16 MiB
+    assert L.reef_b200_linear_w8a8_noalloc(4093, 4096, 8, p, p, p, None, p, None) == 7
+    assert L.reef_b200_linear_w8a8_noalloc(256, 65536, 8, p, p, p, None, p, None) == 7
 
 
 def test_attention_validation_without_gpu(L):

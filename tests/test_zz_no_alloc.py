@@ -45,15 +45,37 @@ def _case(rows, k, n, seed, with_bias):
 
 def test_noalloc_matches_scratch_entry_point_on_consecutive_calls(cuda_lib):
     # two calls in a row through the shared scratch: a wide-K call, then a
-    # ragged one that leaves stale bytes of the first beyond its own rows
+    # ragged one that leaves stale bytes of the first beyond its own rows;
+    # each is compared with the scratch-taking entry point and with the oracle
     for rows, k, n, seed, with_bias in [(384, 4096, 1024, 11, True), (37, 200, 300, 12, False)]:
         x, w, ws, b = _case(rows, k, n, seed, with_bias)
         got = _noalloc(x, w, ws, b)
         want = K.linear_w8a8(x, w, ws, b)
         torch.cuda.synchronize()
-        np.testing.assert_array_equal(got.cpu().numpy().view(np.uint32),
-                                      want.cpu().numpy().view(np.uint32))
+        got_np = got.cpu().numpy()
+        np.testing.assert_array_equal(got_np.view(np.uint32), want.cpu().numpy().view(np.uint32))
+        oracle = ro.linear_w8a8(x.cpu().numpy(), w.cpu().numpy()[:, :k], ws.cpu().numpy(),
+                                None if b is None else b.cpu().numpy())
+        np.testing.assert_array_equal(got_np.view(np.uint32), oracle.view(np.uint32))
     K.check_device_error()
+
+
+def test_noalloc_largest_accepted_shape_and_first_refused(cuda_lib):
+    # at in = 4096 the scratch is rows * 4096 (a multiple of 256) + 4 * rows
+    # bytes: 4092 rows need 16,777,200 of the 16,777,216 and run; 4093 rows
+    # need 16,781,300 and are refused before anything is launched
+    rows, k, n = 4092, 4096, 256
+    x, w, ws, b = _case(rows, k, n, 21, True)
+    got = _noalloc(x, w, ws, b)
+    want = K.linear_w8a8(x, w, ws, b)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint32),
+                                  want.cpu().numpy().view(np.uint32))
+    K.check_device_error()
+    p = torch.empty(16, device="cuda")
+    rc = _lib.lib().reef_b200_linear_w8a8_noalloc(rows + 1, k, n, p.data_ptr(), p.data_ptr(),
+                                                   p.data_ptr(), None, p.data_ptr(), None)
+    assert rc == 7  # REEF_B200_ERR_TOO_LARGE
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(cuda_lib):
