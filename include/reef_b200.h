@@ -156,10 +156,11 @@ int reef_b200_linear_w8a8_swiglu(size_t rows, size_t in, size_t ffn, const int8_
  * every GPU that loads it until the process exits.  Limit:
  *   round_up(rows * reef_b200_kpad(in), 256) + 4 * rows
  *     <= REEF_B200_NOALLOC_SCRATCH_BYTES,
- * else REEF_B200_ERR_TOO_LARGE (e.g. 2048 rows of 4096, or 128 rows of
- * 65536).  The first call on a device looks up the array's device address
- * (with that device current); make that first call before any stream
- * capture.  Every call shares the array and it keeps the last call's
+ * else REEF_B200_ERR_TOO_LARGE: at in = 4096, 4092 rows fit and 4093 are
+ * refused; at in = 65536, 255 rows fit.  The first call in a CUDA context
+ * (normally the device's primary context) looks up the array's device
+ * address in that context and caches it under the context's id; make that
+ * first call on each device before any stream capture.  Every call shares the array and it keeps the last call's
  * contents, so calls that overlap on the GPU (other streams or host threads
  * on the same device) race: serialise them.  No device memory is allocated. */
 #define REEF_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
@@ -382,6 +383,17 @@ int reef_b200_linear_w8a8_qkv_rope(size_t batch, size_t seq, size_t in, size_t h
  * (device int) becomes 2 (1 would mean the wait was satisfied).  The device
  * stays usable. */
 int reef_b200_selftest_wait_timeout(unsigned limit_us, int* done, reef_b200_stream_t stream);
+
+/* Failure-detection self-test of the cross-rank wait (no counterpart in
+ * reef): runs the wait the pipelined tensor-parallel forward puts before a
+ * step, on one device counter (a device unsigned int the caller owns), with
+ * a limit of limit_us microseconds (1 .. 2e6): the wait ends when *counter
+ * reaches target (wrap-around >=, as the forward's counters only grow), or
+ * after the limit, when it records 0x106 (a peer never signalled) in the
+ * device error word and returns.  A counter nothing increments is how a dead
+ * peer looks to this rank; the device stays usable. */
+int reef_b200_selftest_peer_wait_timeout(unsigned limit_us, const unsigned* counter,
+                                         unsigned target, reef_b200_stream_t stream);
 
 /* Flash attention over int8 q / k and f16 v (attend_head,
  * attention.hpp:117-123, on the dequantised values, with score scale

@@ -59,6 +59,7 @@ SIGNATURES = {
     "reef_b200_linear_w8a8_swiglu": ([_sz, _sz, _sz] + [_p] * 7, _i),
     "reef_b200_rmsnorm_quant": ([_sz, _sz, C.c_float] + [_p] * 5, _i),
     "reef_b200_selftest_wait_timeout": ([C.c_uint, _p, _p], _i),
+    "reef_b200_selftest_peer_wait_timeout": ([C.c_uint, _p, C.c_uint, _p], _i),
     "reef_b200_linear_w8a8_qkv_rope": ([_sz] * 5 + [C.c_float] + [_p] * 13, _i),
     "reef_b200_gemm_skinny_workspace_bytes": ([_sz, _sz, _sz], _sz),
     "reef_b200_gemm_w8a8_skinny": ([_sz, _sz, _sz] + [_p] * 6 + [_sz, _p, _p], _i),

@@ -419,6 +419,17 @@ int reef_b200_selftest_wait_timeout(unsigned limit_us, int* done, reef_b200_stre
   return selftest_wait_timeout(1000ull * limit_us, done, S(stream));
 }
 
+int reef_b200_selftest_peer_wait_timeout(unsigned limit_us, const unsigned* counter,
+                                         unsigned target, reef_b200_stream_t stream) {
+  if (counter == nullptr || limit_us == 0 || limit_us > 2000000u) return REEF_B200_ERR_INVALID;
+  if (int rc = check_device()) return rc;
+  CounterWaits w;
+  w.n = 1;
+  w.p[0] = counter;
+  w.target[0] = target;
+  return signal_and_wait(PeerFlags{}, w, 1000ull * limit_us, S(stream));
+}
+
 int reef_b200_linear_w8a8_qkv_rope(size_t batch, size_t seq, size_t in, size_t heads_q,
                                    size_t heads_kv, float rope_base, const int8_t* x_q,
                                    const float* x_scale, const int8_t* w_qkv,

@@ -67,29 +67,6 @@ int settle(Comm* c, ncclResult_t r) {
   }
 }
 
-// Stream memory operations (driver entry points, no link-time libcuda).
-using WaitValue32 = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
-using WriteValue32 = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
-struct StreamOps {
-  WaitValue32 wait = nullptr;
-  WriteValue32 write = nullptr;
-};
-const StreamOps& stream_ops() {
-  static StreamOps ops;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuStreamWaitValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      ops.wait = reinterpret_cast<WaitValue32>(p);
-    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      ops.write = reinterpret_cast<WriteValue32>(p);
-  });
-  return ops;
-}
-
 void arena_free(Comm* c) {
   for (int r = 0; r < static_cast<int>(c->peer.size()); ++r)
     if (r != c->rank && c->peer[r] != nullptr) cudaIpcCloseMemHandle(c->peer[r]);
@@ -230,8 +207,6 @@ int allgather_bytes(Comm* c, const void* send, void* recv, size_t bytes, cudaStr
 int comm_arena_reserve(Comm* c, size_t data_bytes, int slots) {
   if (c == nullptr || c->world < 2 || slots < 1) return kErrInvalid;
   if (c->arena != nullptr && c->arena_data >= data_bytes && c->arena_slots >= slots) return kOk;
-  const StreamOps& ops = stream_ops();
-  if (ops.wait == nullptr || ops.write == nullptr) return kErrUnsupported;
   // every rank reaches this point with the same sizes; drain before replacing
   if (cudaDeviceSynchronize() != cudaSuccess) return kErrCuda;
   arena_free(c);
@@ -288,14 +263,13 @@ unsigned int* comm_counter(Comm* c, int slot, int r) {
                                                            sizeof(uint32_t));
 }
 
-int comm_wait_count(Comm* c, int slot, uint32_t value, cudaStream_t s) {
-  if (c == nullptr || c->arena == nullptr || slot < 0 || slot >= c->arena_slots) return kErrInvalid;
-  const StreamOps& ops = stream_ops();
-  const size_t off = static_cast<size_t>(slot) * c->world * sizeof(uint32_t);
-  return ops.wait(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(c->arena + off), value,
-                  CU_STREAM_WAIT_VALUE_GEQ) == CUDA_SUCCESS
-             ? kOk
-             : kErrCuda;
+unsigned int* comm_local_counter(Comm* c, int slot) {
+  return c ? comm_counter(c, slot, c->rank) : nullptr;
+}
+
+unsigned long long comm_wait_limit_ns(const Comm* c) {
+  const double s = c ? c->timeout_s : 60.0;
+  return static_cast<unsigned long long>(s * 1e9);
 }
 
 uint32_t comm_next_round(Comm* c) { return c ? ++c->round : 0; }

@@ -23,25 +23,28 @@ int comm_ctas(const Comm* c);
 constexpr int kComputeStreams = 4;
 cudaStream_t comm_compute_stream(const Comm* c, int i);
 
-// ---- Symmetric arena: peer stores over NVLink, stream-ordered flags
+// ---- Symmetric arena: peer stores over NVLink, counters with bounded waits
 //
 // Every rank holds an arena of the same size, mapped into every peer's
 // address space (CUDA IPC), laid out alike: `slots` x world uint32 flags, then
 // data.  Kernels write into peers' data regions directly (comm_peer_data).
-// A slot's first flag word is a counter that peers increment with
-// signal_peers (ops.h) after their kernels; comm_wait_count makes a stream
-// wait, in its front end, until the local counter reaches a value.  Counts
-// only grow, so a counter never needs resetting.
+// A slot's first flag word is a counter that peers increment after their
+// kernels, and that a stream waits on before its next kernels, both with
+// signal_and_wait (ops.h): its wait gives up after comm_wait_limit_ns and
+// records kDevTimeoutPeer, so a peer that never signals cannot hang a stream.
+// Counts only grow, so a counter never needs resetting.
 // (Re)creates the arena when it is smaller than asked; collective (every rank
 // calls it with the same sizes in the same order).
 int comm_arena_reserve(Comm* c, size_t data_bytes, int slots);
 uint8_t* comm_arena_data(Comm* c);  // this rank's data region
 // rank r's data region as mapped here (r = this rank: comm_arena_data)
 uint8_t* comm_peer_data(Comm* c, int r);
-// The counter of `slot` in rank r's arena (for signal_peers), and a stream
-// wait until the local counter of `slot` reaches `value`.
+// The counter of `slot` in rank r's arena (for the signals), this rank's own
+// counter of `slot` (for the waits), and how long a wait may last (the
+// communicator's timeout).
 unsigned int* comm_counter(Comm* c, int slot, int r);
-int comm_wait_count(Comm* c, int slot, uint32_t value, cudaStream_t s);
+unsigned int* comm_local_counter(Comm* c, int slot);
+unsigned long long comm_wait_limit_ns(const Comm* c);
 // A counter the pipelined forward advances once per call (identical on all
 // ranks, which make the same calls), from which flag values derive.
 uint32_t comm_next_round(Comm* c);

@@ -763,17 +763,20 @@ struct EventSet {
 // mapped arenas; on 4 GPUs that moves ~550-620 GB/s per GPU against
 // ~300-350 GB/s for copy-engine copies, and no separate transfer step waits
 // in between).  The gate/up GEMM takes its row maxima with atomics locally,
-// and a small kernel pushes them.  After a producing step the stream raises
-// the region's data flag (region, rank) in every peer's arena (the stream
-// write fences the kernel's stores first); a consuming step's stream waits
-// for every peer's data flag, and afterwards raises the region's "consumed"
-// flag in every peer's arena; a producing step writes a region only once
-// every peer has consumed its previous contents.  Flag values are (forward
-// round, use) counters that only grow.  Steps are issued wavefront-wise so
-// that every rank issues the same sequence; each wait depends only on steps
-// issued earlier on some rank, so the pipeline cannot deadlock.  Each chunk
-// computes exactly what the unpipelined plan computes for its rows, so the
-// result is identical.
+// and a small kernel pushes them.  After a producing step the rank increments
+// the region's "delivered" counter in every peer's arena (a system-wide fence
+// orders the kernel's stores first); a consuming step waits until its local
+// counter shows every peer's delivery, and afterwards increments the
+// region's "consumed" counter in every peer's arena; a producing step writes
+// a region only once every peer has consumed its previous contents.  Counter
+// targets derive from (forward round, use), so counters only grow.  Every
+// wait is a bounded spin on the device (signal_and_wait): after the
+// communicator's timeout it records kDevTimeoutPeer and lets the stream go
+// on, so a peer that died cannot leave this rank's streams waiting.  Steps
+// are issued wavefront-wise so that every rank issues the same sequence;
+// each wait depends only on steps issued earlier on some rank, so the
+// pipeline cannot deadlock.  Each chunk computes exactly what the
+// unpipelined plan computes for its rows, so the result is identical.
 static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const float* x, float* y,
                                       const LlamaAgBufs& b, int chunks, cudaStream_t st) {
   Comm* c = C(L->comm);
@@ -828,8 +831,8 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
   // rank's arena, its own included); after the kernels it marks its inputs
   // consumed and its outputs delivered, on every peer: each region has a
   // "delivered" and a "consumed" counter that every peer increments once per
-  // use (one warp's system-scope atomics after the step), so a step waits on
-  // one counter per region instead of one flag per peer.  A peer cannot run
+  // use (system-scope atomics after the step), so a step waits on one
+  // counter per region instead of one flag per peer.  A peer cannot run
   // two uses ahead (producing use e + 1 needs this rank's consumption of use
   // e), so a counter never passes a target early.  Chunk k's step also
   // waits for chunk k - 1's same step, so the chunks run one step apart: the
@@ -840,23 +843,38 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
     Kind kind;
     int use;
   };
+  // Chunk k's signals of its last step wait to go out with the first kernel
+  // of its next step: one launch increments the peers' counters (after a
+  // system-wide fence) and then waits, with the communicator's deadline, for
+  // this step's local counters.  A wait that runs out records
+  // kDevTimeoutPeer and returns, so a peer that never signals cannot hang
+  // this stream.
+  std::vector<PeerFlags> pending(chunks);
+  const unsigned long long limit_ns = comm_wait_limit_ns(c);
   auto step = [&](int k, std::initializer_list<Use> ins, std::initializer_list<Use> outs,
                   auto&& fn) -> int {
-    if (k > 0 && cudaStreamWaitEvent(sk(k), done.ev[k - 1], 0) != cudaSuccess) return kErrCuda;
     const uint32_t peers = static_cast<uint32_t>(N - 1);
-    for (const Use& i : ins)
-      REEF_TRY(comm_wait_count(c, data_slot(k, i.kind), epoch(i.kind, i.use) * peers, sk(k)));
-    for (const Use& o : outs)
-      REEF_TRY(comm_wait_count(c, cons_slot(k, o.kind), (epoch(o.kind, o.use) - 1) * peers, sk(k)));
+    CounterWaits w;
+    if (static_cast<int>(ins.size() + outs.size()) > kMaxWaits) return kErrInvalid;
+    for (const Use& i : ins) {
+      w.p[w.n] = comm_local_counter(c, data_slot(k, i.kind));
+      w.target[w.n++] = epoch(i.kind, i.use) * peers;
+    }
+    for (const Use& o : outs) {
+      w.p[w.n] = comm_local_counter(c, cons_slot(k, o.kind));
+      w.target[w.n++] = (epoch(o.kind, o.use) - 1) * peers;
+    }
+    REEF_TRY(signal_and_wait(pending[k], w, limit_ns, sk(k)));
+    pending[k] = PeerFlags{};
+    if (k > 0 && cudaStreamWaitEvent(sk(k), done.ev[k - 1], 0) != cudaSuccess) return kErrCuda;
     REEF_TRY(fn(sk(k)));
-    PeerFlags f;
+    PeerFlags& f = pending[k];
     if ((N - 1) * static_cast<int>(ins.size() + outs.size()) > kMaxFlags) return kErrInvalid;
     for (int r = 0; r < N; ++r) {
       if (r == rank) continue;
       for (const Use& i : ins) f.p[f.n++] = comm_counter(c, cons_slot(k, i.kind), r);
       for (const Use& o : outs) f.p[f.n++] = comm_counter(c, data_slot(k, o.kind), r);
     }
-    REEF_TRY(signal_peers(f, sk(k)));
     return cudaEventRecord(done.ev[k], sk(k)) == cudaSuccess ? kOk : kErrCuda;
   };
   // this rank's segment of region (k, kind) in every rank's arena (the [N][Tc][w]
@@ -982,9 +1000,13 @@ static int llama_forward_ag_pipelined(const reef_b200_llama_layer* L, const floa
       p.args.residual = hk(k);
       return gemm_i8(p, kEpiF32W8A8, s);
     }));
-  // join: the caller's stream waits for every chunk's last kernel
-  for (int k = 0; k < chunks; ++k)
+  // the last steps' signals, then join: the caller's stream waits for every
+  // chunk's last kernel
+  for (int k = 0; k < chunks; ++k) {
+    REEF_TRY(signal_and_wait(pending[k], CounterWaits{}, limit_ns, sk(k)));
+    if (cudaEventRecord(done.ev[k], sk(k)) != cudaSuccess) return REEF_B200_ERR_CUDA;
     if (cudaStreamWaitEvent(st, done.ev[k], 0) != cudaSuccess) return REEF_B200_ERR_CUDA;
+  }
   return REEF_B200_OK;
 }
 

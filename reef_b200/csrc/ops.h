@@ -162,6 +162,23 @@ struct PeerFlags {
 };
 int signal_peers(const PeerFlags& f, cudaStream_t stream);
 
+// Local counters a stream waits on before its next kernels: lane i of one
+// warp spins (system-scope acquire loads) until counter p[i] reaches
+// target[i] (wrap-around >=, as the counters only grow), or until `limit_ns`
+// of %globaltimer pass, in which case it records kDevTimeoutPeer in the
+// device error word and returns, so no wait outlives its limit (the host
+// reads REEF_B200_ERR_TIMEOUT).
+constexpr int kMaxWaits = 8;
+struct CounterWaits {
+  int n = 0;
+  const unsigned int* p[kMaxWaits] = {};
+  unsigned int target[kMaxWaits] = {};
+};
+// One launch: signal `f` (fence, then the increments, as signal_peers), then
+// wait for `w`.  Either may be empty; nothing is launched when both are.
+int signal_and_wait(const PeerFlags& f, const CounterWaits& w, unsigned long long limit_ns,
+                    cudaStream_t stream);
+
 // lm_head.cu -- the token embedding, reef's float linear(x, w) for one row
 // (bit-identical) and argmax
 int embedding_f32(int width, long long count, const uint32_t* ids, long long first_position,

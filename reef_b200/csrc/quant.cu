@@ -133,6 +133,33 @@ __global__ void signal_peers_kernel(PeerFlags f) {
   for (int i = threadIdx.x; i < f.n; i += blockDim.x) atomicAdd_system(f.p[i], 1u);
 }
 
+// Lanes [0, f.n) signal after the system-wide fence (every earlier kernel on
+// the stream has finished); lanes [0, w.n) then wait on their counter, each
+// with its own deadline.  The increments come first so that two ranks that
+// each signal and then wait for the other cannot both wait.
+__global__ void signal_and_wait_kernel(PeerFlags f, CounterWaits w, unsigned long long limit_ns,
+                                       int* err) {
+  if (f.n > 0) {
+    __threadfence_system();
+    for (int i = threadIdx.x; i < f.n; i += blockDim.x) atomicAdd_system(f.p[i], 1u);
+  }
+  const int i = threadIdx.x;
+  if (i >= w.n) return;
+  const unsigned int target = w.target[i];
+  const unsigned long long start = globaltimer();
+  unsigned int spin = 0;
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(w.p[i]) : "memory");
+    if (static_cast<int>(v - target) >= 0) break;
+    if ((++spin & 63u) == 0 && globaltimer() - start > limit_ns) {
+      record_error(err, kDevTimeoutPeer);
+      break;
+    }
+    __nanosleep(32);
+  }
+}
+
 __global__ void push_f32_kernel(long long n, const float* __restrict__ src, PeerDst dst) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -244,6 +271,19 @@ int signal_peers(const PeerFlags& f, cudaStream_t stream) {
   for (int i = 0; i < f.n; ++i)
     if (f.p[i] == nullptr) return kErrInvalid;
   signal_peers_kernel<<<1, 32, 0, stream>>>(f);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int signal_and_wait(const PeerFlags& f, const CounterWaits& w, unsigned long long limit_ns,
+                    cudaStream_t stream) {
+  if (f.n < 0 || f.n > kMaxFlags || w.n < 0 || w.n > kMaxWaits || limit_ns == 0)
+    return kErrInvalid;
+  if (f.n == 0 && w.n == 0) return kOk;
+  for (int i = 0; i < f.n; ++i)
+    if (f.p[i] == nullptr) return kErrInvalid;
+  for (int i = 0; i < w.n; ++i)
+    if (w.p[i] == nullptr) return kErrInvalid;
+  signal_and_wait_kernel<<<1, 32, 0, stream>>>(f, w, limit_ns, device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
