@@ -1,10 +1,10 @@
-"""The Llama RMSNorm + int8 kernel against a numpy float32 restatement of its
-fixed summation order (bit for bit).  The order is the definition that makes
-the tensor-parallel shards (rms_stats / rms_apply) reproduce TP=1 exactly: 8
-chunks, 128 ordered partial sums per chunk, an xor butterfly per 32 partials,
-then fixed trees.  No counterpart in reef (its GPT-Neo block uses LayerNorm),
-so the restatement here is the specification; parity with a reference is
-unpinned.
+"""The Llama RMSNorm + int8 kernel against the numpy float32 restatement of
+its fixed summation order (tests/rms_ref.py), bit for bit.  The order is the
+definition that makes the tensor-parallel shards (rms_stats / rms_apply)
+reproduce TP=1 exactly: 8 chunks, 128 ordered partial sums per chunk, an xor
+butterfly per 32 partials, then fixed trees.  No counterpart in reef (its
+GPT-Neo block uses LayerNorm), so the restatement is the specification;
+parity with a reference is unpinned.
 """
 import numpy as np
 import pytest
@@ -12,47 +12,10 @@ import torch
 
 from reef_b200 import _lib
 
+from tests.rms_ref import rmsnorm_quant_ref
+
 pytestmark = pytest.mark.gpu
 f32 = np.float32
-
-
-def butterfly(p):
-    """xor-shuffle tree over 32 lanes (offsets 16..1); every lane ends equal."""
-    v = p.copy()
-    for o in (16, 8, 4, 2, 1):
-        v = (v + v[np.arange(32) ^ o]).astype(f32)
-    return v[0]
-
-
-def rmsnorm_quant_ref(x, gain, eps):
-    rows, width = x.shape
-    n4 = width // 32  # float4 per chunk
-    q = np.empty((rows, width), np.int8)
-    scales = np.empty(rows, f32)
-    for r in range(rows):
-        chunks = []
-        for c in range(8):
-            xc = x[r, c * n4 * 4:(c + 1) * n4 * 4].reshape(n4, 4)
-            part = np.zeros(128, f32)
-            for i in range(128):
-                s = f32(0)
-                for idx in range(i, n4, 128):
-                    a = xc[idx]
-                    sq = f32(f32(f32(a[0] * a[0]) + f32(a[1] * a[1])) + f32(a[2] * a[2]))
-                    s = f32(s + f32(sq + f32(a[3] * a[3])))
-                part[i] = s
-            w = [butterfly(part[32 * k:32 * k + 32]) for k in range(4)]
-            chunks.append(f32(f32(f32(w[0] + w[1]) + w[2]) + w[3]))
-        c = chunks
-        total = f32(f32(f32(c[0] + c[1]) + f32(c[2] + c[3])) + f32(f32(c[4] + c[5]) + f32(c[6] + c[7])))
-        rr = f32(f32(1) / np.sqrt(f32(f32(total / f32(width)) + f32(eps))))
-        y = (x[r] * gain).astype(f32)
-        mx = f32(np.abs(y).max() * rr)
-        scale = f32(mx / f32(127)) if mx > 0 else f32(1)
-        yr = (y * rr).astype(f32)
-        q[r] = np.clip(np.rint((yr / scale).astype(f32)), -127, 127).astype(np.int8)
-        scales[r] = scale
-    return q, scales
 
 
 # the config-3 hidden width, config-4's, a width whose chunks hold fewer

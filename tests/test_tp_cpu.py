@@ -1,4 +1,4 @@
-"""Tensor-parallel host logic on CPU ranks (gloo, world sizes 2 and 4).
+"""Tensor-parallel host logic on CPU ranks (gloo, world sizes 2, 4 and 8).
 
 The GPU path shards with reef_b200.tp and runs the row-parallel algebra in
 layer.cpp over NCCL.  Here the same shard functions and the same algebra run
@@ -10,6 +10,12 @@ on two gloo ranks with the oracle as the compute:
 * column-parallel q/k/v and gate/up row selections == the TP=1 columns;
 * reef's GPT-Neo W8A8 block at TP=2 (config 2) == Block<float> at TP=1,
   bit for bit;
+* the all-gather plan's algebra: each rank's RMSNorm chunk sums and
+  max|x * gain| over its hidden columns, all-gathered, give TP=1's r and
+  scale (the fixed 8-chunk tree; max|y| = max|x * gain| * r), so its int8
+  columns are TP=1's; a column-sharded activation (SwiGLU's h, the attention
+  output) quantised with the MAX-all-reduced row maxima is TP=1's; and a
+  column-parallel GEMM on the all-gathered int8 rows gives TP=1's columns;
 * a rank that fails before a collective surfaces as an error on its peer
   within the process-group timeout (no hang).
 """
@@ -26,6 +32,7 @@ import torch.multiprocessing as mp
 
 from oracle import oracle as ro
 from reef_b200 import tp
+from tests import rms_ref
 from tests.test_oracle import block_float_weights
 
 
@@ -141,6 +148,52 @@ def _gptneo_tp_case(rank, world):
     return bool(np.array_equal(y.astype(np.float32).view(np.uint32), want.view(np.uint32)))
 
 
+def _allgather_plan_case(rank, world):
+    """The all-gather plan (layer.cpp llama_forward_ag*, llama.cu rms_stats /
+    rms_apply) restated with numpy on this rank's columns."""
+    rng = np.random.default_rng(41)
+    eps = 1e-5
+    ok = True
+    for rows, width in ((6, 1024), (3, 4096), (2, 8192)):
+        x = rng.normal(0, 1, (rows, width)).astype(np.float32)
+        x[1] = 0.0  # a zero row: scale 1
+        gain = rng.normal(1, 0.1, width).astype(np.float32)
+        cols = tp.col_slice(width, world, rank)
+        st = torch.from_numpy(rms_ref.rms_stats_local(x[:, cols], gain[cols], width))
+        parts = [torch.empty_like(st) for _ in range(world)]
+        dist.all_gather(parts, st)
+        q, scale = rms_ref.rms_apply_local(x[:, cols], gain[cols],
+                                           np.stack([t.numpy() for t in parts]), width, eps)
+        q1, s1 = rms_ref.rmsnorm_quant_ref(x, gain, eps)
+        ok &= bool(np.array_equal(q, q1[:, cols]))
+        ok &= bool(np.array_equal(scale.view(np.uint32), s1.view(np.uint32)))
+        # the all-gathered int8 rows [rank][rows][width/N] reassemble TP=1's
+        got = [torch.empty_like(torch.from_numpy(q)) for _ in range(world)]
+        dist.all_gather(got, torch.from_numpy(np.ascontiguousarray(q)))
+        ok &= bool(np.array_equal(np.concatenate([t.numpy() for t in got], axis=1), q1))
+    # a column-sharded activation quantised with the all-reduced row maxima,
+    # then a column-parallel GEMM (this rank's output rows) on the gathered int8
+    rows, width, n = 9, 704 * 8, 64
+    h = rng.normal(0, 3, (rows, width)).astype(np.float32)
+    h[4] = 0.0
+    cols = tp.col_slice(width, world, rank)
+    rm = torch.from_numpy(np.abs(h[:, cols]).max(axis=1).astype(np.float32))
+    dist.all_reduce(rm, op=dist.ReduceOp.MAX)
+    q, s = quantize_with_max(h[:, cols], rm.numpy())
+    qf, sf = ro.quantize_rows(h)
+    ok &= bool(np.array_equal(q, qf[:, cols]))
+    ok &= bool(np.array_equal(s.view(np.uint32), sf.view(np.uint32)))
+    got = [torch.empty_like(torch.from_numpy(q)) for _ in range(world)]
+    dist.all_gather(got, torch.from_numpy(np.ascontiguousarray(q)))
+    qa = np.concatenate([t.numpy() for t in got], axis=1)
+    w, ws = ro.quantize_rows(ro.normal(42, (n * world, width), 0, 0.02))
+    out = slice(rank * n, (rank + 1) * n)
+    mine = ro.w8a8_epilogue(ro.gemm_i8(qa, np.ascontiguousarray(w[out]), threads=1), s, ws[out])
+    full = ro.linear_w8a8(h, w, ws, threads=1)
+    ok &= bool(np.array_equal(mine.view(np.uint32), full[:, out].view(np.uint32)))
+    return ok
+
+
 def _dead_peer_case(rank, world):
     if rank == 1:
         raise RuntimeError("rank 1 fails before the collective")
@@ -152,7 +205,7 @@ def _dead_peer_case(rank, world):
     return "no error"
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_rowpar_linear_bit_identical_to_tp1(world):
     r = _run(_rowpar_case, world=world)
     assert len(r) == world and all(v == ("ok", True) for v in r.values()), r
@@ -167,6 +220,12 @@ def test_colpar_rows_are_the_tp1_columns(world):
 @pytest.mark.parametrize("world", [2, 4])
 def test_gptneo_block_tp_bit_identical_to_tp1(world):
     r = _run(_gptneo_tp_case, world=world)
+    assert len(r) == world and all(v == ("ok", True) for v in r.values()), r
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_allgather_plan_algebra_bit_identical_to_tp1(world):
+    r = _run(_allgather_plan_case, world=world)
     assert len(r) == world and all(v == ("ok", True) for v in r.values()), r
 
 

@@ -1,12 +1,14 @@
-"""Tensor parallelism on two and on four B200s (NCCL and copy-engine
-transfers over NVLink): every rank's output is bit-identical to TP=1.
+"""Tensor parallelism on two, four and eight B200s (NCCL and NVLink peer
+stores): every rank's output is bit-identical to TP=1.
 
 * reef_b200_linear_w8a8_rowpar (all-reduce MAX of row maxima, int32 partial
   GEMM, all-reduce SUM, dequant + bias) == reef_b200_linear_w8a8_bias;
 * the Llama-shape layer at TP=N == the same layer at TP=1 (same seed), with
-  the all-reduce plan and with the pipelined all-gather plan;
+  the all-reduce plan and with the pipelined all-gather plan, on a small
+  shape and at config 3's widths (hidden 4096, 32 x 128 heads, FFN 11008;
+  batch 2 x 2048, so the all-gather plan pipelines two chunks);
 * reef's GPT-Neo block at TP=N (config 2's shape) == the oracle, i.e.
-  Block<float>::forward.
+  Block<float>::forward (its 4 heads split over 2 and 4 ranks).
 Each world size is skipped when fewer GPUs are visible.
 """
 import datetime
@@ -73,28 +75,42 @@ def _worker(rank, world, port, q):
         want = K.linear_w8a8(x, wd, wsd, b)
         res["rowpar"] = bool(np.array_equal(bits(y), bits(want)))
 
-        # Llama-shape layer, TP=2 shard vs TP=1 on this device
-        shape = RL.LlamaShape(hidden=1024, heads_q=8, heads_kv=4, ffn=2816)
-        xin = torch.from_numpy(ro.normal(9, (2 * 256, 1024))).to(dev)
-        L2 = RL.LlamaLayer(shape, 2, 256, seed=5, world=world, rank=rank, comm=comm, device=dev)
-        y2 = L2.forward(xin)
-        L1 = RL.LlamaLayer(shape, 2, 256, seed=5, device=dev)
-        y1 = L1.forward(xin)
-        res["llama"] = bool(np.array_equal(bits(y2), bits(y1)))
-        # the all-gather plan: x / y are this rank's hidden columns
-        cols = tp.col_slice(1024, world, rank)
-        L3 = RL.LlamaLayer(shape, 2, 256, seed=5, world=world, rank=rank, comm=comm, device=dev,
-                           tp_mode=RL.TP_ALLGATHER)
-        y3 = L3.forward(xin[:, cols].contiguous())
-        res["llama_allgather"] = bool(np.array_equal(bits(y3), bits(y1[:, cols].contiguous())))
+        # Llama-shape layers, TP=N shard vs TP=1 on this device, both plans;
+        # the small shape has GQA (2 query heads per kv head) where the kv
+        # heads split, and config 3's widths at two sequences of 2048
+        kv_small = 4 if world <= 4 else 8
+        cases = [("llama", RL.LlamaShape(hidden=1024, heads_q=8, heads_kv=kv_small, ffn=2816),
+                  256, 9),
+                 ("llama7b", RL.LLAMA_7B, 2048, 19)]
+        for name, shape, seq, seed in cases:
+            xin = torch.from_numpy(ro.normal(seed, (2 * seq, shape.hidden))).to(dev)
+            L1 = RL.LlamaLayer(shape, 2, seq, seed=seed + 1, device=dev)
+            y1 = L1.forward(xin)
+            del L1
+            L2 = RL.LlamaLayer(shape, 2, seq, seed=seed + 1, world=world, rank=rank, comm=comm,
+                               device=dev)
+            y2 = L2.forward(xin)
+            res[name] = bool(np.array_equal(bits(y2), bits(y1)))
+            del L2
+            # the all-gather plan: x / y are this rank's hidden columns
+            cols = tp.col_slice(shape.hidden, world, rank)
+            L3 = RL.LlamaLayer(shape, 2, seq, seed=seed + 1, world=world, rank=rank, comm=comm,
+                               device=dev, tp_mode=RL.TP_ALLGATHER)
+            y3 = L3.forward(xin[:, cols].contiguous())
+            res[name + "_allgather"] = bool(np.array_equal(bits(y3),
+                                                           bits(y1[:, cols].contiguous())))
+            del L3, y1, y2, y3, xin
+            torch.cuda.synchronize(dev)
+            torch.cuda.empty_cache()
 
-        # GPT-Neo block (config 2 shape), TP=2 vs the oracle (reef's Block<float>)
-        fw = block_float_weights(256, 1024, seed=80)
-        xb = ro.normal(81, (128, 256))
-        blk = RL.GptNeoBlock(fw, 4, 128, world=world, rank=rank, comm=comm, device=dev)
-        yb = blk.forward(torch.from_numpy(xb).to(dev))
-        wantb = ro.gptneo_block_w8a8(xb, ro.quantize_block(fw), 4)
-        res["gptneo"] = bool(np.array_equal(bits(yb), wantb.view(np.uint32)))
+        # GPT-Neo block (config 2 shape), TP=N vs the oracle (reef's Block<float>)
+        if 4 % world == 0:
+            fw = block_float_weights(256, 1024, seed=80)
+            xb = ro.normal(81, (128, 256))
+            blk = RL.GptNeoBlock(fw, 4, 128, world=world, rank=rank, comm=comm, device=dev)
+            yb = blk.forward(torch.from_numpy(xb).to(dev))
+            wantb = ro.gptneo_block_w8a8(xb, ro.quantize_block(fw), 4)
+            res["gptneo"] = bool(np.array_equal(bits(yb), wantb.view(np.uint32)))
         torch.cuda.synchronize(dev)
         K.check_device_error()
         comm.close()
@@ -106,7 +122,7 @@ def _worker(rank, world, port, q):
 
 
 @needs2
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_bit_identical_to_tp1(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -120,8 +136,11 @@ def test_tp_bit_identical_to_tp1(world):
     out = dict(q.get(timeout=600) for _ in procs)
     for p in procs:
         p.join(timeout=60)
+    want = {"rowpar": True, "llama": True, "llama_allgather": True, "llama7b": True,
+            "llama7b_allgather": True}
+    if 4 % world == 0:
+        want["gptneo"] = True
     for r in range(world):
         status, res = out[r]
         assert status == "ok", res
-        assert res == {"rowpar": True, "llama": True, "llama_allgather": True,
-                       "gptneo": True}, (r, res)
+        assert res == want, (r, res)
