@@ -6,9 +6,11 @@ into the int8 KV cache; the step's output for token t must match the prefill
 layer's row t over the same inputs.  The q / k / v codes are identical in the
 two paths (the same exact W8A8 GEMMs and quantiser); the attention kernels
 differ (flash: f16 P on tensor cores; decode: fp32 P on CUDA cores), so the
-outputs agree within the layer tolerance of test_layer_gpu.py.  Also runs
-one step at config 4's TP=8 shard shape (hidden 8192, 8 q / 1 kv heads, FFN
-3584, 64 sequences, 4096-row cache).
+outputs agree within the layer tolerance of test_layer_gpu.py.  At config
+4's TP=8 shard shape (hidden 8192, 8 q / 1 kv heads, FFN 3584, 64 sequences,
+4096-row cache, ragged positions) one step is checked against a float64
+restatement on the oracle's exact W8A8 linear, and so are the cache rows it
+appends.
 """
 import numpy as np
 import pytest
@@ -17,6 +19,7 @@ import torch
 from oracle import oracle as ro
 from reef_b200 import kernels as K
 from reef_b200 import layer as RL
+from tests.test_layer_gpu import quant_heads
 
 pytestmark = pytest.mark.gpu
 
@@ -46,21 +49,92 @@ def test_decode_steps_match_prefill():
     assert np.mean(mean) < 5e-3, np.mean(mean)
 
 
-def test_decode_config4_tp8_shard_runs():
+def decode_reference(x, W, shape, pos, k8, ks, v8, vs):
+    """One decode step of a rank's shard (float64 RMSNorm / RoPE / softmax /
+    SwiGLU, the oracle's exact W8A8 linear at every projection): x [B][H]
+    at positions pos [B] over the int8 caches k8 / v8 [B][hkv][L][128] with
+    scales ks / vs [B][hkv][L] as they were before the step.  Without a
+    communicator the shard quantises the row-parallel inputs with its own
+    row maxima, and so does this restatement.  Returns (y, k_new, v_new)
+    with the appended rows dequantised."""
+    s = shape
+    B, H = x.shape
+    hq, hkv, d, F = s.heads_q, s.heads_kv, 128, s.ffn
+
+    def rms_q(v, g):
+        ms = (v.astype(np.float64) ** 2).mean(1, keepdims=True)
+        return ro.quantize_rows((v / np.sqrt(ms + s.rms_eps) * g).astype(np.float32))
+
+    def lin(xq_s, w, ws):
+        xq, xs = xq_s
+        return ro.w8a8_epilogue(ro.gemm_i8(xq, w[:, :xq.shape[1]]), xs, ws)
+
+    qkv = lin(rms_q(x, W["attn_norm"]), W["w_qkv"], W["s_qkv"]).astype(np.float64)
+    ang = pos[:, None].astype(np.float64) * (s.rope_base ** (-np.arange(64) * 2 / 128.0))[None]
+    c, sn = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+
+    def rope(a, h):
+        a = a.reshape(B, h, 128)
+        lo, hi = a[..., :64], a[..., 64:]
+        return np.concatenate([lo * c - hi * sn, hi * c + lo * sn], axis=2).reshape(B, h * 128)
+
+    q = quant_heads(rope(qkv[:, :hq * d], hq), hq).reshape(B, hq, d)
+    kn = quant_heads(rope(qkv[:, hq * d:(hq + hkv) * d], hkv), hkv).reshape(B, hkv, d)
+    vn = quant_heads(qkv[:, (hq + hkv) * d:], hkv).reshape(B, hkv, d)
+    attn = np.zeros((B, hq * d))
+    for b in range(B):
+        n = int(pos[b])
+        for kh in range(hkv):
+            K = np.concatenate([k8[b, kh, :n] * ks[b, kh, :n, None], kn[b, kh][None]])
+            V = np.concatenate([v8[b, kh, :n] * vs[b, kh, :n, None], vn[b, kh][None]])
+            for h in range(kh * (hq // hkv), (kh + 1) * (hq // hkv)):
+                sc = K @ q[b, h] / np.sqrt(128.0)
+                p = np.exp(sc - sc.max())
+                attn[b, h * d:(h + 1) * d] = (p / p.sum()) @ V
+    h1 = x + lin(ro.quantize_rows(attn.astype(np.float32)), W["w_o"], W["s_o"])
+    gu = lin(rms_q(h1, W["mlp_norm"]), W["w_gu"], W["s_gu"]).astype(np.float64)
+    g, u = gu[:, :F], gu[:, F:]
+    act = (g / (1 + np.exp(-g)) * u).astype(np.float32)
+    y = h1 + lin(ro.quantize_rows(act), W["w_down"], W["s_down"])
+    return y, kn, vn
+
+
+def test_decode_config4_tp8_shard_matches_reference():
     # config 4 at TP=8, one rank's shard: hidden 8192, 64/8 = 8 q heads,
-    # 8/8 = 1 kv head, FFN 28672/8 = 3584; 64 sequences, 4096-row cache
+    # 8/8 = 1 kv head, FFN 28672/8 = 3584; 64 sequences at ragged positions
+    # up to the 4096-row cache's last row (each sees its first pos + 1 keys)
     shape = RL.LlamaShape(hidden=8192, heads_q=64, heads_kv=8, ffn=28672)
-    L = RL.LlamaLayer(shape, 64, 8, seed=3, world=8, rank=0)
-    cache = L.alloc_cache(4096)
+    B, Lmax = 64, 4096
+    L = RL.LlamaLayer(shape, B, 8, seed=3, world=8, rank=0)
+    cache = L.alloc_cache(Lmax)
     g = torch.Generator(device="cuda").manual_seed(5)
     cache["k"].random_(-127, 128, generator=g)
     cache["v"].random_(-127, 128, generator=g)
-    cache["ks"].fill_(0.01)
-    cache["vs"].fill_(0.01)
-    x = torch.randn((64, 8192), generator=g, device="cuda")
-    pos = torch.full((64,), 4095, dtype=torch.int32, device="cuda")
+    cache["ks"].uniform_(0.005, 0.015, generator=g)
+    cache["vs"].uniform_(0.005, 0.015, generator=g)
+    x = torch.randn((B, 8192), generator=g, device="cuda")
+    pos_h = np.array([Lmax - 1 - (61 * b) % 1500 for b in range(B)], np.int32)
+    pos_h[0] = 0  # a sequence whose only key is the new token
+    pos = torch.from_numpy(pos_h).cuda()
+    before = {k: cache[k].cpu().numpy().astype(np.float64) for k in ("k", "ks", "v", "vs")}
     y = L.decode(x, pos, cache)
     torch.cuda.synchronize()
-    assert torch.isfinite(y).all()
-    # the new token's k / v rows were written at row 4095
-    assert cache["ks"][:, :, 4095].gt(0).all() and cache["vs"][:, :, 4095].ne(0.01).any()
+    local = RL.LlamaShape(hidden=8192, heads_q=8, heads_kv=1, ffn=3584)
+    want, kn, vn = decode_reference(x.cpu().numpy(), L.host_weights(), local, pos_h,
+                                    before["k"], before["ks"], before["v"], before["vs"])
+    err = np.abs(y.cpu().numpy() - want)
+    # the layer tolerance of tests/test_layer_gpu.py
+    assert err.max() < 5e-2, err.max()
+    assert err.mean() < 5e-3, err.mean()
+    # the appended rows: the new token's k / v, dequantised, at row pos
+    b_idx = np.arange(B)
+    after = {k: cache[k].cpu().numpy() for k in ("k", "ks", "v", "vs")}
+    got_k = after["k"][b_idx, :, pos_h] * after["ks"][b_idx, :, pos_h][..., None]
+    got_v = after["v"][b_idx, :, pos_h] * after["vs"][b_idx, :, pos_h][..., None]
+    np.testing.assert_allclose(got_k, kn, atol=0.02 * np.abs(kn).max())
+    np.testing.assert_allclose(got_v, vn, atol=0.02 * np.abs(vn).max())
+    # nothing but row pos changed
+    changed = np.zeros(after["ks"].shape, bool)
+    changed[b_idx, :, pos_h] = True
+    assert np.array_equal(after["ks"][~changed], before["ks"][~changed].astype(np.float32))
+    assert np.array_equal(after["k"][~changed], before["k"][~changed].astype(np.int8))

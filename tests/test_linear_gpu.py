@@ -4,7 +4,8 @@
   with and without bias (incl. the all-zero row), int8 linear with shift-1
   ties and int32 biases;
 * the CPU oracle on seeded odd shapes (ragged M/N/K, partial tiles, tiny and
-  wide) and on every config-5 sweep shape (sampled rows at full size);
+  wide) and on every config-5 sweep shape at full size (a row of every
+  128-row block, all columns);
 * the raw int32 partial-sum epilogue.
 All comparisons are exact (bit patterns for fp32).
 """
@@ -133,7 +134,7 @@ def test_gemm_i32_matches_oracle(m, n, k):
     np.testing.assert_array_equal(got, ro.gemm_i8(a, b))
 
 
-# ---- config 5: the GEMM sweep at full size, sampled rows --------------------------
+# ---- config 5: the GEMM sweep at full size, a row of every 128-row block ------------
 
 SWEEP_NK = [(4096, 4096), (11008, 4096), (4096, 11008), (28672, 8192), (8192, 28672)]
 SWEEP_M = [1, 16, 128, 1024, 8192, 16384]
@@ -148,7 +149,12 @@ def test_sweep_shapes_sampled(m, n, k):
     xs = torch.rand((m,), generator=g, device="cuda") * 1e-3 + 1e-3
     ws = torch.rand((n,), generator=g, device="cuda") * 1e-3 + 1e-3
     y = K.gemm_w8a8(a, xs, b, ws)
-    rows = sorted({0, m - 1, *np.random.default_rng(m + n).integers(0, m, 6).tolist()})
+    # one row of every 128-row block (at a seeded offset inside it) and the
+    # last row, each across all N columns: every output tile of the
+    # persistent, raster-grouped schedule is compared, group boundaries
+    # included
+    off = np.random.default_rng(m + n).integers(0, 128, (m + 127) // 128)
+    rows = sorted({m - 1, *[min(m - 1, 128 * i + int(o)) for i, o in enumerate(off)]})
     idx = torch.tensor(rows, device="cuda")
     acc = ro.gemm_i8(host(a.index_select(0, idx)), host(b))
     want = ro.w8a8_epilogue(acc, host(xs)[rows], host(ws))
