@@ -328,6 +328,88 @@ def decode_attention(dev, pk: dict) -> dict:
                       f"{reps} replays"}
 
 
+def decode_step(dev, pk: dict, world: int, rank: int, comm) -> dict:
+    """Config 4's whole decode layer (Llama-70B shape, 64 sequences, one new
+    token each at position 4095 of a 4096-row int8 KV cache): at one GPU the
+    TP=8 shard of one rank (8 q / 1 kv heads, FFN 3584, no collectives); at N
+    GPUs the TP=N layer with its row-parallel all-reduces.  Each of `copies`
+    layer copies has its own weights and caches (together past L2, so every
+    step streams its weights and cache from DRAM, as successive layers of a
+    model do); a CUDA graph of `calls` steps over the copies is replayed
+    `reps` times.  HBM roofline: the shard's int8 weights + fp32 scales and
+    the int8 K / V rows + fp32 scales the attention reads, per step."""
+    import torch
+    import torch.distributed as dist
+
+    from reef_b200 import kernels as K
+    from reef_b200.layer import LLAMA_70B, LlamaLayer
+    s = LLAMA_70B
+    B, Lmax, copies, calls, reps = 64, 4096, 4, 8, 20
+    tp = world if world > 1 else 8
+    layers, caches = [], []
+    g = torch.Generator(device=dev).manual_seed(7)
+    for c in range(copies):
+        if world > 1:
+            L = LlamaLayer(s, B, 8, seed=11 + c, world=world, rank=rank, comm=comm, device=dev)
+        else:
+            L = LlamaLayer(s, B, 8, seed=11 + c, world=8, rank=0, device=dev)
+        cache = L.alloc_cache(Lmax)
+        cache["k"].random_(-127, 128, generator=g)
+        cache["v"].random_(-127, 128, generator=g)
+        cache["ks"].uniform_(0.005, 0.015, generator=g)
+        cache["vs"].uniform_(0.005, 0.015, generator=g)
+        layers.append(L)
+        caches.append(cache)
+    x = torch.randn((B, s.hidden), generator=g, device=dev)
+    y = torch.empty_like(x)
+    pos = torch.full((B,), Lmax - 1, dtype=torch.int32, device=dev)
+    for c in range(copies):  # workspaces allocated, tensor maps warmed
+        layers[c].decode(x, pos, caches[c], out=y)
+    torch.cuda.synchronize(dev)
+    K.check_device_error()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cap), torch.cuda.graph(graph, stream=cap):
+        for i in range(calls):
+            layers[i % copies].decode(x, pos, caches[i % copies], out=y)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    K.check_device_error()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+    if world > 1:
+        t = torch.tensor([us], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+    del graph
+    torch.cuda.synchronize(dev)
+    L = layers[0]
+    w_bytes = sum(getattr(L, n).numel() for n in ("w_qkv", "w_o", "w_gu", "w_down")) + \
+        4 * sum(getattr(L, n).numel() for n in ("s_qkv", "s_o", "s_gu", "s_down"))
+    kv_bytes = 2 * B * (s.heads_kv // tp) * Lmax * (128 + 4)
+    nbytes = w_bytes + kv_bytes
+    gbs = nbytes / (us * 1e-6) / 1e9
+    ops = 2.0 * B * (w_bytes - 4 * sum(getattr(L, n).numel()
+                                       for n in ("s_qkv", "s_o", "s_gu", "s_down"))) + \
+        2.0 * 2 * B * (s.heads_q // tp) * 128 * Lmax
+    return {"workload": "llama70b-w8a8-decode-layer (config 4)",
+            "parallelism": (f"tp{world}" if world > 1 else "tp8 shard of rank 0, no collectives"),
+            "us": us, "tokens_per_s": B / (us * 1e-6), "tops_per_gpu": ops / (us * 1e-6) / 1e12,
+            "bytes_per_gpu": nbytes, "achieved_gbs": gbs, "peak_gbs": pk["hbm"],
+            "frac": gbs / pk["hbm"], "peak_source": pk["source"],
+            "timing": f"CUDA graph of {calls} steps over {copies} layer copies (weights and "
+                      f"caches past L2), {reps} replays"}
+
+
 def run_reef(args) -> int:
     import torch
     import torch.distributed as dist
@@ -475,6 +557,27 @@ def run_reef(args) -> int:
     e2e_ms = e0.elapsed_time(e1) / e_steps
     barrier()
 
+    # Parity at N > 1, outside every timed region: this rank runs the same
+    # layer at TP=1 on its own GPU (same seed, same input) and compares its
+    # output shard with it bit for bit; the line reports the AND over ranks.
+    tp_ok = None
+    if world > 1:
+        L.forward(x, y)
+        L1 = LlamaLayer(s, BATCH, SEQ, seed=1, device=dev)
+        g1 = torch.Generator(device=dev).manual_seed(1234)
+        xf = torch.randn((T, s.hidden), generator=g1, device=dev)
+        y1 = L1.forward(xf)
+        if mode == TP_ALLGATHER:
+            y1 = y1[:, tp.col_slice(s.hidden, world, rank)].contiguous()
+        torch.cuda.synchronize(dev)
+        K.check_device_error()
+        same = torch.tensor([int(torch.equal(y.view(torch.int32), y1.view(torch.int32)))],
+                            device=dev)
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        tp_ok = bool(same.item())
+        del L1, xf, y1
+        torch.cuda.empty_cache()
+
     # max over ranks
     t = torch.tensor([ms, e2e_ms, gemm_ms, flash_ms], device=dev)
     if world > 1:
@@ -522,6 +625,8 @@ def run_reef(args) -> int:
                 "h2d_bytes_per_step": x.numel() * 4, "d2h_bytes_per_step": y.numel() * 4,
                 "ms_per_step": e2e_ms},
         "gpu_launches": int(launches) * K_steps,
+        "tp_bit_identical": tp_ok,
+        "exchange": exchange_bytes(s, T, world, args.tp_mode, ms),
         "clocks": dict(clocks.summary(w0, w1),
                        window="the timed region and the 1 s of the same forward just before it"),
     }
@@ -530,6 +635,11 @@ def run_reef(args) -> int:
             out["decode_attention"] = decode_attention(dev, pk)
         except Exception as e:  # noqa: BLE001
             out["decode_attention"] = {"error": str(e)[:200]}
+    try:  # after the measured line's own work; every rank takes part at N > 1
+        dstep = decode_step(dev, pk, world, rank, comm)
+    except Exception as e:  # noqa: BLE001
+        dstep = {"error": str(e)[:200]}
+    out["decode_step"] = dstep
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(s, host_threads())
     if comm is not None:
@@ -541,6 +651,27 @@ def run_reef(args) -> int:
     if rank == 0:
         emit(out)
     return 0
+
+
+def exchange_bytes(s, tokens: int, world: int, plan: str, ms: float) -> dict | None:
+    """Bytes that cross NVLink into each rank per layer forward, and how long
+    they take at the pool's measured 770 GB/s per direction (a lower bound
+    on the exchange, set beside the step time).  All-gather plan: the int8
+    activations of the four projections (3 x hidden + ffn bytes per token)
+    from the N - 1 peers, plus the RMSNorm chunk sums and the row maxima.
+    All-reduce plan: two int32 all-reduces of [tokens][hidden] (a ring moves
+    2 (N - 1) / N of it in) and two fp32 MAX all-reduces of [tokens]."""
+    if world <= 1:
+        return None
+    f = (world - 1) / world
+    if plan == "allgather":
+        s_words = 8 // world + 1
+        b = f * tokens * (3 * s.hidden + s.ffn) + (world - 1) * tokens * (2 * 4 * s_words + 2 * 4)
+    else:
+        b = 2 * f * 2 * tokens * s.hidden * 4 + 2 * 2 * f * tokens * 4
+    link_ms = b / 770e9 * 1e3
+    return {"plan": plan, "bytes_in_per_rank": b, "link_ms_at_770_gbs": link_ms,
+            "link_share_of_step": link_ms / ms}
 
 
 _JSON_OUT = None
