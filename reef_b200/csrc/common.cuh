@@ -40,6 +40,20 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
 }
 
+// ---- programmatic dependent launch ----------------------------------------------
+//
+// A kernel launched as a programmatic dependent (launch_k under a PdlScope,
+// ops.h) may start while the kernel before it in the stream still runs.
+// pdl_wait() returns once that kernel has completed and its memory is
+// visible (at once for an ordinary launch); every such kernel calls it before
+// it touches anything an earlier kernel writes, and calls pdl_trigger() only
+// after it, so the next kernel's early part overlaps this kernel alone, never
+// an older one.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- shared-memory addresses ------------------------------------------------
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -63,6 +77,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
       "mbarrier.arrive.release.cta.shared::cta.b64 st, [%0];\n\t}" ::"r"(
           smem_u32(bar))
       : "memory");
+}
+
+// Raise the bytes the current phase expects without arriving (the arrival,
+// and any more bytes, follow with mbar_arrive_expect_tx).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,

@@ -70,6 +70,7 @@ struct DecodeArgs {
   const float* k_scale;    // [B][Hkv][max_len]
   const float* v_scale;
   const int* lens;         // [B] keys per sequence, or null
+  const int* positions;    // [B] rows appended this step (lens - 1), or null
   int len;                 // keys per sequence when lens is null
   float* part;             // [ctas + B*Hkv][G][kPartRow]: row c + pair
   float* out;              // [B][Hq][128]
@@ -200,9 +201,28 @@ __global__ void __launch_bounds__(kDThreads, G > 8 ? 1 : 2)  // 16 heads: twice 
     }
     fence_barrier_init();
   }
+  // Before waiting for the kernel ahead (which appends this step's rows and
+  // writes q and lens), thread 0 requests the K / V tiles of its first units
+  // that lie wholly below the row each sequence appends: nothing running
+  // writes them.  Their scales, and every other tile, follow the wait.
+  uint32_t pre = 0;  // bit j: unit j's K / V were requested early
+  if (tid == 0 && a.positions != nullptr) {
+    for (int j = 0; j < kStages && j < nunits; ++j) {
+      const long long u = u0 + j;
+      const int pair = static_cast<int>(u / a.tiles);
+      const int key0 = static_cast<int>(u % a.tiles) * kTileKeys;
+      if (key0 + kTileKeys > a.positions[pair / a.heads_kv]) continue;
+      uint8_t* kv = sm + j * DL::kKV;
+      mbar_expect_tx(&full[j], static_cast<uint32_t>(2 * kTileKeys * 128));
+      tma_load_3d(kv, &kmap, &full[j], 0, key0, pair);
+      tma_load_3d(kv + kTileKeys * 128, &vmap, &full[j], 0, key0, pair);
+      pre |= 1u << j;
+    }
+  }
+  pdl_wait();
   // the combine kernel may be scheduled now; it waits for this grid's
   // completion (and its memory) before reading the partials
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_trigger();
   __syncthreads();
 
   // unit j of this CTA into stage j % kStages (thread 0).  The TMA boxes are
@@ -229,9 +249,13 @@ __global__ void __launch_bounds__(kDThreads, G > 8 ? 1 : 2)  // 16 heads: twice 
     const long long srow = static_cast<long long>(pair) * a.max_len + key0;
     uint8_t* kv = sm + s * DL::kKV;
     float* sc = reinterpret_cast<float*>(sm + DL::kScales + s * 1024);
-    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(2 * kTileKeys * 128 + 2 * n4 * 4));
-    tma_load_3d(kv, &kmap, &full[s], 0, key0, pair);
-    tma_load_3d(kv + kTileKeys * 128, &vmap, &full[s], 0, key0, pair);
+    if (j < kStages && ((pre >> j) & 1u)) {  // K / V already requested
+      mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(2 * n4 * 4));
+    } else {
+      mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(2 * kTileKeys * 128 + 2 * n4 * 4));
+      tma_load_3d(kv, &kmap, &full[s], 0, key0, pair);
+      tma_load_3d(kv + kTileKeys * 128, &vmap, &full[s], 0, key0, pair);
+    }
     bulk_load(sc, a.k_scale + srow, n4 * 4, &full[s]);
     bulk_load(sc + kTileKeys, a.v_scale + srow, n4 * 4, &full[s]);
   };
@@ -503,7 +527,8 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a) {
   const float* pb = a.part + (static_cast<long long>(c0) + pair) * stride + hg * kPartRow;
   // launched early (programmatic dependent launch): wait for the main
   // kernel's completion and memory before reading its partials
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_wait();
+  pdl_trigger();
   // one pass over the rows: warp w holds rows w, w + 8, ... (m, l and a
   // float4 of O per lane) in registers while the block finds the max
   constexpr int kRows = (kMaxRowsPerPair + kDWarps - 1) / kDWarps;
@@ -580,8 +605,9 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodeArgs& a, c
   const long long pairs = static_cast<long long>(a.batch) * a.heads_kv;
   a.ctas = static_cast<int>(std::min({static_cast<long long>(per_sm) * num_sms(), a.units,
                                       pairs * (kMaxRowsPerPair - 1)}));
-  decode_mma_kernel<G><<<static_cast<unsigned>(a.ctas), kDThreads, DL::bytes(G), st>>>(km, vm, a);
-  if (cudaGetLastError() != cudaSuccess) return kErrCuda;
+  if (int rc = launch_k(decode_mma_kernel<G>, dim3(static_cast<unsigned>(a.ctas)), dim3(kDThreads),
+                        DL::bytes(G), st, km, vm, a))
+    return rc;
   // the combine launches as a programmatic dependent of the main kernel, so
   // its launch overlaps the main kernel's tail
   cudaLaunchConfig_t cfg{};
@@ -604,13 +630,24 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodeArgs& a, c
 // rule (quant.hpp:51-81); q goes to q8 / q_scale, k and v are appended to the
 // cache at row `pos`, and lens[b] = pos + 1.  A position outside the cache is
 // recorded in the device error word and the row is skipped.
+// The projection comes either as fp32 rows qkv [B][(Hq + 2 Hkv) * 128], or
+// (kPartials) as the skinny GEMM's int32 split-K partials part[s][B][...]
+// (`splits` of them, B * (Hq + 2 Hkv) * 128 apart) that this kernel sums and
+// dequantises itself with the W8A8 epilogue (linear.hpp:125-127: float(sum) *
+// (x_scale[b] * w_scale[n])), the values a separate reduce would have stored.
+template <bool kPartials>
 __global__ void decode_rope_append_kernel(int batch, int hq, int hkv, int max_len, float base,
                                           const int* __restrict__ positions,
-                                          const float* __restrict__ qkv, int8_t* __restrict__ q8,
+                                          const float* __restrict__ qkv,
+                                          const int32_t* __restrict__ part, int splits,
+                                          const float* __restrict__ xs,
+                                          const float* __restrict__ ws, int8_t* __restrict__ q8,
                                           float* __restrict__ q_scale, int8_t* __restrict__ k_cache,
                                           float* __restrict__ k_scale, int8_t* __restrict__ v_cache,
                                           float* __restrict__ v_scale, int* __restrict__ lens,
                                           int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int heads = hq + 2 * hkv;
@@ -622,8 +659,25 @@ __global__ void decode_rope_append_kernel(int batch, int hq, int hkv, int max_le
     return;
   }
   if (hh == 0 && lane == 0) lens[b] = pos + 1;
-  const float* x = qkv + static_cast<long long>(b) * heads * 128 + hh * 128;
-  float v[4] = {x[lane], x[lane + 32], x[lane + 64], x[lane + 96]};
+  float v[4];
+  if constexpr (kPartials) {
+    const long long row = static_cast<long long>(b) * heads * 128;
+    const long long stride = static_cast<long long>(batch) * heads * 128;
+    const float rs = xs[b];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int n = hh * 128 + lane + 32 * p;
+      int32_t acc = part[row + n];
+      for (int sp = 1; sp < splits; ++sp) acc += part[sp * stride + row + n];
+      v[p] = __fmul_rn(__int2float_rn(acc), __fmul_rn(rs, ws[n]));
+    }
+  } else {
+    const float* x = qkv + static_cast<long long>(b) * heads * 128 + hh * 128;
+    v[0] = x[lane];
+    v[1] = x[lane + 32];
+    v[2] = x[lane + 64];
+    v[3] = x[lane + 96];
+  }
   if (hh < hq + hkv) {  // q or k: rotate-half RoPE, pairs (i, i + 64)
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
@@ -666,10 +720,27 @@ int decode_rope_append(int batch, int heads_q, int heads_kv, int max_len, float 
                        int8_t* k_cache, float* k_scale, int8_t* v_cache, float* v_scale, int* lens,
                        cudaStream_t stream) {
   const long long warps = static_cast<long long>(batch) * (heads_q + 2 * heads_kv);
-  decode_rope_append_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(
-      batch, heads_q, heads_kv, max_len, rope_base, positions, qkv, q8, q_scale, k_cache, k_scale,
-      v_cache, v_scale, lens, device_error_ptr());
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_k(decode_rope_append_kernel<false>,
+                  dim3(static_cast<unsigned>((warps * 32 + 255) / 256)), dim3(256), 0, stream,
+                  batch, heads_q, heads_kv, max_len, rope_base, positions, qkv,
+                  static_cast<const int32_t*>(nullptr), 1, static_cast<const float*>(nullptr),
+                  static_cast<const float*>(nullptr), q8, q_scale, k_cache, k_scale, v_cache,
+                  v_scale, lens, device_error_ptr());
+}
+
+int decode_rope_append_partials(int batch, int heads_q, int heads_kv, int max_len,
+                                float rope_base, const int* positions, const int32_t* part,
+                                int splits, const float* x_scale, const float* w_scale,
+                                int8_t* q8, float* q_scale, int8_t* k_cache, float* k_scale,
+                                int8_t* v_cache, float* v_scale, int* lens, cudaStream_t stream) {
+  if (part == nullptr || splits < 1 || x_scale == nullptr || w_scale == nullptr)
+    return kErrInvalid;
+  const long long warps = static_cast<long long>(batch) * (heads_q + 2 * heads_kv);
+  return launch_k(decode_rope_append_kernel<true>,
+                  dim3(static_cast<unsigned>((warps * 32 + 255) / 256)), dim3(256), 0, stream,
+                  batch, heads_q, heads_kv, max_len, rope_base, positions,
+                  static_cast<const float*>(nullptr), part, splits, x_scale, w_scale, q8, q_scale,
+                  k_cache, k_scale, v_cache, v_scale, lens, device_error_ptr());
 }
 
 
@@ -704,6 +775,7 @@ int decode_attn_i8(const DecodeProblem& p, cudaStream_t st) {
   a.k_scale = p.k_scale;
   a.v_scale = p.v_scale;
   a.lens = p.lens;
+  a.positions = p.lens != nullptr ? p.positions : nullptr;
   a.len = p.len;
   a.part = p.partial;
   a.out = p.out;

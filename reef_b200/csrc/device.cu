@@ -8,6 +8,8 @@
 
 namespace reef {
 
+thread_local bool t_pdl = false;
+
 namespace {
 
 // One error word per device.  Bounded waits in the kernels record their

@@ -152,9 +152,6 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // a programmatic dependent (the split-K reduce) may be scheduled now; it
-  // waits for this grid's completion and memory before reading the outputs
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -163,21 +160,46 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
+      // When A depends on no earlier kernel (the weights of a swap-AB skinny
+      // GEMM), the first item's leading k-blocks of A are requested before
+      // waiting for the kernel before this one (a programmatic dependent
+      // launch lets the two overlap); their B halves follow the wait.  The
+      // ring is fresh, so those stages need no "empty" wait.
+      int pre = 0;
+      if (args.a_first && static_cast<int>(blockIdx.x) < num_items) {
+        int mb, nb;
+        tile_coords(blockIdx.x / splits, num_m, num_n, args.group_m, mb, nb);
+        const int split = blockIdx.x % splits;
+        const int kb0 = split * num_k / splits, kb1 = (split + 1) * num_k / splits;
+        pre = min(STAGES, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          const int kb = kb0 + i, seg = kb / kbs, kx = (kb - seg * kbs) * kBK;
+          mbar_arrive_expect_tx(&full[i], L::kStageBytes);
+          tma_load_3d(smem + i * L::kStageBytes, &tma_a, &full[i], kx, mb * kBM, seg);
+        }
+      }
+      pdl_wait();
+      // a programmatic dependent may be scheduled now; it waits for this
+      // grid's completion and memory before reading the outputs
+      pdl_trigger();
       for (int t = blockIdx.x; t < num_items && ok; t += gridDim.x) {
         int mb, nb;
         tile_coords(t / splits, num_m, num_n, args.group_m, mb, nb);
         const int split = t % splits;
         const int kb0 = split * num_k / splits, kb1 = (split + 1) * num_k / splits;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutEmpty)) {
+          const bool prefetched = t == static_cast<int>(blockIdx.x) && kb - kb0 < pre;
+          if (!prefetched && !mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
           uint8_t* sa = smem + stage * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
           const int seg = kb / kbs, kx = (kb - seg * kbs) * kBK;
-          tma_load_3d(sa, &tma_a, &full[stage], kx, mb * kBM, seg);
+          if (!prefetched) {
+            mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+            tma_load_3d(sa, &tma_a, &full[stage], kx, mb * kBM, seg);
+          }
           if constexpr (EPI == kEpiSwiGLU) {
             tma_load_3d(sb, &tma_b, &full[stage], kx, nb * kOut, seg);
             tma_load_3d(sb + kOut * kBK, &tma_b, &full[stage], kx,
@@ -261,6 +283,9 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
     // ways), then each thread requantises 4 consecutive columns of 8 rows,
     // so a store instruction writes 4 rows x 32 contiguous columns and the
     // per-column scale / bias are loaded once per chunk.
+    // the epilogue reads scales and residuals and writes outputs that the
+    // kernel before this one may touch
+    pdl_wait();
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
     uint32_t* tbuf = reinterpret_cast<uint32_t*>(smem + L::kTransposeOff) +
                      (warp - 2) * kTransposeWords;
@@ -515,6 +540,33 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
         if (acc == 0) acc_phase ^= 1u;
         continue;
       }
+      if constexpr (EPI == kEpiI32T) {
+        // split-K partials of a swap-AB GEMM, token-major: y[split][n][m],
+        // straight from the accumulator (lane = row m, so a token's 32 rows
+        // are one contiguous 128-byte store)
+        int32_t* yp = static_cast<int32_t*>(args.y) + y_off;
+        const int m = row0 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col0 = nb * BN + c * 32;
+          if (col0 >= N) break;  // warp-uniform
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                 static_cast<uint32_t>(acc * BN + c * 32),
+                             r);
+          tmem_ld_wait();
+          if (m < M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) yp[static_cast<long long>(col0 + j) * args.ldy + m] = static_cast<int32_t>(r[j]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = nb * BN + c * 32;
@@ -702,51 +754,65 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
     const uintptr_t r = reinterpret_cast<uintptr_t>(args.residual);
     args.vec_ok = (y % align == 0) && (r % 16 == 0) && (args.ldy % 4 == 0) ? 1 : 0;
   }
-  kernel<<<grid, threads_for<EPI>(), L::kAlloc, stream>>>(ma, mb, args);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_k(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads_for<EPI>()), L::kAlloc,
+                  stream, ma, mb, args);
 }
 
-// Sums the K-split partials part[s][n][m] (n = weight row, m = token) and
-// applies the epilogue in token-major order: y[m][n].  A 32 x 32 tile goes
-// through shared memory so the partial reads (along m) and the output writes
-// (along n) are both contiguous.
-template <int EPI>
-__global__ void splitk_reduce_kernel(int splits, int M, int N, const int32_t* __restrict__ part,
-                                     const float* __restrict__ xs, const float* __restrict__ ws,
-                                     const float* __restrict__ bias,
-                                     const float* __restrict__ residual, void* __restrict__ y) {
-  __shared__ int32_t tile[32][33];
-  const int n0 = blockIdx.x * 32, m0 = blockIdx.y * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
-  // launched early (programmatic dependent launch): wait for the split-K
-  // GEMM's completion and memory before reading its partials
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int n = n0 + ty + 8 * i, m = m0 + tx;
-    int32_t acc = 0;
-    if (n < N && m < M) {
-      for (int s = 0; s < splits; ++s)
-        acc += part[(static_cast<long long>(s) * N + n) * M + m];
+// Sums the K-split partials part[s][m][n] (token-major, m * n apart) and
+// applies the epilogue: y[m][n].  kVec: four consecutive outputs per thread
+// (n % 4 == 0), else one.  Launched as a programmatic dependent of the GEMM
+// that writes the partials.
+template <int EPI, bool kVec>
+__global__ void __launch_bounds__(256)
+    skinny_reduce_kernel(int splits, int M, int N, const int32_t* __restrict__ part,
+                         const float* __restrict__ xs, const float* __restrict__ ws,
+                         const float* __restrict__ bias, const float* __restrict__ residual,
+                         void* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  const long long total = static_cast<long long>(M) * N;
+  constexpr int V = kVec ? 4 : 1;
+  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * V;
+  if (i >= total) return;
+  int32_t a[V];
+  if constexpr (kVec) {
+    int4 v = *reinterpret_cast<const int4*>(part + i);
+    for (int s = 1; s < splits; ++s) {
+      const int4 w = *reinterpret_cast<const int4*>(part + static_cast<long long>(s) * total + i);
+      v.x += w.x;
+      v.y += w.y;
+      v.z += w.z;
+      v.w += w.w;
     }
-    tile[ty + 8 * i][tx] = acc;
+    a[0] = v.x;
+    a[1] = v.y;
+    a[2] = v.z;
+    a[3] = v.w;
+  } else {
+    int32_t v = part[i];
+    for (int s = 1; s < splits; ++s) v += part[static_cast<long long>(s) * total + i];
+    a[0] = v;
   }
-  __syncthreads();
+  const int m = static_cast<int>(i / N), n = static_cast<int>(i % N);
+  if constexpr (EPI == kEpiF32W8A8) {
+    const float rs = xs[m];
+    float o[V];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = m0 + ty + 8 * i, n = n0 + tx;
-    if (m < M && n < N) {
-      const int32_t a = tile[tx][ty + 8 * i];
-      const long long off = static_cast<long long>(m) * N + n;
-      if constexpr (EPI == kEpiF32W8A8) {
-        float v = __fmul_rn(__int2float_rn(a), __fmul_rn(xs[m], ws[n]));
-        if (bias != nullptr) v = __fadd_rn(v, bias[n]);
-        if (residual != nullptr) v = __fadd_rn(residual[off], v);
-        static_cast<float*>(y)[off] = v;
-      } else {
-        static_cast<int32_t*>(y)[off] = a;
-      }
+    for (int e = 0; e < V; ++e) {
+      // linear.hpp:125-127: float(sum) * (row_scale * w_scale[c]), then + bias
+      o[e] = __fmul_rn(__int2float_rn(a[e]), __fmul_rn(rs, ws[n + e]));
+      if (bias != nullptr) o[e] = __fadd_rn(o[e], bias[n + e]);
+      if (residual != nullptr) o[e] = __fadd_rn(residual[i + e], o[e]);
     }
+    if constexpr (kVec)
+      *reinterpret_cast<float4*>(static_cast<float*>(y) + i) = make_float4(o[0], o[1], o[2], o[3]);
+    else
+      static_cast<float*>(y)[i] = o[0];
+  } else {
+    if constexpr (kVec)
+      *reinterpret_cast<int4*>(static_cast<int32_t*>(y) + i) = make_int4(a[0], a[1], a[2], a[3]);
+    else
+      static_cast<int32_t*>(y)[i] = a[0];
   }
 }
 
@@ -786,12 +852,12 @@ size_t skinny_partial_bytes(int m, int n, int k) {
   return static_cast<size_t>(skinny_splits(m, n, k)) * n * m * sizeof(int32_t);
 }
 
-int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int epilogue,
-                   const float* x_scale, const float* w_scale, const float* bias,
-                   const float* residual, void* y, void* partial, cudaStream_t stream) {
-  if (m <= 0 || n <= 0 || k <= 0 || m > 128 || partial == nullptr || y == nullptr)
+int skinny_split_count(int m, int n, int k) { return skinny_splits(m, n, k); }
+
+int gemm_i8_skinny_partials(int m, int n, int k, const int8_t* x, const int8_t* w,
+                            int32_t* part, cudaStream_t stream) {
+  if (m <= 0 || n <= 0 || k <= 0 || m > 128 || part == nullptr || x == nullptr || w == nullptr)
     return kErrInvalid;
-  if (epilogue != kEpiF32W8A8 && epilogue != kEpiI32) return kErrInvalid;
   const int splits = skinny_splits(m, n, k);
   GemmProblem p{};
   p.M = n;  // weight rows on the MMA's M side (swap-AB)
@@ -803,33 +869,48 @@ int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int ep
   p.ldb = static_cast<long long>(kpad(k));
   p.args.k_splits = splits;
   p.args.split_stride = static_cast<long long>(n) * m;
-  p.args.y = partial;
-  p.args.ldy = m;
-  const int rc = m <= 64 ? launch<64, 8, kEpiI32>(p, stream) : launch<128, 6, kEpiI32>(p, stream);
-  if (rc) return rc;
+  p.args.y = part;
+  p.args.ldy = n;
+  p.args.a_first = 1;  // the weights: no earlier kernel writes them
+  return m <= 64 ? launch<64, 8, kEpiI32T>(p, stream) : launch<128, 6, kEpiI32T>(p, stream);
+}
+
+int skinny_reduce(int m, int n, int splits, const int32_t* part, int epilogue,
+                  const float* x_scale, const float* w_scale, const float* bias,
+                  const float* residual, void* y, cudaStream_t stream) {
+  if (m <= 0 || n <= 0 || splits < 1 || part == nullptr || y == nullptr) return kErrInvalid;
+  if (epilogue == kEpiF32W8A8 && (x_scale == nullptr || w_scale == nullptr)) return kErrInvalid;
+  if (epilogue != kEpiF32W8A8 && epilogue != kEpiI32) return kErrInvalid;
+  const bool vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(part) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+  const long long total = static_cast<long long>(m) * n;
+  const long long threads = vec ? total / 4 : total;
+  const dim3 grid(static_cast<unsigned>((threads + 255) / 256)), block(256);
+  if (epilogue == kEpiF32W8A8)
+    return vec ? launch_k(skinny_reduce_kernel<kEpiF32W8A8, true>, grid, block, 0, stream, splits,
+                          m, n, part, x_scale, w_scale, bias, residual, y)
+               : launch_k(skinny_reduce_kernel<kEpiF32W8A8, false>, grid, block, 0, stream, splits,
+                          m, n, part, x_scale, w_scale, bias, residual, y);
+  const float* none = nullptr;
+  return vec ? launch_k(skinny_reduce_kernel<kEpiI32, true>, grid, block, 0, stream, splits, m, n,
+                        part, none, none, none, none, y)
+             : launch_k(skinny_reduce_kernel<kEpiI32, false>, grid, block, 0, stream, splits, m, n,
+                        part, none, none, none, none, y);
+}
+
+int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int epilogue,
+                   const float* x_scale, const float* w_scale, const float* bias,
+                   const float* residual, void* y, void* partial, cudaStream_t stream) {
+  if (m <= 0 || n <= 0 || k <= 0 || m > 128 || partial == nullptr || y == nullptr)
+    return kErrInvalid;
+  if (epilogue != kEpiF32W8A8 && epilogue != kEpiI32) return kErrInvalid;
+  int32_t* part = static_cast<int32_t*>(partial);
+  if (int rc = gemm_i8_skinny_partials(m, n, k, x, w, part, stream)) return rc;
   // the reduce launches as a programmatic dependent of the GEMM, so its launch
   // overlaps the GEMM's tail
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>((m + 31) / 32));
-  cfg.blockDim = dim3(32, 8);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const int32_t* part = static_cast<const int32_t*>(partial);
-  const cudaError_t e =
-      epilogue == kEpiF32W8A8
-          ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<kEpiF32W8A8>, splits, m, n, part,
-                               x_scale, w_scale, bias, residual, y)
-          : cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<kEpiI32>, splits, m, n, part,
-                               static_cast<const float*>(nullptr),
-                               static_cast<const float*>(nullptr),
-                               static_cast<const float*>(nullptr),
-                               static_cast<const float*>(nullptr), y);
-  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  PdlScope pdl;
+  return skinny_reduce(m, n, skinny_splits(m, n, k), part, epilogue, x_scale, w_scale, bias,
+                       residual, y, stream);
 }
 
 int gemm_i8(const GemmProblem& p, int epilogue, cudaStream_t stream) {

@@ -323,6 +323,7 @@ int llama_check(const reef_b200_llama_layer* L) {
 struct DecodeBufs {
   int8_t* xq;
   float* xs;
+  float* xs2;  // the down projection's input scales (xs holds gate/up's while they are read)
   float* row_max;
   float* big;
   int8_t* q8;
@@ -341,6 +342,7 @@ size_t decode_carve(const reef_b200_llama_layer* L, size_t max_len, void* ws, De
   Carve c(ws, ~static_cast<size_t>(0));
   b->xq = c.take<int8_t>(B * std::max({kpad(H), kpad(hq * D), kpad(F)}));
   b->xs = c.take<float>(B);
+  b->xs2 = c.take<float>(B);
   b->row_max = c.take<float>(B);
   b->big = c.take<float>(B * std::max((hq + 2 * hkv) * D, 2 * F));
   b->q8 = c.take<int8_t>(B * hq * D);
@@ -1224,11 +1226,20 @@ int reef_b200_llama_decode_forward(const reef_b200_llama_layer* L, const float* 
             hq = static_cast<int>(L->heads_q), hkv = static_cast<int>(L->heads_kv),
             F = static_cast<int>(L->ffn), D = 128;
   const int qkv_w = (hq + 2 * hkv) * D;
+  int32_t* part = static_cast<int32_t*>(b.partial);
+  // Every kernel of the step launches as a programmatic dependent of the one
+  // before it: its launch and set-up, and the skinny GEMMs' weight loads (no
+  // kernel writes the weights), overlap the kernel ahead.  The QKV and
+  // gate/up GEMMs leave int32 split-K partials that the next kernel sums
+  // itself (RoPE + cache append; SwiGLU + quantisation), so no separate
+  // reduce runs between them.
+  PdlScope pdl;
   REEF_TRY(rmsnorm_quant(B, H, L->rms_eps, x, L->attn_norm, b.xq, b.xs, st));
-  REEF_TRY(gemm_i8_skinny(B, qkv_w, H, b.xq, L->w_qkv, kEpiF32W8A8, b.xs, L->s_qkv, nullptr,
-                          nullptr, b.big, b.partial, st));
-  REEF_TRY(decode_rope_append(B, hq, hkv, static_cast<int>(max_len), L->rope_base, positions,
-                              b.big, b.q8, b.qs, k_cache, k_scale, v_cache, v_scale, b.lens, st));
+  const int s_qkv = skinny_split_count(B, qkv_w, H);
+  REEF_TRY(gemm_i8_skinny_partials(B, qkv_w, H, b.xq, L->w_qkv, part, st));
+  REEF_TRY(decode_rope_append_partials(B, hq, hkv, static_cast<int>(max_len), L->rope_base,
+                                       positions, part, s_qkv, b.xs, L->s_qkv, b.q8, b.qs,
+                                       k_cache, k_scale, v_cache, v_scale, b.lens, st));
   DecodeProblem dp{};
   dp.batch = B;
   dp.heads_q = hq;
@@ -1242,6 +1253,7 @@ int reef_b200_llama_decode_forward(const reef_b200_llama_layer* L, const float* 
   dp.v_cache = v_cache;
   dp.v_scale = v_scale;
   dp.lens = b.lens;
+  dp.positions = positions;
   dp.partial = b.dpart;
   dp.out = b.attn;
   REEF_TRY(decode_attn_i8(dp, st));
@@ -1255,12 +1267,16 @@ int reef_b200_llama_decode_forward(const reef_b200_llama_layer* L, const float* 
                            b.row_max, b.acc, b.partial, b.h, st));
   }
   REEF_TRY(rmsnorm_quant(B, H, L->rms_eps, b.h, L->mlp_norm, b.xq, b.xs, st));
-  REEF_TRY(gemm_i8_skinny(B, 2 * F, H, b.xq, L->w_gu, kEpiF32W8A8, b.xs, L->s_gu, nullptr,
-                          nullptr, b.big, b.partial, st));
+  const int s_gu = skinny_split_count(B, 2 * F, H);
+  REEF_TRY(gemm_i8_skinny_partials(B, 2 * F, H, b.xq, L->w_gu, part, st));
   {
-    auto quant = [&](const float* rm) { return swiglu_quant(B, F, b.big, rm, b.xq, b.xs, st); };
-    auto absmax = [&](float* rm) { return swiglu_absmax(B, F, b.big, rm, st); };
-    REEF_TRY(rowpar_skinny(c, B, F, H, quant, absmax, L->w_down, L->s_down, b.h, b.xq, b.xs,
+    auto quant = [&](const float* rm) {
+      return swiglu_partials(B, F, part, s_gu, b.xs, L->s_gu, rm, nullptr, b.xq, b.xs2, st);
+    };
+    auto absmax = [&](float* rm) {
+      return swiglu_partials(B, F, part, s_gu, b.xs, L->s_gu, nullptr, rm, nullptr, nullptr, st);
+    };
+    REEF_TRY(rowpar_skinny(c, B, F, H, quant, absmax, L->w_down, L->s_down, b.h, b.xq, b.xs2,
                            b.row_max, b.acc, b.partial, y, st));
   }
   return REEF_B200_OK;

@@ -157,6 +157,8 @@ __global__ void __launch_bounds__(kChunks * 32)
                          long long ldq, float* __restrict__ xs) {
   __shared__ float csum[kChunks];
   __shared__ float cmax[kChunks];
+  pdl_wait();
+  pdl_trigger();
   const long long row = blockIdx.x;
   const int c = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int n4 = width / (4 * kChunks);  // float4 per chunk
@@ -310,6 +312,67 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) row_max[row] = m;
 }
 
+// SwiGLU on the split-K partials of the gate/up projection (one CTA per
+// row): g and u are the W8A8 epilogue values of columns n and ffn + n
+// (float(sum) * (x_scale * w_scale), linear.hpp:125-127), h = silu_mul(g, u)
+// as everywhere else.  row_max_out: write max |h| only.  Else quantise with
+// row_max_in, or the row's own max when it is null.
+template <int CACHE>
+__global__ void __launch_bounds__(kThreads)
+    swiglu_partials_kernel(int ffn, int splits, const int32_t* __restrict__ part,
+                           const float* __restrict__ xs, const float* __restrict__ ws,
+                           const float* __restrict__ row_max_in, float* __restrict__ row_max_out,
+                           int8_t* __restrict__ xq, long long ldq, float* __restrict__ qs) {
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
+  const long long row = blockIdx.x;
+  const long long stride = static_cast<long long>(gridDim.x) * 2 * ffn;
+  const int4* p4 = reinterpret_cast<const int4*>(part + row * 2 * ffn);
+  const float4* ws4 = reinterpret_cast<const float4*>(ws);
+  const int n4 = ffn >> 2;
+  const float rs = xs[row];
+  float4 c[CACHE];
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < CACHE; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < n4) {
+      int4 g = p4[idx], u = p4[n4 + idx];
+      for (int s = 1; s < splits; ++s) {
+        const int4 g2 = p4[s * stride / 4 + idx], u2 = p4[s * stride / 4 + n4 + idx];
+        g.x += g2.x; g.y += g2.y; g.z += g2.z; g.w += g2.w;
+        u.x += u2.x; u.y += u2.y; u.z += u2.z; u.w += u2.w;
+      }
+      const float4 wg = ws4[idx], wu = ws4[n4 + idx];
+      const float4 gf = make_float4(__fmul_rn(__int2float_rn(g.x), __fmul_rn(rs, wg.x)),
+                                    __fmul_rn(__int2float_rn(g.y), __fmul_rn(rs, wg.y)),
+                                    __fmul_rn(__int2float_rn(g.z), __fmul_rn(rs, wg.z)),
+                                    __fmul_rn(__int2float_rn(g.w), __fmul_rn(rs, wg.w)));
+      const float4 uf = make_float4(__fmul_rn(__int2float_rn(u.x), __fmul_rn(rs, wu.x)),
+                                    __fmul_rn(__int2float_rn(u.y), __fmul_rn(rs, wu.y)),
+                                    __fmul_rn(__int2float_rn(u.z), __fmul_rn(rs, wu.z)),
+                                    __fmul_rn(__int2float_rn(u.w), __fmul_rn(rs, wu.w)));
+      c[i] = swiglu4(gf, uf);
+      m = fmaxf(m, amax4(c[i]));
+    }
+  }
+  if (row_max_out != nullptr) {
+    m = block_max(m, red);
+    if (threadIdx.x == 0) row_max_out[row] = m;
+    return;
+  }
+  const float mx = row_max_in != nullptr ? row_max_in[row] : block_max(m, red);
+  const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  if (threadIdx.x == 0) qs[row] = scale;
+  char4* out = reinterpret_cast<char4*>(xq + row * ldq);
+#pragma unroll
+  for (int i = 0; i < CACHE; ++i) {
+    const int idx = threadIdx.x + i * kThreads;
+    if (idx < n4) out[idx] = q8x4(c[i], scale);
+  }
+}
+
 }  // namespace
 
 // Smallest supported per-thread cache (float4) that holds n4 float4.
@@ -342,13 +405,12 @@ int rmsnorm_quant(long long rows, int width, float eps, const float* x, const fl
   if (width <= 0 || width % (4 * kChunks) != 0) return kErrInvalid;
   const unsigned grid = static_cast<unsigned>(rows);
   const int P = per_thread(width);
-  const int T = kChunks * 32;
+  const dim3 T(kChunks * 32);
   const long long ld = width;
-  if (P <= 1) rmsnorm_quant_kernel<1><<<grid, T, 0, stream>>>(width, eps, x, gain, x_q, ld, x_scale);
-  else if (P <= 2) rmsnorm_quant_kernel<2><<<grid, T, 0, stream>>>(width, eps, x, gain, x_q, ld, x_scale);
-  else if (P <= 4) rmsnorm_quant_kernel<4><<<grid, T, 0, stream>>>(width, eps, x, gain, x_q, ld, x_scale);
-  else return kErrInvalid;
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  if (P <= 1) return launch_k(rmsnorm_quant_kernel<1>, dim3(grid), T, 0, stream, width, eps, x, gain, x_q, ld, x_scale);
+  if (P <= 2) return launch_k(rmsnorm_quant_kernel<2>, dim3(grid), T, 0, stream, width, eps, x, gain, x_q, ld, x_scale);
+  if (P <= 4) return launch_k(rmsnorm_quant_kernel<4>, dim3(grid), T, 0, stream, width, eps, x, gain, x_q, ld, x_scale);
+  return kErrInvalid;
 }
 
 int rms_stats(long long rows, int width, int ranks, const float* x_local, const float* gain_local,
@@ -392,6 +454,33 @@ int swiglu_quant(long long rows, int ffn, const float* gu, const float* row_max,
   REEF_DISPATCH_CACHE(c, swiglu_quant_kernel, ffn, gu, row_max, x_q,
                       static_cast<long long>(ffn), x_scale);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int swiglu_partials(long long rows, int ffn, const int32_t* part, int splits, const float* x_scale,
+                    const float* w_scale, const float* row_max_in, float* row_max_out,
+                    int8_t* x_q, float* q_scale, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  const int c = cache_for(ffn / 4);
+  if (ffn <= 0 || ffn % 4 != 0 || c == 0 || splits < 1 || !part || !x_scale || !w_scale)
+    return kErrInvalid;
+  if (row_max_out == nullptr && (x_q == nullptr || q_scale == nullptr)) return kErrInvalid;
+  if ((reinterpret_cast<uintptr_t>(part) | reinterpret_cast<uintptr_t>(w_scale)) & 15u)
+    return kErrAlignment;
+  const dim3 grid(static_cast<unsigned>(rows)), block(kThreads);
+  const long long ld = ffn;
+#define REEF_SWIGLU_PARTIALS(C)                                                               \
+  return launch_k(swiglu_partials_kernel<C>, grid, block, 0, stream, ffn, splits, part, x_scale, \
+                  w_scale, row_max_in, row_max_out, x_q, ld, q_scale)
+  switch (c) {
+    case 1: REEF_SWIGLU_PARTIALS(1);
+    case 2: REEF_SWIGLU_PARTIALS(2);
+    case 4: REEF_SWIGLU_PARTIALS(4);
+    case 6: REEF_SWIGLU_PARTIALS(6);
+    case 8: REEF_SWIGLU_PARTIALS(8);
+    case 12: REEF_SWIGLU_PARTIALS(12);
+    default: REEF_SWIGLU_PARTIALS(16);
+  }
+#undef REEF_SWIGLU_PARTIALS
 }
 
 int swiglu_absmax(long long rows, int ffn, const float* gu, float* row_max, cudaStream_t stream) {

@@ -33,6 +33,10 @@ enum Epilogue : int {
   // the kEpiF32W8A8 values of a QKV projection (heads of 128 columns: q, then
   // k, then v), then RoPE on q / k and int8 per (token, head): see QkvOut
   kEpiQkvRope = 4,
+  // y = acc, the split-K partials of a swap-AB skinny GEMM stored
+  // token-major: y[split][n][m] (n: the kernel's N, a token; m: its M, a
+  // weight row), row stride ldy = M
+  kEpiI32T = 5,
 };
 
 // kEpiQkvRope outputs (the layout rope_qkv_quant writes).  Rows are tokens
@@ -48,6 +52,41 @@ struct QkvOut {
   float* vs;           // [B][Hkv][S] or null
   void* vt;            // [B][Hkv][128][S] f16, f16(v code * v scale)
 };
+
+// ---- launches --------------------------------------------------------------------
+//
+// While a PdlScope lives on a host thread, the kernels that thread launches
+// through launch_k go out as programmatic dependents of the kernel before
+// them in the stream: their launch and set-up (and, in the skinny GEMM, the
+// weight loads, which no earlier kernel writes) overlap that kernel's work.
+// Each such kernel waits for its predecessor (pdl_wait, common.cuh) before
+// reading or writing anything the predecessor may touch.  Without a scope,
+// launch_k is an ordinary launch.
+extern thread_local bool t_pdl;
+struct PdlScope {
+  bool prev;
+  PdlScope() : prev(t_pdl) { t_pdl = true; }
+  ~PdlScope() { t_pdl = prev; }
+  PdlScope(const PdlScope&) = delete;
+  PdlScope& operator=(const PdlScope&) = delete;
+};
+
+template <typename... KArgs, typename... Args>
+int launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+             Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = t_pdl ? attr : nullptr;
+  cfg.numAttrs = t_pdl ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) != cudaSuccess) return kErrCuda;
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
 
 // Row stride (bytes) of every int8 matrix the tensor cores read: TMA needs
 // 16-byte aligned row strides.
@@ -73,6 +112,9 @@ struct GemmArgs {
   int vec_ok;             // 16-byte (int8: 4-byte) output stores allowed (launcher)
   int max_ctas;           // > 0: at most this many persistent CTAs (SMs left to others)
   int gelu;               // kEpiF32W8A8: y = gelu(dequant + bias), reef's tanh form, before any residual
+  // A depends on no earlier kernel (the weights of a swap-AB GEMM): its first
+  // stages are requested before the kernel waits for its predecessor
+  int a_first;
   int* err;               // device error word (set by the launcher)
 };
 
@@ -130,6 +172,17 @@ size_t skinny_partial_bytes(int m, int n, int k);
 int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int epilogue,
                    const float* x_scale, const float* w_scale, const float* bias,
                    const float* residual, void* y, void* partial, cudaStream_t stream);
+// The two halves of gemm_i8_skinny, for consumers that fold the split-K sum
+// into their own pass: the GEMM writes skinny_split_count(m, n, k) int32
+// partials part[s][m][n] (token-major, m * n apart); skinny_reduce sums them
+// and applies the epilogue (kEpiF32W8A8: dequant [+ bias] [+ residual] ->
+// fp32 y; kEpiI32: the int32 sums), y [m][n].
+int skinny_split_count(int m, int n, int k);
+int gemm_i8_skinny_partials(int m, int n, int k, const int8_t* x, const int8_t* w,
+                            int32_t* part, cudaStream_t stream);
+int skinny_reduce(int m, int n, int splits, const int32_t* part, int epilogue,
+                  const float* x_scale, const float* w_scale, const float* bias,
+                  const float* residual, void* y, cudaStream_t stream);
 
 // One output written alike to up to kMaxDst places: the same offset in every
 // rank's symmetric arena, so an exchanged activation goes from the kernel that
@@ -233,6 +286,15 @@ int w8a8_epilogue_i32(long long rows, long long out, const int32_t* acc,
 // llama.cu -- fused RMSNorm / SwiGLU + per-token quantisation
 int rmsnorm_quant(long long rows, int width, float eps, const float* x, const float* gain,
                   int8_t* x_q, float* x_scale, cudaStream_t stream);
+// SwiGLU of the gate/up projection's split-K partials (token-major int32
+// sums part[s][row][2 ffn], splits of them, rows * 2 ffn apart), dequantised
+// with the W8A8 epilogue: h = silu(g) * u, one CTA per row.  row_max_out set:
+// write max |h| per row and nothing else.  Otherwise quantise h to x_q / x_scale
+// with row_max_in (the all-reduced maximum) or, when it is null, the row's
+// own maximum.
+int swiglu_partials(long long rows, int ffn, const int32_t* part, int splits, const float* x_scale,
+                    const float* w_scale, const float* row_max_in, float* row_max_out,
+                    int8_t* x_q, float* q_scale, cudaStream_t stream);
 int swiglu_quant(long long rows, int ffn, const float* gu, const float* row_max, int8_t* x_q,
                  float* x_scale, cudaStream_t stream);
 int swiglu_absmax(long long rows, int ffn, const float* gu, float* row_max,
@@ -298,6 +360,11 @@ struct DecodeProblem {
   const int8_t* v_cache;
   const float* v_scale;
   const int* lens;        // [B] cached keys per sequence (device), or null
+  // [B] device, or null: the row each sequence appends in this step (lens =
+  // positions + 1), unchanged while the step runs.  Lets the kernel request
+  // the K / V tiles wholly below it before the kernel ahead of it (the one
+  // that appends those rows) has finished.
+  const int* positions;
   int len;                // cached keys of every sequence when lens is null
   float* partial;         // decode_attn_partial_floats() floats of scratch
   float* out;             // [B][Hq][128]
@@ -307,6 +374,14 @@ int decode_rope_append(int batch, int heads_q, int heads_kv, int max_len, float 
                        const int* positions, const float* qkv, int8_t* q8, float* q_scale,
                        int8_t* k_cache, float* k_scale, int8_t* v_cache, float* v_scale, int* lens,
                        cudaStream_t stream);
+// decode_rope_append on the QKV projection's split-K partials (the skinny
+// GEMM's token-major int32 sums, gemm_i8_skinny_partials), summed and
+// dequantised here: the same outputs, without a separate reduce.
+int decode_rope_append_partials(int batch, int heads_q, int heads_kv, int max_len,
+                                float rope_base, const int* positions, const int32_t* part,
+                                int splits, const float* x_scale, const float* w_scale,
+                                int8_t* q8, float* q_scale, int8_t* k_cache, float* k_scale,
+                                int8_t* v_cache, float* v_scale, int* lens, cudaStream_t stream);
 int decode_attn_i8(const DecodeProblem& p, cudaStream_t stream);
 
 }  // namespace reef

@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(kQuantThreads)
     quantize_rows_vec4(int in, const float* __restrict__ x, PeerDst xq, long long ldq,
                        float* __restrict__ xs, const float* __restrict__ row_max) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const long long row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * in);
   const int n4 = in >> 2;
@@ -104,6 +106,8 @@ __global__ void __launch_bounds__(kQuantThreads)
                          long long ldq, float* __restrict__ xs,
                          const float* __restrict__ row_max) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const long long row = blockIdx.x;
   const float* xr = x + row * in;
   float m = 0.0f;
@@ -118,6 +122,8 @@ __global__ void __launch_bounds__(kQuantThreads)
 __global__ void __launch_bounds__(kQuantThreads)
     row_absmax_kernel(int in, const float* __restrict__ x, PeerDst out) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const float* xr = x + static_cast<long long>(blockIdx.x) * in;
   float m = 0.0f;
   for (int c = threadIdx.x; c < in; c += kQuantThreads) m = fmaxf(m, fabsf(xr[c]));
@@ -206,6 +212,8 @@ __global__ void w8a8_epilogue_kernel(long long rows, int out, const int32_t* __r
                                      const float* __restrict__ ws,
                                      const float* __restrict__ bias,
                                      const float* __restrict__ residual, float* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= rows * out) return;
   const long long r = i / out;
@@ -224,20 +232,13 @@ static int quantize_vec4(long long rows, long long in, const float* x, const Pee
   const int per = static_cast<int>((in / 4 + kQuantThreads - 1) / kQuantThreads);
   const unsigned grid = static_cast<unsigned>(rows);
   const int ii = static_cast<int>(in);
-  if (per <= 1) {
-    quantize_rows_vec4<1><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-  } else if (per <= 2) {
-    quantize_rows_vec4<2><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-  } else if (per <= 4) {
-    quantize_rows_vec4<4><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-  } else if (per <= 8) {
-    quantize_rows_vec4<8><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-  } else if (per <= 12) {
-    quantize_rows_vec4<12><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-  } else {
-    quantize_rows_vec4<16><<<grid, kQuantThreads, 0, stream>>>(ii, x, x_q, ldq, x_scale, row_max);
-  }
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  const dim3 g(grid), t(kQuantThreads);
+  if (per <= 1) return launch_k(quantize_rows_vec4<1>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
+  if (per <= 2) return launch_k(quantize_rows_vec4<2>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
+  if (per <= 4) return launch_k(quantize_rows_vec4<4>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
+  if (per <= 8) return launch_k(quantize_rows_vec4<8>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
+  if (per <= 12) return launch_k(quantize_rows_vec4<12>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
+  return launch_k(quantize_rows_vec4<16>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
 }
 
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q, long long ldq,
@@ -249,9 +250,8 @@ int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q, lon
                    (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(x_q) % 4 == 0);
   if (vec) return quantize_vec4(rows, in, x, one_dst(x_q), ldq, x_scale, row_max, stream);
-  quantize_rows_scalar<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
-      static_cast<int>(in), x, x_q, ldq, x_scale, row_max);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_k(quantize_rows_scalar, dim3(static_cast<unsigned>(rows)), dim3(kQuantThreads), 0,
+                  stream, static_cast<int>(in), x, x_q, ldq, x_scale, row_max);
 }
 
 int quantize_rows_to(long long rows, long long in, const float* x, const PeerDst& x_q,
@@ -298,9 +298,8 @@ int row_absmax_to(long long rows, long long in, const float* x, const PeerDst& r
                   cudaStream_t stream) {
   if (rows == 0) return kOk;
   if (in <= 0 || x == nullptr || !dst_ok(row_max)) return kErrInvalid;
-  row_absmax_kernel<<<static_cast<unsigned>(rows), kQuantThreads, 0, stream>>>(
-      static_cast<int>(in), x, row_max);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_k(row_absmax_kernel, dim3(static_cast<unsigned>(rows)), dim3(kQuantThreads), 0,
+                  stream, static_cast<int>(in), x, row_max);
 }
 
 int row_absmax(long long rows, long long in, const float* x, float* row_max,
@@ -340,9 +339,8 @@ int w8a8_epilogue_i32(long long rows, long long out, const int32_t* acc, const f
                       cudaStream_t stream) {
   if (rows == 0) return kOk;
   const long long n = rows * out;
-  w8a8_epilogue_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
-      rows, static_cast<int>(out), acc, x_scale, w_scale, bias, residual, y);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_k(w8a8_epilogue_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                  stream, rows, static_cast<int>(out), acc, x_scale, w_scale, bias, residual, y);
 }
 
 }  // namespace reef

@@ -77,9 +77,19 @@ def parse_header(text: str):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get(
-        "REEF_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=None,
+                    help="the reef checkout (default: $REEF_REFERENCE, else a checkout "
+                         "named 'reference' beside this repository)")
     args = ap.parse_args()
+    if args.reference is None:
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(
+            os.path.abspath(__file__)))))
+        from oracle.oracle import reference_root
+        args.reference = reference_root()
+    if args.reference is None:
+        print("reef checkout not found: pass --reference or set REEF_REFERENCE",
+              file=sys.stderr)
+        return 1
     ie = os.path.join(args.reference, "inference-engine")
     src = os.path.join(ie, "coral", "host", "gen_golden.cpp")
     if not os.path.exists(src):

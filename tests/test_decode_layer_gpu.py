@@ -122,10 +122,16 @@ def test_decode_config4_tp8_shard_matches_reference():
     local = RL.LlamaShape(hidden=8192, heads_q=8, heads_kv=1, ffn=3584)
     want, kn, vn = decode_reference(x.cpu().numpy(), L.host_weights(), local, pos_h,
                                     before["k"], before["ks"], before["v"], before["vs"])
-    err = np.abs(y.cpu().numpy() - want)
-    # the layer tolerance of tests/test_layer_gpu.py
-    assert err.max() < 5e-2, err.max()
-    assert err.mean() < 5e-3, err.mean()
+    xh = x.cpu().numpy()
+    err = y.cpu().numpy() - want
+    sub = want - xh  # the two sublayers' contribution
+    rel = float(np.sqrt((err ** 2).mean() / (sub ** 2).mean()))
+    worst = float(np.abs(err).max())
+    # the tolerance of tests/test_llama_config3_gpu.py at these widths: int8
+    # code flips between faithful float orders give ~1.5 % rms of the
+    # sublayers' output; a wrong head, position or scale gives tens of percent
+    assert rel < 0.05, (rel, worst)
+    assert worst < 0.5, (rel, worst)
     # the appended rows: the new token's k / v, dequantised, at row pos
     b_idx = np.arange(B)
     after = {k: cache[k].cpu().numpy() for k in ("k", "ks", "v", "vs")}

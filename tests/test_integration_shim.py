@@ -16,8 +16,10 @@ import subprocess
 
 import pytest
 
+from oracle.oracle import reference_root
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.environ.get("REEF_REFERENCE", "/root/reference")
+REF = reference_root() or ""
 CORAL_INC = os.path.join(REF, "inference-engine", "coral", "include")
 CUDA_INC = "/usr/local/cuda/include"
 
