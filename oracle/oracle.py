@@ -35,13 +35,25 @@ _u16p = C.POINTER(C.c_uint16)
 _sz = C.c_size_t
 
 
+def reference_root() -> str | None:
+    """The reef checkout the in-place reference builds from: $REEF_REFERENCE,
+    else a checkout named ``reference`` beside this repository; None when
+    neither holds reef's engine headers."""
+    cands = [os.environ.get("REEF_REFERENCE", "")]
+    cands.append(os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference"))
+    for c in cands:
+        if c and os.path.isdir(os.path.join(c, "inference-engine", "reference", "cpp",
+                                            "include")):
+            return c
+    return None
+
+
 def build(reference: bool = True) -> None:
-    """Compile the restatement (and the in-place reference when present)."""
+    """Compile the restatement (and the in-place reference when the reef
+    checkout is found; an existing _ref build is kept otherwise)."""
     subprocess.run(["make", "-s", "-C", _HERE, "all"], check=True)
-    ref_root = os.environ.get("REEF_REFERENCE", "/root/reference")
-    if reference and os.path.isdir(
-            os.path.join(ref_root, "inference-engine", "reference", "cpp",
-                         "include")):
+    ref_root = reference_root()
+    if reference and ref_root is not None:
         subprocess.run(["make", "-s", "-C", _HERE, "ref",
                         f"REEF_REFERENCE={ref_root}"], check=True)
 
@@ -118,6 +130,11 @@ def ref() -> C.CDLL:
         R.ref_quantize_rows.argtypes = [_sz, _sz, _f32p, _i8p, _f32p]
         R.ref_linear_w8a8.argtypes = [_sz, _sz, _sz, _f32p, _i8p, _f32p,
                                       _f32p, _f32p]
+        R.ref_weight_new.argtypes = [_sz, _sz, _i8p, _f32p]
+        R.ref_weight_new.restype = C.c_void_p
+        R.ref_weight_free.argtypes = [C.c_void_p]
+        R.ref_weight_free.restype = None
+        R.ref_linear_w8a8_weight.argtypes = [C.c_void_p, _sz, _sz, _f32p, _f32p]
         R.ref_linear_int8.argtypes = [_sz, _sz, _sz, _i8p, _i8p, C.c_uint,
                                       _i32p, _i8p]
         R.ref_matmul_i8.argtypes = [_sz, _sz, _sz, _i8p, _i8p, _i32p]

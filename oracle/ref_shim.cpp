@@ -93,6 +93,35 @@ int ref_linear_w8a8(std::size_t rows, std::size_t in, std::size_t out,
     });
 }
 
+// A W8A8 weight built once as the engine's QuantizedWeight (quant.hpp:38-43),
+// for repeated linear() calls on it: each call still does the engine's own
+// per-call work (linear.hpp:106-134 transposes W inside), but the weight is
+// not copied into a new Tensor per call.  NULL on failure.
+void* ref_weight_new(std::size_t out, std::size_t in, const std::int8_t* w,
+                     const float* w_scale) {
+    try {
+        return new ie::QuantizedWeight<float>{
+            matrix(out, in, w), std::vector<float>(w_scale, w_scale + out)};
+    } catch (const std::exception&) {
+        return nullptr;
+    }
+}
+
+void ref_weight_free(void* weight) {
+    delete static_cast<ie::QuantizedWeight<float>*>(weight);
+}
+
+// W8A8 linear (operator/linear.hpp:106-134) of x [rows][in] by a weight from
+// ref_weight_new: y [rows][out].
+int ref_linear_w8a8_weight(const void* weight, std::size_t rows, std::size_t in,
+                           const float* x, float* y) {
+    return guarded([&] {
+        const auto& qw = *static_cast<const ie::QuantizedWeight<float>*>(weight);
+        const ie::Tensor<float> result = ie::linear<float>(matrix(rows, in, x), qw);
+        std::memcpy(y, result.values.data(), result.values.size() * sizeof(float));
+    });
+}
+
 // linear_int8 (int8.hpp:74-101); bias may be NULL.
 int ref_linear_int8(std::size_t rows, std::size_t in, std::size_t out,
                     const std::int8_t* x, const std::int8_t* w,
