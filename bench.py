@@ -78,57 +78,86 @@ def layer_ops(s, tokens: int, seq: int) -> dict:
 
 class RefSample:
     """reef's own W8A8 linear (operator/linear.hpp:106-134) and float head
-    (attention.hpp:117-123), compiled in place (oracle/_ref), run on a
-    bounded sample of the layer: each host thread pushes one token through
-    the four projections (a fraction `frac` of their output columns) and its
-    32 heads of causal attention at a position spread over the sequence."""
+    (attention.hpp:117-123), compiled in place (oracle/_ref), on a bounded
+    sample of the layer.  Each host thread pushes ROWS tokens per linear()
+    call, as a prefill does, through a slice (fraction `frac`) of each
+    projection's output rows; the engine's QuantizedWeight for each slice is
+    built once, outside the timed calls (reef's linear still transposes W
+    inside every call, as it does in its own prefill).  Attention: the same
+    ROWS queries, ending at a position spread over the sequence, through
+    `frac` of the 32 heads."""
 
-    def __init__(self, s, threads: int):
+    ROWS = 128
+
+    def __init__(self, s, threads: int, frac: float):
         import numpy as np
 
         from oracle import oracle as ro
-        self.ro, self.np, self.s, self.threads = ro, np, s, threads
+        self.ro, self.np, self.s, self.threads, self.frac = ro, np, s, threads, frac
         self.lib = ro.ref()
         rng = np.random.default_rng(5)
         h, d = s.hidden, s.head_dim
         dims = [((s.heads_q + 2 * s.heads_kv) * d, h), (h, s.heads_q * d), (2 * s.ffn, h),
                 (h, s.ffn)]
-        self.w = [rng.integers(-127, 128, (n, k), dtype=np.int8) for n, k in dims]
-        self.ws = [np.full(n, 1e-3, np.float32) for n, _ in dims]
-        self.kv = rng.standard_normal((2, SEQ, d)).astype(np.float32)
-
-    def _token(self, i: int, frac: float) -> float:
-        np, s, L = self.np, self.s, self.lib
-        f = C.POINTER(C.c_float)
         i8 = C.POINTER(C.c_int8)
+        f = C.POINTER(C.c_float)
+        self.handles, self.shapes = [], []
+        for n, k in dims:
+            ns = max(1, int(round(n * frac)))
+            w = rng.integers(-127, 128, (ns, k), dtype=np.int8)
+            ws = np.full(ns, 1e-3, np.float32)
+            hnd = self.lib.ref_weight_new(ns, k, w.ctypes.data_as(i8), ws.ctypes.data_as(f))
+            if not hnd:
+                raise RuntimeError("reef engine could not build a weight")
+            self.handles.append(hnd)
+            self.shapes.append((ns, k))
+        self.heads = max(1, int(round(s.heads_q * frac)))
+        self.kv = rng.standard_normal((2, SEQ, d)).astype(np.float32)
+        self.x = [[rng.standard_normal((self.ROWS, k)).astype(np.float32) for _, k in self.shapes]
+                  for _ in range(threads)]
+        self.q = [rng.standard_normal((self.ROWS, d)).astype(np.float32) for _ in range(threads)]
+
+    def close(self):
+        for hnd in self.handles:
+            self.lib.ref_weight_free(hnd)
+        self.handles = []
+
+    def _rows(self, i: int) -> float:
+        np, s, L, R = self.np, self.s, self.lib, self.ROWS
+        f = C.POINTER(C.c_float)
         ops = 0.0
-        for w, ws in zip(self.w, self.ws):
-            n = max(1, int(round(w.shape[0] * frac)))
-            k = w.shape[1]
-            x = np.random.default_rng(i).standard_normal((1, k)).astype(np.float32)
-            y = np.empty((1, n), np.float32)
-            wn = w[:n]
-            L.ref_linear_w8a8(1, k, n, x.ctypes.data_as(f), wn.ctypes.data_as(i8),
-                              ws.ctypes.data_as(f), None, y.ctypes.data_as(f))
-            ops += 2.0 * k * n
-        pos = (i * SEQ) // self.threads + SEQ // (2 * self.threads)
-        heads = max(1, int(round(s.heads_q * frac)))
-        q = np.random.default_rng(i + 99).standard_normal((1, s.head_dim)).astype(np.float32)
-        kk = np.ascontiguousarray(self.kv[0, :pos + 1])
-        vv = np.ascontiguousarray(self.kv[1, :pos + 1])
-        o = np.empty((1, s.head_dim), np.float32)
-        for _ in range(heads):
-            L.ref_attend_head_f32(1, pos + 1, s.head_dim, pos, 0, q.ctypes.data_as(f),
-                                  kk.ctypes.data_as(f), vv.ctypes.data_as(f),
-                                  o.ctypes.data_as(f))
-            ops += 2.0 * 2 * s.head_dim * (pos + 1)
+        for hnd, (n, k), x in zip(self.handles, self.shapes, self.x[i]):
+            y = np.empty((R, n), np.float32)
+            rc = L.ref_linear_w8a8_weight(hnd, R, k, x.ctypes.data_as(f), y.ctypes.data_as(f))
+            if rc != 0:
+                raise RuntimeError(f"reef linear failed ({rc})")
+            ops += 2.0 * R * n * k
+        # queries at positions last - R + 1 .. last, causal over keys 0..last
+        last = R - 1 + (i * (SEQ - R)) // max(1, self.threads - 1)
+        kk = np.ascontiguousarray(self.kv[0, :last + 1])
+        vv = np.ascontiguousarray(self.kv[1, :last + 1])
+        o = np.empty((R, s.head_dim), np.float32)
+        for _ in range(self.heads):
+            L.ref_attend_head_f32(R, last + 1, s.head_dim, last - R + 1, 0,
+                                  self.q[i].ctypes.data_as(f), kk.ctypes.data_as(f),
+                                  vv.ctypes.data_as(f), o.ctypes.data_as(f))
+            ops += 2.0 * 2 * s.head_dim * sum(last - R + 2 + j for j in range(R))
         return ops
 
-    def run(self, frac: float = 1.0):
+    def run(self):
         t0 = time.perf_counter()
         with cf.ThreadPoolExecutor(self.threads) as ex:
-            ops = sum(ex.map(lambda i: self._token(i, frac), range(self.threads)))
+            ops = sum(ex.map(self._rows, range(self.threads)))
         return ops, time.perf_counter() - t0
+
+    def describe(self) -> str:
+        cols = ", ".join(f"{n}x{k}" for n, k in self.shapes)
+        return (f"reef engine (oracle/_ref, -O2 -ffp-contract=off), {self.threads} threads: each "
+                f"pushes {self.ROWS} tokens per linear() call through slices of the 4 W8A8 "
+                f"projections ({self.frac:.3g} of their output rows: {cols}; QuantizedWeight "
+                f"built once, reef transposes W inside each call) and {self.heads} head(s) of "
+                f"causal float attention for the same {self.ROWS} queries at a position spread "
+                f"over 0..{SEQ - 1}")
 
 
 def host_threads() -> int:
@@ -138,19 +167,29 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_baseline(s, threads: int, frac: float = 1.0) -> dict:
+def calibrated_sample(s, threads: int, seconds: float):
+    """A RefSample whose run() takes about `seconds` on these host cores:
+    one small run measures the engine's rate, the slice is then scaled."""
+    probe = RefSample(s, threads, 0.002)
+    probe.run()
+    _, t = probe.run()
+    probe.close()
+    frac = min(1.0, max(0.002, 0.002 * seconds / max(t, 1e-3)))
+    return RefSample(s, threads, frac)
+
+
+def cpu_baseline(s, threads: int, seconds: float = 10.0) -> dict:
     from oracle import oracle as ro
     if not ro.ref_available():
         return {"value": None, "unit": "TOPS", "cores": threads, "kind": "reference",
                 "sample": "unavailable: oracle/_ref was not built (needs the reference checkout)"}
-    rs = RefSample(s, threads)
-    ops, sec = rs.run(frac)
-    return {"value": ops / sec / 1e12, "unit": "TOPS", "cores": threads, "kind": "reference",
-            "seconds": sec, "tokens_per_s": threads / sec,
-            "sample": (f"reef engine (oracle/_ref, -O2 -ffp-contract=off): {threads} threads x 1 "
-                       f"token through the 4 W8A8 projections ({frac:.3g} of their output "
-                       f"columns) + its 32-head causal float attention at positions spread over "
-                       f"0..{SEQ - 1}; W8A8 linear re-transposes W per call as reef does")}
+    rs = calibrated_sample(s, threads, seconds)
+    ops, sec = rs.run()
+    out = {"value": ops / sec / 1e12, "unit": "TOPS", "cores": threads, "kind": "reference",
+           "seconds": sec, "tokens_per_s": ops / sec / layer_ops(s, 1, SEQ)["total"],
+           "sample": rs.describe()}
+    rs.close()
+    return out
 
 
 def run_reference(args) -> int:
@@ -165,15 +204,13 @@ def run_reference(args) -> int:
               "unavailable": "oracle/_ref not built: reef's engine headers were absent when "
                              "build() ran"})
         return 0
-    rs = RefSample(s, threads)
-    # warm-up steps: a token through 1% of every projection
+    # each timed step a bounded sample, so the whole run stays within minutes
+    rs = calibrated_sample(s, threads, min(10.0, 150.0 / max(args.steps, 1)))
     for _ in range(max(args.warmup, 0)):
-        rs.run(0.01)
-    # timed steps: each a bounded sample; the whole run stays within minutes
-    frac = min(1.0, 150.0 / (7.0 * max(args.steps, 1)))
+        rs.run()
     total_ops, total_s = 0.0, 0.0
     for _ in range(args.steps):
-        ops, sec = rs.run(frac)
+        ops, sec = rs.run()
         total_ops += ops
         total_s += sec
     v = total_ops / total_s / 1e12
@@ -184,12 +221,14 @@ def run_reference(args) -> int:
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": WORKLOAD, "batch": BATCH, "seq_len": SEQ, "tokens": BATCH * SEQ,
                    "hidden": s.hidden, "heads": s.heads_q, "ffn": s.ffn},
-        "tokens_per_s": threads * args.steps / total_s,
+        # whole-layer tokens/s implied by the sampled rate (the sample's ops
+        # are a fraction of the layer's ops per token)
+        "tokens_per_s": v * 1e12 / (layer_ops(s, 1, SEQ)["total"]),
         "cpu_baseline": {"value": v, "unit": "TOPS", "cores": threads, "kind": "reference",
-                         "sample": f"per step: {threads} threads x 1 token through {frac:.3g} of "
-                                   f"the projections' output columns + attention"},
+                         "sample": "per step: " + rs.describe()},
         "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    rs.close()
     emit(out)
     return 0
 
