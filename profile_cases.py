@@ -1,14 +1,20 @@
-"""Single-kernel cases for profiler captures (ncu) of the hot kernels.
+"""Cases for profiler captures (ncu) of the hot kernels, and the config-5
+GEMM sweep.  The recipe behind the summaries in profiles/.
 
-    python -m reef_b200.profile_cases gemm  [--m 16384 --n 12288 --k 4096]
-    python -m reef_b200.profile_cases flash [--batch 8 --seq 2048 --heads 32]
-    python -m reef_b200.profile_cases qkv   [--batch 8 --seq 2048 --heads 32]
-    python -m reef_b200.profile_cases decode [--batch 64 --heads 8 --kv-heads 1 --seq 4096]
-    python -m reef_b200.profile_cases sweep [--out sweep.json]
+    python profile_cases.py gemm  [--m 16384 --n 12288 --k 4096]
+    python profile_cases.py flash [--batch 8 --seq 2048 --heads 32]
+    python profile_cases.py qkv   [--batch 8 --seq 2048 --heads 32]
+    python profile_cases.py decode [--batch 64 --heads 8 --kv-heads 1 --seq 4096]
+    python profile_cases.py decode_step [--steps 3]
+    python profile_cases.py layer [--batch 8 --steps 2]
+    python profile_cases.py sweep [--out sweep.json] [--tp 1]
 
-Each case allocates its seeded inputs once, launches the kernel twice (a
-warm-up launch, then the one to capture: ``ncu -k regex:<name> -s 1 -c 1``)
-and synchronises.  The default GEMM is the config-3 QKV projection
+Each single-kernel case allocates its seeded inputs once, launches the kernel
+twice (a warm-up launch, then the one to capture: ``ncu -k regex:<name> -s 1
+-c 1``) and synchronises.  ``decode_step`` runs config 4's whole decode step
+(the TP=8 shard of rank 0: 64 sequences at position 4095 of a 4096-row int8
+cache) `--steps` times, and ``layer`` config 3's prefill layer at TP=1
+(`--batch` sequences of 2048), each launch by launch, for the launch list.  The default GEMM is the config-3 QKV projection
 (A 64 MiB + B 48 MiB of int8 and an 768 MiB fp32 output: larger than L2,
 about 1 GiB on the device); the default flash case is config 3's attention.
 
@@ -31,8 +37,8 @@ import os
 
 import torch
 
-from . import _lib
-from . import kernels as K
+from reef_b200 import _lib
+from reef_b200 import kernels as K
 
 
 def gemm(m: int, n: int, k: int) -> None:
@@ -109,13 +115,44 @@ def decode(batch: int, heads: int, kv_heads: int, cache_len: int) -> None:
     torch.cuda.synchronize()
 
 
+def decode_step(steps: int) -> None:
+    """Config 4's decode layer, the TP=8 shard of rank 0 (no collectives)."""
+    from reef_b200.layer import LLAMA_70B, LlamaLayer
+    B, Lmax = 64, 4096
+    L = LlamaLayer(LLAMA_70B, B, 8, seed=11, world=8, rank=0)
+    cache = L.alloc_cache(Lmax)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    cache["k"].random_(-127, 128, generator=g)
+    cache["v"].random_(-127, 128, generator=g)
+    cache["ks"].uniform_(0.005, 0.015, generator=g)
+    cache["vs"].uniform_(0.005, 0.015, generator=g)
+    x = torch.randn((B, LLAMA_70B.hidden), generator=g, device="cuda")
+    y = torch.empty_like(x)
+    pos = torch.full((B,), Lmax - 1, dtype=torch.int32, device="cuda")
+    for _ in range(steps):
+        L.decode(x, pos, cache, out=y)
+    torch.cuda.synchronize()
+
+
+def layer(batch: int, steps: int) -> None:
+    """Config 3's prefill layer at TP=1: `batch` sequences of 2048 tokens."""
+    from reef_b200.layer import LLAMA_7B, LlamaLayer
+    L = LlamaLayer(LLAMA_7B, batch, 2048, seed=1)
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    x = torch.randn((batch * 2048, LLAMA_7B.hidden), generator=g, device="cuda")
+    y = torch.empty_like(x)
+    for _ in range(steps):
+        L.forward(x, y)
+    torch.cuda.synchronize()
+
+
 SWEEP_M = (1, 16, 128, 1024, 8192, 16384)
 SWEEP_NK = ((4096, 4096), (11008, 4096), (4096, 11008), (28672, 8192), (8192, 28672))
 L2_BYTES = 126 << 20
 
 
 def _peaks() -> dict:
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    root = os.path.dirname(os.path.abspath(__file__))
     try:
         with open(os.path.join(root, "MEASURED_PEAKS.json")) as fh:
             m = json.load(fh)
@@ -124,11 +161,25 @@ def _peaks() -> dict:
         return {"int8_tops": 2.0 * 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def sweep(out: str | None, iters: int = 20, reps: int = 3) -> None:
+def _shard_points(tps):
+    """(split, tp, n, k) per config-5 point: the unsplit GEMM at tp 1, and at
+    tp > 1 one GPU's share of a column split (N / tp, K) and of a row split
+    (N, K / tp; its int32 partial sums still need the all-reduce, not timed
+    here)."""
+    for (n, k) in SWEEP_NK:
+        for tp in tps:
+            if tp == 1:
+                yield "none", 1, n, k
+            else:
+                yield "column", tp, n // tp, k
+                yield "row", tp, n, k // tp
+
+
+def sweep(out: str | None, tps=(1,), iters: int = 20, reps: int = 3) -> None:
     peaks = _peaks()
     lib = _lib.lib()
     rows = []
-    for (n, k) in SWEEP_NK:
+    for (split, tp, n, k) in _shard_points(tps):
         kp = K.kpad(k)
         for m in SWEEP_M:
             g = torch.Generator(device="cuda").manual_seed(m + n + k)
@@ -182,7 +233,8 @@ def sweep(out: str | None, iters: int = 20, reps: int = 3) -> None:
             tops = ops / (ms * 1e-3) / 1e12
             gbs = moved / (ms * 1e-3) / 1e9
             tensor = m >= 1024
-            r = {"m": m, "n": n, "k": k, "path": "skinny split-K" if skinny else "tcgen05 persistent",
+            r = {"m": m, "n": n, "k": k, "tp": tp, "split": split,
+                 "path": "skinny split-K" if skinny else "tcgen05 persistent",
                  "ms": ms, "tops": tops, "gbs": gbs, "bound": "tensor" if tensor else "hbm",
                  "frac": tops / peaks["int8_tops"] if tensor else gbs / peaks["hbm_gbs"],
                  "peak_source": peaks["source"], "operand_copies": copies}
@@ -197,7 +249,9 @@ def sweep(out: str | None, iters: int = 20, reps: int = 3) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "flash", "qkv", "decode", "sweep"])
+    ap.add_argument("case", choices=["gemm", "flash", "qkv", "decode", "decode_step", "layer",
+                                     "sweep"])
+    ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=4096)
@@ -206,15 +260,20 @@ def main() -> None:
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--kv-heads", type=int, default=32)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--tp", default="1", help="comma-separated TP degrees for the sweep")
     a = ap.parse_args()
     if a.case == "sweep":
-        sweep(a.out)
+        sweep(a.out, tuple(int(t) for t in a.tp.split(",")))
     elif a.case == "gemm":
         gemm(a.m, a.n, a.k)
     elif a.case == "qkv":
         qkv(a.batch, a.seq, a.heads, a.kv_heads)
     elif a.case == "decode":
         decode(a.batch, a.heads, a.kv_heads, a.seq)
+    elif a.case == "decode_step":
+        decode_step(a.steps)
+    elif a.case == "layer":
+        layer(a.batch, a.steps)
     else:
         flash(a.batch, a.seq, a.heads, a.kv_heads)
     K.check_device_error()
