@@ -168,6 +168,21 @@ int reef_b200_linear_w8a8_noalloc(size_t rows, size_t in, size_t out, const floa
                                   const int8_t* w, const float* w_scale, const float* bias,
                                   float* y, reef_b200_stream_t stream);
 
+/* The decode layout of a K-major int8 weight w [rows][kpad(in)] (no
+ * counterpart in reef): 16 KiB tiles of 128 rows x 128 bytes of K, each stored
+ * exactly as the tensor cores read it from shared memory (128-byte swizzle:
+ * 16-byte chunk c of tile row r at r * 128 + ((c ^ (r % 8)) * 16)), the tiles
+ * of one 128-row block consecutive along K: tile (row block rb, k-block kb)
+ * at byte (rb * ceil(in / 128) + kb) * 16384.  Bytes past the matrix are
+ * zero.  A decode GEMM (few tokens, the weight on the tensor cores' 128-row
+ * side) then reads each of its stages as one contiguous 16 KiB block instead
+ * of 128 row pieces of 128 bytes, each kpad(in) bytes apart, which keeps HBM
+ * streaming.  tiles: reef_b200_weight_tiles_bytes(rows, in) bytes, 1024-byte
+ * aligned. */
+size_t reef_b200_weight_tiles_bytes(size_t rows, size_t in);
+int reef_b200_pack_weight_tiles(size_t rows, size_t in, const int8_t* w, int8_t* tiles,
+                                reef_b200_stream_t stream);
+
 /* The W8A8 GEMM for few rows (decode: one token per sequence, rows <= 128):
  * same result as reef_b200_gemm_w8a8 (bias may be NULL), computed with the
  * weights as the tensor cores' 128-row operand and K split across SMs, so a
@@ -494,6 +509,14 @@ typedef struct reef_b200_llama_layer {
   const int8_t* w_down; const float* s_down;    /* [hidden][ffn] */
   reef_b200_comm* comm;                         /* NULL: TP = 1 */
   int tp_mode;  /* with comm: REEF_B200_TP_ALLREDUCE or REEF_B200_TP_ALLGATHER */
+  /* Optional, for the decode step (NULL: the K-major weights above are read):
+   * w_qkv, w_o, w_gu and w_down again in the layout reef_b200_pack_weight_tiles
+   * writes (1024-byte aligned), which the decode step's GEMMs stream as
+   * contiguous 16 KiB blocks. */
+  const int8_t* t_qkv;
+  const int8_t* t_o;
+  const int8_t* t_gu;
+  const int8_t* t_down;
 } reef_b200_llama_layer;
 
 /* Two tensor-parallel plans for the Llama layer (both bit-identical to TP=1):

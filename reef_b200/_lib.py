@@ -60,6 +60,8 @@ SIGNATURES = {
     "reef_b200_rmsnorm_quant": ([_sz, _sz, C.c_float] + [_p] * 5, _i),
     "reef_b200_selftest_wait_timeout": ([C.c_uint, _p, _p], _i),
     "reef_b200_selftest_peer_wait_timeout": ([C.c_uint, _p, C.c_uint, _p], _i),
+    "reef_b200_weight_tiles_bytes": ([_sz, _sz], _sz),
+    "reef_b200_pack_weight_tiles": ([_sz, _sz, _p, _p, _p], _i),
     "reef_b200_linear_w8a8_qkv_rope": ([_sz] * 5 + [C.c_float] + [_p] * 13, _i),
     "reef_b200_gemm_skinny_workspace_bytes": ([_sz, _sz, _sz], _sz),
     "reef_b200_gemm_w8a8_skinny": ([_sz, _sz, _sz] + [_p] * 6 + [_sz, _p, _p], _i),
@@ -104,7 +106,8 @@ class LlamaLayerDesc(C.Structure):
                 ("heads_kv", _sz), ("head_dim", _sz), ("ffn", _sz), ("rms_eps", C.c_float),
                 ("rope_base", C.c_float), ("attn_norm", _p), ("w_qkv", _p), ("s_qkv", _p),
                 ("w_o", _p), ("s_o", _p), ("mlp_norm", _p), ("w_gu", _p), ("s_gu", _p),
-                ("w_down", _p), ("s_down", _p), ("comm", _p), ("tp_mode", _i)]
+                ("w_down", _p), ("s_down", _p), ("comm", _p), ("tp_mode", _i),
+                ("t_qkv", _p), ("t_o", _p), ("t_gu", _p), ("t_down", _p)]
 
 
 class GptNeoBlockDesc(C.Structure):

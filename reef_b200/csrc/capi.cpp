@@ -419,6 +419,22 @@ int reef_b200_selftest_wait_timeout(unsigned limit_us, int* done, reef_b200_stre
   return selftest_wait_timeout(1000ull * limit_us, done, S(stream));
 }
 
+size_t reef_b200_weight_tiles_bytes(size_t rows, size_t in) {
+  if (rows == 0 || in == 0 || rows > (1u << 31) - 1 || in > (1u << 31) - 1) return 0;
+  return weight_tiles_bytes(static_cast<long long>(rows), static_cast<long long>(in));
+}
+
+int reef_b200_pack_weight_tiles(size_t rows, size_t in, const int8_t* w, int8_t* tiles,
+                                reef_b200_stream_t stream) {
+  if (rows == 0) return REEF_B200_OK;
+  if (in == 0 || rows > (1u << 31) - 1 || in > (1u << 31) - 1 || !w || !tiles)
+    return REEF_B200_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(tiles) % 1024 != 0) return REEF_B200_ERR_ALIGNMENT;
+  if (int rc = check_device()) return rc;
+  return pack_weight_tiles(static_cast<long long>(rows), static_cast<long long>(in), w,
+                           static_cast<long long>(kpad(in)), tiles, S(stream));
+}
+
 int reef_b200_selftest_peer_wait_timeout(unsigned limit_us, const unsigned* counter,
                                          unsigned target, reef_b200_stream_t stream) {
   if (counter == nullptr || limit_us == 0 || limit_us > 2000000u) return REEF_B200_ERR_INVALID;
@@ -536,6 +552,9 @@ int reef_b200_decode_attn_i8(size_t batch, size_t heads_q, size_t heads_kv, size
   p.len = static_cast<int>(len);
   p.partial = static_cast<float*>(workspace);
   p.out = out;
+  // a programmatic dependent of the kernel before it: the launch and set-up
+  // overlap that kernel, and nothing is read before it has finished
+  PdlScope pdl;
   return decode_attn_i8(p, S(stream));
 }
 

@@ -661,15 +661,35 @@ __global__ void decode_rope_append_kernel(int batch, int hq, int hkv, int max_le
   if (hh == 0 && lane == 0) lens[b] = pos + 1;
   float v[4];
   if constexpr (kPartials) {
-    const long long row = static_cast<long long>(b) * heads * 128;
     const long long stride = static_cast<long long>(batch) * heads * 128;
+    const int32_t* base = part + static_cast<long long>(b) * heads * 128 + hh * 128 + lane;
     const float rs = xs[b];
+    // the splits' sums, eight splits' loads in flight at a time (the
+    // partials sit in L2: the loads' latency, not bandwidth, sets the pace)
+    int32_t acc[4] = {0, 0, 0, 0};
+    int sp = 0;
+    for (; sp + 8 <= splits; sp += 8) {
+      int32_t t[8][4];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int32_t* ps = base + (sp + u) * stride;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) t[u][p] = ps[32 * p];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) acc[p] += t[u][p];
+    }
+    for (; sp < splits; ++sp) {
+      const int32_t* ps = base + sp * stride;
+#pragma unroll
+      for (int p = 0; p < 4; ++p) acc[p] += ps[32 * p];
+    }
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const int n = hh * 128 + lane + 32 * p;
-      int32_t acc = part[row + n];
-      for (int sp = 1; sp < splits; ++sp) acc += part[sp * stride + row + n];
-      v[p] = __fmul_rn(__int2float_rn(acc), __fmul_rn(rs, ws[n]));
+      v[p] = __fmul_rn(__int2float_rn(acc[p]), __fmul_rn(rs, ws[n]));
     }
   } else {
     const float* x = qkv + static_cast<long long>(b) * heads * 128 + hh * 128;
@@ -736,8 +756,9 @@ int decode_rope_append_partials(int batch, int heads_q, int heads_kv, int max_le
   if (part == nullptr || splits < 1 || x_scale == nullptr || w_scale == nullptr)
     return kErrInvalid;
   const long long warps = static_cast<long long>(batch) * (heads_q + 2 * heads_kv);
+  // two warps per block, so the (sequence, head) rows spread over every SM
   return launch_k(decode_rope_append_kernel<true>,
-                  dim3(static_cast<unsigned>((warps * 32 + 255) / 256)), dim3(256), 0, stream,
+                  dim3(static_cast<unsigned>((warps * 32 + 63) / 64)), dim3(64), 0, stream,
                   batch, heads_q, heads_kv, max_len, rope_base, positions,
                   static_cast<const float*>(nullptr), part, splits, x_scale, w_scale, q8, q_scale,
                   k_cache, k_scale, v_cache, v_scale, lens, device_error_ptr());

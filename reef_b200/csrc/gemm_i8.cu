@@ -175,7 +175,12 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
         for (int i = 0; i < pre; ++i) {
           const int kb = kb0 + i, seg = kb / kbs, kx = (kb - seg * kbs) * kBK;
           mbar_arrive_expect_tx(&full[i], L::kStageBytes);
-          tma_load_3d(smem + i * L::kStageBytes, &tma_a, &full[i], kx, mb * kBM, seg);
+          if (args.a_tiles != nullptr)
+            bulk_load(smem + i * L::kStageBytes,
+                      args.a_tiles + (static_cast<long long>(mb) * kbs + kb) * L::kABytes,
+                      L::kABytes, &full[i]);
+          else
+            tma_load_3d(smem + i * L::kStageBytes, &tma_a, &full[i], kx, mb * kBM, seg);
         }
       }
       pdl_wait();
@@ -198,7 +203,11 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
           const int seg = kb / kbs, kx = (kb - seg * kbs) * kBK;
           if (!prefetched) {
             mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-            tma_load_3d(sa, &tma_a, &full[stage], kx, mb * kBM, seg);
+            if (args.a_tiles != nullptr)
+              bulk_load(sa, args.a_tiles + (static_cast<long long>(mb) * kbs + kb) * L::kABytes,
+                        L::kABytes, &full[stage]);
+            else
+              tma_load_3d(sa, &tma_a, &full[stage], kx, mb * kBM, seg);
           }
           if constexpr (EPI == kEpiSwiGLU) {
             tma_load_3d(sb, &tma_b, &full[stage], kx, nb * kOut, seg);
@@ -855,9 +864,11 @@ size_t skinny_partial_bytes(int m, int n, int k) {
 int skinny_split_count(int m, int n, int k) { return skinny_splits(m, n, k); }
 
 int gemm_i8_skinny_partials(int m, int n, int k, const int8_t* x, const int8_t* w,
-                            int32_t* part, cudaStream_t stream) {
+                            int32_t* part, cudaStream_t stream, const int8_t* w_tiles) {
   if (m <= 0 || n <= 0 || k <= 0 || m > 128 || part == nullptr || x == nullptr || w == nullptr)
     return kErrInvalid;
+  if (w_tiles != nullptr && (reinterpret_cast<uintptr_t>(w_tiles) & 1023u) != 0)
+    return kErrAlignment;  // the swizzle pattern repeats every 1024 bytes
   const int splits = skinny_splits(m, n, k);
   GemmProblem p{};
   p.M = n;  // weight rows on the MMA's M side (swap-AB)
@@ -872,7 +883,50 @@ int gemm_i8_skinny_partials(int m, int n, int k, const int8_t* x, const int8_t* 
   p.args.y = part;
   p.args.ldy = n;
   p.args.a_first = 1;  // the weights: no earlier kernel writes them
+  p.args.a_tiles = w_tiles;
   return m <= 64 ? launch<64, 8, kEpiI32T>(p, stream) : launch<128, 6, kEpiI32T>(p, stream);
+}
+
+namespace {
+// One thread per 16-byte chunk of the tiled layout (see ops.h).
+__global__ void pack_weight_tiles_kernel(long long rows, long long in, const int8_t* __restrict__ w,
+                                         long long ldw, int kb_count, long long chunks,
+                                         uint4* __restrict__ tiles) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= chunks) return;
+  const long long tile = i >> 10;        // 1024 chunks of 16 bytes per tile
+  const int r = static_cast<int>((i >> 3) & 127), cp = static_cast<int>(i & 7);
+  const int c = cp ^ (r & 7);            // the logical chunk stored at this position
+  const long long rb = tile / kb_count, kb = tile - rb * kb_count;
+  const long long row = rb * kBM + r, col = kb * kBK + c * 16;
+  uint8_t b[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    b[j] = (row < rows && col + j < in) ? static_cast<uint8_t>(w[row * ldw + col + j]) : 0;
+  uint4 v;
+  v.x = b[0] | (b[1] << 8) | (b[2] << 16) | (static_cast<uint32_t>(b[3]) << 24);
+  v.y = b[4] | (b[5] << 8) | (b[6] << 16) | (static_cast<uint32_t>(b[7]) << 24);
+  v.z = b[8] | (b[9] << 8) | (b[10] << 16) | (static_cast<uint32_t>(b[11]) << 24);
+  v.w = b[12] | (b[13] << 8) | (b[14] << 16) | (static_cast<uint32_t>(b[15]) << 24);
+  tiles[i] = v;
+}
+}  // namespace
+
+size_t weight_tiles_bytes(long long rows, long long in) {
+  if (rows <= 0 || in <= 0) return 0;
+  const long long rbs = (rows + kBM - 1) / kBM, kbs = (in + kBK - 1) / kBK;
+  return static_cast<size_t>(rbs * kbs) * kBM * kBK;
+}
+
+int pack_weight_tiles(long long rows, long long in, const int8_t* w, long long ldw, int8_t* tiles,
+                      cudaStream_t stream) {
+  if (rows <= 0 || in <= 0 || ldw < in || w == nullptr || tiles == nullptr) return kErrInvalid;
+  if ((reinterpret_cast<uintptr_t>(tiles) & 1023u) != 0) return kErrAlignment;
+  const int kbs = static_cast<int>((in + kBK - 1) / kBK);
+  const long long chunks = static_cast<long long>(weight_tiles_bytes(rows, in) / 16);
+  pack_weight_tiles_kernel<<<static_cast<unsigned>((chunks + 255) / 256), 256, 0, stream>>>(
+      rows, in, w, ldw, kbs, chunks, reinterpret_cast<uint4*>(tiles));
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int skinny_reduce(int m, int n, int splits, const int32_t* part, int epilogue,
@@ -900,12 +954,13 @@ int skinny_reduce(int m, int n, int splits, const int32_t* part, int epilogue,
 
 int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int epilogue,
                    const float* x_scale, const float* w_scale, const float* bias,
-                   const float* residual, void* y, void* partial, cudaStream_t stream) {
+                   const float* residual, void* y, void* partial, cudaStream_t stream,
+                   const int8_t* w_tiles) {
   if (m <= 0 || n <= 0 || k <= 0 || m > 128 || partial == nullptr || y == nullptr)
     return kErrInvalid;
   if (epilogue != kEpiF32W8A8 && epilogue != kEpiI32) return kErrInvalid;
   int32_t* part = static_cast<int32_t*>(partial);
-  if (int rc = gemm_i8_skinny_partials(m, n, k, x, w, part, stream)) return rc;
+  if (int rc = gemm_i8_skinny_partials(m, n, k, x, w, part, stream, w_tiles)) return rc;
   // the reduce launches as a programmatic dependent of the GEMM, so its launch
   // overlaps the GEMM's tail
   PdlScope pdl;

@@ -152,17 +152,18 @@ int rowpar_linear(Comm* c, long long rows, int in_local, int out, Quant quant, A
 template <typename Quant, typename AbsMax>
 int rowpar_skinny(Comm* c, int rows, int in_local, int out, Quant quant, AbsMax absmax,
                   const int8_t* w, const float* ws, const float* residual, int8_t* xq, float* xs,
-                  float* row_max, int32_t* acc, void* partial, float* y, cudaStream_t st) {
+                  float* row_max, int32_t* acc, void* partial, float* y, cudaStream_t st,
+                  const int8_t* w_tiles = nullptr) {
   if (comm_world(c) == 1) {
     REEF_TRY(quant(static_cast<const float*>(nullptr)));
     return gemm_i8_skinny(rows, out, in_local, xq, w, kEpiF32W8A8, xs, ws, nullptr, residual, y,
-                          partial, st);
+                          partial, st, w_tiles);
   }
   REEF_TRY(absmax(row_max));
   REEF_TRY(allreduce_max_f32(c, row_max, static_cast<size_t>(rows), st));
   REEF_TRY(quant(static_cast<const float*>(row_max)));
   REEF_TRY(gemm_i8_skinny(rows, out, in_local, xq, w, kEpiI32, nullptr, nullptr, nullptr, nullptr,
-                          acc, partial, st));
+                          acc, partial, st, w_tiles));
   REEF_TRY(allreduce_sum_i32(c, acc, static_cast<size_t>(rows) * out, st));
   return w8a8_epilogue_i32(rows, out, acc, xs, ws, nullptr, residual, y, st);
 }
@@ -323,7 +324,7 @@ int llama_check(const reef_b200_llama_layer* L) {
 struct DecodeBufs {
   int8_t* xq;
   float* xs;
-  float* xs2;  // the down projection's input scales (xs holds gate/up's while they are read)
+  float* xs2;  // the gate/up projection's input scales (xs holds the o-proj's or the down's)
   float* row_max;
   float* big;
   int8_t* q8;
@@ -377,6 +378,8 @@ int decode_check(const reef_b200_llama_layer* L, size_t max_len) {
       !L->w_gu || !L->s_gu || !L->w_down || !L->s_down)
     return REEF_B200_ERR_INVALID;
   if (L->hidden % 32 != 0) return REEF_B200_ERR_INVALID;  // 8 RMSNorm chunks of float4
+  for (const int8_t* t : {L->t_qkv, L->t_o, L->t_gu, L->t_down})
+    if (reinterpret_cast<uintptr_t>(t) % 1024 != 0) return REEF_B200_ERR_INVALID;
   if (L->comm != nullptr && L->tp_mode != REEF_B200_TP_ALLREDUCE &&
       L->tp_mode != REEF_B200_TP_ALLGATHER)
     return REEF_B200_ERR_INVALID;
@@ -459,8 +462,7 @@ int neo_forward(const reef_b200_gptneo_block* B, const float* x, float* y, const
   // Attention::forward (attention.hpp:354-372): ln_1, q/k/v projections
   // (column-parallel by heads), every local head, o_proj (row-parallel) with
   // the residual of Block::forward (block.hpp:99-102) fused in.
-  REEF_TRY(layernorm_exact(T, d, B->eps, x, B->ln1_g, B->ln1_b, b.h, st));
-  REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
+  REEF_TRY(layernorm_exact_quant(T, d, B->eps, x, B->ln1_g, B->ln1_b, b.xq, ld, b.xs, st));
   REEF_TRY(gemm_w8a8_f32(T, d, dl, b.xq, b.xs, B->wq, B->sq, nullptr, nullptr, b.q, st));
   // with a cache the key and value rows go straight into it
   const size_t past = kv != nullptr ? kv->position : 0;
@@ -489,8 +491,7 @@ int neo_forward(const reef_b200_gptneo_block* B, const float* x, float* y, const
   }
   // MLP::forward (mlp.hpp:108-133): ln_2, c_fc (column-parallel) with gelu
   // in its epilogue, c_proj (row-parallel) with the second residual fused in.
-  REEF_TRY(layernorm_exact(T, d, B->eps, b.a, B->ln2_g, B->ln2_b, b.h, st));
-  REEF_TRY(quantize_rows(T, d, b.h, b.xq, ld, b.xs, nullptr, st));
+  REEF_TRY(layernorm_exact_quant(T, d, B->eps, b.a, B->ln2_g, B->ln2_b, b.xq, ld, b.xs, st));
   REEF_TRY(gemm_w8a8_f32(T, d, F, b.xq, b.xs, B->wfc, B->sfc, B->bfc, nullptr, b.f, st,
                          /*gelu=*/true));
   {
@@ -1236,7 +1237,7 @@ int reef_b200_llama_decode_forward(const reef_b200_llama_layer* L, const float* 
   PdlScope pdl;
   REEF_TRY(rmsnorm_quant(B, H, L->rms_eps, x, L->attn_norm, b.xq, b.xs, st));
   const int s_qkv = skinny_split_count(B, qkv_w, H);
-  REEF_TRY(gemm_i8_skinny_partials(B, qkv_w, H, b.xq, L->w_qkv, part, st));
+  REEF_TRY(gemm_i8_skinny_partials(B, qkv_w, H, b.xq, L->w_qkv, part, st, L->t_qkv));
   REEF_TRY(decode_rope_append_partials(B, hq, hkv, static_cast<int>(max_len), L->rope_base,
                                        positions, part, s_qkv, b.xs, L->s_qkv, b.q8, b.qs,
                                        k_cache, k_scale, v_cache, v_scale, b.lens, st));
@@ -1257,27 +1258,38 @@ int reef_b200_llama_decode_forward(const reef_b200_llama_layer* L, const float* 
   dp.partial = b.dpart;
   dp.out = b.attn;
   REEF_TRY(decode_attn_i8(dp, st));
-  {
+  // o-proj with the residual, then the MLP's pre-norm: without a peer to
+  // reduce with, the o-proj's split-K sum, the residual and RMSNorm + quant
+  // run as one kernel; the gate/up input scales go to xs2
+  const int kq = static_cast<int>(hq * D);
+  if (comm_world(c) == 1) {
+    REEF_TRY(quantize_rows(B, kq, b.attn, b.xq, static_cast<long long>(kpad(kq)), b.xs, nullptr,
+                           st));
+    REEF_TRY(gemm_i8_skinny_partials(B, H, kq, b.xq, L->w_o, part, st, L->t_o));
+    REEF_TRY(reduce_rmsnorm_quant(B, H, skinny_split_count(B, H, kq), part, b.xs, L->s_o, x, b.h,
+                                  L->rms_eps, L->mlp_norm, b.xq, b.xs2, st));
+  } else {
     auto quant = [&](const float* rm) {
-      return quantize_rows(B, hq * D, b.attn, b.xq, static_cast<long long>(kpad(hq * D)), b.xs,
-                           rm, st);
+      return quantize_rows(B, kq, b.attn, b.xq, static_cast<long long>(kpad(kq)), b.xs, rm, st);
     };
-    auto absmax = [&](float* rm) { return row_absmax(B, hq * D, b.attn, rm, st); };
-    REEF_TRY(rowpar_skinny(c, B, hq * D, H, quant, absmax, L->w_o, L->s_o, x, b.xq, b.xs,
-                           b.row_max, b.acc, b.partial, b.h, st));
+    auto absmax = [&](float* rm) { return row_absmax(B, kq, b.attn, rm, st); };
+    REEF_TRY(rowpar_skinny(c, B, kq, H, quant, absmax, L->w_o, L->s_o, x, b.xq, b.xs, b.row_max,
+                           b.acc, b.partial, b.h, st, L->t_o));
+    REEF_TRY(rmsnorm_quant(B, H, L->rms_eps, b.h, L->mlp_norm, b.xq, b.xs2, st));
   }
-  REEF_TRY(rmsnorm_quant(B, H, L->rms_eps, b.h, L->mlp_norm, b.xq, b.xs, st));
   const int s_gu = skinny_split_count(B, 2 * F, H);
-  REEF_TRY(gemm_i8_skinny_partials(B, 2 * F, H, b.xq, L->w_gu, part, st));
+  REEF_TRY(gemm_i8_skinny_partials(B, 2 * F, H, b.xq, L->w_gu, part, st, L->t_gu));
   {
+    // the down projection's input scales go back to xs (gate/up's are read
+    // from xs2 meanwhile)
     auto quant = [&](const float* rm) {
-      return swiglu_partials(B, F, part, s_gu, b.xs, L->s_gu, rm, nullptr, b.xq, b.xs2, st);
+      return swiglu_partials(B, F, part, s_gu, b.xs2, L->s_gu, rm, nullptr, b.xq, b.xs, st);
     };
     auto absmax = [&](float* rm) {
-      return swiglu_partials(B, F, part, s_gu, b.xs, L->s_gu, nullptr, rm, nullptr, nullptr, st);
+      return swiglu_partials(B, F, part, s_gu, b.xs2, L->s_gu, nullptr, rm, nullptr, nullptr, st);
     };
-    REEF_TRY(rowpar_skinny(c, B, F, H, quant, absmax, L->w_down, L->s_down, b.h, b.xq, b.xs2,
-                           b.row_max, b.acc, b.partial, y, st));
+    REEF_TRY(rowpar_skinny(c, B, F, H, quant, absmax, L->w_down, L->s_down, b.h, b.xq, b.xs,
+                           b.row_max, b.acc, b.partial, y, st, L->t_down));
   }
   return REEF_B200_OK;
 }

@@ -124,10 +124,9 @@ __device__ __forceinline__ float warp_max(float v) {
 // runs each of those warps' xor-shuffle trees (an xor butterfly leaves the
 // same sum in every lane) and adds ((w0 + w1) + w2) + w3.  v (when given)
 // keeps x * gain, m the max of |x * gain|.
-template <int P, bool kKeep>
-__device__ __forceinline__ float chunk_sum(const float4* __restrict__ xr,
-                                           const float4* __restrict__ gr, int n4, int l,
-                                           float4 (&v)[4][P], float& m) {
+template <int P, bool kKeep, typename Load>
+__device__ __forceinline__ float chunk_sum_of(Load load, const float4* __restrict__ gr, int n4,
+                                              int l, float4 (&v)[4][P], float& m) {
   float ws[4];
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
@@ -136,7 +135,7 @@ __device__ __forceinline__ float chunk_sum(const float4* __restrict__ xr,
     for (int k = 0; k < P; ++k) {
       const int idx = l + 32 * w + kChunkThreads * k;
       if (idx < n4) {
-        const float4 x4 = __ldg(xr + idx);
+        const float4 x4 = load(w, k, idx);
         s = s + sumsq4(x4);
         const float4 y4 = mul4(x4, __ldg(gr + idx));
         m = fmaxf(m, amax4(y4));
@@ -146,6 +145,14 @@ __device__ __forceinline__ float chunk_sum(const float4* __restrict__ xr,
     ws[w] = warp_sum_tree(s);
   }
   return ((ws[0] + ws[1]) + ws[2]) + ws[3];
+}
+
+template <int P, bool kKeep>
+__device__ __forceinline__ float chunk_sum(const float4* __restrict__ xr,
+                                           const float4* __restrict__ gr, int n4, int l,
+                                           float4 (&v)[4][P], float& m) {
+  return chunk_sum_of<P, kKeep>([&](int, int, int idx) { return __ldg(xr + idx); }, gr, n4, l, v,
+                                m);
 }
 
 // TP=1: one CTA of 8 warps per row, warp c the chunk c; P float4 per lane
@@ -181,6 +188,109 @@ __global__ void __launch_bounds__(kChunks * 32)
   const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
   if (threadIdx.x == 0) xs[row] = scale;
   char4* out = reinterpret_cast<char4*>(xq + row * ldq) + c * n4;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const int idx = l + 32 * w + kChunkThreads * k;
+      if (idx < n4) out[idx] = q8x4(scale4(v[w][k], r), scale);
+    }
+  }
+}
+
+// The decode step's o-proj output and the MLP's pre-norm in one pass, one
+// CTA of 8 warps per token row: h = residual + float(sum of the split-K
+// partials) * (x_scale * w_scale) (the skinny reduce's W8A8 epilogue,
+// linear.hpp:125-127, then the residual add), written to h_out (the MLP's
+// residual), and rmsnorm_quant_kernel's exact steps on it (the same thread
+// layout and summation order), so x_q / xs_out hold the bits rmsnorm_quant
+// would give on h.  part: [splits][rows][width] int32, token-major.
+template <int P>
+__global__ void __launch_bounds__(kChunks * 32)
+    reduce_rmsnorm_quant_kernel(int width, int splits, const int32_t* __restrict__ part,
+                                const float* __restrict__ xs_in, const float* __restrict__ ws,
+                                const float* __restrict__ residual, float* __restrict__ h_out,
+                                float eps, const float* __restrict__ gain,
+                                int8_t* __restrict__ xq, float* __restrict__ xs_out) {
+  __shared__ float csum[kChunks];
+  __shared__ float cmax[kChunks];
+  pdl_wait();
+  pdl_trigger();
+  const long long row = blockIdx.x;
+  const int c = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int n4 = width / (4 * kChunks);  // float4 per chunk
+  const long long total = static_cast<long long>(gridDim.x) * width;
+  const long long base = row * width + static_cast<long long>(c) * n4 * 4;  // elements
+  const float rs = xs_in[row];
+  const float4* ws4 = reinterpret_cast<const float4*>(ws) + c * n4;
+  const float4* res4 = reinterpret_cast<const float4*>(residual + base);
+  float4* h4 = reinterpret_cast<float4*>(h_out + base);
+  // every load first (the partials, scales and residual of this thread's
+  // float4s), then h and its stores: nothing the stores touch is read after
+  float4 hv[4][P];
+  int4 acc[4][P];
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const int idx = l + 32 * w + kChunkThreads * k;
+      acc[w][k] = idx < n4 ? *reinterpret_cast<const int4*>(part + base + 4ll * idx)
+                           : make_int4(0, 0, 0, 0);
+    }
+  for (int sp = 1; sp < splits; ++sp)
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+#pragma unroll
+      for (int k = 0; k < P; ++k) {
+        const int idx = l + 32 * w + kChunkThreads * k;
+        if (idx < n4) {
+          const int4 b = *reinterpret_cast<const int4*>(part + sp * total + base + 4ll * idx);
+          acc[w][k].x += b.x;
+          acc[w][k].y += b.y;
+          acc[w][k].z += b.z;
+          acc[w][k].w += b.w;
+        }
+      }
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const int idx = l + 32 * w + kChunkThreads * k;
+      if (idx < n4) {
+        const float4 wv = ws4[idx], r = res4[idx];
+        const int4 a = acc[w][k];
+        hv[w][k] = make_float4(__fadd_rn(r.x, __fmul_rn(__int2float_rn(a.x), __fmul_rn(rs, wv.x))),
+                               __fadd_rn(r.y, __fmul_rn(__int2float_rn(a.y), __fmul_rn(rs, wv.y))),
+                               __fadd_rn(r.z, __fmul_rn(__int2float_rn(a.z), __fmul_rn(rs, wv.z))),
+                               __fadd_rn(r.w, __fmul_rn(__int2float_rn(a.w), __fmul_rn(rs, wv.w))));
+      }
+    }
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const int idx = l + 32 * w + kChunkThreads * k;
+      if (idx < n4) h4[idx] = hv[w][k];
+    }
+  const float4* gr = reinterpret_cast<const float4*>(gain) + c * n4;
+  float4 v[4][P];
+  float m = 0.0f;
+  const float cs = chunk_sum_of<P, true>([&](int w, int k, int) { return hv[w][k]; }, gr, n4, l,
+                                         v, m);
+  m = warp_max(m);
+  if (l == 0) {
+    csum[c] = cs;
+    cmax[c] = m;
+  }
+  __syncthreads();
+  const float r = 1.0f / sqrtf(chunk_tree(csum) / static_cast<float>(width) + eps);
+  float mm = cmax[0];
+#pragma unroll
+  for (int j = 1; j < kChunks; ++j) mm = fmaxf(mm, cmax[j]);
+  const float mx = mm * r;
+  const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  if (threadIdx.x == 0) xs_out[row] = scale;
+  char4* out = reinterpret_cast<char4*>(xq + row * static_cast<long long>(width)) + c * n4;
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
 #pragma unroll
@@ -410,6 +520,26 @@ int rmsnorm_quant(long long rows, int width, float eps, const float* x, const fl
   if (P <= 1) return launch_k(rmsnorm_quant_kernel<1>, dim3(grid), T, 0, stream, width, eps, x, gain, x_q, ld, x_scale);
   if (P <= 2) return launch_k(rmsnorm_quant_kernel<2>, dim3(grid), T, 0, stream, width, eps, x, gain, x_q, ld, x_scale);
   if (P <= 4) return launch_k(rmsnorm_quant_kernel<4>, dim3(grid), T, 0, stream, width, eps, x, gain, x_q, ld, x_scale);
+  return kErrInvalid;
+}
+
+int reduce_rmsnorm_quant(long long rows, int width, int splits, const int32_t* part,
+                         const float* x_scale, const float* w_scale, const float* residual,
+                         float* h, float eps, const float* gain, int8_t* x_q, float* q_scale,
+                         cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  if (width <= 0 || width % (4 * kChunks) != 0 || splits < 1 || !part || !x_scale || !w_scale ||
+      !residual || !h || !gain || !x_q || !q_scale)
+    return kErrInvalid;
+  if ((reinterpret_cast<uintptr_t>(part) | reinterpret_cast<uintptr_t>(w_scale) |
+       reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(h) |
+       reinterpret_cast<uintptr_t>(gain)) & 15u)
+    return kErrAlignment;
+  const dim3 grid(static_cast<unsigned>(rows)), T(kChunks * 32);
+  const int P = per_thread(width);
+  if (P <= 1) return launch_k(reduce_rmsnorm_quant_kernel<1>, grid, T, 0, stream, width, splits, part, x_scale, w_scale, residual, h, eps, gain, x_q, q_scale);
+  if (P <= 2) return launch_k(reduce_rmsnorm_quant_kernel<2>, grid, T, 0, stream, width, splits, part, x_scale, w_scale, residual, h, eps, gain, x_q, q_scale);
+  if (P <= 4) return launch_k(reduce_rmsnorm_quant_kernel<4>, grid, T, 0, stream, width, splits, part, x_scale, w_scale, residual, h, eps, gain, x_q, q_scale);
   return kErrInvalid;
 }
 

@@ -115,6 +115,10 @@ struct GemmArgs {
   // A depends on no earlier kernel (the weights of a swap-AB GEMM): its first
   // stages are requested before the kernel waits for its predecessor
   int a_first;
+  // A in the tiled layout of pack_weight_tiles (one contiguous, pre-swizzled
+  // 16 KiB block per 128-row x 128-byte stage, read by one bulk copy) instead
+  // of through the tensor map; one K segment only
+  const int8_t* a_tiles;
   int* err;               // device error word (set by the launcher)
 };
 
@@ -171,15 +175,27 @@ int linear_w8a8_qkv_rope(long long rows, int in, const int8_t* xq, const float* 
 size_t skinny_partial_bytes(int m, int n, int k);
 int gemm_i8_skinny(int m, int n, int k, const int8_t* x, const int8_t* w, int epilogue,
                    const float* x_scale, const float* w_scale, const float* bias,
-                   const float* residual, void* y, void* partial, cudaStream_t stream);
+                   const float* residual, void* y, void* partial, cudaStream_t stream,
+                   const int8_t* w_tiles = nullptr);
 // The two halves of gemm_i8_skinny, for consumers that fold the split-K sum
 // into their own pass: the GEMM writes skinny_split_count(m, n, k) int32
 // partials part[s][m][n] (token-major, m * n apart); skinny_reduce sums them
 // and applies the epilogue (kEpiF32W8A8: dequant [+ bias] [+ residual] ->
 // fp32 y; kEpiI32: the int32 sums), y [m][n].
 int skinny_split_count(int m, int n, int k);
+// w_tiles (optional): the same weights in pack_weight_tiles' layout, streamed
+// as contiguous 16 KiB blocks instead of 128-byte row pieces
 int gemm_i8_skinny_partials(int m, int n, int k, const int8_t* x, const int8_t* w,
-                            int32_t* part, cudaStream_t stream);
+                            int32_t* part, cudaStream_t stream, const int8_t* w_tiles = nullptr);
+// The decode layout of a K-major int8 weight w [rows][ldw]: 16 KiB tiles of
+// 128 rows x 128 bytes of K, each stored as the tensor cores read it
+// (128-byte swizzle: 16-byte chunk c of tile row r at r * 128 + ((c ^ (r & 7))
+// * 16)), the tiles of one 128-row block consecutive along K: tile (rb, kb)
+// at ((rb * KB + kb) * 16384), KB = ceil(in / 128).  Bytes past the matrix
+// are zero.
+size_t weight_tiles_bytes(long long rows, long long in);
+int pack_weight_tiles(long long rows, long long in, const int8_t* w, long long ldw,
+                      int8_t* tiles, cudaStream_t stream);
 int skinny_reduce(int m, int n, int splits, const int32_t* part, int epilogue,
                   const float* x_scale, const float* w_scale, const float* bias,
                   const float* residual, void* y, cudaStream_t stream);
@@ -244,6 +260,11 @@ int argmax_f32(long long n, const float* x, uint32_t* index, cudaStream_t stream
 // gptneo.cu -- reef's float layernorm, bit for bit (one row per CTA)
 int layernorm_exact(long long rows, int width, float eps, const float* x, const float* gain,
                     const float* shift, float* y, cudaStream_t stream);
+// layernorm_exact then quantize_rows (quant.hpp:112-133) in one pass: x_q
+// [rows][ldq] int8 (padding zeroed) and x_scale [rows], the same bits
+int layernorm_exact_quant(long long rows, int width, float eps, const float* x, const float* gain,
+                          const float* shift, int8_t* x_q, long long ldq, float* x_scale,
+                          cudaStream_t stream);
 
 // elementwise.cu -- the rest of reef's Coral operators, bit for bit
 int linear_f32(long long rows, int in, int out, const float* x, const float* wt,
@@ -286,6 +307,13 @@ int w8a8_epilogue_i32(long long rows, long long out, const int32_t* acc,
 // llama.cu -- fused RMSNorm / SwiGLU + per-token quantisation
 int rmsnorm_quant(long long rows, int width, float eps, const float* x, const float* gain,
                   int8_t* x_q, float* x_scale, cudaStream_t stream);
+// skinny_reduce (kEpiF32W8A8 + residual) into h, then rmsnorm_quant on h, in
+// one pass (one CTA per row): the same h, x_q and scales as the two kernels.
+// part [splits][rows][width] int32; x_q [rows][width]; 16-byte alignment.
+int reduce_rmsnorm_quant(long long rows, int width, int splits, const int32_t* part,
+                         const float* x_scale, const float* w_scale, const float* residual,
+                         float* h, float eps, const float* gain, int8_t* x_q, float* q_scale,
+                         cudaStream_t stream);
 // SwiGLU of the gate/up projection's split-K partials (token-major int32
 // sums part[s][row][2 ffn], splits of them, rows * 2 ffn apart), dequantised
 // with the W8A8 epilogue: h = silu(g) * u, one CTA per row.  row_max_out set:

@@ -148,10 +148,31 @@ class LlamaLayer:
                 "v": torch.zeros(shp + (128,), dtype=torch.int8, device=dev),
                 "vs": torch.zeros(shp, device=dev), "max_len": max_len}
 
+    def _decode_tiles(self) -> None:
+        """The four projections again in the decode layout
+        (reef_b200_pack_weight_tiles), which the decode step's GEMMs stream
+        as contiguous 16 KiB blocks; built on the first decode step."""
+        lib = _lib.lib()
+        self._tiles = {}
+        for name, field in (("w_qkv", "t_qkv"), ("w_o", "t_o"), ("w_gu", "t_gu"),
+                            ("w_down", "t_down")):
+            w = getattr(self, name)
+            rows, k = w.shape
+            n = lib.reef_b200_weight_tiles_bytes(rows, k)
+            buf = torch.empty(n + 1024, dtype=torch.uint8, device=w.device)
+            off = (-buf.data_ptr()) % 1024
+            ptr = buf.data_ptr() + off
+            _lib.call("reef_b200_pack_weight_tiles", rows, k, w.data_ptr(), ptr,
+                      torch.cuda.current_stream(w.device).cuda_stream)
+            self._tiles[name] = buf
+            setattr(self.desc, field, ptr)
+
     def decode(self, x: torch.Tensor, positions: torch.Tensor, cache: dict,
                out: torch.Tensor | None = None) -> torch.Tensor:
         """One decode step: x [batch][hidden] (one new token per sequence) at
         `positions` (int32 [batch], device); appends to `cache`."""
+        if getattr(self, "_tiles", None) is None:
+            self._decode_tiles()
         max_len = cache["max_len"]
         ws = getattr(self, "_decode_ws", None)
         if ws is None or getattr(self, "_decode_len", None) != max_len:

@@ -144,3 +144,65 @@ def test_decode_config4_tp8_shard_matches_reference():
     changed[b_idx, :, pos_h] = True
     assert np.array_equal(after["ks"][~changed], before["ks"][~changed].astype(np.float32))
     assert np.array_equal(after["k"][~changed], before["k"][~changed].astype(np.int8))
+
+
+def tiles_reference(w, in_features):
+    """The decode layout of reef_b200_pack_weight_tiles, restated: 16 KiB
+    tiles of 128 rows x 128 bytes of K (rows, then k-blocks), 16-byte chunk c
+    of tile row r stored at r * 128 + ((c ^ (r % 8)) * 16), zeros past the
+    matrix."""
+    rows = w.shape[0]
+    rb, kb = -(-rows // 128), -(-in_features // 128)
+    full = np.zeros((rb * 128, kb * 128), np.int8)
+    full[:rows, :in_features] = w[:, :in_features]
+    t = full.reshape(rb, 128, kb, 8, 16).transpose(0, 2, 1, 3, 4)  # [rb][kb][r][c][16]
+    out = np.empty_like(t)
+    r = np.arange(128)[:, None]
+    c = np.arange(8)[None, :]
+    out[:, :, r, c ^ (r % 8)] = t[:, :, r, c]
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("rows,k", [(1280, 8192), (300, 200), (129, 4096)])
+def test_pack_weight_tiles_layout(rows, k):
+    from reef_b200 import _lib
+    g = torch.Generator(device="cuda").manual_seed(rows + k)
+    w = torch.randint(-127, 128, (rows, K.kpad(k)), generator=g, device="cuda", dtype=torch.int8)
+    w[:, k:] = 0
+    n = _lib.lib().reef_b200_weight_tiles_bytes(rows, k)
+    buf = torch.empty(n + 1024, dtype=torch.uint8, device="cuda")
+    off = (-buf.data_ptr()) % 1024
+    _lib.call("reef_b200_pack_weight_tiles", rows, k, w.data_ptr(), buf.data_ptr() + off,
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = buf[off:off + n].cpu().numpy().view(np.int8)
+    np.testing.assert_array_equal(got, tiles_reference(w.cpu().numpy(), k))
+
+
+def test_decode_tiled_weights_bit_identical():
+    # the decode step streaming its weights from the tiled layout gives the
+    # same bits as the same step reading the K-major weights
+    shape = RL.LlamaShape(hidden=1024, heads_q=8, heads_kv=2, ffn=2816)
+    B, Lmax = 16, 256
+    L = RL.LlamaLayer(shape, B, 8, seed=31)
+    g = torch.Generator(device="cuda").manual_seed(32)
+    x = torch.randn((B, 1024), generator=g, device="cuda")
+    pos = torch.arange(100, 100 + B, dtype=torch.int32, device="cuda")
+    base = L.alloc_cache(Lmax)
+    base["k"].random_(-127, 128, generator=g)
+    base["v"].random_(-127, 128, generator=g)
+    base["ks"].fill_(0.01)
+    base["vs"].fill_(0.01)
+    outs, caches = [], []
+    for tiled in (True, False):
+        cache = {k: (v.clone() if torch.is_tensor(v) else v) for k, v in base.items()}
+        L.decode(x, pos, cache)  # builds the tiles on the first call
+        if not tiled:
+            for f in ("t_qkv", "t_o", "t_gu", "t_down"):
+                setattr(L.desc, f, None)
+        outs.append(L.decode(x, pos, cache).cpu().numpy())
+        caches.append(cache)
+    assert L.desc.t_qkv is None  # the second pass did read the K-major weights
+    np.testing.assert_array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    for key in ("k", "ks", "v", "vs"):
+        assert torch.equal(caches[0][key], caches[1][key])
