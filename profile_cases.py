@@ -8,6 +8,8 @@ GEMM sweep.  The recipe behind the summaries in profiles/.
     python profile_cases.py decode_step [--steps 3]
     python profile_cases.py layer [--batch 8 --steps 2]
     python profile_cases.py sweep [--out sweep.json] [--tp 1]
+    torchrun --nproc-per-node N profile_cases.py tp [--chunks 1,2,4 --steps 20]
+    python profile_cases.py stream [--sizes 35,69,138,276]
 
 Each single-kernel case allocates its seeded inputs once, launches the kernel
 twice (a warm-up launch, then the one to capture: ``ncu -k regex:<name> -s 1
@@ -146,6 +148,104 @@ def layer(batch: int, steps: int) -> None:
     torch.cuda.synchronize()
 
 
+def tp_forward(chunk_list, steps: int = 20) -> None:
+    """Config 3's layer under tensor parallelism, one rank per GPU (launched
+    by torchrun): the pipelined all-gather plan at each chunk count in
+    `chunk_list` and the all-reduce plan, timed over `steps` forwards with
+    CUDA events (max over ranks), beside the host's time to issue one
+    forward.  Rank 0 prints one JSON line."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    from reef_b200 import tp
+    from reef_b200.layer import LLAMA_7B, TP_ALLGATHER, TP_ALLREDUCE, LlamaLayer
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    comm = tp.Comm(rank, world, timeout_s=60.0)
+    s, B, S = LLAMA_7B, 8, 2048
+    res = {"world": world}
+    for name, mode in (("allgather", TP_ALLGATHER), ("allreduce", TP_ALLREDUCE)):
+        L = LlamaLayer(s, B, S, seed=1, world=world, rank=rank, comm=comm, device=dev,
+                       tp_mode=mode)
+        g = torch.Generator(device=dev).manual_seed(1234)
+        x = torch.randn((B * S, s.hidden), generator=g, device=dev)
+        if mode == TP_ALLGATHER:
+            x = x[:, tp.col_slice(s.hidden, world, rank)].contiguous()
+        y = torch.empty_like(x)
+        for chunks in (chunk_list if mode == TP_ALLGATHER else (1,)):
+            os.environ["REEF_B200_TP_CHUNKS"] = str(chunks)
+            for _ in range(5):
+                L.forward(x, y)
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            h0 = time.perf_counter()
+            for _ in range(steps):
+                L.forward(x, y)
+            h1 = time.perf_counter()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            K.check_device_error()
+            t = torch.tensor([e0.elapsed_time(e1) / steps, (h1 - h0) * 1e3 / steps], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            res[f"{name}_chunks{chunks}"] = {"gpu_ms": t[0].item(), "host_issue_ms": t[1].item()}
+            dist.barrier()
+        del L
+        torch.cuda.synchronize(dev)
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def stream(sizes_mb, reps: int = 20) -> None:
+    """The practical ceiling for a read of a given working set: torch's sum
+    over an int32 view of the bytes (one read, a few bytes written), a CUDA
+    graph of calls over enough rotating copies that every call reads DRAM,
+    timed with CUDA events.  One JSON line per size."""
+    peaks = _peaks()
+    for mb in sizes_mb:
+        n = int(mb * 1e6) // 4
+        copies = max(2, -(-2 * L2_BYTES // (4 * n)))
+        bufs = [torch.randint(-1000, 1000, (n,), dtype=torch.int32, device="cuda")
+                for _ in range(copies)]
+        out = torch.empty((), dtype=torch.int64, device="cuda")
+        calls = copies * 3
+        for b in bufs:
+            torch.sum(b, dtype=torch.int64, out=out)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        with torch.cuda.stream(cap), torch.cuda.graph(graph, stream=cap):
+            for i in range(calls):
+                torch.sum(bufs[i % copies], dtype=torch.int64, out=out)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+        gbs = 4 * n / (us * 1e-6) / 1e9
+        print(json.dumps({"mb": 4 * n / 1e6, "us": us, "gbs": gbs,
+                          "frac": gbs / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                          "copies": copies}), flush=True)
+        del bufs, graph
+        torch.cuda.empty_cache()
+
+
 SWEEP_M = (1, 16, 128, 1024, 8192, 16384)
 SWEEP_NK = ((4096, 4096), (11008, 4096), (4096, 11008), (28672, 8192), (8192, 28672))
 L2_BYTES = 126 << 20
@@ -250,7 +350,9 @@ def sweep(out: str | None, tps=(1,), iters: int = 20, reps: int = 3) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "flash", "qkv", "decode", "decode_step", "layer",
-                                     "sweep"])
+                                     "sweep", "tp", "stream"])
+    ap.add_argument("--sizes", default="35,69,138,276", help="stream: working sets in MB")
+    ap.add_argument("--chunks", default="1,2,4", help="tp: chunk counts of the all-gather plan")
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=12288)
@@ -262,6 +364,12 @@ def main() -> None:
     ap.add_argument("--out", default=None)
     ap.add_argument("--tp", default="1", help="comma-separated TP degrees for the sweep")
     a = ap.parse_args()
+    if a.case == "stream":
+        stream([float(v) for v in a.sizes.split(",")])
+        return
+    if a.case == "tp":
+        tp_forward(tuple(int(c) for c in a.chunks.split(",")), max(a.steps, 5))
+        return
     if a.case == "sweep":
         sweep(a.out, tuple(int(t) for t in a.tp.split(",")))
     elif a.case == "gemm":

@@ -6,9 +6,13 @@ Every .cu / .cpp under reef_b200/csrc is compiled to reef_b200/_build/*.o with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo`` and linked into
 reef_b200/libreef_b200.so (static CUDA runtime; NCCL from the wheel torch
 ships, resolved by soname at load time).  Objects are rebuilt when their
-source or any header is newer.  No fast-math: the W8A8 epilogues and the
-exact float kernels depend on IEEE rounding, and -fmad=false keeps nvcc from
-contracting multiply-adds anywhere the source does not ask for one.
+source, any header or this file's flags are newer.  No fast-math: the W8A8
+epilogues and the exact float kernels depend on IEEE rounding.  -fmad=false
+keeps nvcc from contracting multiply-adds where a result is defined bit for
+bit: reef's operators, the RMSNorm order and the RoPE / SwiGLU values that a
+fused epilogue must reproduce.  The two attention kernels whose results are
+checked within a tolerance (the flash and decode heads, FMA_FREE_EXEMPT)
+keep nvcc's contraction.
 """
 from __future__ import annotations
 
@@ -29,7 +33,10 @@ NVCC = os.path.join(CUDA, "bin", "nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
-          "-fmad=false", f"-I{os.path.join(ROOT, 'include')}", f"-I{CSRC}"]
+          f"-I{os.path.join(ROOT, 'include')}", f"-I{CSRC}"]
+# translation units whose float results are checked within a tolerance, not
+# bit for bit: nvcc may contract their multiply-adds
+FMA_FREE_EXEMPT = {"flash_attn.cu", "decode_attn.cu"}
 
 
 def _nccl_dirs():
@@ -47,7 +54,7 @@ def _nccl_dirs():
 
 def _headers():
     return glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
-        glob.glob(os.path.join(ROOT, "include", "*.h"))
+        glob.glob(os.path.join(ROOT, "include", "*.h")) + [os.path.abspath(__file__)]
 
 
 def _stale(src: str, obj: str, newest_header: float) -> bool:
@@ -58,7 +65,8 @@ def _stale(src: str, obj: str, newest_header: float) -> bool:
 
 
 def _compile(src: str, obj: str, nccl_inc: str, verbose: bool) -> str:
-    cmd = [NVCC, *ARCH, *COMMON, f"-I{nccl_inc}", "-c", src, "-o", obj]
+    fmad = [] if os.path.basename(src) in FMA_FREE_EXEMPT else ["-fmad=false"]
+    cmd = [NVCC, *ARCH, *COMMON, *fmad, f"-I{nccl_inc}", "-c", src, "-o", obj]
     if src.endswith(".cpp"):
         cmd.insert(1, "-x")
         cmd.insert(2, "cu")

@@ -699,12 +699,17 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
 
 // M-blocks per raster group when the caller leaves it open.  A group walks
 // all n-blocks together, so B is streamed from DRAM once per group while
-// the group's A rows stay in L2: the largest power of two from 8 to 64 whose
-// A rows (group x 128 x K bytes) fit in 32 MiB.  Measured on config 3 under
-// the power cap: group 8 -> 64 takes the gate/up GEMM (B 90 MB) from 1.09 to
-// 1.00 ms, while the down GEMM (K 11008) is best at 16.
+// the group's A rows stay in L2.
+// * B small enough to stay in L2 beside the streaming A and outputs (at most
+//   44 MiB: config 3's o-proj and down weights): group 1, every n-block of
+//   one m-block before the next, so B is read from DRAM once and A once (the
+//   down projection read B eight times over with group 16).
+// * Else the largest power of two from 8 to 64 whose A rows (group x 128 x K
+//   bytes) fit in 32 MiB: B is read M / (128 group) times.  Measured on
+//   config 3 under the power cap: group 8 -> 64 takes the gate/up GEMM (B
+//   90 MB) from 1.09 to 1.00 ms.
 // REEF_B200_GEMM_GROUP fixes it instead.
-int default_group_m(int K) {
+int default_group_m(long long K, long long b_bytes) {
   static int fixed = -1;
   if (fixed < 0) {
     int x = 0;
@@ -715,6 +720,7 @@ int default_group_m(int K) {
     fixed = x;
   }
   if (fixed > 0) return fixed;
+  if (b_bytes <= (44ll << 20)) return 1;
   int g = 64;
   while (g > 8 && static_cast<long long>(g) * kBM * K > (32ll << 20)) g /= 2;
   return g;
@@ -753,7 +759,11 @@ int launch(const GemmProblem& p, cudaStream_t stream) {
   args.N = p.N;
   args.K = p.K;
   // A's K spans every segment of an all-gathered operand
-  if (args.group_m <= 0) args.group_m = default_group_m(p.K * std::max(1, p.args.k_segments));
+  if (args.group_m <= 0) {
+    const long long k_all = static_cast<long long>(p.K) * std::max(1, p.args.k_segments);
+    const long long b_rows = EPI == kEpiSwiGLU ? p.args.b_up + p.N : p.N;
+    args.group_m = default_group_m(k_all, b_rows * k_all);
+  }
   args.err = device_error_ptr();
   // gelu is an option of the fp32 epilogue of whole (unsplit) outputs only
   if (args.gelu && (EPI != kEpiF32W8A8 || splits > 1)) return kErrInvalid;

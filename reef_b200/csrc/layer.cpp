@@ -1257,14 +1257,22 @@ int reef_b200_llama_decode_forward(const reef_b200_llama_layer* L, const float* 
   dp.positions = positions;
   dp.partial = b.dpart;
   dp.out = b.attn;
-  REEF_TRY(decode_attn_i8(dp, st));
   // o-proj with the residual, then the MLP's pre-norm: without a peer to
-  // reduce with, the o-proj's split-K sum, the residual and RMSNorm + quant
+  // share the rows with, the attention's merge quantises the o-proj input
+  // itself, and the o-proj's split-K sum, the residual and RMSNorm + quant
   // run as one kernel; the gate/up input scales go to xs2
   const int kq = static_cast<int>(hq * D);
-  if (comm_world(c) == 1) {
-    REEF_TRY(quantize_rows(B, kq, b.attn, b.xq, static_cast<long long>(kpad(kq)), b.xs, nullptr,
-                           st));
+  const bool local = comm_world(c) == 1;
+  const bool merge_quant = local && hq <= 96;  // the merge holds a row of heads in shared memory
+  if (merge_quant) {
+    dp.out_q = b.xq;
+    dp.out_q_scale = b.xs;
+  }
+  REEF_TRY(decode_attn_i8(dp, st));
+  if (local) {
+    if (!merge_quant)
+      REEF_TRY(quantize_rows(B, kq, b.attn, b.xq, static_cast<long long>(kpad(kq)), b.xs, nullptr,
+                             st));
     REEF_TRY(gemm_i8_skinny_partials(B, H, kq, b.xq, L->w_o, part, st, L->t_o));
     REEF_TRY(reduce_rmsnorm_quant(B, H, skinny_split_count(B, H, kq), part, b.xs, L->s_o, x, b.h,
                                   L->rms_eps, L->mlp_norm, b.xq, b.xs2, st));

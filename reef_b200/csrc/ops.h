@@ -395,7 +395,12 @@ struct DecodeProblem {
   const int* positions;
   int len;                // cached keys of every sequence when lens is null
   float* partial;         // decode_attn_partial_floats() floats of scratch
-  float* out;             // [B][Hq][128]
+  float* out;             // [B][Hq][128] fp32, or (with out_q) unused
+  // optional: each sequence's row of Hq * 128 outputs quantised as
+  // quantize_rows does (out_q [B][Hq * 128] int8, out_q_scale [B]) instead
+  // of fp32 out: the o-projection's input when no peer shares the row
+  int8_t* out_q;
+  float* out_q_scale;
 };
 size_t decode_attn_partial_floats(int batch, int heads_q, int max_len);
 int decode_rope_append(int batch, int heads_q, int heads_kv, int max_len, float rope_base,
