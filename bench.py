@@ -406,13 +406,27 @@ def decode_step(dev, pk: dict, world: int, rank: int, comm) -> dict:
         layers[c].decode(x, pos, caches[c], out=y)
     torch.cuda.synchronize(dev)
     K.check_device_error()
-    graph = torch.cuda.CUDAGraph()
-    cap = torch.cuda.Stream(dev)
-    with torch.cuda.stream(cap), torch.cuda.graph(graph, stream=cap):
-        for i in range(calls):
-            layers[i % copies].decode(x, pos, caches[i % copies], out=y)
+    # One GPU: the steps replay from a CUDA graph (the host's launch cost off
+    # the clock, as a serving loop would run them).  N > 1: the steps are
+    # launched one by one on the stream, the library's NCCL all-reduces
+    # among them, so the host's issue time is on the clock.
+    graph = None
+    if world == 1:
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        with torch.cuda.stream(cap), torch.cuda.graph(graph, stream=cap):
+            for i in range(calls):
+                layers[i % copies].decode(x, pos, caches[i % copies], out=y)
+
+    def run_once():
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(calls):
+                layers[i % copies].decode(x, pos, caches[i % copies], out=y)
+
     for _ in range(2):
-        graph.replay()
+        run_once()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -420,7 +434,7 @@ def decode_step(dev, pk: dict, world: int, rank: int, comm) -> dict:
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
-        graph.replay()
+        run_once()
     e1.record()
     torch.cuda.synchronize(dev)
     K.check_device_error()
@@ -445,8 +459,10 @@ def decode_step(dev, pk: dict, world: int, rank: int, comm) -> dict:
             "us": us, "tokens_per_s": B / (us * 1e-6), "tops_per_gpu": ops / (us * 1e-6) / 1e12,
             "bytes_per_gpu": nbytes, "achieved_gbs": gbs, "peak_gbs": pk["hbm"],
             "frac": gbs / pk["hbm"], "peak_source": pk["source"],
-            "timing": f"CUDA graph of {calls} steps over {copies} layer copies (weights and "
-                      f"caches past L2), {reps} replays"}
+            "timing": (f"CUDA graph of {calls} steps over {copies} layer copies (weights and "
+                       f"caches past L2), {reps} replays" if world == 1 else
+                       f"{calls} steps over {copies} layer copies (weights and caches past L2) "
+                       f"launched one by one, {reps} times, max over ranks")}
 
 
 def run_reef(args) -> int:

@@ -208,26 +208,25 @@ def tp_forward(chunk_list, steps: int = 20) -> None:
 
 
 def stream(sizes_mb, reps: int = 20) -> None:
-    """The practical ceiling for a read of a given working set: torch's sum
-    over an int32 view of the bytes (one read, a few bytes written), a CUDA
-    graph of calls over enough rotating copies that every call reads DRAM,
-    timed with CUDA events.  One JSON line per size."""
+    """The practical ceiling for a read of a given working set: torch's
+    float32 sum over the bytes (one read, a few bytes written), a CUDA graph
+    of calls over enough rotating copies that every call reads DRAM, timed
+    with CUDA events.  One JSON line per size."""
     peaks = _peaks()
     for mb in sizes_mb:
         n = int(mb * 1e6) // 4
         copies = max(2, -(-2 * L2_BYTES // (4 * n)))
-        bufs = [torch.randint(-1000, 1000, (n,), dtype=torch.int32, device="cuda")
-                for _ in range(copies)]
-        out = torch.empty((), dtype=torch.int64, device="cuda")
+        bufs = [torch.rand((n,), device="cuda") for _ in range(copies)]
+        out = torch.empty((1,), device="cuda")
         calls = copies * 3
         for b in bufs:
-            torch.sum(b, dtype=torch.int64, out=out)
+            torch.sum(b, 0, keepdim=True, out=out)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         cap = torch.cuda.Stream()
         with torch.cuda.stream(cap), torch.cuda.graph(graph, stream=cap):
             for i in range(calls):
-                torch.sum(bufs[i % copies], dtype=torch.int64, out=out)
+                torch.sum(bufs[i % copies], 0, keepdim=True, out=out)
         graph.replay()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)

@@ -510,72 +510,71 @@ __global__ void __launch_bounds__(kDThreads, G > 8 ? 1 : 2)  // 16 heads: twice 
 }
 
 
-// Merge the partials of one sequence, one warp per query head (heads w, w +
-// 8, ...): the rows cta + pair of the CTAs that worked on the head's (sequence,
-// KV head) pair are read twice from L2 -- their maximum, then the weighted
-// sums in row order (a lane holds 4 dims) -- so a head's result does not
-// depend on how the heads are spread over ranks.  With xq set, the sequence's
-// row of heads_q * 128 outputs is quantised here (quant.hpp:112-133: scale =
-// max|x| / 127, 1 for a zero row, rint(x / scale) clamped to +-127) into xq /
-// xs instead of being written as fp32.
+// Merge the partials of one (sequence, query head): rows cta + pair for the
+// CTAs that worked on the pair.  Warp w takes rows w, w + 8, ... (a lane
+// holds 4 dims); the eight warp sums are added in a fixed order.
 template <int G>
-__global__ void __launch_bounds__(256)
-    decode_combine_kernel(DecodeArgs a, int8_t* __restrict__ xq, float* __restrict__ xs) {
-  extern __shared__ float orow[];  // [heads_q][128] when quantising
-  __shared__ float red[kDWarps];
-  const int b = blockIdx.x;
+__global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a) {
+  __shared__ float4 osm[kDWarps][32];
+  __shared__ float lsm[kDWarps], red[kDWarps];
+  const int bh = blockIdx.x;  // b * Hq + h
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = bh / a.heads_q, h = bh % a.heads_q;
+  const int pair = b * a.heads_kv + h / G, hg = h % G;
+  const int c0 = cta_of(a, static_cast<long long>(pair) * a.tiles);
+  const int nc = cta_of(a, static_cast<long long>(pair + 1) * a.tiles - 1) - c0 + 1;
   const long long stride = static_cast<long long>(G) * kPartRow;  // one row
+  const float* pb = a.part + (static_cast<long long>(c0) + pair) * stride + hg * kPartRow;
   // launched early (programmatic dependent launch): wait for the main
   // kernel's completion and memory before reading its partials
   pdl_wait();
   pdl_trigger();
-  float amax = 0.0f;
-  for (int h = warp; h < a.heads_q; h += kDWarps) {
-    const int pair = b * a.heads_kv + h / G, hg = h % G;
-    const int c0 = cta_of(a, static_cast<long long>(pair) * a.tiles);
-    const int nc = cta_of(a, static_cast<long long>(pair + 1) * a.tiles - 1) - c0 + 1;
-    const float* pb = a.part + (static_cast<long long>(c0) + pair) * stride + hg * kPartRow;
-    float m = -INFINITY;
-    for (int c = 0; c < nc; ++c) m = fmaxf(m, pb[c * stride]);
-    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    float l = 0.0f;
-    for (int c = 0; c < nc; ++c) {
+  // one pass over the rows: warp w holds rows w, w + 8, ... (m, l and a
+  // float4 of O per lane) in registers while the block finds the max
+  constexpr int kRows = (kMaxRowsPerPair + kDWarps - 1) / kDWarps;
+  float mr[kRows], lr[kRows];
+  float4 vr[kRows];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    const int c = warp + i * kDWarps;
+    mr[i] = -INFINITY;
+    if (c < nc) {
       const float* pr = pb + c * stride;
-      const float mc = pr[0];
-      // a CTA whose tiles all lay past the sequence's end has m = -inf
-      if (mc == -INFINITY) continue;
-      const float w = exp2f(mc - m);
-      const float4 v = reinterpret_cast<const float4*>(pr + 4)[lane];
-      l += w * pr[1];
-      o.x += w * v.x;
-      o.y += w * v.y;
-      o.z += w * v.z;
-      o.w += w * v.w;
-    }
-    const float4 r = make_float4(o.x / l, o.y / l, o.z / l, o.w / l);
-    if (xq != nullptr) {
-      reinterpret_cast<float4*>(orow + h * 128)[lane] = r;
-      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(r.x), fabsf(r.y)), fmaxf(fabsf(r.z), fabsf(r.w))));
-    } else {
-      reinterpret_cast<float4*>(a.out + (static_cast<long long>(b) * a.heads_q + h) * 128)[lane] = r;
+      mr[i] = pr[0];
+      lr[i] = pr[1];
+      vr[i] = reinterpret_cast<const float4*>(pr + 4)[lane];
+      m = fmaxf(m, mr[i]);
     }
   }
-  if (xq == nullptr) return;
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-  if (lane == 0) red[warp] = amax;
+  if (lane == 0) red[warp] = m;
   __syncthreads();
-  float mx = red[0];
 #pragma unroll
-  for (int w = 1; w < kDWarps; ++w) mx = fmaxf(mx, red[w]);
-  const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
-  if (tid == 0) xs[b] = scale;
-  const int width = a.heads_q * 128;
-  for (int i = tid; i < width; i += blockDim.x) {
-    int c = __float2int_rn(__fdiv_rn(orow[i], scale));
-    c = c < -127 ? -127 : (c > 127 ? 127 : c);
-    xq[static_cast<long long>(b) * width + i] = static_cast<int8_t>(c);
+  for (int w = 0; w < kDWarps; ++w) m = fmaxf(m, red[w]);
+  float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float l = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) {
+    // a CTA whose tiles all lay past the sequence's end has m = -inf
+    if (mr[i] == -INFINITY) continue;
+    const float w = exp2f(mr[i] - m);
+    l += w * lr[i];
+    o.x += w * vr[i].x;
+    o.y += w * vr[i].y;
+    o.z += w * vr[i].z;
+    o.w += w * vr[i].w;
+  }
+  osm[warp][lane] = o;
+  if (lane == 0) lsm[warp] = l;
+  __syncthreads();
+  if (tid < 128) {
+    float acc = 0.0f, ls = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kDWarps; ++w) {
+      acc += reinterpret_cast<const float*>(&osm[w][0])[tid];
+      ls += lsm[w];
+    }
+    a.out[static_cast<long long>(bh) * 128 + tid] = acc / ls;
   }
 }
 
@@ -599,8 +598,7 @@ int tile_ctas_per_sm() {
 }
 
 template <int G>
-int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodeArgs& a, int8_t* xq,
-                  float* xs, cudaStream_t st) {
+int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodeArgs& a, cudaStream_t st) {
   const int per_sm = tile_ctas_per_sm<G>();
   if (per_sm <= 0) return kErrCuda;
   // one wave, and at most kMaxRowsPerPair CTAs on any (sequence, KV head)
@@ -613,9 +611,8 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, DecodeArgs& a, i
   // the combine launches as a programmatic dependent of the main kernel, so
   // its launch overlaps the main kernel's tail
   PdlScope pdl;
-  const size_t smem = xq != nullptr ? static_cast<size_t>(a.heads_q) * 128 * sizeof(float) : 0;
-  return launch_k(decode_combine_kernel<G>, dim3(static_cast<unsigned>(a.batch)), dim3(kDThreads),
-                  smem, st, a, xq, xs);
+  return launch_k(decode_combine_kernel<G>, dim3(static_cast<unsigned>(a.batch * a.heads_q)),
+                  dim3(kDThreads), 0, st, a);
 }
 
 // One decode step's q / k / v: one warp per (sequence, head) of the QKV
@@ -769,9 +766,7 @@ size_t decode_attn_partial_floats(int batch, int heads_q, int max_len) {
 int decode_attn_i8(const DecodeProblem& p, cudaStream_t st) {
   if (p.batch <= 0 || p.heads_q <= 0 || p.heads_kv <= 0 || p.max_len <= 0) return kErrInvalid;
   if (p.heads_q % p.heads_kv != 0) return kErrInvalid;
-  if ((p.out_q == nullptr) != (p.out_q_scale == nullptr) ||
-      (p.out_q == nullptr && p.out == nullptr) || (p.out_q != nullptr && p.heads_q > 96))
-    return kErrInvalid;
+  if (p.out == nullptr) return kErrInvalid;
   // the bulk copies read scale groups of 16 bytes; TMA wants 16-byte bases
   if (p.max_len % 4 != 0 ||
       ((reinterpret_cast<uintptr_t>(p.k_cache) | reinterpret_cast<uintptr_t>(p.v_cache) |
@@ -807,11 +802,11 @@ int decode_attn_i8(const DecodeProblem& p, cudaStream_t st) {
   if (int rc = make_tma_3d_i8(&vm, p.v_cache, p.max_len, 128, 128, pairs, seg, 128, kTileKeys))
     return rc;
   switch (G) {
-    case 1: return launch_decode<1>(km, vm, a, p.out_q, p.out_q_scale, st);
-    case 2: return launch_decode<2>(km, vm, a, p.out_q, p.out_q_scale, st);
-    case 4: return launch_decode<4>(km, vm, a, p.out_q, p.out_q_scale, st);
-    case 8: return launch_decode<8>(km, vm, a, p.out_q, p.out_q_scale, st);
-    case 16: return launch_decode<16>(km, vm, a, p.out_q, p.out_q_scale, st);
+    case 1: return launch_decode<1>(km, vm, a, st);
+    case 2: return launch_decode<2>(km, vm, a, st);
+    case 4: return launch_decode<4>(km, vm, a, st);
+    case 8: return launch_decode<8>(km, vm, a, st);
+    case 16: return launch_decode<16>(km, vm, a, st);
     default: return kErrInvalid;
   }
 }

@@ -173,6 +173,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
     mbar_init(drain, 1);
     fence_barrier_init();
   }
+  // everything above touches only this CTA's shared memory: as a programmatic
+  // dependent it overlaps the kernel ahead, which must finish before q, k, v
+  // or their scales are read
+  pdl_wait();
+  pdl_trigger();
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -486,6 +491,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
 // forward so the per-element RoPE is two table loads.  i-major: table[i][pos],
 // so a warp of consecutive tokens reads one contiguous run per i.
 __global__ void rope_table_kernel(int seq, float base, float2* __restrict__ table) {
+  pdl_wait();
+  pdl_trigger();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= seq * 64) return;
   const int i = idx / seq, pos = idx - i * seq;
@@ -650,15 +657,14 @@ int flash_prefill_i8(const FlashProblem& p, cudaStream_t stream) {
   a.k_scale = p.k_scale;
   a.err = device_error_ptr();
   const int grid = (((p.seq + kTile - 1) / kTile + 1) / 2) * p.batch * p.heads_q;
-  flash_prefill_kernel<<<grid, kFThreads, FL::kAlloc, stream>>>(mq, mk, mv, mo, a);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_k(flash_prefill_kernel, dim3(static_cast<unsigned>(grid)), dim3(kFThreads),
+                  FL::kAlloc, stream, mq, mk, mv, mo, a);
 }
 
 int rope_table(int seq, float rope_base, void* table, cudaStream_t stream) {
   if (seq <= 0 || table == nullptr) return kErrInvalid;
-  rope_table_kernel<<<(seq * 64 + 255) / 256, 256, 0, stream>>>(seq, rope_base,
-                                                                 static_cast<float2*>(table));
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_k(rope_table_kernel, dim3(static_cast<unsigned>((seq * 64 + 255) / 256)), dim3(256),
+                  0, stream, seq, rope_base, static_cast<float2*>(table));
 }
 
 int rope_qkv_quant(int batch, int seq, int heads_q, int heads_kv, float rope_base,

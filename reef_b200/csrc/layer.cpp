@@ -85,8 +85,7 @@ int linear_w8a8_swiglu(long long rows, int in, int ffn, const int8_t* xq, const 
                        const int8_t* w_gu, const float* ws, float* h, float* row_max,
                        cudaStream_t st) {
   if (rows == 0) return kOk;
-  if (cudaMemsetAsync(row_max, 0, static_cast<size_t>(rows) * sizeof(float), st) != cudaSuccess)
-    return kErrCuda;
+  REEF_TRY(zero_f32(rows, row_max, st));  // the epilogue's atomic maxima start at 0
   GemmProblem p = problem(rows, in, ffn, xq, w_gu);
   p.args.x_scale = xs;
   p.args.w_scale = ws;
@@ -257,6 +256,21 @@ int ag_gemm_sms() {
     v = x;
   }
   return v;
+}
+
+// Whether the TP=1 prefill forward launches its kernels as programmatic
+// dependents of one another: off unless REEF_B200_PREFILL_PDL=1.  Measured
+// on config 3 under the power cap, the chain made the layer slower (4.16 and
+// 4.26 ms against 4.03 and 4.05 ms without, same box, interleaved runs): the
+// dependents' CTAs that fit beside a persistent GEMM's wait there, and the
+// GEMMs leave no tail worth overlapping.
+bool prefill_pdl() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("REEF_B200_PREFILL_PDL");
+    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
 }
 
 bool llama_allgather(const reef_b200_llama_layer* L) {
@@ -1140,6 +1154,12 @@ static int llama_forward(const reef_b200_llama_layer* L, const float* x, float* 
   const int H = static_cast<int>(L->hidden), hq = static_cast<int>(L->heads_q),
             hkv = static_cast<int>(L->heads_kv), F = static_cast<int>(L->ffn), D = 128;
   const int qkv_w = (hq + 2 * hkv) * D;
+  // With REEF_B200_PREFILL_PDL=1 (and no communicator, no per-kernel spans)
+  // every kernel goes out as a programmatic dependent of the one before: its
+  // CTAs start on the SMs the previous kernel's last CTAs free, and each
+  // waits for that kernel to finish before it reads its output.
+  PdlScope pdl;
+  if (comm_world(c) != 1 || ev != nullptr || !prefill_pdl()) t_pdl = pdl.prev;
 
   // attention block: y_attn = x + o_proj(attn(rope(qkv(rmsnorm(x)))))
   REEF_TRY(rmsnorm_quant(T, H, L->rms_eps, x, L->attn_norm, b.xq, b.xs, st));
@@ -1257,22 +1277,14 @@ int reef_b200_llama_decode_forward(const reef_b200_llama_layer* L, const float* 
   dp.positions = positions;
   dp.partial = b.dpart;
   dp.out = b.attn;
-  // o-proj with the residual, then the MLP's pre-norm: without a peer to
-  // share the rows with, the attention's merge quantises the o-proj input
-  // itself, and the o-proj's split-K sum, the residual and RMSNorm + quant
-  // run as one kernel; the gate/up input scales go to xs2
-  const int kq = static_cast<int>(hq * D);
-  const bool local = comm_world(c) == 1;
-  const bool merge_quant = local && hq <= 96;  // the merge holds a row of heads in shared memory
-  if (merge_quant) {
-    dp.out_q = b.xq;
-    dp.out_q_scale = b.xs;
-  }
   REEF_TRY(decode_attn_i8(dp, st));
-  if (local) {
-    if (!merge_quant)
-      REEF_TRY(quantize_rows(B, kq, b.attn, b.xq, static_cast<long long>(kpad(kq)), b.xs, nullptr,
-                             st));
+  // o-proj with the residual, then the MLP's pre-norm: without a peer to
+  // share the rows with, the o-proj's split-K sum, the residual and RMSNorm +
+  // quant run as one kernel; the gate/up input scales go to xs2
+  const int kq = static_cast<int>(hq * D);
+  if (comm_world(c) == 1) {
+    REEF_TRY(quantize_rows(B, kq, b.attn, b.xq, static_cast<long long>(kpad(kq)), b.xs, nullptr,
+                           st));
     REEF_TRY(gemm_i8_skinny_partials(B, H, kq, b.xq, L->w_o, part, st, L->t_o));
     REEF_TRY(reduce_rmsnorm_quant(B, H, skinny_split_count(B, H, kq), part, b.xs, L->s_o, x, b.h,
                                   L->rms_eps, L->mlp_norm, b.xq, b.xs2, st));

@@ -290,6 +290,9 @@ int quantize_rows_to(long long rows, long long in, const float* x, const PeerDst
                      long long ldq, float* x_scale, const float* row_max, cudaStream_t stream);
 // src [n] fp32 copied to every destination by SM stores
 int push_f32(long long n, const float* src, const PeerDst& dst, cudaStream_t stream);
+// p[0, n) = 0 by a kernel (a link of a programmatic-dependent chain, where a
+// memset node would make the next kernel wait for the whole one before)
+int zero_f32(long long n, float* p, cudaStream_t stream);
 // out[r] = max_s in[s][r] for in [segs][rows]
 int max_segments(int segs, long long rows, const float* in, float* out, cudaStream_t stream);
 int row_absmax(long long rows, long long in, const float* x, float* row_max,
@@ -395,12 +398,7 @@ struct DecodeProblem {
   const int* positions;
   int len;                // cached keys of every sequence when lens is null
   float* partial;         // decode_attn_partial_floats() floats of scratch
-  float* out;             // [B][Hq][128] fp32, or (with out_q) unused
-  // optional: each sequence's row of Hq * 128 outputs quantised as
-  // quantize_rows does (out_q [B][Hq * 128] int8, out_q_scale [B]) instead
-  // of fp32 out: the o-projection's input when no peer shares the row
-  int8_t* out_q;
-  float* out_q_scale;
+  float* out;             // [B][Hq][128]
 };
 size_t decode_attn_partial_floats(int batch, int heads_q, int max_len);
 int decode_rope_append(int batch, int heads_q, int heads_kv, int max_len, float rope_base,

@@ -11,6 +11,8 @@
 #include "common.cuh"
 #include "ops.h"
 
+#include <algorithm>
+
 namespace reef {
 
 namespace {
@@ -166,6 +168,14 @@ __global__ void signal_and_wait_kernel(PeerFlags f, CounterWaits w, unsigned lon
   }
 }
 
+__global__ void zero_f32_kernel(long long n, float* __restrict__ p) {
+  pdl_wait();
+  pdl_trigger();
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    p[i] = 0.0f;
+}
+
 __global__ void push_f32_kernel(long long n, const float* __restrict__ src, PeerDst dst) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -285,6 +295,13 @@ int signal_and_wait(const PeerFlags& f, const CounterWaits& w, unsigned long lon
     if (w.p[i] == nullptr) return kErrInvalid;
   signal_and_wait_kernel<<<1, 32, 0, stream>>>(f, w, limit_ns, device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int zero_f32(long long n, float* p, cudaStream_t stream) {
+  if (n == 0) return kOk;
+  if (n < 0 || p == nullptr) return kErrInvalid;
+  const long long blocks = std::min<long long>((n + 255) / 256, 1024);
+  return launch_k(zero_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, n, p);
 }
 
 int push_f32(long long n, const float* src, const PeerDst& dst, cudaStream_t stream) {
