@@ -387,21 +387,35 @@ def decode_step(dev, pk: dict, world: int, rank: int, comm) -> dict:
     tp = world if world > 1 else 8
     layers, caches = [], []
     g = torch.Generator(device=dev).manual_seed(7)
-    for c in range(copies):
-        if world > 1:
-            L = LlamaLayer(s, B, 8, seed=11 + c, world=world, rank=rank, comm=comm, device=dev)
-        else:
-            L = LlamaLayer(s, B, 8, seed=11 + c, world=8, rank=0, device=dev)
-        cache = L.alloc_cache(Lmax)
-        cache["k"].random_(-127, 128, generator=g)
-        cache["v"].random_(-127, 128, generator=g)
-        cache["ks"].uniform_(0.005, 0.015, generator=g)
-        cache["vs"].uniform_(0.005, 0.015, generator=g)
-        layers.append(L)
-        caches.append(cache)
-    x = torch.randn((B, s.hidden), generator=g, device=dev)
-    y = torch.empty_like(x)
-    pos = torch.full((B,), Lmax - 1, dtype=torch.int32, device=dev)
+    err = None
+    try:  # every allocation and weight before any step with a collective
+        for c in range(copies):
+            if world > 1:
+                L = LlamaLayer(s, B, 8, seed=11 + c, world=world, rank=rank, comm=comm,
+                               device=dev)
+            else:
+                L = LlamaLayer(s, B, 8, seed=11 + c, world=8, rank=0, device=dev)
+            cache = L.alloc_cache(Lmax)
+            cache["k"].random_(-127, 128, generator=g)
+            cache["v"].random_(-127, 128, generator=g)
+            cache["ks"].uniform_(0.005, 0.015, generator=g)
+            cache["vs"].uniform_(0.005, 0.015, generator=g)
+            L._decode_tiles()
+            layers.append(L)
+            caches.append(cache)
+        x = torch.randn((B, s.hidden), generator=g, device=dev)
+        y = torch.empty_like(x)
+        pos = torch.full((B,), Lmax - 1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+    except Exception as e:  # noqa: BLE001
+        err = e
+    if world > 1:  # every rank set up, or none runs a step
+        ok = torch.tensor([0 if err is not None else 1], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0:
+            raise RuntimeError(f"decode set-up failed on some rank: {err}")
+    elif err is not None:
+        raise err
     for c in range(copies):  # workspaces allocated, tensor maps warmed
         layers[c].decode(x, pos, caches[c], out=y)
     torch.cuda.synchronize(dev)

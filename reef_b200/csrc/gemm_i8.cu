@@ -97,6 +97,30 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int gro
   nb = r / gsize;
 }
 
+// One unit of a CTA's work: k-blocks [kb0, kb1) of output tile (mb, nb),
+// written to partial slot `slot` (its K split).
+struct Item {
+  int mb, nb, kb0, kb1, slot;
+};
+
+// The CTA's idx-th item, or false when it has no more: (tile, split) items
+// dealt round-robin over the persistent grid; split s of `splits` takes
+// k-blocks [s nk / splits, (s + 1) nk / splits).  (A stream-K cut -- every
+// CTA an equal range of the tiles' k-blocks, crossing tile boundaries --
+// measured slower for the decode GEMMs: a CTA's second piece adds a whole
+// item's epilogue and hand-off at the end.)
+__device__ __forceinline__ bool get_item(const GemmArgs& args, int num_m, int num_n, int num_k,
+                                         int splits, int idx, Item& it) {
+  const int t = static_cast<int>(blockIdx.x) + idx * static_cast<int>(gridDim.x);
+  if (t >= num_m * num_n * splits) return false;
+  tile_coords(t / splits, num_m, num_n, args.group_m, it.mb, it.nb);
+  const int split = t % splits;
+  it.kb0 = split * num_k / splits;
+  it.kb1 = (split + 1) * num_k / splits;
+  it.slot = split;
+  return true;
+}
+
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(threads_for<EPI>(), 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -125,9 +149,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
   const int segs = args.k_segments > 1 ? args.k_segments : 1;
   const int kbs = (K + kBK - 1) / kBK;
   const int num_k = kbs * segs;
-  const int num_tiles = num_m * num_n;
   const int splits = args.k_splits > 1 ? args.k_splits : 1;
-  const int num_items = num_tiles * splits;  // (tile, K-split) pairs
   int* err = args.err;
 
   if (threadIdx.x == 0) {
@@ -166,12 +188,10 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
       // launch lets the two overlap); their B halves follow the wait.  The
       // ring is fresh, so those stages need no "empty" wait.
       int pre = 0;
-      if (args.a_first && static_cast<int>(blockIdx.x) < num_items) {
-        int mb, nb;
-        tile_coords(blockIdx.x / splits, num_m, num_n, args.group_m, mb, nb);
-        const int split = blockIdx.x % splits;
-        const int kb0 = split * num_k / splits, kb1 = (split + 1) * num_k / splits;
-        pre = min(STAGES, kb1 - kb0);
+      Item first;
+      if (args.a_first && get_item(args, num_m, num_n, num_k, splits, 0, first)) {
+        const int mb = first.mb, kb0 = first.kb0;
+        pre = min(STAGES, first.kb1 - kb0);
         for (int i = 0; i < pre; ++i) {
           const int kb = kb0 + i, seg = kb / kbs, kx = (kb - seg * kbs) * kBK;
           mbar_arrive_expect_tx(&full[i], L::kStageBytes);
@@ -187,13 +207,11 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
       // a programmatic dependent may be scheduled now; it waits for this
       // grid's completion and memory before reading the outputs
       pdl_trigger();
-      for (int t = blockIdx.x; t < num_items && ok; t += gridDim.x) {
-        int mb, nb;
-        tile_coords(t / splits, num_m, num_n, args.group_m, mb, nb);
-        const int split = t % splits;
-        const int kb0 = split * num_k / splits, kb1 = (split + 1) * num_k / splits;
+      Item it;
+      for (int idx = 0; ok && get_item(args, num_m, num_n, num_k, splits, idx, it); ++idx) {
+        const int mb = it.mb, nb = it.nb, kb0 = it.kb0, kb1 = it.kb1;
         for (int kb = kb0; kb < kb1; ++kb) {
-          const bool prefetched = t == static_cast<int>(blockIdx.x) && kb - kb0 < pre;
+          const bool prefetched = idx == 0 && kb - kb0 < pre;
           if (!prefetched && !mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutEmpty)) {
             ok = false;
             break;
@@ -246,15 +264,15 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_items && ok; t += gridDim.x) {
+      Item it;
+      for (int idx = 0; ok && get_item(args, num_m, num_n, num_k, splits, idx, it); ++idx) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, err, kDevTimeoutAccEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        const int split = t % splits;
-        const int kb0 = split * num_k / splits, kb1 = (split + 1) * num_k / splits;
+        const int kb0 = it.kb0, kb1 = it.kb1;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, kDevTimeoutFull)) {
             ok = false;
@@ -303,11 +321,11 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
     const int sub_col = (lane & 7) * 4;  // 0, 4, ..., 28
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_items; t += gridDim.x) {
-      int mb, nb;
-      tile_coords(t / splits, num_m, num_n, args.group_m, mb, nb);
+    Item it;
+    for (int idx = 0; get_item(args, num_m, num_n, num_k, splits, idx, it); ++idx) {
+      const int mb = it.mb, nb = it.nb;
       // K-split partial outputs land in their own slice of y
-      const long long y_off = static_cast<long long>(t % splits) * args.split_stride;
+      const long long y_off = static_cast<long long>(it.slot) * args.split_stride;
       // warp-uniform outcome: the tcgen05.ld below is warp-collective
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, err, kDevTimeoutAccFull)))
         break;

@@ -58,12 +58,11 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return r;
 }
 
+// reef's int8 codes (quant.hpp:68-81) of four values through quant_code
+// (common.cuh): the same codes as rint(x / scale), clamped
 __device__ __forceinline__ char4 q8x4(float4 v, float scale) {
-  auto q = [scale](float x) {
-    int c = __float2int_rn(__fdiv_rn(x, scale));
-    c = c < -127 ? -127 : (c > 127 ? 127 : c);
-    return static_cast<signed char>(c);
-  };
+  const float rcp = __frcp_rn(scale);
+  auto q = [scale, rcp](float x) { return static_cast<signed char>(quant_code(x, scale, rcp)); };
   return make_char4(q(v.x), q(v.y), q(v.z), q(v.w));
 }
 

@@ -37,10 +37,11 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return r;
 }
 
-__device__ __forceinline__ int8_t q8(float x, float scale) {
-  int v = __float2int_rn(__fdiv_rn(x, scale));
-  v = v < -127 ? -127 : (v > 127 ? 127 : v);
-  return static_cast<int8_t>(v);
+// reef's int8 code (quant.hpp:68-81) through quant_code (common.cuh): the
+// quotient by the reciprocal, with the correctly rounded division wherever it
+// could round differently, so the same code as rint(x / scale) always.
+__device__ __forceinline__ int8_t q8(float x, float scale, float rcp) {
+  return static_cast<int8_t>(quant_code(x, scale, rcp));
 }
 
 // One CTA per row.  row_max (optional) supplies a precomputed max |x| per
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(kQuantThreads)
     mx = block_max(m, red);
   }
   const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  const float rcp = __frcp_rn(scale);
   if (threadIdx.x == 0) xs[row] = scale;
   // each int8 row goes to every destination
 #pragma unroll
@@ -86,14 +88,16 @@ __global__ void __launch_bounds__(kQuantThreads)
     const int idx = threadIdx.x + i * kQuantThreads;
     if (idx < n4) {
       const float4 v = cache[i];
-      const char4 q = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
+      const char4 q = make_char4(q8(v.x, scale, rcp), q8(v.y, scale, rcp), q8(v.z, scale, rcp),
+                                 q8(v.w, scale, rcp));
       for (int d = 0; d < xq.n; ++d)
         reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + row * ldq)[idx] = q;
     }
   }
   for (int idx = threadIdx.x + CACHE * kQuantThreads; idx < n4; idx += kQuantThreads) {
     const float4 v = __ldg(xr + idx);
-    const char4 q = make_char4(q8(v.x, scale), q8(v.y, scale), q8(v.z, scale), q8(v.w, scale));
+    const char4 q = make_char4(q8(v.x, scale, rcp), q8(v.y, scale, rcp), q8(v.z, scale, rcp),
+                               q8(v.w, scale, rcp));
     for (int d = 0; d < xq.n; ++d)
       reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + row * ldq)[idx] = q;
   }
@@ -116,9 +120,10 @@ __global__ void __launch_bounds__(kQuantThreads)
   for (int c = threadIdx.x; c < in; c += kQuantThreads) m = fmaxf(m, fabsf(xr[c]));
   const float mx = row_max != nullptr ? row_max[row] : block_max(m, red);
   const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  const float rcp = __frcp_rn(scale);
   if (threadIdx.x == 0) xs[row] = scale;
   for (long long c = threadIdx.x; c < ldq; c += kQuantThreads)
-    xq[row * ldq + c] = c < in ? q8(xr[c], scale) : static_cast<int8_t>(0);
+    xq[row * ldq + c] = c < in ? q8(xr[c], scale, rcp) : static_cast<int8_t>(0);
 }
 
 __global__ void __launch_bounds__(kQuantThreads)
