@@ -48,7 +48,10 @@ __device__ __forceinline__ int8_t q8(float x, float scale, float rcp) {
 // row (the all-reduced maximum of a tensor-parallel shard).  CACHE float4
 // per thread stay in registers (the smallest that holds the row, so
 // registers and occupancy follow the width); longer rows re-read the rest.
-template <int CACHE>
+// kMulti: the int8 row goes to every destination of xq (the all-gather plan's
+// peer copies); otherwise only to xq.p[0], named by a constant index so the
+// pointer list stays in the parameter space instead of a local-memory copy.
+template <int CACHE, bool kMulti>
 __global__ void __launch_bounds__(kQuantThreads)
     quantize_rows_vec4(int in, const float* __restrict__ x, PeerDst xq, long long ldq,
                        float* __restrict__ xs, const float* __restrict__ row_max) {
@@ -90,20 +93,33 @@ __global__ void __launch_bounds__(kQuantThreads)
       const float4 v = cache[i];
       const char4 q = make_char4(q8(v.x, scale, rcp), q8(v.y, scale, rcp), q8(v.z, scale, rcp),
                                  q8(v.w, scale, rcp));
-      for (int d = 0; d < xq.n; ++d)
-        reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + row * ldq)[idx] = q;
+      if constexpr (kMulti) {
+        for (int d = 0; d < xq.n; ++d)
+          reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + row * ldq)[idx] = q;
+      } else {
+        reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[0]) + row * ldq)[idx] = q;
+      }
     }
   }
   for (int idx = threadIdx.x + CACHE * kQuantThreads; idx < n4; idx += kQuantThreads) {
     const float4 v = __ldg(xr + idx);
     const char4 q = make_char4(q8(v.x, scale, rcp), q8(v.y, scale, rcp), q8(v.z, scale, rcp),
                                q8(v.w, scale, rcp));
-    for (int d = 0; d < xq.n; ++d)
-      reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + row * ldq)[idx] = q;
+    if constexpr (kMulti) {
+      for (int d = 0; d < xq.n; ++d)
+        reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[d]) + row * ldq)[idx] = q;
+    } else {
+      reinterpret_cast<char4*>(static_cast<int8_t*>(xq.p[0]) + row * ldq)[idx] = q;
+    }
   }
   // zero the stride padding [in, ldq)
-  for (long long c = in + threadIdx.x; c < ldq; c += kQuantThreads)
-    for (int d = 0; d < xq.n; ++d) static_cast<int8_t*>(xq.p[d])[row * ldq + c] = 0;
+  for (long long c = in + threadIdx.x; c < ldq; c += kQuantThreads) {
+    if constexpr (kMulti) {
+      for (int d = 0; d < xq.n; ++d) static_cast<int8_t*>(xq.p[d])[row * ldq + c] = 0;
+    } else {
+      static_cast<int8_t*>(xq.p[0])[row * ldq + c] = 0;
+    }
+  }
 }
 
 // Any width / alignment.
@@ -248,12 +264,19 @@ static int quantize_vec4(long long rows, long long in, const float* x, const Pee
   const unsigned grid = static_cast<unsigned>(rows);
   const int ii = static_cast<int>(in);
   const dim3 g(grid), t(kQuantThreads);
-  if (per <= 1) return launch_k(quantize_rows_vec4<1>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
-  if (per <= 2) return launch_k(quantize_rows_vec4<2>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
-  if (per <= 4) return launch_k(quantize_rows_vec4<4>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
-  if (per <= 8) return launch_k(quantize_rows_vec4<8>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
-  if (per <= 12) return launch_k(quantize_rows_vec4<12>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
-  return launch_k(quantize_rows_vec4<16>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, row_max);
+#define REEF_QUANT_VEC4(C)                                                                       \
+  return x_q.n > 1                                                                               \
+             ? launch_k(quantize_rows_vec4<C, true>, g, t, 0, stream, ii, x, x_q, ldq, x_scale,  \
+                        row_max)                                                                 \
+             : launch_k(quantize_rows_vec4<C, false>, g, t, 0, stream, ii, x, x_q, ldq, x_scale, \
+                        row_max)
+  if (per <= 1) REEF_QUANT_VEC4(1);
+  if (per <= 2) REEF_QUANT_VEC4(2);
+  if (per <= 4) REEF_QUANT_VEC4(4);
+  if (per <= 8) REEF_QUANT_VEC4(8);
+  if (per <= 12) REEF_QUANT_VEC4(12);
+  REEF_QUANT_VEC4(16);
+#undef REEF_QUANT_VEC4
 }
 
 int quantize_rows(long long rows, long long in, const float* x, int8_t* x_q, long long ldq,
