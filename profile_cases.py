@@ -7,6 +7,7 @@ GEMM sweep.  The recipe behind the summaries in profiles/.
     python profile_cases.py decode [--batch 64 --heads 8 --kv-heads 1 --seq 4096]
     python profile_cases.py decode_step [--steps 3]
     python profile_cases.py layer [--batch 8 --steps 2]
+    python profile_cases.py layer_timing [--batch 8 --steps 10]
     python profile_cases.py sweep [--out sweep.json] [--tp 1]
     torchrun --nproc-per-node N profile_cases.py tp [--chunks 1,2,4 --steps 20]
     python profile_cases.py stream [--sizes 35,69,138,276]
@@ -134,6 +135,61 @@ def decode_step(steps: int) -> None:
     for _ in range(steps):
         L.decode(x, pos, cache, out=y)
     torch.cuda.synchronize()
+
+
+def layer_timing(batch: int, steps: int) -> None:
+    """Config 3's prefill layer at TP=1: the plain forward timed over `steps`
+    calls (CUDA events around the whole run), then the instrumented forward
+    (reef_b200_llama_layer_forward_events: an event pair around the QKV GEMM,
+    flash, o-proj, gate/up and down) with its spans, the time between them and
+    its total.  One JSON line."""
+    import ctypes as C
+
+    from reef_b200.layer import LLAMA_7B, LlamaLayer
+    L = LlamaLayer(LLAMA_7B, batch, 2048, seed=1)
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    x = torch.randn((batch * 2048, LLAMA_7B.hidden), generator=g, device="cuda")
+    y = torch.empty_like(x)
+    for _ in range(3):
+        L.forward(x, y)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        L.forward(x, y)
+    e1.record()
+    torch.cuda.synchronize()
+    plain = e0.elapsed_time(e1) / steps
+    st = torch.cuda.current_stream().cuda_stream
+    rows = []
+    for _ in range(steps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(10)]
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        handles = (C.c_void_p * 10)(*[e.cuda_event for e in ev])
+        _lib.call("reef_b200_llama_layer_forward_events", C.byref(L.desc), x.data_ptr(),
+                  y.data_ptr(), L.workspace.data_ptr(), L.workspace.numel(), handles, st)
+        end.record()
+        torch.cuda.synchronize()
+        spans = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(5)]
+        gaps = [ev[2 * i + 1].elapsed_time(ev[2 * i + 2]) for i in range(4)]
+        rows.append((start.elapsed_time(end), start.elapsed_time(ev[0]), spans, gaps,
+                     ev[9].elapsed_time(end)))
+    K.check_device_error()
+    n = len(rows)
+    avg = lambda f: sum(f(r) for r in rows) / n
+    names = ["qkv", "flash", "o_proj", "gate_up", "down"]
+    print(json.dumps({
+        "plain_ms": plain,
+        "instrumented_total_ms": avg(lambda r: r[0]),
+        "before_qkv_ms": avg(lambda r: r[1]),
+        "spans_ms": {nm: avg(lambda r, i=i: r[2][i]) for i, nm in enumerate(names)},
+        "between_ms": {f"{names[i]}->{names[i + 1]}": avg(lambda r, i=i: r[3][i])
+                       for i in range(4)},
+        "after_down_ms": avg(lambda r: r[4]),
+    }), flush=True)
 
 
 def layer(batch: int, steps: int) -> None:
@@ -349,7 +405,7 @@ def sweep(out: str | None, tps=(1,), iters: int = 20, reps: int = 3) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "flash", "qkv", "decode", "decode_step", "layer",
-                                     "sweep", "tp", "stream"])
+                                     "layer_timing", "sweep", "tp", "stream"])
     ap.add_argument("--sizes", default="35,69,138,276", help="stream: working sets in MB")
     ap.add_argument("--chunks", default="1,2,4", help="tp: chunk counts of the all-gather plan")
     ap.add_argument("--steps", type=int, default=3)
@@ -381,6 +437,8 @@ def main() -> None:
         decode_step(a.steps)
     elif a.case == "layer":
         layer(a.batch, a.steps)
+    elif a.case == "layer_timing":
+        layer_timing(a.batch, max(a.steps, 5))
     else:
         flash(a.batch, a.seq, a.heads, a.kv_heads)
     K.check_device_error()
