@@ -405,8 +405,10 @@ int reef_b200_selftest_wait_timeout(unsigned limit_us, int* done, reef_b200_stre
  * a limit of limit_us microseconds (1 .. 2e6): the wait ends when *counter
  * reaches target (wrap-around >=, as the forward's counters only grow), or
  * after the limit, when it records 0x106 (a peer never signalled) in the
- * device error word and returns.  A counter nothing increments is how a dead
- * peer looks to this rank; the device stays usable. */
+ * device error word and returns.  While the error word holds 0x106 (until
+ * reef_b200_device_error reads it), a wait returns at once: a rank that lost
+ * a peer pays one limit, not one per step.  A counter nothing increments is
+ * how a dead peer looks to this rank; the device stays usable. */
 int reef_b200_selftest_peer_wait_timeout(unsigned limit_us, const unsigned* counter,
                                          unsigned target, reef_b200_stream_t stream);
 

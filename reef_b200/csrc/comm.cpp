@@ -67,14 +67,55 @@ int settle(Comm* c, ncclResult_t r) {
   }
 }
 
-void arena_free(Comm* c) {
+// Wait for the stream with the communicator's deadline (a collective that a
+// peer never joins would otherwise block the host for good).
+int sync_bounded(Comm* c, cudaStream_t s) {
+  const auto start = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(s);
+    if (e == cudaSuccess) return kOk;
+    if (e != cudaErrorNotReady) return kErrCuda;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count() >
+        c->timeout_s)
+      return kErrTimeout;
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+
+void close_peers(Comm* c) {
   for (int r = 0; r < static_cast<int>(c->peer.size()); ++r)
     if (r != c->rank && c->peer[r] != nullptr) cudaIpcCloseMemHandle(c->peer[r]);
   c->peer.clear();
+}
+
+void arena_free(Comm* c) {
+  close_peers(c);
   if (c->arena != nullptr) cudaFree(c->arena);
   c->arena = nullptr;
   c->arena_data = 0;
   c->arena_slots = 0;
+}
+
+// Every rank drops its mappings of the peers' arenas, then waits until all
+// ranks have (an all-reduce of one word as the barrier) before any rank frees
+// its own: an exported allocation must not be freed while another process
+// still has it open.  The caller has drained this rank's work, so none of its
+// kernels still stores into a peer's arena.  Used where every rank takes the
+// same step (a larger arena, the communicator's teardown).
+int arena_release_collective(Comm* c) {
+  if (c->arena == nullptr) return kOk;
+  close_peers(c);
+  int* word = nullptr;
+  if (cudaMalloc(&word, sizeof(int)) != cudaSuccess) return kErrCuda;
+  int rc = cudaMemsetAsync(word, 0, sizeof(int), c->stream) == cudaSuccess ? kOk : kErrCuda;
+  if (rc == kOk) rc = settle(c, ncclAllReduce(word, word, 1, ncclInt32, ncclSum, c->nccl, c->stream));
+  if (rc == kOk) rc = sync_bounded(c, c->stream);
+  // after a timeout the all-reduce may still be pending on the stream: the
+  // word stays allocated (cudaFree would wait for it) until the abort
+  if (rc != kErrTimeout) cudaFree(word);
+  if (rc != kOk) return rc;
+  arena_free(c);
+  return kOk;
 }
 
 size_t flag_bytes(int slots, int world) {
@@ -138,7 +179,13 @@ int comm_destroy(Comm* c) {
   int rc = kOk;
   if (c->arena != nullptr) {
     cudaDeviceSynchronize();
-    arena_free(c);
+    // a peer that never reaches the barrier leaves its all-reduce on our
+    // stream: abort (which ends it) instead of waiting on the stream
+    rc = arena_release_collective(c);
+    if (rc != kOk) {
+      comm_abort(c);
+      return rc;
+    }
   }
   if (c->stream != nullptr) {
     cudaStreamSynchronize(c->stream);
@@ -209,13 +256,17 @@ int comm_arena_reserve(Comm* c, size_t data_bytes, int slots) {
   if (c->arena != nullptr && c->arena_data >= data_bytes && c->arena_slots >= slots) return kOk;
   // every rank reaches this point with the same sizes; drain before replacing
   if (cudaDeviceSynchronize() != cudaSuccess) return kErrCuda;
-  arena_free(c);
+  if (int rc = arena_release_collective(c)) return rc;
   const size_t fb = flag_bytes(slots, c->world);
   const size_t total = fb + ((data_bytes + 255) & ~static_cast<size_t>(255));
   if (cudaMalloc(&c->arena, total) != cudaSuccess) return kErrCuda;
-  if (cudaMemset(c->arena, 0, fb) != cudaSuccess) return kErrCuda;
-  // exchange IPC handles (an all-gather through NCCL, which also orders the
-  // zeroed flags before any peer can signal)
+  // the new counters start at zero, and so do the forward rounds their
+  // targets derive from
+  c->round = 0;
+  if (cudaMemsetAsync(c->arena, 0, fb, c->stream) != cudaSuccess) return kErrCuda;
+  // exchange IPC handles (an all-gather through NCCL on the same stream as the
+  // zeroing, so a peer holds this arena's handle only once its counters are
+  // zero)
   cudaIpcMemHandle_t mine;
   if (cudaIpcGetMemHandle(&mine, c->arena) != cudaSuccess) return kErrCuda;
   const size_t hb = sizeof(cudaIpcMemHandle_t);
@@ -223,12 +274,14 @@ int comm_arena_reserve(Comm* c, size_t data_bytes, int slots) {
   if (cudaMalloc(&dev, hb * (c->world + 1)) != cudaSuccess) return kErrCuda;
   std::vector<cudaIpcMemHandle_t> all(c->world);
   int rc = kOk;
-  if (cudaMemcpy(dev + hb * c->world, &mine, hb, cudaMemcpyHostToDevice) != cudaSuccess) rc = kErrCuda;
+  if (cudaMemcpyAsync(dev + hb * c->world, &mine, hb, cudaMemcpyHostToDevice, c->stream) !=
+      cudaSuccess)
+    rc = kErrCuda;
   if (rc == kOk) rc = allgather_bytes(c, dev + hb * c->world, dev, hb, c->stream);
-  if (rc == kOk && cudaStreamSynchronize(c->stream) != cudaSuccess) rc = kErrCuda;
+  if (rc == kOk) rc = sync_bounded(c, c->stream);
   if (rc == kOk && cudaMemcpy(all.data(), dev, hb * c->world, cudaMemcpyDeviceToHost) != cudaSuccess)
     rc = kErrCuda;
-  cudaFree(dev);
+  if (rc != kErrTimeout) cudaFree(dev);  // (as in arena_release_collective)
   if (rc != kOk) return rc;
   c->peer.assign(c->world, nullptr);
   for (int r = 0; r < c->world; ++r) {

@@ -32,9 +32,11 @@ cudaStream_t comm_compute_stream(const Comm* c, int i);
 // kernels, and that a stream waits on before its next kernels, both with
 // signal_and_wait (ops.h): its wait gives up after comm_wait_limit_ns and
 // records kDevTimeoutPeer, so a peer that never signals cannot hang a stream.
-// Counts only grow, so a counter never needs resetting.
+// Counts only grow while an arena lives, so a counter never needs resetting.
 // (Re)creates the arena when it is smaller than asked; collective (every rank
-// calls it with the same sizes in the same order).
+// calls it with the same sizes in the same order).  A new arena's counters
+// start at zero and comm_next_round starts again at 1 with them; the old one
+// is freed only after every rank has dropped its mapping of it.
 int comm_arena_reserve(Comm* c, size_t data_bytes, int slots);
 uint8_t* comm_arena_data(Comm* c);  // this rank's data region
 // rank r's data region as mapped here (r = this rank: comm_arena_data)
@@ -45,8 +47,9 @@ uint8_t* comm_peer_data(Comm* c, int r);
 unsigned int* comm_counter(Comm* c, int slot, int r);
 unsigned int* comm_local_counter(Comm* c, int slot);
 unsigned long long comm_wait_limit_ns(const Comm* c);
-// A counter the pipelined forward advances once per call (identical on all
-// ranks, which make the same calls), from which flag values derive.
+// A counter the pipelined forward advances once per call after reserving
+// the arena (identical on all ranks, which make the same calls), from which
+// the counters' targets derive; it restarts with every new arena.
 uint32_t comm_next_round(Comm* c);
 int allreduce_max_f32(Comm* c, float* buf, size_t n, cudaStream_t stream);
 int allreduce_sum_i32(Comm* c, int32_t* buf, size_t n, cudaStream_t stream);

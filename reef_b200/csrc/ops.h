@@ -236,7 +236,8 @@ int signal_peers(const PeerFlags& f, cudaStream_t stream);
 // target[i] (wrap-around >=, as the counters only grow), or until `limit_ns`
 // of %globaltimer pass, in which case it records kDevTimeoutPeer in the
 // device error word and returns, so no wait outlives its limit (the host
-// reads REEF_B200_ERR_TIMEOUT).
+// reads REEF_B200_ERR_TIMEOUT).  While the word holds kDevTimeoutPeer (until
+// the host reads it), later waits return at once.
 constexpr int kMaxWaits = 8;
 struct CounterWaits {
   int n = 0;

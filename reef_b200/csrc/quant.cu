@@ -165,7 +165,11 @@ __global__ void signal_peers_kernel(PeerFlags f) {
 // Lanes [0, f.n) signal after the system-wide fence (every earlier kernel on
 // the stream has finished); lanes [0, w.n) then wait on their counter, each
 // with its own deadline.  The increments come first so that two ranks that
-// each signal and then wait for the other cannot both wait.
+// each signal and then wait for the other cannot both wait.  Once a wait on
+// this device has given up (the error word holds kDevTimeoutPeer until the
+// host reads it), the ranks are out of step and every later wait would run
+// out too: those return at once, so a dead peer costs one deadline, not one
+// per step.
 __global__ void signal_and_wait_kernel(PeerFlags f, CounterWaits w, unsigned long long limit_ns,
                                        int* err) {
   if (f.n > 0) {
@@ -181,9 +185,12 @@ __global__ void signal_and_wait_kernel(PeerFlags f, CounterWaits w, unsigned lon
     unsigned int v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(w.p[i]) : "memory");
     if (static_cast<int>(v - target) >= 0) break;
-    if ((++spin & 63u) == 0 && globaltimer() - start > limit_ns) {
-      record_error(err, kDevTimeoutPeer);
-      break;
+    if ((++spin & 63u) == 0) {
+      if (err != nullptr && *reinterpret_cast<volatile int*>(err) == kDevTimeoutPeer) break;
+      if (globaltimer() - start > limit_ns) {
+        record_error(err, kDevTimeoutPeer);
+        break;
+      }
     }
     __nanosleep(32);
   }

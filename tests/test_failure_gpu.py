@@ -6,6 +6,7 @@ the context stays usable (a W8A8 linear right after is still bit-exact with
 the oracle).
 """
 import ctypes as C
+import time
 
 import numpy as np
 import pytest
@@ -63,3 +64,21 @@ def test_peer_counter_wait_times_out_and_context_survives():
                       torch.from_numpy(ws).cuda())
     want = ro.linear_w8a8(x, w, ws)
     np.testing.assert_array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_peer_wait_after_a_timeout_returns_at_once():
+    """Once a peer wait has given up (0x106 in the error word, not yet read),
+    later waits return at once instead of each running out its own limit: a
+    wait with a 1.5 s limit on a counter nothing increments ends in well
+    under that."""
+    assert device_error() == 0
+    stream = torch.cuda.current_stream().cuda_stream
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.call("reef_b200_selftest_peer_wait_timeout", 2000, counter.data_ptr(), 1, stream)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    _lib.call("reef_b200_selftest_peer_wait_timeout", 1500000, counter.data_ptr(), 1, stream)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 0.5
+    assert device_error() == 0x106
+    assert device_error() == 0
