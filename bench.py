@@ -711,14 +711,17 @@ def run_reef(args) -> int:
     out["decode_step"] = dstep
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(s, host_threads())
+    if rank == 0:  # the line first: teardown cannot take it away
+        emit(out)
     if comm is not None:
         torch.cuda.synchronize(dev)
-        comm.close()
+        try:
+            comm.close()
+        except Exception as e:  # noqa: BLE001
+            print(f"rank {rank}: communicator teardown: {e}", file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    if rank == 0:
-        emit(out)
     return 0
 
 
