@@ -462,7 +462,10 @@ size_t reef_b200_comm_unique_id_bytes(void);
 int reef_b200_comm_unique_id(void* id, size_t bytes);
 int reef_b200_comm_init(int rank, int world, const void* id, double timeout_s,
                         reef_b200_comm** comm);
-/* Finalizes and frees; REEF_B200_ERR_TIMEOUT (and an abort) when peers stall. */
+/* Finalizes and frees; collective (every rank calls it).  When a pipelined
+ * forward has made the peer-mapped arena, the ranks first drop their
+ * mappings and meet at a barrier, so no rank frees memory a peer still maps.
+ * REEF_B200_ERR_TIMEOUT (and an abort) when peers stall past the timeout. */
 int reef_b200_comm_destroy(reef_b200_comm* comm);
 /* Frees without waiting for peers (after a peer failed). */
 int reef_b200_comm_abort(reef_b200_comm* comm);
