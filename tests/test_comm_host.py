@@ -40,9 +40,11 @@ from reef_b200 import build
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def _build_and_run(tmp_path, name: str, sources: list[str]) -> set[str]:
+def _build_and_run(tmp_path, name: str, sources: list[str], sanitize: bool = False) -> set[str]:
     """Compile `sources` with the fakes into one program, run it, and return
-    the names of its passing cases."""
+    the names of its passing cases.  sanitize: AddressSanitizer, so a copy
+    outside a host buffer (a collective into a mis-sized workspace region)
+    fails the run."""
     cuda_inc = os.path.join(build.CUDA, "include")
     nccl_inc, _ = build._nccl_dirs()
     if shutil.which("g++") is None or not os.path.isfile(os.path.join(cuda_inc, "cuda_runtime.h")) \
@@ -52,9 +54,12 @@ def _build_and_run(tmp_path, name: str, sources: list[str]) -> set[str]:
     cmd = ["g++", "-std=c++20", "-O1", "-pthread", "-Wall", "-Werror=return-type",
            f"-I{os.path.join(build.ROOT, 'include')}", f"-I{build.CSRC}", f"-I{cuda_inc}",
            f"-I{nccl_inc}", *sources, os.path.join(HERE, "host", "fake_cuda_nccl.cpp"), "-o", exe]
+    if sanitize:
+        cmd.insert(1, "-fsanitize=address")
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-4000:]
-    r = subprocess.run([exe], capture_output=True, text=True, timeout=180)
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=0")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=180, env=env)
     assert r.returncode == 0, r.stdout + r.stderr[-4000:]
     return {line[3:] for line in r.stdout.splitlines() if line.startswith("ok ")}
 
@@ -69,5 +74,5 @@ def test_pipelined_forward_schedule(tmp_path):
     passed = _build_and_run(tmp_path, "layer_host_test", [
         os.path.join(build.CSRC, "layer.cpp"), os.path.join(build.CSRC, "comm.cpp"),
         os.path.join(HERE, "host", "fake_ops.cpp"),
-        os.path.join(HERE, "host", "layer_host_test.cpp")])
+        os.path.join(HERE, "host", "layer_host_test.cpp")], sanitize=True)
     assert passed == {"world 2", "world 4", "world 8"}
