@@ -13,6 +13,8 @@
 //   layer at 2 chunks (a larger arena again), the all-reduce plan, the
 //   instrumented forward, and the first layer at 2 chunks once more (the arena
 //   is kept).
+// Then, on a new communicator per world size, the decode step under both
+// plans and reef's GPT-Neo block (other_drivers_case).
 // After each step: every forward returned OK, no counter wait ran out, and
 // each rank's local counters add up to what the forwards since the arena was
 // made must have signalled: every use of a region (per chunk: 4 int8
@@ -203,6 +205,70 @@ void world_case(int world) {
   CHECK_EQ(fake_live_allocations(), 0);
 }
 
+// The decode step (both plans) and reef's GPT-Neo block at TP = world on one
+// communicator: every call returns OK and every rank issues the same
+// collectives in the same order (the fake NCCL counts a mismatch as a
+// violation).
+void other_drivers_case(int world) {
+  std::vector<unsigned char> id(comm_unique_id_bytes());
+  fake_set_rank(0);
+  CHECK(comm_unique_id(id.data(), id.size()) == kOk);
+  std::vector<Comm*> comms(world, nullptr);
+  run_ranks(world, [&](int r) {
+    CHECK(comm_init(r, world, id.data(), 5.0, &comms[r]) == kOk);
+  });
+  for (Comm* c : comms)
+    if (c == nullptr) return;
+  const Shape d{1024, 16, 8, 2816, 8, 1};  // 8 sequences, one new token each
+  const size_t max_len = 256;
+  run_ranks(world, [&](int r) {
+    for (int mode : {REEF_B200_TP_ALLREDUCE, REEF_B200_TP_ALLGATHER}) {
+      const reef_b200_llama_layer L = layer_for(d, world, comms[r], mode);
+      const size_t ws = reef_b200_llama_decode_workspace_bytes(&L, max_len);
+      CHECK(ws != 0);
+      if (ws == 0) continue;
+      const size_t cache = L.batch * L.heads_kv * max_len;
+      std::vector<int8_t> kc(cache * 128), vc(cache * 128);
+      std::vector<float> ks(cache), vs(cache), x(L.batch * L.hidden), y(L.batch * L.hidden);
+      std::vector<int32_t> pos(L.batch, 7);
+      void* w = std::aligned_alloc(256, (ws + 255) / 256 * 256);
+      for (int step = 0; step < 3; ++step)
+        CHECK_EQ(reef_b200_llama_decode_forward(&L, x.data(), y.data(), pos.data(), kc.data(),
+                                                ks.data(), vc.data(), vs.data(), max_len, w, ws,
+                                                nullptr),
+                 0);
+      std::free(w);
+    }
+    // GPT-Neo (config 2's widths): heads split over the ranks
+    reef_b200_gptneo_block B{};
+    B.seq = 128;
+    B.hidden = 256;
+    B.heads = 8 / world;
+    B.head_dim = 32;
+    B.ffn = 1024 / world;
+    B.window = 0;
+    B.eps = 1e-5f;
+    const auto* f = reinterpret_cast<const float*>(g_dummy);
+    const auto* w8 = reinterpret_cast<const int8_t*>(g_dummy);
+    B.ln1_g = B.ln1_b = B.ln2_g = B.ln2_b = f;
+    B.wq = B.wk = B.wv = B.wo = B.wfc = B.wproj = w8;
+    B.sq = B.sk = B.sv = B.so = B.sfc = B.sproj = f;
+    B.bo = B.bfc = B.bproj = f;
+    B.comm = reinterpret_cast<reef_b200_comm*>(comms[r]);
+    const size_t ws = reef_b200_gptneo_block_workspace_bytes(&B);
+    CHECK(ws != 0);
+    if (ws == 0) return;
+    std::vector<float> x(B.seq * B.hidden), y(B.seq * B.hidden);
+    void* w = std::aligned_alloc(256, (ws + 255) / 256 * 256);
+    for (int k = 0; k < 2; ++k)
+      CHECK_EQ(reef_b200_gptneo_block_forward(&B, x.data(), y.data(), w, ws, nullptr), 0);
+    std::free(w);
+  });
+  CHECK_EQ(fake_ops_timeouts(), 0);
+  run_ranks(world, [&](int r) { CHECK(comm_destroy(comms[r]) == kOk); });
+  CHECK_EQ(fake_violations(), 0);
+}
+
 }  // namespace
 
 int main() {
@@ -210,6 +276,11 @@ int main() {
     const int before = g_fail.load();
     world_case(world);
     if (g_fail.load() == before) std::printf("ok world %d\n", world);
+  }
+  for (int world : {2, 4, 8}) {
+    const int before = g_fail.load();
+    other_drivers_case(world);
+    if (g_fail.load() == before) std::printf("ok decode and gptneo world %d\n", world);
   }
   std::fflush(stdout);
   return g_fail.load() == 0 ? 0 : 1;

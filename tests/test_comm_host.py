@@ -21,6 +21,8 @@ deadline (tests/host/fake_ops.cpp, tests/host/layer_host_test.cpp): at world
 2 and then 4 chunks, the unpipelined one, a wider layer, the all-reduce plan,
 the instrumented forward and the first layer again; no counter wait may run
 out, and each rank's counters must add up to the signals those forwards send.
+The decode step under both plans and reef's GPT-Neo block run at the same
+world sizes, every rank issuing the same collectives in the same order.
 The communicator from before the arena fix (a new arena that kept counting
 forward rounds) makes these waits run out, as it stalled the tensor-parallel
 GPU test.
@@ -75,4 +77,5 @@ def test_pipelined_forward_schedule(tmp_path):
         os.path.join(build.CSRC, "layer.cpp"), os.path.join(build.CSRC, "comm.cpp"),
         os.path.join(HERE, "host", "fake_ops.cpp"),
         os.path.join(HERE, "host", "layer_host_test.cpp")], sanitize=True)
-    assert passed == {"world 2", "world 4", "world 8"}
+    assert passed == {"world 2", "world 4", "world 8", "decode and gptneo world 2",
+                      "decode and gptneo world 4", "decode and gptneo world 8"}
