@@ -531,6 +531,16 @@ def run_reef(args) -> int:
         dist.all_reduce(t_pre, op=dist.ReduceOp.MAX)
         n_pre = int(t_pre.item())
 
+    # The instrumented forwards' events (below), made before the timed region
+    # so that nothing idles the GPU between the two: torch makes a CUDA event
+    # at its first record.
+    n_inst = max(3, min(200, n_pre // 2))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(12)] for _ in range(n_inst)]
+    for row in evs:
+        for e in row:
+            e.record(stream)
+    handles = [(C.c_void_p * 10)(*[e.cuda_event for e in row[1:11]]) for row in evs]
+
     # The timed region: K forwards through the public entry point.  A second
     # of the same forward runs just before it, so that the clock samples
     # (one per 50 ms) cover sustained load even when the region is short.
@@ -551,31 +561,52 @@ def run_reef(args) -> int:
     t_end.record(stream)
     torch.cuda.synchronize(dev)
     w1 = time.time()
+    K.check_device_error()
+    ms = t_start.elapsed_time(t_end) / K_steps
+
+    # Per-kernel spans (QKV, flash, o-proj, gate/up, down) from the
+    # instrumented forward, which runs its steps in sequence.  They run right
+    # after the timed region, with no idle time between (an idle GPU leaves
+    # the power cap and boosts its clock), for about half a second, with the
+    # clock still sampled, so the spans are taken under the same load as the
+    # timed forwards.  n_pre is the same on every rank, so is n_inst.
+    wi0 = time.time()
+    for k in range(n_inst):
+        evs[k][0].record(stream)
+        _lib.call("reef_b200_llama_layer_forward_events", C.byref(L.desc), x.data_ptr(),
+                  y.data_ptr(), L.workspace.data_ptr(), L.workspace.numel(), handles[k],
+                  stream.cuda_stream)
+        evs[k][11].record(stream)
+    torch.cuda.synchronize(dev)
+    wi1 = time.time()
     barrier()
     time.sleep(0.25)
     clocks.stop()
     K.check_device_error()
-    ms = t_start.elapsed_time(t_end) / K_steps
-
-    # per-kernel spans (QKV, flash, o-proj, gate/up, down) from the
-    # instrumented forward, which runs its steps in sequence
-    n_inst = max(3, min(K_steps, 10))
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(10)] for _ in range(n_inst)]
-    for row in evs:
-        for e in row:
-            e.record(stream)
-    torch.cuda.synchronize(dev)
-    handles = [(C.c_void_p * 10)(*[e.cuda_event for e in row]) for row in evs]
-    for k in range(n_inst):
-        _lib.call("reef_b200_llama_layer_forward_events", C.byref(L.desc), x.data_ptr(),
-                  y.data_ptr(), L.workspace.data_ptr(), L.workspace.numel(), handles[k],
-                  stream.cuda_stream)
-    torch.cuda.synchronize(dev)
-    K.check_device_error()
-    spans = [[row[2 * i].elapsed_time(row[2 * i + 1]) for i in range(5)] for row in evs]
+    spans = [[row[1 + 2 * i].elapsed_time(row[2 + 2 * i]) for i in range(5)] for row in evs]
     gemm_ms = statistics.mean(sum(r[i] for i in (0, 2, 3, 4)) for r in spans)
     flash_ms = statistics.mean(r[1] for r in spans)
     per_gemm = [statistics.mean(r[i] for r in spans) for i in (0, 2, 3, 4)]
+    instrumented = None
+    try:  # where the instrumented forward's time goes; never fails the line
+        names = ["qkv", "flash", "o_proj", "gate_up", "down"]
+        mean = lambda f: statistics.mean(f(row) for row in evs)
+        instrumented = {
+            "forwards": n_inst,
+            "forward_ms": mean(lambda r: r[0].elapsed_time(r[11])),
+            "spans_ms": {nm: statistics.mean(sp[i] for sp in spans)
+                         for i, nm in enumerate(names)},
+            "before_qkv_ms": mean(lambda r: r[0].elapsed_time(r[1])),
+            "between_ms": {f"{names[i]}->{names[i + 1]}":
+                           mean(lambda r, i=i: r[2 + 2 * i].elapsed_time(r[3 + 2 * i]))
+                           for i in range(4)},
+            "after_down_ms": mean(lambda r: r[10].elapsed_time(r[11])),
+            "clocks": clocks.summary(wi0, wi1),
+            "note": "same kernels as the timed forward, an event pair around each GEMM and "
+                    "flash; run right after the timed region under the same load",
+        }
+    except Exception as e:  # noqa: BLE001
+        instrumented = {"error": str(e)[:200]}
 
     # end to end through the C ABI with host buffers: step i copies x in on
     # s_in, runs the forward on `stream` and reads y back on s_out; buffers
@@ -695,6 +726,7 @@ def run_reef(args) -> int:
                 "ms_per_step": e2e_ms},
         "gpu_launches": int(launches) * K_steps,
         "tp_bit_identical": tp_ok,
+        "instrumented_forward": instrumented,
         "exchange": exchange_bytes(s, T, world, args.tp_mode, ms),
         "clocks": dict(clocks.summary(w0, w1),
                        window="the timed region and the 1 s of the same forward just before it"),
