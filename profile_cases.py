@@ -165,6 +165,8 @@ def layer_timing(batch: int, steps: int) -> None:
     rows = []
     for _ in range(steps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(10)]
+        for e in ev:  # torch makes the CUDA event at its first record
+            e.record()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record()
