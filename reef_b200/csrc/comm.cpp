@@ -226,7 +226,6 @@ cudaStream_t comm_stream(const Comm* c) { return c ? c->stream : nullptr; }
 cudaStream_t comm_compute_stream(const Comm* c, int i) {
   return (c && i >= 0 && i < kComputeStreams) ? c->compute[i] : nullptr;
 }
-int comm_ctas(const Comm* c) { return c ? c->ctas : 0; }
 
 int allreduce_max_f32(Comm* c, float* buf, size_t n, cudaStream_t stream) {
   if (c == nullptr || c->world == 1 || n == 0) return kOk;

@@ -15,10 +15,10 @@ int comm_abort(Comm* c);
 int comm_rank(const Comm* c);
 int comm_world(const Comm* c);
 // The communicator's own stream (high priority) for collectives that overlap
-// compute, and the SMs its kernels may occupy (NCCL's maxCTAs): a compute
-// kernel meant to run beside them leaves that many SMs free.
+// compute.  NCCL's kernels are capped at a few CTAs (maxCTAs: 8 at 2 ranks, 16
+// above; REEF_B200_NCCL_CTAS overrides), so they leave the GPU's other SMs to
+// the layer's kernels.
 cudaStream_t comm_stream(const Comm* c);
-int comm_ctas(const Comm* c);
 // Compute streams for work pipelined against the collectives (kComputeStreams).
 constexpr int kComputeStreams = 4;
 cudaStream_t comm_compute_stream(const Comm* c, int i);

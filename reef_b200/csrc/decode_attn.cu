@@ -726,19 +726,6 @@ __global__ void decode_rope_append_kernel(int batch, int hq, int hkv, int max_le
 
 }  // namespace
 
-int decode_rope_append(int batch, int heads_q, int heads_kv, int max_len, float rope_base,
-                       const int* positions, const float* qkv, int8_t* q8, float* q_scale,
-                       int8_t* k_cache, float* k_scale, int8_t* v_cache, float* v_scale, int* lens,
-                       cudaStream_t stream) {
-  const long long warps = static_cast<long long>(batch) * (heads_q + 2 * heads_kv);
-  return launch_k(decode_rope_append_kernel<false>,
-                  dim3(static_cast<unsigned>((warps * 32 + 255) / 256)), dim3(256), 0, stream,
-                  batch, heads_q, heads_kv, max_len, rope_base, positions, qkv,
-                  static_cast<const int32_t*>(nullptr), 1, static_cast<const float*>(nullptr),
-                  static_cast<const float*>(nullptr), q8, q_scale, k_cache, k_scale, v_cache,
-                  v_scale, lens, device_error_ptr());
-}
-
 int decode_rope_append_partials(int batch, int heads_q, int heads_kv, int max_len,
                                 float rope_base, const int* positions, const int32_t* part,
                                 int splits, const float* x_scale, const float* w_scale,

@@ -8,9 +8,8 @@
 // GEMM inputs follow reef's rule exactly.
 //
 //   rmsnorm_quant   y = x * (1 / sqrt(mean(x^2) + eps)) * gain  -> int8 + scale
-//   swiglu_quant    y = silu(gate) * up = gate / (1 + e^-gate) * up -> int8 + scale
-//   swiglu_absmax   max |silu(gate) * up| per row (the tensor-parallel shard's
-//                   partial maximum, all-reduced before swiglu_quant)
+//   swiglu_partials y = silu(gate) * up = gate / (1 + e^-gate) * up on the decode
+//                   gate/up GEMM's split-K partials -> int8 + scale
 // One CTA per row; the row stays in registers between the reduction and the
 // quantisation, so each input is read from HBM once.
 #include "common.cuh"
@@ -375,52 +374,6 @@ __global__ void __launch_bounds__(kChunks * 32)
   }
 }
 
-// gu [rows][2*ffn]: gate in [0, ffn), up in [ffn, 2 ffn).  ffn % 4 == 0.
-// row_max == nullptr: quantise with this row's own maximum; else with the
-// given (all-reduced) maximum.
-template <int CACHE>
-__global__ void __launch_bounds__(kThreads)
-    swiglu_quant_kernel(int ffn, const float* __restrict__ gu, const float* __restrict__ row_max,
-                        int8_t* __restrict__ xq, long long ldq, float* __restrict__ xs) {
-  __shared__ float red[32];
-  const long long row = blockIdx.x;
-  const float4* g4 = reinterpret_cast<const float4*>(gu + row * 2 * ffn);
-  const float4* u4 = g4 + (ffn >> 2);
-  const int n4 = ffn >> 2;
-  float4 c[CACHE];
-  float m = 0.0f;
-#pragma unroll
-  for (int i = 0; i < CACHE; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
-    if (idx < n4) {
-      c[i] = swiglu4(__ldg(g4 + idx), __ldg(u4 + idx));
-      m = fmaxf(m, amax4(c[i]));
-    }
-  }
-  const float mx = row_max != nullptr ? row_max[row] : block_max(m, red);
-  const float scale = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
-  if (threadIdx.x == 0) xs[row] = scale;
-  char4* out = reinterpret_cast<char4*>(xq + row * ldq);
-#pragma unroll
-  for (int i = 0; i < CACHE; ++i) {
-    const int idx = threadIdx.x + i * kThreads;
-    if (idx < n4) out[idx] = q8x4(c[i], scale);
-  }
-}
-
-__global__ void __launch_bounds__(kThreads)
-    swiglu_absmax_kernel(int ffn, const float* __restrict__ gu, float* __restrict__ row_max) {
-  __shared__ float red[32];
-  const long long row = blockIdx.x;
-  const float4* g4 = reinterpret_cast<const float4*>(gu + row * 2 * ffn);
-  const float4* u4 = g4 + (ffn >> 2);
-  float m = 0.0f;
-  for (int idx = threadIdx.x; idx < (ffn >> 2); idx += kThreads)
-    m = fmaxf(m, amax4(swiglu4(__ldg(g4 + idx), __ldg(u4 + idx))));
-  m = block_max(m, red);
-  if (threadIdx.x == 0) row_max[row] = m;
-}
-
 // SwiGLU on the split-K partials of the gate/up projection (one CTA per
 // row): g and u are the W8A8 epilogue values of columns n and ffn + n
 // (float(sum) * (x_scale * w_scale), linear.hpp:125-127), h = silu_mul(g, u)
@@ -491,17 +444,6 @@ static int cache_for(int n4) {
     if (per <= c) return c;
   return 0;
 }
-
-#define REEF_DISPATCH_CACHE(c, KERNEL, ...)                                   \
-  switch (c) {                                                              \
-    case 1: KERNEL<1><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
-    case 2: KERNEL<2><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
-    case 4: KERNEL<4><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
-    case 6: KERNEL<6><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
-    case 8: KERNEL<8><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break;   \
-    case 12: KERNEL<12><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break; \
-    default: KERNEL<16><<<grid, kThreads, 0, stream>>>(__VA_ARGS__); break; \
-  }
 
 static int per_thread(int width) {  // float4 per thread in the chunked RMSNorm
   const int n4 = width / (4 * kChunks);
@@ -574,17 +516,6 @@ int rms_apply_quant(long long rows, int width, int ranks, float eps, const float
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
-int swiglu_quant(long long rows, int ffn, const float* gu, const float* row_max, int8_t* x_q,
-                 float* x_scale, cudaStream_t stream) {
-  if (rows == 0) return kOk;
-  const int c = cache_for(ffn / 4);
-  if (ffn <= 0 || ffn % 4 != 0 || c == 0) return kErrInvalid;
-  const unsigned grid = static_cast<unsigned>(rows);
-  REEF_DISPATCH_CACHE(c, swiglu_quant_kernel, ffn, gu, row_max, x_q,
-                      static_cast<long long>(ffn), x_scale);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
-}
-
 int swiglu_partials(long long rows, int ffn, const int32_t* part, int splits, const float* x_scale,
                     const float* w_scale, const float* row_max_in, float* row_max_out,
                     int8_t* x_q, float* q_scale, cudaStream_t stream) {
@@ -610,13 +541,6 @@ int swiglu_partials(long long rows, int ffn, const int32_t* part, int splits, co
     default: REEF_SWIGLU_PARTIALS(16);
   }
 #undef REEF_SWIGLU_PARTIALS
-}
-
-int swiglu_absmax(long long rows, int ffn, const float* gu, float* row_max, cudaStream_t stream) {
-  if (rows == 0) return kOk;
-  if (ffn <= 0 || ffn % 4 != 0) return kErrInvalid;
-  swiglu_absmax_kernel<<<static_cast<unsigned>(rows), kThreads, 0, stream>>>(ffn, gu, row_max);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 }  // namespace reef

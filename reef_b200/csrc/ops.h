@@ -229,7 +229,6 @@ struct PeerFlags {
   int n = 0;
   unsigned int* p[kMaxFlags] = {};
 };
-int signal_peers(const PeerFlags& f, cudaStream_t stream);
 
 // Local counters a stream waits on before its next kernels: lane i of one
 // warp spins (system-scope acquire loads) until counter p[i] reaches
@@ -244,7 +243,7 @@ struct CounterWaits {
   const unsigned int* p[kMaxWaits] = {};
   unsigned int target[kMaxWaits] = {};
 };
-// One launch: signal `f` (fence, then the increments, as signal_peers), then
+// One launch: signal `f` (a system-wide fence, then the increments), then
 // wait for `w`.  Either may be empty; nothing is launched when both are.
 int signal_and_wait(const PeerFlags& f, const CounterWaits& w, unsigned long long limit_ns,
                     cudaStream_t stream);
@@ -327,10 +326,6 @@ int reduce_rmsnorm_quant(long long rows, int width, int splits, const int32_t* p
 int swiglu_partials(long long rows, int ffn, const int32_t* part, int splits, const float* x_scale,
                     const float* w_scale, const float* row_max_in, float* row_max_out,
                     int8_t* x_q, float* q_scale, cudaStream_t stream);
-int swiglu_quant(long long rows, int ffn, const float* gu, const float* row_max, int8_t* x_q,
-                 float* x_scale, cudaStream_t stream);
-int swiglu_absmax(long long rows, int ffn, const float* gu, float* row_max,
-                  cudaStream_t stream);
 // TP-sharded RMSNorm (columns split over `ranks`): per-rank stats, all-gather,
 // then quantise this rank's columns with the full row's scale.
 // stats and x_q go to every destination of their PeerDst (x_scale is local).
@@ -402,13 +397,11 @@ struct DecodeProblem {
   float* out;             // [B][Hq][128]
 };
 size_t decode_attn_partial_floats(int batch, int heads_q, int max_len);
-int decode_rope_append(int batch, int heads_q, int heads_kv, int max_len, float rope_base,
-                       const int* positions, const float* qkv, int8_t* q8, float* q_scale,
-                       int8_t* k_cache, float* k_scale, int8_t* v_cache, float* v_scale, int* lens,
-                       cudaStream_t stream);
-// decode_rope_append on the QKV projection's split-K partials (the skinny
-// GEMM's token-major int32 sums, gemm_i8_skinny_partials), summed and
-// dequantised here: the same outputs, without a separate reduce.
+// The decode step's q / k / v from the QKV projection's split-K partials (the
+// skinny GEMM's token-major int32 sums, gemm_i8_skinny_partials), summed and
+// dequantised here, so no separate reduce runs: RoPE at each sequence's
+// position, q quantised per head into q8 / q_scale, k and v quantised per head
+// and appended to the cache at row positions[b], lens[b] = positions[b] + 1.
 int decode_rope_append_partials(int batch, int heads_q, int heads_kv, int max_len,
                                 float rope_base, const int* positions, const int32_t* part,
                                 int splits, const float* x_scale, const float* w_scale,

@@ -155,15 +155,9 @@ __global__ void __launch_bounds__(kQuantThreads)
     for (int d = 0; d < out.n; ++d) static_cast<float*>(out.p[d])[blockIdx.x] = m;
 }
 
-// Every earlier kernel on the stream has finished; the fence orders their
-// stores (peer stores included) before the increments.
-__global__ void signal_peers_kernel(PeerFlags f) {
-  __threadfence_system();
-  for (int i = threadIdx.x; i < f.n; i += blockDim.x) atomicAdd_system(f.p[i], 1u);
-}
-
 // Lanes [0, f.n) signal after the system-wide fence (every earlier kernel on
-// the stream has finished); lanes [0, w.n) then wait on their counter, each
+// the stream has finished, and the fence orders their stores, peer stores
+// included, before the increments); lanes [0, w.n) then wait on their counter, each
 // with its own deadline.  The increments come first so that two ranks that
 // each signal and then wait for the other cannot both wait.  Once a wait on
 // this device has given up (the error word holds kDevTimeoutPeer until the
@@ -308,15 +302,6 @@ int quantize_rows_to(long long rows, long long in, const float* x, const PeerDst
   for (int d = 0; d < x_q.n; ++d)
     if (reinterpret_cast<uintptr_t>(x_q.p[d]) % 4 != 0) return kErrInvalid;
   return quantize_vec4(rows, in, x, x_q, ldq, x_scale, row_max, stream);
-}
-
-int signal_peers(const PeerFlags& f, cudaStream_t stream) {
-  if (f.n == 0) return kOk;
-  if (f.n < 0 || f.n > kMaxFlags) return kErrInvalid;
-  for (int i = 0; i < f.n; ++i)
-    if (f.p[i] == nullptr) return kErrInvalid;
-  signal_peers_kernel<<<1, 32, 0, stream>>>(f);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int signal_and_wait(const PeerFlags& f, const CounterWaits& w, unsigned long long limit_ns,
