@@ -539,9 +539,10 @@ typedef struct reef_b200_llama_layer {
  *    groups of whole sequences, the forward pipelines over them on the
  *    communicator's compute streams, one group a step behind the other; the
  *    kernels that produce exchanged data write it into every rank's memory
- *    over NVLink, and stream-ordered counters in a symmetric arena say when it
- *    has arrived and been consumed (same result; `stream` still orders
- *    everything before the call's last kernel). */
+ *    over NVLink, and counters in a symmetric arena say when it has arrived
+ *    and been consumed; each wait on them is a spin on the device with the
+ *    communicator's timeout (same result; `stream` still orders everything
+ *    before the call's last kernel). */
 #define REEF_B200_TP_ALLREDUCE 0
 #define REEF_B200_TP_ALLGATHER 1
 
