@@ -76,6 +76,26 @@ def test_argument_validation_without_gpu(L):
     assert L.reef_b200_linear_w8a8_noalloc(256, 65536, 8, p, p, p, None, p, None) == 7
 
 
+def test_decode_tiles_and_peer_wait_validation_without_gpu(L):
+    p = C.c_void_p(16)
+    # the decode layout: one 16 KiB block (128 rows x 128 bytes of K) per tile,
+    # ragged edges rounded up to whole tiles
+    assert L.reef_b200_weight_tiles_bytes(1280, 8192) == 10 * 64 * 16384
+    assert L.reef_b200_weight_tiles_bytes(1, 1) == 16384
+    assert L.reef_b200_weight_tiles_bytes(129, 130) == 2 * 2 * 16384
+    assert L.reef_b200_weight_tiles_bytes(0, 8192) == 0
+    assert L.reef_b200_weight_tiles_bytes(1280, 0) == 0
+    # packing: no rows is a no-op; null pointers are invalid; the tiles'
+    # base must be 1024-byte aligned, as the header requires
+    assert L.reef_b200_pack_weight_tiles(0, 8192, p, p, None) == 0
+    assert L.reef_b200_pack_weight_tiles(128, 128, None, C.c_void_p(1024), None) == 1
+    assert L.reef_b200_pack_weight_tiles(128, 128, p, C.c_void_p(1024 + 16), None) == 2
+    # the cross-rank wait's self-test: a counter and a limit of 1 us .. 2 s
+    assert L.reef_b200_selftest_peer_wait_timeout(1000, None, 1, None) == 1
+    assert L.reef_b200_selftest_peer_wait_timeout(0, p, 1, None) == 1
+    assert L.reef_b200_selftest_peer_wait_timeout(2000001, p, 1, None) == 1
+
+
 def test_attention_validation_without_gpu(L):
     p = C.c_void_p(16)
     # a row that sees no key: query 9 at window 3 over 5 keys
