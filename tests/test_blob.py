@@ -134,3 +134,28 @@ def test_oracle_float_model_reproduces_reef_generation():
     got = BF.oracle_logits_f32(blob, seq)[prompt.size - 1:]
     np.testing.assert_array_equal(got.view(np.uint32), logits.view(np.uint32))
     assert [ro.argmax_f32(r) for r in got] == list(tokens)
+
+
+def test_reader_survives_corrupted_blobs(tmp_path):
+    """A blob is read from a file the caller may not control: corrupted ones
+    must end in an error status, never a read outside the blob or a write
+    outside the arena.  blob.cpp is compiled with AddressSanitizer over
+    host-side copies (tests/host/blob_fuzz_test.cpp) and fed the layer
+    fixture and both kGptNeo models (W8A8 and fp32): each must load intact,
+    then 4000 seeded corruptions each (header and layer-table fields set to
+    boundary and random values, truncations, flipped bytes) go through
+    read_info and, where it accepts them, the layer and model loads."""
+    import os
+
+    from reef_b200 import build
+    from tests.test_comm_host import HERE, _build_and_run
+    paths = [BF.BLOB]
+    for precision in ("w8a8", "fp32"):
+        blob, _, _, _ = BF.golden_model(precision)
+        p = tmp_path / f"kgptneo_{precision}.blob"
+        p.write_bytes(blob)
+        paths.append(str(p))
+    passed = _build_and_run(tmp_path, "blob_fuzz_test", [
+        os.path.join(build.CSRC, "blob.cpp"), os.path.join(HERE, "host", "blob_fuzz_test.cpp")],
+        sanitize=True, args=tuple(paths))
+    assert {line.split()[0] for line in passed} == set(paths)

@@ -42,7 +42,8 @@ from reef_b200 import build
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def _build_and_run(tmp_path, name: str, sources: list[str], sanitize: bool = False) -> set[str]:
+def _build_and_run(tmp_path, name: str, sources: list[str], sanitize: bool = False,
+                   args: tuple[str, ...] = ()) -> set[str]:
     """Compile `sources` with the fakes into one program, run it, and return
     the names of its passing cases.  sanitize: AddressSanitizer, so a copy
     outside a host buffer (a collective into a mis-sized workspace region)
@@ -57,11 +58,11 @@ def _build_and_run(tmp_path, name: str, sources: list[str], sanitize: bool = Fal
            f"-I{os.path.join(build.ROOT, 'include')}", f"-I{build.CSRC}", f"-I{cuda_inc}",
            f"-I{nccl_inc}", *sources, os.path.join(HERE, "host", "fake_cuda_nccl.cpp"), "-o", exe]
     if sanitize:
-        cmd.insert(1, "-fsanitize=address")
+        cmd.insert(1, "-fsanitize=address,undefined")
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-4000:]
     env = dict(os.environ, ASAN_OPTIONS="detect_leaks=0")
-    r = subprocess.run([exe], capture_output=True, text=True, timeout=180, env=env)
+    r = subprocess.run([exe, *args], capture_output=True, text=True, timeout=180, env=env)
     assert r.returncode == 0, r.stdout + r.stderr[-4000:]
     return {line[3:] for line in r.stdout.splitlines() if line.startswith("ok ")}
 
