@@ -320,13 +320,22 @@ size_t llama_ag_carve(const reef_b200_llama_layer* L, int world, void* ws, Llama
   return c.used + 256;
 }
 
+// Widths far above any model's, and small enough that no workspace size or
+// index built from them (tokens x width x 4 bytes) can overflow.
+int dims_in_range(size_t hidden, size_t ffn, size_t heads_a, size_t heads_b) {
+  if (hidden > (1u << 20) || ffn > (1u << 22) || heads_a > 4096 || heads_b > 4096)
+    return REEF_B200_ERR_INVALID;
+  return REEF_B200_OK;
+}
+
 int llama_check(const reef_b200_llama_layer* L) {
   if (L == nullptr) return REEF_B200_ERR_INVALID;
   if (L->batch == 0 || L->seq == 0 || L->hidden == 0 || L->heads_q == 0 || L->heads_kv == 0 ||
       L->ffn == 0 || L->head_dim != 128 || L->heads_q % L->heads_kv != 0 ||
       L->hidden % 16 != 0 || L->ffn % 16 != 0 || L->seq % 8 != 0 ||
-      L->batch * L->seq > (1u << 30))
+      L->batch > (1u << 30) || L->seq > (1u << 30) || L->batch * L->seq > (1u << 30))
     return REEF_B200_ERR_INVALID;
+  if (int rc = dims_in_range(L->hidden, L->ffn, L->heads_q, L->heads_kv)) return rc;
   if (!L->attn_norm || !L->w_qkv || !L->s_qkv || !L->w_o || !L->s_o || !L->mlp_norm ||
       !L->w_gu || !L->s_gu || !L->w_down || !L->s_down)
     return REEF_B200_ERR_INVALID;
@@ -386,6 +395,7 @@ int decode_check(const reef_b200_llama_layer* L, size_t max_len) {
       L->heads_kv == 0 || L->ffn == 0 || L->head_dim != 128 || L->heads_q % L->heads_kv != 0 ||
       L->hidden % 16 != 0 || L->ffn % 16 != 0)
     return REEF_B200_ERR_INVALID;
+  if (int rc = dims_in_range(L->hidden, L->ffn, L->heads_q, L->heads_kv)) return rc;
   const size_t g = L->heads_q / L->heads_kv;
   if (g != 1 && g != 2 && g != 4 && g != 8 && g != 16) return REEF_B200_ERR_INVALID;
   if (!L->attn_norm || !L->w_qkv || !L->s_qkv || !L->w_o || !L->s_o || !L->mlp_norm ||
@@ -444,6 +454,7 @@ int neo_check(const reef_b200_gptneo_block* B) {
   if (B->seq == 0 || B->hidden == 0 || B->heads == 0 || B->head_dim == 0 || B->ffn == 0 ||
       B->seq > static_cast<size_t>(kMaxKeysExact))
     return REEF_B200_ERR_INVALID;
+  if (int rc = dims_in_range(B->hidden, B->ffn, B->heads, B->head_dim)) return rc;
   if (!B->ln1_g || !B->ln2_g || !B->wq || !B->wk || !B->wv || !B->sq || !B->sk || !B->sv ||
       !B->wo || !B->so || !B->wfc || !B->sfc || !B->wproj || !B->sproj)
     return REEF_B200_ERR_INVALID;

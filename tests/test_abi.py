@@ -96,6 +96,41 @@ def test_decode_tiles_and_peer_wait_validation_without_gpu(L):
     assert L.reef_b200_selftest_peer_wait_timeout(2000001, p, 1, None) == 1
 
 
+def test_layer_shapes_are_bounded_without_gpu(L):
+    """The layer descriptions' workspace queries are arithmetic only: a
+    config-3 layer and config 2's GPT-Neo block get a size; widths past the
+    bounds, and a batch x seq whose product wraps around, get 0 (invalid)
+    instead of a wrapped-around, too small workspace."""
+    p = C.c_void_p(1 << 20)  # aligned, never dereferenced
+    ptrs = {f: p for f in ("attn_norm", "w_qkv", "s_qkv", "w_o", "s_o", "mlp_norm", "w_gu",
+                           "s_gu", "w_down", "s_down")}
+
+    def llama(**over):
+        kw = dict(batch=8, seq=2048, hidden=4096, heads_q=32, heads_kv=32, head_dim=128,
+                  ffn=11008, rms_eps=1e-5, rope_base=1e4, **ptrs)
+        kw.update(over)
+        return L.reef_b200_llama_layer_workspace_bytes(C.byref(_lib.LlamaLayerDesc(**kw)))
+
+    assert llama() > 0
+    assert llama(hidden=1 << 21) == 0
+    assert llama(ffn=1 << 23) == 0
+    assert llama(heads_q=8192, heads_kv=8192) == 0
+    assert llama(batch=1 << 62, seq=256) == 0  # 2^70 tokens wraps to 0 in 64 bits
+    assert llama(batch=1 << 20, seq=1 << 11) == 0  # 2^31 tokens
+
+    def neo(**over):
+        kw = dict(seq=128, hidden=256, heads=4, head_dim=64, ffn=1024, window=0, eps=1e-5)
+        kw.update({f: p for f in ("ln1_g", "ln1_b", "wq", "sq", "wk", "sk", "wv", "sv", "wo",
+                                  "so", "bo", "ln2_g", "ln2_b", "wfc", "sfc", "bfc", "wproj",
+                                  "sproj", "bproj")})
+        kw.update(over)
+        return L.reef_b200_gptneo_block_workspace_bytes(C.byref(_lib.GptNeoBlockDesc(**kw)))
+
+    assert neo() > 0
+    assert neo(hidden=1 << 21) == 0
+    assert neo(head_dim=8192) == 0
+
+
 def test_attention_validation_without_gpu(L):
     p = C.c_void_p(16)
     # a row that sees no key: query 9 at window 3 over 5 keys
