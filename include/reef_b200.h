@@ -500,11 +500,11 @@ int reef_b200_linear_w8a8_rowpar(reef_b200_comm* comm, size_t rows, size_t in_lo
  * Weights are this rank's shards, K-major; scales fp32.  Sizes are local
  * (heads_q, heads_kv, ffn = totals / TP degree); hidden is the full width. */
 typedef struct reef_b200_llama_layer {
-  size_t batch, seq;         /* tokens = batch * seq; seq % 8 == 0 */
-  size_t hidden;             /* model width, multiple of 16 */
-  size_t heads_q, heads_kv;  /* this rank's heads */
+  size_t batch, seq;         /* tokens = batch * seq <= 2^30; seq % 8 == 0 */
+  size_t hidden;             /* model width, multiple of 16, <= 2^20 */
+  size_t heads_q, heads_kv;  /* this rank's heads, <= 4096 each */
   size_t head_dim;           /* 128 */
-  size_t ffn;                /* this rank's FFN width, multiple of 16 */
+  size_t ffn;                /* this rank's FFN width, multiple of 16, <= 2^22 */
   float rms_eps, rope_base;
   const float* attn_norm;                       /* [hidden] */
   const int8_t* w_qkv; const float* s_qkv;      /* [(heads_q+2 heads_kv)*128][hidden] */
@@ -592,7 +592,8 @@ int reef_b200_llama_decode_forward(const reef_b200_llama_layer* layer, const flo
  * every TP degree.  heads / ffn are this rank's (column-parallel q/k/v by
  * heads and c_fc by columns; row-parallel o_proj and c_proj). */
 typedef struct reef_b200_gptneo_block {
-  size_t seq, hidden, heads, head_dim, ffn, window;
+  size_t seq, hidden, heads, head_dim, ffn, window;  /* hidden <= 2^20, heads and
+                                                       head_dim <= 4096, ffn <= 2^22 */
   float eps;
   const float* ln1_g; const float* ln1_b;       /* [hidden] */
   const int8_t* wq; const float* sq;            /* [heads*head_dim][hidden] */
