@@ -170,6 +170,76 @@ def test_w8a8_matches_engine(rows, k, n, seed):
     np.testing.assert_array_equal(bits(got), bits(want))
 
 
+def _sweep_activation(rng, rows: int, k: int) -> np.ndarray:
+    """Activations at the quantiser's hard cases: magnitudes from denormal to
+    1e3, exact zeros and negative zeros, all-zero rows, and rows whose scale
+    is a power of two with values at c + 1/2 exactly (ties to even)."""
+    x = (rng.standard_normal((rows, k)) * 10.0 ** rng.uniform(-6, 3, (rows, 1))).astype(np.float32)
+    x[rng.random((rows, k)) < 0.05] = 0.0
+    x[rng.random((rows, k)) < 0.02] = -0.0
+    x[rng.random((rows, k)) < 0.02] = np.float32(1e-40) * rng.choice([-1, 1])
+    for r in range(rows):
+        kind = rng.integers(0, 6)
+        if kind == 0:
+            x[r] = 0.0
+        elif kind == 1:  # scale 2^e: the maximum is 127 * 2^e, the rest ties
+            e = int(rng.integers(-20, 10))
+            codes = rng.integers(-126, 126, k).astype(np.float32) + 0.5
+            x[r] = np.ldexp(codes, e).astype(np.float32)
+            x[r, int(rng.integers(0, k))] = np.float32(np.ldexp(127.0, e)) * rng.choice([-1, 1])
+    return x
+
+
+@needs_ref
+def test_random_sweep_matches_engine():
+    """120 seeded random shapes (rows 1-24, in 1-300 around the 16-byte
+    padding edges, out 1-70) through quantize_rows, the W8A8 linear with and
+    without bias, the int8 linear (shift 1-31, int32 bias) and the int8
+    matmul: the restatement equals reef's engine bit for bit in every one."""
+    import ctypes as C
+    f32, i8, i32 = C.POINTER(C.c_float), C.POINTER(C.c_int8), C.POINTER(C.c_int32)
+    rng = np.random.default_rng(20261202)
+    R = ro.ref()
+    for case in range(120):
+        rows = int(rng.integers(1, 25))
+        k = int(rng.choice([1, 2, 15, 16, 17, 31, 33, 64, 127, 129, int(rng.integers(1, 301))]))
+        n = int(rng.integers(1, 71))
+        x = _sweep_activation(rng, rows, k)
+        wf = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+        # quantize_rows
+        q_want = np.empty((rows, k), np.int8)
+        s_want = np.empty(rows, np.float32)
+        assert R.ref_quantize_rows(rows, k, _c(x, f32), _c(q_want, i8), _c(s_want, f32)) == 0
+        q, sc = ro.quantize_rows(x)
+        np.testing.assert_array_equal(q, q_want, err_msg=f"case {case}")
+        np.testing.assert_array_equal(bits(sc), bits(s_want), err_msg=f"case {case}")
+        # the W8A8 linear, with and without bias
+        w, ws = ro.quantize_rows(wf)
+        b = (rng.standard_normal(n) * 0.02).astype(np.float32)
+        for bias in (None, b):
+            want = np.empty((rows, n), np.float32)
+            assert R.ref_linear_w8a8(rows, k, n, _c(x, f32), _c(w, i8), _c(ws, f32),
+                                     None if bias is None else _c(bias, f32),
+                                     _c(want, f32)) == 0
+            got = ro.linear_w8a8(x, w, ws, bias)
+            np.testing.assert_array_equal(bits(got), bits(want), err_msg=f"case {case}")
+        # the int8 linear and the exact int8 matmul
+        xi = rng.integers(-128, 128, (rows, k)).astype(np.int8)
+        wi = rng.integers(-128, 128, (n, k)).astype(np.int8)
+        shift = int(rng.integers(1, 32))
+        bi = rng.integers(-(1 << 20), 1 << 20, n).astype(np.int32)
+        for bias in (None, bi):
+            want8 = np.empty((rows, n), np.int8)
+            assert R.ref_linear_int8(rows, k, n, _c(xi, i8), _c(wi, i8), shift,
+                                     None if bias is None else _c(bias, i32),
+                                     _c(want8, i8)) == 0
+            np.testing.assert_array_equal(ro.linear_int8(xi, wi, shift, bias), want8,
+                                          err_msg=f"case {case}")
+        acc = np.empty((rows, n), np.int32)
+        assert R.ref_matmul_i8(rows, n, k, _c(xi, i8), _c(wi, i8), _c(acc, i32)) == 0
+        np.testing.assert_array_equal(ro.gemm_i8(xi, wi), acc, err_msg=f"case {case}")
+
+
 @needs_ref
 def test_attention_int8_matches_engine():
     import ctypes as C
