@@ -241,6 +241,54 @@ def test_random_sweep_matches_engine():
 
 
 @needs_ref
+def test_random_attention_sweep_matches_engine():
+    """160 seeded random heads, int8 and float: query and key lengths 1-70,
+    head dims 1-128, query offsets up to past the last key, windows from 1
+    to wider than the keys (0 = global), score and output shifts.  The
+    restatement equals reef's engine bit for bit, and refuses exactly the
+    configurations the engine refuses (a query row that sees no key)."""
+    import ctypes as C
+    f32, i8 = C.POINTER(C.c_float), C.POINTER(C.c_int8)
+    rng = np.random.default_rng(4096)
+    R = ro.ref()
+    refused = 0
+    for case in range(160):
+        ql, kl = int(rng.integers(1, 21)), int(rng.integers(1, 71))
+        d = int(rng.choice([1, 4, 8, 32, 64, 128, int(rng.integers(1, 129))]))
+        start = int(rng.integers(0, kl + 3))
+        window = int(rng.choice([0, 0, 1, 2, int(rng.integers(1, kl + 4))]))
+        if case % 2 == 0:
+            q = rng.integers(-128, 128, (ql, d)).astype(np.int8)
+            k = rng.integers(-128, 128, (kl, d)).astype(np.int8)
+            v = rng.integers(-128, 128, (kl, d)).astype(np.int8)
+            sh, osh = int(rng.integers(0, 17)), int(rng.integers(4, 13))
+            want = np.empty((ql, d), np.int8)
+            rc = R.ref_attend_head_int8(ql, kl, d, start, window, _c(q, i8), _c(k, i8),
+                                        _c(v, i8), sh, osh, _c(want, i8))
+            call = lambda: ro.attention_head_int8(q, k, v, start, window, sh, osh)
+        else:
+            scale = float(10.0 ** rng.uniform(-2, 1))
+            q = (rng.standard_normal((ql, d)) * scale).astype(np.float32)
+            k = (rng.standard_normal((kl, d)) * scale).astype(np.float32)
+            v = rng.standard_normal((kl, d)).astype(np.float32)
+            want = np.empty((ql, d), np.float32)
+            rc = R.ref_attend_head_f32(ql, kl, d, start, window, _c(q, f32), _c(k, f32),
+                                       _c(v, f32), _c(want, f32))
+            call = lambda: ro.attention_head_f32(q, k, v, start, window)
+        if rc != 0:
+            refused += 1
+            with pytest.raises(ValueError):
+                call()
+            continue
+        got = call()
+        if want.dtype == np.float32:
+            np.testing.assert_array_equal(bits(got), bits(want), err_msg=f"case {case}")
+        else:
+            np.testing.assert_array_equal(got, want, err_msg=f"case {case}")
+    assert 0 < refused < 80  # both kinds of configuration occurred
+
+
+@needs_ref
 def test_attention_int8_matches_engine():
     import ctypes as C
     i8 = C.POINTER(C.c_int8)
