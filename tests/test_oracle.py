@@ -325,6 +325,39 @@ def test_gptneo_block_matches_engine():
     np.testing.assert_array_equal(bits(got), bits(want))
 
 
+@needs_ref
+def test_random_block_sweep_matches_engine():
+    """Ten seeded random GPT-Neo W8A8 blocks: widths 32-96, head dims 8-32,
+    FFN widths not a multiple of 16, 1-24 positions, global and local
+    (windows 1, 3, 8) attention, and LayerNorm gains and shifts away from 1
+    and 0.  The restatement equals Block<float>::forward bit for bit."""
+    import ctypes as C
+    f = C.POINTER(C.c_float)
+    rng = np.random.default_rng(97)
+    for case in range(10):
+        d = int(rng.choice([32, 64, 96]))
+        hd = int(rng.choice([8, 16, 32]))
+        heads = d // hd
+        ffn = int(rng.choice([40, 72, 136, 4 * d]))
+        seq = int(rng.integers(1, 25))
+        local = int(rng.integers(0, 2))
+        window = int(rng.choice([1, 3, 8])) if local else 0
+        fw = block_float_weights(d, ffn, seed=300 + 20 * case)
+        for g in ("ln1_g", "ln2_g"):
+            fw[g] = (1.0 + 0.3 * rng.standard_normal(d)).astype(np.float32)
+        for b in ("ln1_b", "ln2_b"):
+            fw[b] = (0.1 * rng.standard_normal(d)).astype(np.float32)
+        x = (rng.standard_normal((seq, d)) * 2.0).astype(np.float32)
+        want = np.empty((seq, d), np.float32)
+        args = [fw[k] for k in ("ln1_g", "ln1_b", "wq", "wk", "wv", "wo", "bo",
+                                "ln2_g", "ln2_b", "wfc", "bfc", "wproj", "bproj")]
+        rc = ro.ref().ref_block_w8a8(seq, d, heads, ffn, window, local, np.float32(1e-5),
+                                     _c(x, f), *[_c(a, f) for a in args], _c(want, f))
+        assert rc == 0, f"case {case}"
+        got = ro.gptneo_block_w8a8(x, ro.quantize_block(fw), heads, window=window)
+        np.testing.assert_array_equal(bits(got), bits(want), err_msg=f"case {case}")
+
+
 def block_float_weights(d, ffn, seed):
     """Config-1 block weights: projections N(0, 0.02), biases N(0, 0.02),
     LayerNorm gains 1 and shifts 0."""
