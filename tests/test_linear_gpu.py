@@ -125,6 +125,38 @@ def test_int8_linear_matches_oracle(rows, k, n, shift):
     np.testing.assert_array_equal(got, want)
 
 
+def test_random_shapes_match_oracle():
+    """24 seeded random W8A8 shapes (rows 1-600, in 1-2100, out 1-700: both
+    the skinny and the persistent GEMM paths, partial tiles on every side),
+    each with and without bias, on activations with exact ties, zeros,
+    negative zeros, denormals and all-zero rows; and 12 int8 linears with
+    random shifts 0-31 and int32 biases.  Bit for bit against the oracle."""
+    from tests.test_oracle import _sweep_activation
+    rng = np.random.default_rng(31337)
+    for case in range(24):
+        rows = int(rng.integers(1, 601))
+        k = int(rng.integers(1, 2101))
+        n = int(rng.integers(1, 701))
+        x = _sweep_activation(rng, rows, k)
+        w, ws = ro.quantize_rows((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+        bias = (rng.standard_normal(n) * 0.02).astype(np.float32)
+        for b in (bias, None):
+            want = ro.linear_w8a8(x, w, ws, b)
+            got = host(K.linear_w8a8(dev(x), dev(padk(w)), dev(ws),
+                                     None if b is None else dev(b)))
+            np.testing.assert_array_equal(bits(got), bits(want),
+                                          err_msg=f"case {case}: {rows}x{k}x{n}")
+    for case in range(12):
+        rows, k, n = int(rng.integers(1, 300)), int(rng.integers(1, 1500)), int(rng.integers(1, 500))
+        shift = int(rng.integers(0, 32))
+        x = rng.integers(-128, 128, (rows, k)).astype(np.int8)
+        w = rng.integers(-128, 128, (n, k)).astype(np.int8)
+        bias = rng.integers(-(1 << 20), 1 << 20, n).astype(np.int32)
+        want = ro.linear_int8(x, w, shift, bias)
+        got = host(K.linear_int8(dev(padk(x)), dev(padk(w)), shift, dev(bias), in_features=k))
+        np.testing.assert_array_equal(got, want, err_msg=f"int8 case {case}: {rows}x{k}x{n}")
+
+
 @pytest.mark.parametrize("m,n,k", [(1, 8, 16), (128, 256, 128), (200, 300, 4096),
                                    (1000, 129, 28672)])
 def test_gemm_i32_matches_oracle(m, n, k):
