@@ -92,6 +92,48 @@ def test_attention_f32_matches_oracle(ql, kl, d, qs, win, sh):
     np.testing.assert_array_equal(bits(host(got)), bits(want))
 
 
+def test_random_heads_match_oracle():
+    """80 seeded random heads, int8 and float (query lengths 1-40, key
+    lengths 1-600, head dims 1-128, offsets past the last key, windows from 1
+    to wider than the keys, shifts): bit for bit against the oracle, and the
+    GPU entry points refuse exactly the configurations the oracle refuses
+    (a query row that sees no key)."""
+    from reef_b200._lib import ReefError
+    rng = np.random.default_rng(2718)
+    table = K.exp_table_device(ro.exp_table())
+    refused = 0
+    for case in range(80):
+        ql, kl = int(rng.integers(1, 41)), int(rng.integers(1, 601))
+        d = int(rng.choice([1, 8, 32, 64, 128, int(rng.integers(1, 129))]))
+        qs = int(rng.integers(0, kl + 3))
+        win = int(rng.choice([0, 0, 1, 2, int(rng.integers(1, kl + 4))]))
+        if case % 2 == 0:
+            q = rng.integers(-128, 128, (ql, d)).astype(np.int8)
+            k = rng.integers(-128, 128, (kl, d)).astype(np.int8)
+            v = rng.integers(-128, 128, (kl, d)).astype(np.int8)
+            sh, osh = int(rng.integers(0, 17)), int(rng.integers(4, 13))
+            oracle = lambda: ro.attention_head_int8(q, k, v, qs, win, sh, osh)
+            gpu = lambda: host(K.attention_head_int8(dev(q), dev(k), dev(v), qs, win, sh,
+                                                     table, osh))
+        else:
+            scale = float(10.0 ** rng.uniform(-2, 0.5))
+            q = (rng.standard_normal((ql, d)) * scale).astype(np.float32)
+            k = (rng.standard_normal((kl, d)) * scale).astype(np.float32)
+            v = rng.standard_normal((kl, d)).astype(np.float32)
+            oracle = lambda: ro.attention_head_f32(q, k, v, qs, win)
+            gpu = lambda: host(K.attention_head_f32(dev(q), dev(k), dev(v), qs, win))
+        try:
+            want = oracle()
+        except ValueError:
+            refused += 1
+            with pytest.raises(ReefError):
+                gpu()
+            continue
+        np.testing.assert_array_equal(bits(gpu()), bits(want),
+                                      err_msg=f"case {case}: {ql}x{kl}x{d} at {qs}, window {win}")
+    assert 0 < refused < 40
+
+
 def test_context_all_heads_config1_shape():
     """Attention::context at config 1: seq 128, 4 heads x 64, causal."""
     seq, dm, heads = 128, 256, 4
